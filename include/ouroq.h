@@ -1,0 +1,157 @@
+/*
+ * ouroq.h -- C ABI of the B200 (sm_100a) quantized-weight matmul path.
+ *
+ * This is the drop-in boundary for OuroborOS's packed-weight matmul operators.
+ * The reference calls them from Rust (crate ouro-cluster, cluster/src/infer/):
+ *
+ *   ops::matvec_q(payload, kind, out_len, in_len, x) -> Vec<f32>   ops.rs:76-84
+ *   ops::matmul_q(payload, kind, out_len, in_len, x[k][in], k)     ops.rs:219-230
+ *       -> y[k][out] ("column-major": y[c*out_len + r], ops.rs:158-161)
+ *   hadamard::rotate_fwd(x, signs, block) / rotate_inv             hadamard.rs:41-66
+ *   Stage::wm / wmat_batched (per named tensor, width check)       infer/mod.rs:138-167
+ *
+ * Plain C types only (no CUDA or torch types): streams are passed as void*
+ * holding a cudaStream_t, device buffers as plain pointers. Every function
+ * returns an ouroq_status; nothing throws or aborts across the ABI. A context
+ * is bound to one device and is not thread-safe: callers serialise, as the
+ * reference serialises calls through its per-process stage Mutex
+ * (agent/src/stage.rs:11-14).
+ *
+ * Formats accepted by ouroq_weight_upload (host layouts, row-major [M][*]):
+ *   OUROQ_FMT_TERNARY2   codes c = w + 1 in {0,1,2}, 4 per byte, element k of a
+ *                        row in byte k/4 bits 2*(k%4); one fp32 scale per tensor.
+ *   OUROQ_FMT_SIGN1G128  bit = 1 -> +1, bit = 0 -> -1, 8 per byte, element k in
+ *                        byte k/8 bit k%8; fp16 scales [M][K/128].
+ * Activation arithmetic for both: per-token absmax int8 (s_x = absmax/127,
+ * q = clamp(rint(x/s_x), -127, 127)), int32 accumulation, fp32 epilogue
+ *   ternary: y = ((float)acc * w_scale) * s_x
+ *   sign:    y = (sum over groups g ascending of (float)acc_g * scale_g) * s_x
+ */
+#ifndef OUROQ_H
+#define OUROQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OUROQ_ABI_VERSION 1
+
+typedef enum {
+  OUROQ_OK = 0,
+  OUROQ_ERR_BAD_SHAPE = 1,    /* dimensions not supported (reference: assert!/bail!) */
+  OUROQ_ERR_BAD_ALIGN = 2,    /* pointer not 16-byte aligned where required */
+  OUROQ_ERR_CUDA = 3,         /* CUDA runtime error; see ouroq_last_error */
+  OUROQ_ERR_NCCL = 4,         /* NCCL error in the sharded path */
+  OUROQ_ERR_TIMEOUT = 5,      /* a bounded device or collective wait expired */
+  OUROQ_ERR_UNSUPPORTED = 6,  /* format / batch combination not implemented */
+  OUROQ_ERR_BAD_ARG = 7,      /* null handle or pointer, bad enum value */
+  OUROQ_ERR_NO_DEVICE = 8,    /* no CUDA device / not sm_100 */
+  OUROQ_ERR_OOM = 9           /* device allocation failed */
+} ouroq_status;
+
+typedef enum {
+  OUROQ_FMT_TERNARY2 = 1,
+  OUROQ_FMT_SIGN1G128 = 2
+} ouroq_format;
+
+typedef struct ouroq_ctx ouroq_ctx;
+typedef struct ouroq_weight ouroq_weight;
+
+/* ---- library / context ---- */
+int ouroq_abi_version(void);
+const char *ouroq_status_string(ouroq_status s);
+
+/* Create a context on CUDA device `device` (sm_100 required). */
+ouroq_status ouroq_ctx_create(int device, ouroq_ctx **out);
+ouroq_status ouroq_ctx_destroy(ouroq_ctx *ctx);
+/* Text of the last error on this context ("" if none). Valid until the next call. */
+const char *ouroq_last_error(const ouroq_ctx *ctx);
+/* Read and clear the device status word that bounded in-kernel waits write on
+ * expiry (synchronises the device). OUROQ_ERR_TIMEOUT if a wait gave up. */
+ouroq_status ouroq_check_device(ouroq_ctx *ctx);
+/* Number of kernels this context has launched (for bench accounting). */
+uint64_t ouroq_launch_count(const ouroq_ctx *ctx);
+/* 1 = launch GEMV kernels with programmatic dependent launch (default), 0 = off. */
+ouroq_status ouroq_set_pdl(ouroq_ctx *ctx, int enable);
+
+/* ---- weights ----
+ * Upload a packed matrix (HOST pointers, canonical layout above) to device
+ * memory owned by the context, converting it to the device layout.
+ * Replaces the per-call borrowed payload of matvec_q (ops.rs:76) and the
+ * Weight{payload, kind, in_len, out_len} record (infer/mod.rs:95-100):
+ * M = out_len, K = in_len. K must be a multiple of 128.
+ *   TERNARY2:  scales = NULL, w_scale = per-tensor scale.
+ *   SIGN1G128: scales = uint16_t fp16 [M][K/128], w_scale ignored. */
+ouroq_status ouroq_weight_upload(ouroq_ctx *ctx, ouroq_format fmt, const void *packed, int M, int K,
+                                 const void *scales, float w_scale, ouroq_weight **out);
+/* Same, from DEVICE pointers holding the canonical layout. */
+ouroq_status ouroq_weight_upload_device(ouroq_ctx *ctx, ouroq_format fmt, const void *packed_dev,
+                                        int M, int K, const void *scales_dev, float w_scale,
+                                        ouroq_weight **out);
+ouroq_status ouroq_weight_free(ouroq_ctx *ctx, ouroq_weight *w);
+ouroq_status ouroq_weight_info(const ouroq_weight *w, int *fmt, int *M, int *K,
+                               size_t *device_bytes);
+
+/* ---- stream-ordered device API (all buffers DEVICE pointers) ---- */
+
+/* K1: per-token absmax int8 quantisation of x [B][K], optionally preceded by
+ * the blockwise rotation of hadamard::rotate_fwd (hadamard.rs:41-53) with
+ * `hadamard_block` (power of two 2..1024 dividing K; 0 = no rotation) and
+ * `signs` (fp32 +-1 [K], NULL = all +1). q [B][K] int8, s_x [B] fp32.
+ * x, q: 16-byte aligned; K multiple of 4 (of 32 when hadamard_block < 32). */
+ouroq_status ouroq_quantize_act(ouroq_ctx *ctx, const float *x, int B, int K, const float *signs,
+                                int hadamard_block, int8_t *q, float *s_x, void *stream);
+
+/* Grouped K1: quantise n (<= 8) independent activation sets in ONE launch.
+ * Set i: x[i] [B][K[i]] -> q[i] [B][K[i]], s_x[i] [B]; optional rotation per
+ * set (signs[i] nullable, blocks[i] = 0 for none). signs / blocks may be NULL. */
+ouroq_status ouroq_quantize_group(ouroq_ctx *ctx, int n, const float *const *x, const int *K,
+                                  const float *const *signs, const int *blocks, int B,
+                                  int8_t *const *q, float *const *s_x, void *stream);
+
+/* rotate_fwd (inverse = 0) / rotate_inv (inverse = 1) of hadamard.rs:41-66 on
+ * B rows of K floats; out may equal x. */
+ouroq_status ouroq_rotate(ouroq_ctx *ctx, const float *x, float *out, int B, int K,
+                          const float *signs, int block, int inverse, void *stream);
+
+/* y [B][M] = W . q for pre-quantised activations q [B][K] (16-byte aligned)
+ * and scales s_x [B]. acc_debug (nullable) receives the exact int32
+ * accumulators: TERNARY2 [B][M], SIGN1G128 [B][M][K/128]. */
+ouroq_status ouroq_gemm(ouroq_ctx *ctx, const ouroq_weight *w, const int8_t *q, const float *s_x,
+                        int B, float *y, int32_t *acc_debug, void *stream);
+
+/* Grouped GEMV: n (<= 8) independent products y_i = W_i . q_i in ONE launch.
+ * All weights share one format; B <= 8. Used for the projections of a layer. */
+ouroq_status ouroq_gemm_group(ouroq_ctx *ctx, int n, const ouroq_weight *const *w,
+                              const int8_t *const *q, const float *const *s_x, int B,
+                              float *const *y, void *stream);
+
+/* fp32 activations in, fp32 outputs out: quantise (with optional rotation)
+ * into context-owned scratch, then ouroq_gemm. Mirrors matvec_q / matmul_q's
+ * "f32 x in, f32 y out" contract on device buffers. */
+ouroq_status ouroq_gemm_f32act(ouroq_ctx *ctx, const ouroq_weight *w, const float *x, int B,
+                               const float *signs, int hadamard_block, float *y, void *stream);
+
+/* ---- host-buffer mirrors of the reference operators (synchronous) ---- */
+
+/* ops::matvec_q (ops.rs:76-84): x_host [K] fp32 -> y_host [M] fp32. */
+ouroq_status ouroq_matvec_q(ouroq_ctx *ctx, const ouroq_weight *w, const float *x_host,
+                            float *y_host);
+/* ops::matmul_q (ops.rs:219-230): x_host [k][K] -> y_host [k][M]
+ * (= the reference's y[c*out_len + r]). */
+ouroq_status ouroq_matmul_q(ouroq_ctx *ctx, const ouroq_weight *w, const float *x_host, int k,
+                            float *y_host);
+/* hadamard::rotate_fwd (hadamard.rs:41-53) in place on a host buffer of n floats. */
+ouroq_status ouroq_rotate_fwd(ouroq_ctx *ctx, float *x_host, const float *signs_host, size_t n,
+                              size_t block);
+/* hadamard::rotate_inv (hadamard.rs:57-66) in place on a host buffer. */
+ouroq_status ouroq_rotate_inv(ouroq_ctx *ctx, float *x_host, const float *signs_host, size_t n,
+                              size_t block);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OUROQ_H */

@@ -1,0 +1,301 @@
+"""ouroboros_b200 -- B200-native packed-weight matmul path of OuroborOS.
+
+Python mirror of the C ABI in include/ouroq.h, loaded from the in-tree
+libouroq.so with ctypes. The shipped compute path is the CUDA library; there
+is no CPU fallback: if the library is missing or no sm_100 device is present,
+every entry point raises.
+
+The operator names follow the reference's Rust API (crate ouro-cluster):
+  matvec_q   cluster/src/infer/ops.rs:76-84
+  matmul_q   cluster/src/infer/ops.rs:219-230  (output [k][out_len])
+  rotate_fwd cluster/src/infer/hadamard.rs:41-53
+  rotate_inv cluster/src/infer/hadamard.rs:57-66
+Errors raise OuroqError, the counterpart of the reference's assert!/bail!
+(hadamard.rs:33-37, infer/mod.rs:139-145).
+
+torch is used only to own device memory and streams (plumbing).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import numpy as np
+
+__all__ = [
+    "OuroqError", "Context", "Weight", "TERNARY2", "SIGN1G128", "load_library", "LIB_PATH",
+    "ABI_FUNCTIONS",
+]
+
+LIB_PATH = Path(__file__).resolve().parent / "libouroq.so"
+
+TERNARY2 = 1
+SIGN1G128 = 2
+
+OK = 0
+_STATUS = {
+    0: "ok", 1: "bad shape", 2: "bad alignment", 3: "cuda error", 4: "nccl error", 5: "timeout",
+    6: "unsupported", 7: "bad argument", 8: "no device", 9: "out of memory",
+}
+
+_p = ctypes.c_void_p
+_i = ctypes.c_int
+_f = ctypes.c_float
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); every function declared in include/ouroq.h
+ABI_FUNCTIONS = {
+    "ouroq_abi_version": (_i, []),
+    "ouroq_status_string": (ctypes.c_char_p, [_i]),
+    "ouroq_ctx_create": (_i, [_i, ctypes.POINTER(_p)]),
+    "ouroq_ctx_destroy": (_i, [_p]),
+    "ouroq_last_error": (ctypes.c_char_p, [_p]),
+    "ouroq_check_device": (_i, [_p]),
+    "ouroq_launch_count": (ctypes.c_uint64, [_p]),
+    "ouroq_set_pdl": (_i, [_p, _i]),
+    "ouroq_weight_upload": (_i, [_p, _i, _p, _i, _i, _p, _f, ctypes.POINTER(_p)]),
+    "ouroq_weight_upload_device": (_i, [_p, _i, _p, _i, _i, _p, _f, ctypes.POINTER(_p)]),
+    "ouroq_weight_free": (_i, [_p, _p]),
+    "ouroq_weight_info": (_i, [_p, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i),
+                               ctypes.POINTER(_sz)]),
+    "ouroq_quantize_act": (_i, [_p, _p, _i, _i, _p, _i, _p, _p, _p]),
+    "ouroq_quantize_group": (_i, [_p, _i, _p, _p, _p, _p, _i, _p, _p, _p]),
+    "ouroq_rotate": (_i, [_p, _p, _p, _i, _i, _p, _i, _i, _p]),
+    "ouroq_gemm": (_i, [_p, _p, _p, _p, _i, _p, _p, _p]),
+    "ouroq_gemm_group": (_i, [_p, _i, _p, _p, _p, _i, _p, _p]),
+    "ouroq_gemm_f32act": (_i, [_p, _p, _p, _i, _p, _i, _p, _p]),
+    "ouroq_matvec_q": (_i, [_p, _p, _p, _p]),
+    "ouroq_matmul_q": (_i, [_p, _p, _p, _i, _p]),
+    "ouroq_rotate_fwd": (_i, [_p, _p, _p, _sz, _sz]),
+    "ouroq_rotate_inv": (_i, [_p, _p, _p, _sz, _sz]),
+}
+
+_lib = None
+
+
+class OuroqError(RuntimeError):
+    def __init__(self, status: int, msg: str = ""):
+        self.status = status
+        super().__init__(f"{_STATUS.get(status, status)}: {msg}" if msg else _STATUS.get(status, str(status)))
+
+
+def load_library(path: str | os.PathLike | None = None) -> ctypes.CDLL:
+    """Load libouroq.so and declare every C-ABI signature. Raises if absent."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise OuroqError(6, f"{p} not built (run python -m ouroboros_b200.build)")
+    lib = ctypes.CDLL(str(p))
+    for name, (res, args) in ABI_FUNCTIONS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def _ptr(t) -> int | None:
+    """Device/host address of a torch tensor or numpy array (None passes through)."""
+    if t is None:
+        return None
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data
+    return t.data_ptr()
+
+
+def _stream_ptr(stream) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+class Weight:
+    """A packed matrix resident on the device (ouroq_weight handle)."""
+
+    def __init__(self, ctx: "Context", handle: int, fmt: int, M: int, K: int):
+        self.ctx, self.handle, self.fmt, self.M, self.K = ctx, handle, fmt, M, K
+        self.w_scale = 0.0
+
+    @property
+    def out_len(self) -> int:
+        return self.M
+
+    @property
+    def in_len(self) -> int:
+        return self.K
+
+    def device_bytes(self) -> int:
+        n = _sz()
+        self.ctx._check(self.ctx.lib.ouroq_weight_info(self.handle, None, None, None, ctypes.byref(n)))
+        return n.value
+
+    def free(self) -> None:
+        if self.handle:
+            self.ctx._check(self.ctx.lib.ouroq_weight_free(self.ctx.ctx, self.handle))
+            self.handle = None
+
+
+class Context:
+    """One ouroq context per CUDA device (not thread-safe, like the reference's stage slot)."""
+
+    def __init__(self, device: int = 0, lib_path=None):
+        self.lib = load_library(lib_path)
+        self.device = device
+        h = _p()
+        st = self.lib.ouroq_ctx_create(device, ctypes.byref(h))
+        if st != OK:
+            raise OuroqError(st, f"ouroq_ctx_create(device={device})")
+        self.ctx = h.value
+
+    # -- plumbing --
+    def _check(self, st: int) -> None:
+        if st != OK:
+            raise OuroqError(st, (self.lib.ouroq_last_error(self.ctx) or b"").decode())
+
+    def close(self) -> None:
+        if getattr(self, "ctx", None):
+            self.lib.ouroq_ctx_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def launch_count(self) -> int:
+        return int(self.lib.ouroq_launch_count(self.ctx))
+
+    def set_pdl(self, enable: bool) -> None:
+        self._check(self.lib.ouroq_set_pdl(self.ctx, 1 if enable else 0))
+
+    def check_device(self) -> None:
+        self._check(self.lib.ouroq_check_device(self.ctx))
+
+    # -- weights --
+    def upload(self, fmt: int, packed: np.ndarray, M: int, K: int, scales: np.ndarray | None = None,
+               w_scale: float = 1.0) -> Weight:
+        packed = np.ascontiguousarray(packed, dtype=np.uint8)
+        if scales is not None:
+            scales = np.ascontiguousarray(scales, dtype=np.uint16)
+        h = _p()
+        self._check(self.lib.ouroq_weight_upload(self.ctx, fmt, _ptr(packed), M, K, _ptr(scales),
+                                                 float(w_scale), ctypes.byref(h)))
+        w = Weight(self, h.value, fmt, M, K)
+        w.w_scale = float(w_scale)
+        return w
+
+    def upload_device(self, fmt: int, packed_dev, M: int, K: int, scales_dev=None,
+                      w_scale: float = 1.0) -> Weight:
+        h = _p()
+        self._check(self.lib.ouroq_weight_upload_device(self.ctx, fmt, _ptr(packed_dev), M, K,
+                                                        _ptr(scales_dev), float(w_scale),
+                                                        ctypes.byref(h)))
+        w = Weight(self, h.value, fmt, M, K)
+        w.w_scale = float(w_scale)
+        return w
+
+    # -- device API (torch CUDA tensors) --
+    def quantize_act(self, x, signs=None, hadamard_block: int = 0, q=None, s_x=None, stream=None):
+        import torch
+        B, K = x.shape
+        if q is None:
+            q = torch.empty((B, K), dtype=torch.int8, device=x.device)
+        if s_x is None:
+            s_x = torch.empty((B,), dtype=torch.float32, device=x.device)
+        self._check(self.lib.ouroq_quantize_act(self.ctx, _ptr(x), B, K, _ptr(signs), hadamard_block,
+                                                _ptr(q), _ptr(s_x), _stream_ptr(stream)))
+        return q, s_x
+
+    def quantize_group(self, xs, qs, sxs, signs=None, blocks=None, stream=None):
+        """One launch quantising several activation sets (same batch B)."""
+        n = len(xs)
+        B = xs[0].shape[0]
+        arr = lambda vals: (_p * max(n, 1))(*vals)  # noqa: E731
+        Ks = (_i * max(n, 1))(*[x.shape[1] for x in xs])
+        sg = arr([_ptr(s) for s in signs]) if signs is not None else None
+        bl = (_i * max(n, 1))(*blocks) if blocks is not None else None
+        self._check(self.lib.ouroq_quantize_group(
+            self.ctx, n, arr([_ptr(x) for x in xs]), Ks, sg, bl, B, arr([_ptr(q) for q in qs]),
+            arr([_ptr(s) for s in sxs]), _stream_ptr(stream)))
+        return qs, sxs
+
+    def rotate(self, x, signs=None, block: int = 128, inverse: bool = False, out=None, stream=None):
+        import torch
+        B, K = x.shape
+        if out is None:
+            out = torch.empty_like(x)
+        self._check(self.lib.ouroq_rotate(self.ctx, _ptr(x), _ptr(out), B, K, _ptr(signs), block,
+                                          1 if inverse else 0, _stream_ptr(stream)))
+        return out
+
+    def gemm(self, w: Weight, q, s_x, y=None, acc=None, stream=None):
+        import torch
+        B = q.shape[0]
+        if y is None:
+            y = torch.empty((B, w.M), dtype=torch.float32, device=q.device)
+        self._check(self.lib.ouroq_gemm(self.ctx, w.handle, _ptr(q), _ptr(s_x), B, _ptr(y),
+                                        _ptr(acc), _stream_ptr(stream)))
+        return y
+
+    def gemm_group(self, ws, qs, sxs, ys, stream=None):
+        n = len(ws)
+        B = qs[0].shape[0]
+        arr = lambda vals: (_p * max(n, 1))(*vals)  # noqa: E731
+        self._check(self.lib.ouroq_gemm_group(
+            self.ctx, n, arr([w.handle for w in ws]), arr([_ptr(q) for q in qs]),
+            arr([_ptr(s) for s in sxs]), B, arr([_ptr(y) for y in ys]), _stream_ptr(stream)))
+        return ys
+
+    def gemm_f32act(self, w: Weight, x, signs=None, hadamard_block: int = 0, y=None, stream=None):
+        import torch
+        B = x.shape[0]
+        if y is None:
+            y = torch.empty((B, w.M), dtype=torch.float32, device=x.device)
+        self._check(self.lib.ouroq_gemm_f32act(self.ctx, w.handle, _ptr(x), B, _ptr(signs),
+                                               hadamard_block, _ptr(y), _stream_ptr(stream)))
+        return y
+
+    # -- host-buffer mirrors of the reference operators (numpy in, numpy out) --
+    def matvec_q(self, w: Weight, x: np.ndarray) -> np.ndarray:
+        """ops::matvec_q: y[out_len] = W . x[in_len] (fp32)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.shape != (w.K,):
+            raise OuroqError(1, f"in_len {w.K} != x len {x.size}")
+        y = np.empty(w.M, dtype=np.float32)
+        self._check(self.lib.ouroq_matvec_q(self.ctx, w.handle, _ptr(x), _ptr(y)))
+        return y
+
+    def matmul_q(self, w: Weight, x: np.ndarray) -> np.ndarray:
+        """ops::matmul_q: x [k][in_len] -> y [k][out_len] (= y[c*out_len + r])."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.ndim != 2 or x.shape[1] != w.K:
+            raise OuroqError(1, f"in_len {w.K} != x width {x.shape[-1]}")
+        k = x.shape[0]
+        y = np.empty((k, w.M), dtype=np.float32)
+        self._check(self.lib.ouroq_matmul_q(self.ctx, w.handle, _ptr(x), k, _ptr(y)))
+        return y
+
+    def rotate_fwd(self, x: np.ndarray, signs: np.ndarray | None, block: int) -> np.ndarray:
+        """hadamard::rotate_fwd in place on a host fp32 buffer (returns it)."""
+        return self._rotate_host(x, signs, block, self.lib.ouroq_rotate_fwd)
+
+    def rotate_inv(self, x: np.ndarray, signs: np.ndarray | None, block: int) -> np.ndarray:
+        return self._rotate_host(x, signs, block, self.lib.ouroq_rotate_inv)
+
+    def _rotate_host(self, x, signs, block, fn):
+        if x.dtype != np.float32 or not x.flags.c_contiguous:
+            raise OuroqError(7, "x must be a contiguous float32 array")
+        if signs is not None:
+            signs = np.ascontiguousarray(signs, dtype=np.float32)
+            if signs.size != x.size:
+                raise OuroqError(1, "sign vector must match activation")
+        self._check(fn(self.ctx, _ptr(x), _ptr(signs), x.size, block))
+        return x

@@ -1,0 +1,585 @@
+// api.cpp -- implementation of the C ABI declared in include/ouroq.h.
+//
+// Host-side responsibilities: argument validation with the reference's error
+// rules (shape / width mismatches are errors, never silent), device memory
+// ownership for uploaded weights, dispatch to the kernels, and the
+// host-buffer mirrors of ops::matvec_q / matmul_q / hadamard::rotate_*.
+// No exception or abort crosses the ABI.
+#include "ouroq.h"
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "kernels.h"
+
+using namespace ouroq;
+
+struct ouroq_ctx {
+  int device = 0;
+  int num_sms = 0;
+  bool pdl = true;
+  std::string err;
+  unsigned* d_status = nullptr;
+  uint64_t launches = 0;
+  cudaStream_t host_stream = nullptr;  // stream of the host-buffer mirrors
+  // quantisation scratch of ouroq_gemm_f32act / the host mirrors
+  int8_t* q_scratch = nullptr;
+  size_t q_cap = 0;
+  float* s_scratch = nullptr;
+  size_t s_cap = 0;
+  // staging for host-buffer calls
+  float* x_stage = nullptr;
+  size_t x_cap = 0;
+  float* y_stage = nullptr;
+  size_t y_cap = 0;
+  float* sign_stage = nullptr;
+  size_t sign_cap = 0;
+};
+
+struct ouroq_weight {
+  int fmt = 0;
+  int M = 0, K = 0;
+  uint8_t* w = nullptr;        // device layout
+  uint16_t* scales = nullptr;  // sign: [M][gpad]
+  int gpad = 0;
+  float w_scale = 0.0f;
+  size_t bytes = 0;
+};
+
+namespace {
+
+ouroq_status fail(ouroq_ctx* ctx, ouroq_status st, const char* fmt, ...) {
+  if (ctx) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    ctx->err = buf;
+  }
+  return st;
+}
+
+ouroq_status cuda_fail(ouroq_ctx* ctx, cudaError_t e, const char* what) {
+  if (e == cudaErrorMemoryAllocation)
+    return fail(ctx, OUROQ_ERR_OOM, "%s: %s", what, cudaGetErrorString(e));
+  return fail(ctx, OUROQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CU(ctx, call, what)                                   \
+  do {                                                        \
+    cudaError_t e_ = (call);                                  \
+    if (e_ != cudaSuccess) return cuda_fail((ctx), e_, what); \
+  } while (0)
+
+// Makes ctx->device current for the scope, restoring the caller's device.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename T>
+ouroq_status grow(ouroq_ctx* ctx, T*& buf, size_t& cap, size_t n, const char* what) {
+  if (n <= cap) return OUROQ_OK;
+  if (buf) cudaFree(buf);
+  buf = nullptr;
+  cap = 0;
+  size_t want = n < 256 ? 256 : n;
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&buf), want * sizeof(T));
+  if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+  cap = want;
+  return OUROQ_OK;
+}
+
+bool valid_block(int b) { return b >= 2 && b <= 1024 && (b & (b - 1)) == 0; }
+
+ouroq_status check_quant_args(ouroq_ctx* ctx, int B, int K, int block) {
+  if (B < 0 || K <= 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d K=%d", B, K);
+  if (K % 4) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "K=%d not a multiple of 4", K);
+  if (block != 0) {
+    if (!valid_block(block))
+      return fail(ctx, OUROQ_ERR_BAD_SHAPE, "hadamard block %d not a power of two in [2,1024]",
+                  block);
+    if (K % block) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "len %d not multiple of block %d", K, block);
+    if (block < 32 && K % 32)
+      return fail(ctx, OUROQ_ERR_BAD_SHAPE, "K=%d must be a multiple of 32 for block %d", K, block);
+  }
+  if ((size_t)K * 4 > 200 * 1024)
+    return fail(ctx, OUROQ_ERR_BAD_SHAPE, "K=%d too wide for the quantiser (max 51200)", K);
+  return OUROQ_OK;
+}
+
+// Largest token batch per small-batch GEMV launch for this K.
+int gemv_chunk(int K) {
+  int c = (int)(kGemvMaxXBytes / (size_t)K);
+  return c > kGemvMaxB ? kGemvMaxB : c;
+}
+
+GemvJob make_job(const ouroq_weight* w, const int8_t* q, const float* s_x, float* y, int32_t* acc) {
+  GemvJob j{};
+  j.w = w->w;
+  j.scales = w->scales;
+  j.q = q;
+  j.s_x = s_x;
+  j.y = y;
+  j.acc = acc;
+  j.w_scale = w->w_scale;
+  j.M = w->M;
+  j.K = w->K;
+  j.ldy = w->M;
+  j.gpad = w->gpad;
+  return j;
+}
+
+ouroq_status run_gemv(ouroq_ctx* ctx, GemvLaunch& L, cudaStream_t s) {
+  int tiles = 0;
+  for (int j = 0; j < L.njobs; ++j) {
+    L.jobs[j].tile_begin = tiles;
+    tiles += (L.jobs[j].M + 31) / 32;
+  }
+  L.ntiles = tiles;
+  L.status = ctx->d_status;
+  if (tiles == 0 || L.B == 0) return OUROQ_OK;
+  CU(ctx, launch_gemv(L, ctx->num_sms, s, ctx->pdl), "gemv launch");
+  ctx->launches++;
+  return OUROQ_OK;
+}
+
+ouroq_status gemm_impl(ouroq_ctx* ctx, const ouroq_weight* w, const int8_t* q, const float* s_x,
+                       int B, float* y, int32_t* acc, cudaStream_t s) {
+  const int chunk = gemv_chunk(w->K);
+  if (chunk < 1) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "K=%d too wide for the GEMV path", w->K);
+  const int G = w->K / 128;
+  for (int b0 = 0; b0 < B; b0 += chunk) {
+    const int nb = B - b0 < chunk ? B - b0 : chunk;
+    GemvLaunch L{};
+    L.njobs = 1;
+    L.B = nb;
+    L.fmt = w->fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
+    int32_t* a = nullptr;
+    if (acc) a = acc + (size_t)b0 * w->M * (w->fmt == OUROQ_FMT_TERNARY2 ? 1 : G);
+    L.jobs[0] = make_job(w, q + (size_t)b0 * w->K, s_x + b0, y + (size_t)b0 * w->M, a);
+    ouroq_status st = run_gemv(ctx, L, s);
+    if (st != OUROQ_OK) return st;
+  }
+  return OUROQ_OK;
+}
+
+ouroq_status quantize_impl(ouroq_ctx* ctx, const float* x, int B, int K, const float* signs,
+                           int block, int8_t* q, float* s_x, cudaStream_t s) {
+  QuantLaunch L{};
+  L.njobs = 1;
+  L.B = B;
+  QuantJob& J = L.jobs[0];
+  J.x = x;
+  J.signs = signs;
+  J.q = q;
+  J.s_x = s_x;
+  J.x_rot = nullptr;
+  J.K = K;
+  J.had_block = block;
+  J.had_scale = block ? 1.0f / std::sqrt((float)block) : 1.0f;
+  if (B == 0) return OUROQ_OK;
+  CU(ctx, launch_quantize(L, s, ctx->pdl), "quantize launch");
+  ctx->launches++;
+  return OUROQ_OK;
+}
+
+ouroq_status check_weight_shape(ouroq_ctx* ctx, ouroq_format fmt, int M, int K) {
+  if (fmt != OUROQ_FMT_TERNARY2 && fmt != OUROQ_FMT_SIGN1G128)
+    return fail(ctx, OUROQ_ERR_BAD_ARG, "unknown format %d", (int)fmt);
+  if (M <= 0 || K <= 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "M=%d K=%d", M, K);
+  if (K % 128) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "K=%d not a multiple of 128", K);
+  return OUROQ_OK;
+}
+
+ouroq_status upload_impl(ouroq_ctx* ctx, ouroq_format fmt, const void* packed, int M, int K,
+                         const void* scales, float w_scale, ouroq_weight** out, bool from_device) {
+  if (!ctx || !packed || !out) return fail(ctx, OUROQ_ERR_BAD_ARG, "null argument");
+  *out = nullptr;
+  ouroq_status st = check_weight_shape(ctx, fmt, M, K);
+  if (st != OUROQ_OK) return st;
+  if (fmt == OUROQ_FMT_SIGN1G128 && !scales)
+    return fail(ctx, OUROQ_ERR_BAD_ARG, "SIGN1G128 needs group scales");
+  DeviceGuard g(ctx->device);
+  // device-side inputs may still be in flight on the caller's streams
+  if (from_device) CU(ctx, cudaDeviceSynchronize(), "upload input sync");
+  ouroq_weight* w = new (std::nothrow) ouroq_weight;
+  if (!w) return fail(ctx, OUROQ_ERR_OOM, "host allocation");
+  w->fmt = fmt;
+  w->M = M;
+  w->K = K;
+  w->w_scale = w_scale;
+  const size_t rb = fmt == OUROQ_FMT_TERNARY2 ? (size_t)K / 4 : (size_t)K / 8;
+  const size_t wbytes = rb * (size_t)M;
+  const int G = K / 128;
+  w->gpad = fmt == OUROQ_FMT_SIGN1G128 ? (G + 15) / 16 * 16 : 0;
+  uint8_t* canon = nullptr;
+  cudaStream_t s = ctx->host_stream;
+  auto cleanup = [&](ouroq_status r) {
+    if (canon && !from_device) cudaFree(canon);
+    if (r != OUROQ_OK) {
+      if (w->w) cudaFree(w->w);
+      if (w->scales) cudaFree(w->scales);
+      delete w;
+    }
+    return r;
+  };
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&w->w), wbytes);
+  if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "weight alloc"));
+  if (from_device) {
+    canon = static_cast<uint8_t*>(const_cast<void*>(packed));
+  } else {
+    e = cudaMalloc(reinterpret_cast<void**>(&canon), wbytes);
+    if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "staging alloc"));
+    e = cudaMemcpyAsync(canon, packed, wbytes, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "weight upload"));
+  }
+  e = fmt == OUROQ_FMT_TERNARY2 ? launch_repack_tern2(canon, w->w, M, K, s)
+                                : launch_repack_sign1(canon, w->w, M, K, s);
+  if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "repack"));
+  ctx->launches++;
+  w->bytes = wbytes;
+  if (fmt == OUROQ_FMT_SIGN1G128) {
+    const size_t sbytes = (size_t)M * w->gpad * 2;
+    e = cudaMalloc(reinterpret_cast<void**>(&w->scales), sbytes);
+    if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "scale alloc"));
+    e = cudaMemsetAsync(w->scales, 0, sbytes, s);
+    if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "scale memset"));
+    e = cudaMemcpy2DAsync(w->scales, (size_t)w->gpad * 2, scales, (size_t)G * 2, (size_t)G * 2, M,
+                          from_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "scale upload"));
+    w->bytes += sbytes;
+  }
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "upload sync"));
+  *out = w;
+  return cleanup(OUROQ_OK);
+}
+
+}  // namespace
+
+extern "C" {
+
+int ouroq_abi_version(void) { return OUROQ_ABI_VERSION; }
+
+const char* ouroq_status_string(ouroq_status s) {
+  switch (s) {
+    case OUROQ_OK: return "ok";
+    case OUROQ_ERR_BAD_SHAPE: return "bad shape";
+    case OUROQ_ERR_BAD_ALIGN: return "bad alignment";
+    case OUROQ_ERR_CUDA: return "cuda error";
+    case OUROQ_ERR_NCCL: return "nccl error";
+    case OUROQ_ERR_TIMEOUT: return "timeout";
+    case OUROQ_ERR_UNSUPPORTED: return "unsupported";
+    case OUROQ_ERR_BAD_ARG: return "bad argument";
+    case OUROQ_ERR_NO_DEVICE: return "no device";
+    case OUROQ_ERR_OOM: return "out of memory";
+  }
+  return "unknown status";
+}
+
+ouroq_status ouroq_ctx_create(int device, ouroq_ctx** out) {
+  if (!out) return OUROQ_ERR_BAD_ARG;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return OUROQ_ERR_NO_DEVICE;
+  if (device < 0 || device >= n) return OUROQ_ERR_NO_DEVICE;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return OUROQ_ERR_NO_DEVICE;
+  if (prop.major != 10) return OUROQ_ERR_NO_DEVICE;  // built for sm_100a only
+  ouroq_ctx* ctx = new (std::nothrow) ouroq_ctx;
+  if (!ctx) return OUROQ_ERR_OOM;
+  ctx->device = device;
+  ctx->num_sms = prop.multiProcessorCount;
+  DeviceGuard g(device);
+  if (cudaMalloc(reinterpret_cast<void**>(&ctx->d_status), sizeof(unsigned)) != cudaSuccess ||
+      cudaMemset(ctx->d_status, 0, sizeof(unsigned)) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&ctx->host_stream, cudaStreamNonBlocking) != cudaSuccess) {
+    if (ctx->d_status) cudaFree(ctx->d_status);
+    delete ctx;
+    return OUROQ_ERR_CUDA;
+  }
+  *out = ctx;
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_ctx_destroy(ouroq_ctx* ctx) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  DeviceGuard g(ctx->device);
+  cudaStreamSynchronize(ctx->host_stream);
+  cudaStreamDestroy(ctx->host_stream);
+  cudaFree(ctx->d_status);
+  cudaFree(ctx->q_scratch);
+  cudaFree(ctx->s_scratch);
+  cudaFree(ctx->x_stage);
+  cudaFree(ctx->y_stage);
+  cudaFree(ctx->sign_stage);
+  delete ctx;
+  return OUROQ_OK;
+}
+
+const char* ouroq_last_error(const ouroq_ctx* ctx) { return ctx ? ctx->err.c_str() : ""; }
+
+uint64_t ouroq_launch_count(const ouroq_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+ouroq_status ouroq_set_pdl(ouroq_ctx* ctx, int enable) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  ctx->pdl = enable != 0;
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_check_device(ouroq_ctx* ctx) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  DeviceGuard g(ctx->device);
+  CU(ctx, cudaDeviceSynchronize(), "device sync");
+  unsigned v = 0;
+  CU(ctx, cudaMemcpy(&v, ctx->d_status, sizeof v, cudaMemcpyDeviceToHost), "status read");
+  if (v != 0) {
+    CU(ctx, cudaMemset(ctx->d_status, 0, sizeof v), "status clear");
+    return fail(ctx, OUROQ_ERR_TIMEOUT, "device wait expired (code %u)", v);
+  }
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_weight_upload(ouroq_ctx* ctx, ouroq_format fmt, const void* packed, int M, int K,
+                                 const void* scales, float w_scale, ouroq_weight** out) {
+  return upload_impl(ctx, fmt, packed, M, K, scales, w_scale, out, false);
+}
+
+ouroq_status ouroq_weight_upload_device(ouroq_ctx* ctx, ouroq_format fmt, const void* packed_dev,
+                                        int M, int K, const void* scales_dev, float w_scale,
+                                        ouroq_weight** out) {
+  return upload_impl(ctx, fmt, packed_dev, M, K, scales_dev, w_scale, out, true);
+}
+
+ouroq_status ouroq_weight_free(ouroq_ctx* ctx, ouroq_weight* w) {
+  if (!ctx || !w) return fail(ctx, OUROQ_ERR_BAD_ARG, "null argument");
+  DeviceGuard g(ctx->device);
+  cudaFree(w->w);
+  cudaFree(w->scales);
+  delete w;
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_weight_info(const ouroq_weight* w, int* fmt, int* M, int* K,
+                               size_t* device_bytes) {
+  if (!w) return OUROQ_ERR_BAD_ARG;
+  if (fmt) *fmt = w->fmt;
+  if (M) *M = w->M;
+  if (K) *K = w->K;
+  if (device_bytes) *device_bytes = w->bytes;
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_quantize_act(ouroq_ctx* ctx, const float* x, int B, int K, const float* signs,
+                                int hadamard_block, int8_t* q, float* s_x, void* stream) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  if (B > 0 && (!x || !q || !s_x)) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  ouroq_status st = check_quant_args(ctx, B, K, hadamard_block);
+  if (st != OUROQ_OK) return st;
+  if (!aligned16(x) || !aligned16(q)) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "x/q not 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  return quantize_impl(ctx, x, B, K, signs, hadamard_block, q, s_x,
+                       static_cast<cudaStream_t>(stream));
+}
+
+ouroq_status ouroq_quantize_group(ouroq_ctx* ctx, int n, const float* const* x, const int* K,
+                                  const float* const* signs, const int* blocks, int B,
+                                  int8_t* const* q, float* const* s_x, void* stream) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  if (n < 0 || n > kMaxQuantJobs)
+    return fail(ctx, OUROQ_ERR_BAD_SHAPE, "group size %d (max %d)", n, kMaxQuantJobs);
+  if (B < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d", B);
+  if (n == 0 || B == 0) return OUROQ_OK;
+  if (!x || !K || !q || !s_x) return fail(ctx, OUROQ_ERR_BAD_ARG, "null array");
+  QuantLaunch L{};
+  L.njobs = n;
+  L.B = B;
+  for (int i = 0; i < n; ++i) {
+    const int blk = blocks ? blocks[i] : 0;
+    ouroq_status st = check_quant_args(ctx, B, K[i], blk);
+    if (st != OUROQ_OK) return st;
+    if (!x[i] || !q[i] || !s_x[i]) return fail(ctx, OUROQ_ERR_BAD_ARG, "null entry %d", i);
+    if (!aligned16(x[i]) || !aligned16(q[i]))
+      return fail(ctx, OUROQ_ERR_BAD_ALIGN, "x[%d]/q[%d] not 16-byte aligned", i, i);
+    QuantJob& J = L.jobs[i];
+    J.x = x[i];
+    J.signs = signs ? signs[i] : nullptr;
+    J.q = q[i];
+    J.s_x = s_x[i];
+    J.x_rot = nullptr;
+    J.K = K[i];
+    J.had_block = blk;
+    J.had_scale = blk ? 1.0f / std::sqrt((float)blk) : 1.0f;
+  }
+  DeviceGuard g(ctx->device);
+  CU(ctx, launch_quantize(L, static_cast<cudaStream_t>(stream), ctx->pdl), "quantize launch");
+  ctx->launches++;
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_rotate(ouroq_ctx* ctx, const float* x, float* out, int B, int K,
+                          const float* signs, int block, int inverse, void* stream) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  if (B > 0 && (!x || !out)) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  if (!valid_block(block)) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "block %d", block);
+  ouroq_status st = check_quant_args(ctx, B, K, block);
+  if (st != OUROQ_OK) return st;
+  DeviceGuard g(ctx->device);
+  const float scale = 1.0f / std::sqrt((float)block);
+  CU(ctx, launch_rotate(x, out, signs, B, K, block, scale, inverse, static_cast<cudaStream_t>(stream)),
+     "rotate launch");
+  if (B > 0) ctx->launches++;
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_gemm(ouroq_ctx* ctx, const ouroq_weight* w, const int8_t* q, const float* s_x,
+                        int B, float* y, int32_t* acc_debug, void* stream) {
+  if (!ctx || !w) return fail(ctx, OUROQ_ERR_BAD_ARG, "null handle");
+  if (B < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d", B);
+  if (B == 0) return OUROQ_OK;
+  if (!q || !s_x || !y) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  if (!aligned16(q)) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "q not 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  return gemm_impl(ctx, w, q, s_x, B, y, acc_debug, static_cast<cudaStream_t>(stream));
+}
+
+ouroq_status ouroq_gemm_group(ouroq_ctx* ctx, int n, const ouroq_weight* const* w,
+                              const int8_t* const* q, const float* const* s_x, int B,
+                              float* const* y, void* stream) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  if (n < 0 || n > kMaxGemvJobs) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "group size %d (max %d)", n, kMaxGemvJobs);
+  if (B < 0 || B > kGemvMaxB) return fail(ctx, OUROQ_ERR_UNSUPPORTED, "grouped GEMV needs B <= %d", kGemvMaxB);
+  if (n == 0 || B == 0) return OUROQ_OK;
+  if (!w || !q || !s_x || !y) return fail(ctx, OUROQ_ERR_BAD_ARG, "null array");
+  GemvLaunch L{};
+  L.njobs = n;
+  L.B = B;
+  for (int i = 0; i < n; ++i) {
+    if (!w[i] || !q[i] || !s_x[i] || !y[i]) return fail(ctx, OUROQ_ERR_BAD_ARG, "null entry %d", i);
+    if (w[i]->fmt != w[0]->fmt) return fail(ctx, OUROQ_ERR_UNSUPPORTED, "mixed formats in a group");
+    if ((size_t)B * w[i]->K > kGemvMaxXBytes)
+      return fail(ctx, OUROQ_ERR_UNSUPPORTED, "B*K=%d exceeds the grouped GEMV limit", B * w[i]->K);
+    if (!aligned16(q[i])) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "q[%d] not 16-byte aligned", i);
+    L.jobs[i] = make_job(w[i], q[i], s_x[i], y[i], nullptr);
+  }
+  L.fmt = w[0]->fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
+  DeviceGuard g(ctx->device);
+  return run_gemv(ctx, L, static_cast<cudaStream_t>(stream));
+}
+
+ouroq_status ouroq_gemm_f32act(ouroq_ctx* ctx, const ouroq_weight* w, const float* x, int B,
+                               const float* signs, int hadamard_block, float* y, void* stream) {
+  if (!ctx || !w) return fail(ctx, OUROQ_ERR_BAD_ARG, "null handle");
+  if (B < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d", B);
+  if (B == 0) return OUROQ_OK;
+  if (!x || !y) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  ouroq_status st = check_quant_args(ctx, B, w->K, hadamard_block);
+  if (st != OUROQ_OK) return st;
+  if (!aligned16(x)) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "x not 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  st = grow(ctx, ctx->q_scratch, ctx->q_cap, (size_t)B * w->K, "q scratch");
+  if (st != OUROQ_OK) return st;
+  st = grow(ctx, ctx->s_scratch, ctx->s_cap, (size_t)B, "s scratch");
+  if (st != OUROQ_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = quantize_impl(ctx, x, B, w->K, signs, hadamard_block, ctx->q_scratch, ctx->s_scratch, s);
+  if (st != OUROQ_OK) return st;
+  return gemm_impl(ctx, w, ctx->q_scratch, ctx->s_scratch, B, y, nullptr, s);
+}
+
+ouroq_status ouroq_matmul_q(ouroq_ctx* ctx, const ouroq_weight* w, const float* x_host, int k,
+                            float* y_host) {
+  if (!ctx || !w) return fail(ctx, OUROQ_ERR_BAD_ARG, "null handle");
+  if (k < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "k=%d", k);
+  if (k == 0) return OUROQ_OK;
+  if (!x_host || !y_host) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  DeviceGuard g(ctx->device);
+  ouroq_status st = grow(ctx, ctx->x_stage, ctx->x_cap, (size_t)k * w->K, "x stage");
+  if (st != OUROQ_OK) return st;
+  st = grow(ctx, ctx->y_stage, ctx->y_cap, (size_t)k * w->M, "y stage");
+  if (st != OUROQ_OK) return st;
+  cudaStream_t s = ctx->host_stream;
+  CU(ctx, cudaMemcpyAsync(ctx->x_stage, x_host, (size_t)k * w->K * 4, cudaMemcpyHostToDevice, s),
+     "x upload");
+  st = ouroq_gemm_f32act(ctx, w, ctx->x_stage, k, nullptr, 0, ctx->y_stage, s);
+  if (st != OUROQ_OK) return st;
+  CU(ctx, cudaMemcpyAsync(y_host, ctx->y_stage, (size_t)k * w->M * 4, cudaMemcpyDeviceToHost, s),
+     "y download");
+  CU(ctx, cudaStreamSynchronize(s), "stream sync");
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_matvec_q(ouroq_ctx* ctx, const ouroq_weight* w, const float* x_host,
+                            float* y_host) {
+  return ouroq_matmul_q(ctx, w, x_host, 1, y_host);
+}
+
+static ouroq_status rotate_host(ouroq_ctx* ctx, float* x_host, const float* signs_host, size_t n,
+                                size_t block, int inverse) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  if (n == 0) return OUROQ_OK;
+  if (!x_host) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  // hadamard.rs:33-37: block must be a power of two and divide the length
+  if (!valid_block((int)block) || n % block)
+    return fail(ctx, OUROQ_ERR_BAD_SHAPE, "len %zu not multiple of block %zu", n, block);
+  // one row per block-aligned segment of at most 32768 elements
+  size_t K = n;
+  while (K > 32768) K /= 2;
+  if (n % K || K % block) K = block;
+  const int B = (int)(n / K);
+  DeviceGuard g(ctx->device);
+  ouroq_status st = grow(ctx, ctx->x_stage, ctx->x_cap, n, "x stage");
+  if (st != OUROQ_OK) return st;
+  cudaStream_t s = ctx->host_stream;
+  CU(ctx, cudaMemcpyAsync(ctx->x_stage, x_host, n * 4, cudaMemcpyHostToDevice, s), "x upload");
+  const float* sd = nullptr;
+  if (signs_host) {
+    st = grow(ctx, ctx->sign_stage, ctx->sign_cap, n, "sign stage");
+    if (st != OUROQ_OK) return st;
+    CU(ctx, cudaMemcpyAsync(ctx->sign_stage, signs_host, n * 4, cudaMemcpyHostToDevice, s),
+       "signs upload");
+    sd = ctx->sign_stage;
+  }
+  // rows of K elements; the sign vector repeats per row only when rows == 1,
+  // so for B > 1 pass per-row sign slices by launching row by row.
+  const float scale = 1.0f / std::sqrt((float)block);
+  for (int b = 0; b < B; ++b) {
+    CU(ctx,
+       launch_rotate(ctx->x_stage + (size_t)b * K, ctx->x_stage + (size_t)b * K,
+                     sd ? sd + (size_t)b * K : nullptr, 1, (int)K, (int)block, scale, inverse, s),
+       "rotate launch");
+    ctx->launches++;
+  }
+  CU(ctx, cudaMemcpyAsync(x_host, ctx->x_stage, n * 4, cudaMemcpyDeviceToHost, s), "x download");
+  CU(ctx, cudaStreamSynchronize(s), "stream sync");
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_rotate_fwd(ouroq_ctx* ctx, float* x_host, const float* signs_host, size_t n,
+                              size_t block) {
+  return rotate_host(ctx, x_host, signs_host, n, block, 0);
+}
+
+ouroq_status ouroq_rotate_inv(ouroq_ctx* ctx, float* x_host, const float* signs_host, size_t n,
+                              size_t block) {
+  return rotate_host(ctx, x_host, signs_host, n, block, 1);
+}
+
+}  // extern "C"

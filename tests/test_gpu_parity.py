@@ -1,0 +1,272 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle.
+
+Tolerances (north_star): int32 accumulators bit-exact; fp32 outputs and the
+Hadamard transform within 1e-5 relative. The kernels are built to reproduce
+the oracle's IEEE operation sequence, so every comparison below is exact
+equality, which implies both bounds; `assert_rel` states the 1e-5 bound
+explicitly where it is the contract.
+"""
+import numpy as np
+import pytest
+
+import ouroboros_b200 as oq
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-5
+
+
+def assert_rel(got, want, tol=REL_TOL):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    scale = np.maximum(np.abs(want), np.finfo(np.float32).tiny)
+    assert np.all(np.abs(got - want) <= tol * scale), float(np.max(np.abs(got - want) / scale))
+
+
+def dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+def tern_case(oracle, M, K, B, seed):
+    w = oracle.ternary(seed, M * K).reshape(M, K)
+    x = oracle.normals(seed + 1, B * K).reshape(B, K)
+    ws = oracle.absmean_scale(w, 0.02)
+    return oracle.pack_tern2(w), ws, x
+
+
+def sign_case(oracle, M, K, B, seed):
+    w = oracle.signs(seed, M * K).reshape(M, K)
+    sc = oracle.group_scales(seed + 1, M * (K // 128), 0.02)
+    x = oracle.outliers(seed + 2, oracle.normals(seed + 3, B * K), 0.01, 20.0).reshape(B, K)
+    return oracle.pack_sign1(w), sc, x
+
+
+# ---------------------------------------------------------------- K1
+@pytest.mark.parametrize("B,K", [(1, 2560), (8, 2560), (3, 6912), (64, 2560), (2, 128), (5, 4096)])
+def test_quantize_matches_oracle(ctx, oracle, B, K):
+    x = oracle.normals(100 + B, B * K).reshape(B, K)
+    x[0, 3] = 40.0
+    if B > 2:
+        x[1] = 0.0
+        x[2] = -0.25
+    q, s = ctx.quantize_act(dev(x))
+    qr, sr = oracle.quantize_act(x)
+    assert np.array_equal(host(s), sr)
+    assert np.array_equal(host(q), qr)
+
+
+@pytest.mark.parametrize("block", [16, 32, 64, 128, 256, 1024])
+@pytest.mark.parametrize("B", [1, 32])
+def test_quantize_hadamard_matches_oracle(ctx, oracle, B, block):
+    K = 4096
+    x = oracle.outliers(7, oracle.normals(8 + block, B * K), 0.01, 20.0).reshape(B, K)
+    sg = oracle.signs(9, K).astype(np.float32)
+    q, s = ctx.quantize_act(dev(x), signs=dev(sg), hadamard_block=block)
+    qr, sr, xr = oracle.quantize_act(x, sg, block, want_rot=True)
+    assert np.array_equal(host(s), sr)
+    assert np.array_equal(host(q), qr)
+    rot = host(ctx.rotate(dev(x), signs=dev(sg), block=block))
+    assert np.array_equal(rot, xr)  # bit-identical butterfly network
+    assert_rel(rot[np.abs(xr) > 1e-6], xr[np.abs(xr) > 1e-6])
+
+
+@pytest.mark.parametrize("block", [16, 64, 128, 1024])
+def test_rotate_inv_matches_oracle(ctx, oracle, block):
+    K = 2048
+    x = oracle.normals(21, 3 * K).reshape(3, K)
+    sg = oracle.signs(22, K).astype(np.float32)
+    got = host(ctx.rotate(dev(x), signs=dev(sg), block=block, inverse=True))
+    for b in range(3):
+        assert np.array_equal(got[b], oracle.rotate_inv(x[b], sg, block))
+
+
+def test_rotate_host_mirror_reference_kats(ctx, oracle):
+    # hadamard.rs:96-141 inputs through the host-buffer mirror of rotate_fwd / rotate_inv
+    n = 16
+    x = np.array([((i * 11) % 7) - 3.0 for i in range(n)], np.float32)
+    s = np.array([-1.0 if i % 3 == 0 else 1.0 for i in range(n)], np.float32)
+    assert np.array_equal(ctx.rotate_fwd(x.copy(), s, 16), oracle.rotate_fwd(x, s, 16))
+    x = np.array([((i * 91) % 23) * 0.37 - 4.0 for i in range(128)], np.float32)
+    s = np.array([-1.0 if (i // 5) % 2 == 0 else 1.0 for i in range(128)], np.float32)
+    y = ctx.rotate_fwd(ctx.rotate_inv(x.copy(), s, 64), s, 64)
+    assert np.all(np.abs(x - y) < 1e-3)
+    with pytest.raises(oq.OuroqError):
+        ctx.rotate_fwd(np.zeros(96, np.float32), None, 48)
+
+
+# ---------------------------------------------------------------- K2 ternary
+TERN_SHAPES = [
+    (6912, 2560, 1),   # C1
+    (3840, 2560, 1), (2560, 2560, 1), (6912, 2560, 8), (2560, 6912, 1), (2560, 6912, 8),  # C2
+    (37, 384, 1), (1, 128, 1), (33, 256, 3), (100, 640, 5), (32, 128, 7),  # ragged / tiny
+]
+
+
+@pytest.mark.parametrize("M,K,B", TERN_SHAPES)
+def test_gemm_tern2_matches_oracle(ctx, oracle, M, K, B):
+    packed, ws, x = tern_case(oracle, M, K, B, seed=M * 7 + K + B)
+    qr, sr = oracle.quantize_act(x)
+    accr, yr = oracle.gemm_tern2(packed, M, K, ws, qr, sr)
+    w = ctx.upload(oq.TERNARY2, packed, M, K, w_scale=ws)
+    import torch
+    acc = torch.empty((B, M), dtype=torch.int32, device="cuda")
+    y = ctx.gemm(w, dev(qr), dev(sr), acc=acc)
+    assert np.array_equal(host(acc), accr)
+    assert np.array_equal(host(y), yr)
+    assert_rel(host(y)[yr != 0], yr[yr != 0])
+    w.free()
+
+
+@pytest.mark.parametrize("B", [16, 64])
+def test_gemm_tern2_batched_c2(ctx, oracle, B):
+    M, K = 6912, 2560
+    packed, ws, x = tern_case(oracle, M, K, B, seed=5 + B)
+    qr, sr = oracle.quantize_act(x)
+    accr, yr = oracle.gemm_tern2(packed, M, K, ws, qr, sr)
+    w = ctx.upload(oq.TERNARY2, packed, M, K, w_scale=ws)
+    import torch
+    acc = torch.empty((B, M), dtype=torch.int32, device="cuda")
+    y = ctx.gemm(w, dev(qr), dev(sr), acc=acc)
+    assert np.array_equal(host(acc), accr)
+    assert np.array_equal(host(y), yr)
+    w.free()
+
+
+def test_gemm_tern2_zero_and_extreme_activations(ctx, oracle):
+    M, K, B = 96, 512, 4
+    packed, ws, x = tern_case(oracle, M, K, B, seed=77)
+    x[0] = 0.0            # s_x = 0 -> y = 0
+    x[1] = 1.0            # all codes 127
+    x[2, ::2] = -1e6      # saturating negatives
+    qr, sr = oracle.quantize_act(x)
+    accr, yr = oracle.gemm_tern2(packed, M, K, ws, qr, sr)
+    w = ctx.upload(oq.TERNARY2, packed, M, K, w_scale=ws)
+    q, s = ctx.quantize_act(dev(x))
+    assert np.array_equal(host(q), qr)
+    y = ctx.gemm(w, q, s)
+    assert np.array_equal(host(y), yr)
+    assert np.all(host(y)[0] == 0)
+
+
+# ---------------------------------------------------------------- K3 sign
+@pytest.mark.parametrize("M,K,B", [(4096, 4096, 1), (11008, 4096, 1), (4096, 4096, 8),
+                                   (77, 256, 3), (50, 2176, 2), (16, 128, 1)])
+def test_gemm_sign1_hadamard_matches_oracle(ctx, oracle, M, K, B):
+    packed, sc, x = sign_case(oracle, M, K, B, seed=M + K + B)
+    sg = oracle.signs(1234, K).astype(np.float32)
+    qr, sr = oracle.quantize_act(x, sg, 128)
+    accr, yr = oracle.gemm_sign1(packed, sc, M, K, qr, sr)
+    w = ctx.upload(oq.SIGN1G128, packed, M, K, scales=sc)
+    q, s = ctx.quantize_act(dev(x), signs=dev(sg), hadamard_block=128)
+    assert np.array_equal(host(q), qr) and np.array_equal(host(s), sr)
+    import torch
+    acc = torch.empty((B, M, K // 128), dtype=torch.int32, device="cuda")
+    y = ctx.gemm(w, q, s, acc=acc)
+    assert np.array_equal(host(acc), accr)
+    assert np.array_equal(host(y), yr)
+    w.free()
+
+
+@pytest.mark.parametrize("M", [4096, 11008])
+def test_gemm_sign1_c3_batch32(ctx, oracle, M):
+    K, B = 4096, 32
+    packed, sc, x = sign_case(oracle, M, K, B, seed=M)
+    qr, sr = oracle.quantize_act(x, None, 128)
+    _, yr = oracle.gemm_sign1(packed, sc, M, K, qr, sr)
+    w = ctx.upload(oq.SIGN1G128, packed, M, K, scales=sc)
+    y = ctx.gemm_f32act(w, dev(x), hadamard_block=128)
+    assert np.array_equal(host(y), yr)
+    w.free()
+
+
+# ---------------------------------------------------------------- grouped / host mirrors
+def test_gemm_group_c2_layer(ctx, oracle):
+    shapes = [(3840, 2560), (2560, 2560), (6912, 2560), (6912, 2560), (2560, 6912)]
+    B = 1
+    ws_, qs, ss, ys, want = [], [], [], [], []
+    import torch
+    for i, (M, K) in enumerate(shapes):
+        packed, wsc, x = tern_case(oracle, M, K, B, seed=300 + i)
+        qr, sr = oracle.quantize_act(x)
+        want.append(oracle.gemm_tern2(packed, M, K, wsc, qr, sr)[1])
+        ws_.append(ctx.upload(oq.TERNARY2, packed, M, K, w_scale=wsc))
+        qs.append(dev(qr))
+        ss.append(dev(sr))
+        ys.append(torch.empty((B, M), dtype=torch.float32, device="cuda"))
+    ctx.gemm_group(ws_, qs, ss, ys)
+    for y, yr in zip(ys, want):
+        assert np.array_equal(host(y), yr)
+    for w in ws_:
+        w.free()
+
+
+def test_host_mirrors_matvec_matmul(ctx, oracle):
+    M, K = 1000, 2560
+    packed, ws, x = tern_case(oracle, M, K, 5, seed=42)
+    w = ctx.upload(oq.TERNARY2, packed, M, K, w_scale=ws)
+    y1 = ctx.matvec_q(w, x[0])
+    qr, sr = oracle.quantize_act(x)
+    _, yr = oracle.gemm_tern2(packed, M, K, ws, qr, sr)
+    assert np.array_equal(y1, yr[0])
+    yk = ctx.matmul_q(w, x)
+    assert yk.shape == (5, M)
+    assert np.array_equal(yk, yr)
+    with pytest.raises(oq.OuroqError):
+        ctx.matvec_q(w, x[0, :100])
+    w.free()
+
+
+# ---------------------------------------------------------------- C5 sizes
+@pytest.mark.parametrize("M,K", [(28672, 8192), (8192, 28672)])
+def test_c5_shapes_batch1_exact(ctx, oracle, M, K):
+    packed, ws, x = tern_case(oracle, M, K, 1, seed=M ^ K)
+    qr, sr = oracle.quantize_act(x)
+    accr, yr = oracle.gemm_tern2(packed, M, K, ws, qr, sr)
+    w = ctx.upload(oq.TERNARY2, packed, M, K, w_scale=ws)
+    import torch
+    acc = torch.empty((1, M), dtype=torch.int32, device="cuda")
+    y = ctx.gemm(w, dev(qr), dev(sr), acc=acc)
+    assert np.array_equal(host(acc), accr)
+    assert np.array_equal(host(y), yr)
+    w.free()
+
+
+def test_c5_batch16_accumulators_vs_float64(ctx, oracle):
+    # size-independent property at full size: acc == exact integer product
+    import torch
+    M, K, B = 8192, 28672, 16
+    wt = oracle.ternary(555, M * K).reshape(M, K)
+    x = oracle.normals(556, B * K).reshape(B, K)
+    qr, sr = oracle.quantize_act(x)
+    w = ctx.upload(oq.TERNARY2, oracle.pack_tern2(wt), M, K, w_scale=0.02)
+    acc = torch.empty((B, M), dtype=torch.int32, device="cuda")
+    ctx.gemm(w, dev(qr), dev(sr), acc=acc)
+    exact = dev(qr).double() @ dev(wt).double().T
+    assert torch.equal(acc.double(), exact)
+    w.free()
+
+
+# ---------------------------------------------------------------- errors
+def test_error_behaviour(ctx, oracle):
+    with pytest.raises(oq.OuroqError) as e:
+        ctx.upload(oq.TERNARY2, np.zeros((4, 25), np.uint8), 4, 100)
+    assert e.value.status == 1
+    packed, ws, x = tern_case(oracle, 64, 256, 1, seed=1)
+    w = ctx.upload(oq.TERNARY2, packed, 64, 256, w_scale=ws)
+    import torch
+    qbuf = torch.zeros(2 * 256 + 16, dtype=torch.int8, device="cuda")
+    q_mis = qbuf[1:257].view(1, 256)
+    s = torch.ones(1, device="cuda")
+    with pytest.raises(oq.OuroqError) as e:
+        ctx.gemm(w, q_mis, s)
+    assert e.value.status == 2
+    with pytest.raises(oq.OuroqError) as e:
+        ctx.quantize_act(dev(np.zeros((1, 384), np.float32)), hadamard_block=256)
+    assert e.value.status == 1
+    w.free()
+    ctx.check_device()
