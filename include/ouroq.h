@@ -129,9 +129,20 @@ ouroq_status ouroq_gemm_group(ouroq_ctx *ctx, int n, const ouroq_weight *const *
                               const int8_t *const *q, const float *const *s_x, int B,
                               float *const *y, void *stream);
 
+/* Grouped GEMV with the quantisation fused in: n (<= 8) products
+ * y_i = W_i . quant(rotate(x_i)) in ONE launch, x_i fp32 [B][K_i] (16-byte
+ * aligned). Per entry optional rotation: signs[i] (nullable) and blocks[i]
+ * (0 = none, else 32, 64 or 128, the same for every entry); both arrays may be
+ * NULL. OUROQ_ERR_UNSUPPORTED when B > 8 or the activations of the matrices
+ * one CTA covers do not fit in shared memory. */
+ouroq_status ouroq_gemm_group_f32act(ouroq_ctx *ctx, int n, const ouroq_weight *const *w,
+                                     const float *const *x, int B, const float *const *signs,
+                                     const int *blocks, float *const *y, void *stream);
+
 /* fp32 activations in, fp32 outputs out: quantise (with optional rotation)
- * into context-owned scratch, then ouroq_gemm. Mirrors matvec_q / matmul_q's
- * "f32 x in, f32 y out" contract on device buffers. */
+ * and multiply. Mirrors matvec_q / matmul_q's "f32 x in, f32 y out" contract
+ * on device buffers. Small batches run as one fused launch; otherwise the
+ * activations are quantised into context-owned scratch first. */
 ouroq_status ouroq_gemm_f32act(ouroq_ctx *ctx, const ouroq_weight *w, const float *x, int B,
                                const float *signs, int hadamard_block, float *y, void *stream);
 

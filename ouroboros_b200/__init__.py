@@ -64,6 +64,7 @@ ABI_FUNCTIONS = {
     "ouroq_rotate": (_i, [_p, _p, _p, _i, _i, _p, _i, _i, _p]),
     "ouroq_gemm": (_i, [_p, _p, _p, _p, _i, _p, _p, _p]),
     "ouroq_gemm_group": (_i, [_p, _i, _p, _p, _p, _i, _p, _p]),
+    "ouroq_gemm_group_f32act": (_i, [_p, _i, _p, _p, _i, _p, _p, _p, _p]),
     "ouroq_gemm_f32act": (_i, [_p, _p, _p, _i, _p, _i, _p, _p]),
     "ouroq_matvec_q": (_i, [_p, _p, _p, _p]),
     "ouroq_matmul_q": (_i, [_p, _p, _p, _i, _p]),
@@ -252,6 +253,18 @@ class Context:
         self._check(self.lib.ouroq_gemm_group(
             self.ctx, n, arr([w.handle for w in ws]), arr([_ptr(q) for q in qs]),
             arr([_ptr(s) for s in sxs]), B, arr([_ptr(y) for y in ys]), _stream_ptr(stream)))
+        return ys
+
+    def gemm_group_f32act(self, ws, xs, ys, signs=None, blocks=None, stream=None):
+        """One launch: fused quantisation (+ optional rotation) and GEMV for each (W, x)."""
+        n = len(ws)
+        B = xs[0].shape[0]
+        arr = lambda vals: (_p * max(n, 1))(*vals)  # noqa: E731
+        sg = arr([_ptr(s) for s in signs]) if signs is not None else None
+        bl = (_i * max(n, 1))(*blocks) if blocks is not None else None
+        self._check(self.lib.ouroq_gemm_group_f32act(
+            self.ctx, n, arr([w.handle for w in ws]), arr([_ptr(x) for x in xs]), B, sg, bl,
+            arr([_ptr(y) for y in ys]), _stream_ptr(stream)))
         return ys
 
     def gemm_f32act(self, w: Weight, x, signs=None, hadamard_block: int = 0, y=None, stream=None):

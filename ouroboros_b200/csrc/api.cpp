@@ -23,6 +23,7 @@ using namespace ouroq;
 struct ouroq_ctx {
   int device = 0;
   int num_sms = 0;
+  int smem_optin = 0;  // opt-in shared memory per block (bytes)
   bool pdl = true;
   std::string err;
   unsigned* d_status = nullptr;
@@ -46,8 +47,7 @@ struct ouroq_weight {
   int fmt = 0;
   int M = 0, K = 0;
   uint8_t* w = nullptr;        // device layout
-  uint16_t* scales = nullptr;  // sign: [M][gpad]
-  int gpad = 0;
+  uint16_t* scales = nullptr;  // sign: tiled fp16 group scales
   float w_scale = 0.0f;
   size_t bytes = 0;
 };
@@ -130,6 +130,13 @@ int gemv_chunk(int K) {
   return c > kGemvMaxB ? kGemvMaxB : c;
 }
 
+// Can this GEMV launch keep each CTA's activations in shared memory?
+bool gemv_fits(const ouroq_ctx* ctx, GemvLaunch L) {
+  int grid = 0;
+  size_t smem = 0;
+  return gemv_prepare(L, ctx->num_sms, ctx->smem_optin, &grid, &smem);
+}
+
 GemvJob make_job(const ouroq_weight* w, const int8_t* q, const float* s_x, float* y, int32_t* acc) {
   GemvJob j{};
   j.w = w->w;
@@ -142,21 +149,17 @@ GemvJob make_job(const ouroq_weight* w, const int8_t* q, const float* s_x, float
   j.M = w->M;
   j.K = w->K;
   j.ldy = w->M;
-  j.gpad = w->gpad;
   return j;
 }
 
 ouroq_status run_gemv(ouroq_ctx* ctx, GemvLaunch& L, cudaStream_t s) {
-  int tiles = 0;
-  for (int j = 0; j < L.njobs; ++j) {
-    L.jobs[j].tile_begin = tiles;
-    tiles += (L.jobs[j].M + 31) / 32;
-  }
-  L.ntiles = tiles;
   L.status = ctx->d_status;
-  if (tiles == 0 || L.B == 0) return OUROQ_OK;
-  CU(ctx, launch_gemv(L, ctx->num_sms, s, ctx->pdl), "gemv launch");
-  ctx->launches++;
+  if (L.njobs == 0 || L.B == 0) return OUROQ_OK;
+  if (!gemv_fits(ctx, L))
+    return fail(ctx, OUROQ_ERR_UNSUPPORTED,
+                "B=%d: the activations of one CTA's matrices do not fit in shared memory", L.B);
+  CU(ctx, launch_gemv(L, ctx->num_sms, ctx->smem_optin, s, ctx->pdl), "gemv launch");
+  if (L.ntiles > 0) ctx->launches++;
   return OUROQ_OK;
 }
 
@@ -225,14 +228,19 @@ ouroq_status upload_impl(ouroq_ctx* ctx, ouroq_format fmt, const void* packed, i
   w->M = M;
   w->K = K;
   w->w_scale = w_scale;
+  const int dfmt = fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
   const size_t rb = fmt == OUROQ_FMT_TERNARY2 ? (size_t)K / 4 : (size_t)K / 8;
-  const size_t wbytes = rb * (size_t)M;
-  const int G = K / 128;
-  w->gpad = fmt == OUROQ_FMT_SIGN1G128 ? (G + 15) / 16 * 16 : 0;
+  const size_t canon_bytes = rb * (size_t)M;
+  const size_t canon_sbytes = (size_t)M * (K / 128) * 2;
+  const size_t wbytes = tiled_weight_bytes(dfmt, M, K);
   uint8_t* canon = nullptr;
+  uint16_t* canon_s = nullptr;
   cudaStream_t s = ctx->host_stream;
   auto cleanup = [&](ouroq_status r) {
-    if (canon && !from_device) cudaFree(canon);
+    if (!from_device) {
+      if (canon) cudaFree(canon);
+      if (canon_s) cudaFree(canon_s);
+    }
     if (r != OUROQ_OK) {
       if (w->w) cudaFree(w->w);
       if (w->scales) cudaFree(w->scales);
@@ -240,30 +248,37 @@ ouroq_status upload_impl(ouroq_ctx* ctx, ouroq_format fmt, const void* packed, i
     }
     return r;
   };
+  if (from_device && ((reinterpret_cast<uintptr_t>(packed) & 3u) ||
+                      (scales && (reinterpret_cast<uintptr_t>(scales) & 1u))))
+    return cleanup(fail(ctx, OUROQ_ERR_BAD_ALIGN, "device weights must be 4-byte aligned"));
   cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&w->w), wbytes);
   if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "weight alloc"));
   if (from_device) {
     canon = static_cast<uint8_t*>(const_cast<void*>(packed));
+    canon_s = static_cast<uint16_t*>(const_cast<void*>(scales));
   } else {
-    e = cudaMalloc(reinterpret_cast<void**>(&canon), wbytes);
+    e = cudaMalloc(reinterpret_cast<void**>(&canon), canon_bytes);
     if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "staging alloc"));
-    e = cudaMemcpyAsync(canon, packed, wbytes, cudaMemcpyHostToDevice, s);
+    e = cudaMemcpyAsync(canon, packed, canon_bytes, cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "weight upload"));
+    if (scales) {
+      e = cudaMalloc(reinterpret_cast<void**>(&canon_s), canon_sbytes);
+      if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "staging alloc"));
+      e = cudaMemcpyAsync(canon_s, scales, canon_sbytes, cudaMemcpyHostToDevice, s);
+      if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "scale upload"));
+    }
   }
-  e = fmt == OUROQ_FMT_TERNARY2 ? launch_repack_tern2(canon, w->w, M, K, s)
-                                : launch_repack_sign1(canon, w->w, M, K, s);
+  e = launch_repack(dfmt, canon, w->w, M, K, s);
   if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "repack"));
   ctx->launches++;
   w->bytes = wbytes;
   if (fmt == OUROQ_FMT_SIGN1G128) {
-    const size_t sbytes = (size_t)M * w->gpad * 2;
+    const size_t sbytes = tiled_scale_bytes(M, K);
     e = cudaMalloc(reinterpret_cast<void**>(&w->scales), sbytes);
     if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "scale alloc"));
-    e = cudaMemsetAsync(w->scales, 0, sbytes, s);
-    if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "scale memset"));
-    e = cudaMemcpy2DAsync(w->scales, (size_t)w->gpad * 2, scales, (size_t)G * 2, (size_t)G * 2, M,
-                          from_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s);
-    if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "scale upload"));
+    e = launch_repack_scales(canon_s, w->scales, M, K, s);
+    if (e != cudaSuccess) return cleanup(cuda_fail(ctx, e, "scale repack"));
+    ctx->launches++;
     w->bytes += sbytes;
   }
   e = cudaStreamSynchronize(s);
@@ -307,6 +322,7 @@ ouroq_status ouroq_ctx_create(int device, ouroq_ctx** out) {
   if (!ctx) return OUROQ_ERR_OOM;
   ctx->device = device;
   ctx->num_sms = prop.multiProcessorCount;
+  ctx->smem_optin = (int)prop.sharedMemPerBlockOptin;
   DeviceGuard g(device);
   if (cudaMalloc(reinterpret_cast<void**>(&ctx->d_status), sizeof(unsigned)) != cudaSuccess ||
       cudaMemset(ctx->d_status, 0, sizeof(unsigned)) != cudaSuccess ||
@@ -484,6 +500,47 @@ ouroq_status ouroq_gemm_group(ouroq_ctx* ctx, int n, const ouroq_weight* const* 
   return run_gemv(ctx, L, static_cast<cudaStream_t>(stream));
 }
 
+ouroq_status ouroq_gemm_group_f32act(ouroq_ctx* ctx, int n, const ouroq_weight* const* w,
+                                     const float* const* x, int B, const float* const* signs,
+                                     const int* blocks, float* const* y, void* stream) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  if (n < 0 || n > kMaxGemvJobs)
+    return fail(ctx, OUROQ_ERR_BAD_SHAPE, "group size %d (max %d)", n, kMaxGemvJobs);
+  if (B < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d", B);
+  if (n == 0 || B == 0) return OUROQ_OK;
+  if (!w || !x || !y) return fail(ctx, OUROQ_ERR_BAD_ARG, "null array");
+  GemvLaunch L{};
+  L.njobs = n;
+  L.B = B;
+  L.fused = 1;
+  int maxK = 0;
+  for (int i = 0; i < n; ++i) {
+    if (!w[i] || !x[i] || !y[i]) return fail(ctx, OUROQ_ERR_BAD_ARG, "null entry %d", i);
+    if (w[i]->fmt != w[0]->fmt) return fail(ctx, OUROQ_ERR_UNSUPPORTED, "mixed formats in a group");
+    const int blk = blocks ? blocks[i] : 0;
+    ouroq_status st = check_quant_args(ctx, B, w[i]->K, blk);
+    if (st != OUROQ_OK) return st;
+    if (blk != 0 && (blk < 32 || blk > 128))
+      return fail(ctx, OUROQ_ERR_UNSUPPORTED, "fused rotation needs a hadamard block of 32..128");
+    if (blk != (blocks ? blocks[0] : 0))
+      return fail(ctx, OUROQ_ERR_UNSUPPORTED, "all entries of a fused group share one hadamard block");
+    if (!aligned16(x[i])) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "x[%d] not 16-byte aligned", i);
+    L.jobs[i] = make_job(w[i], nullptr, nullptr, y[i], nullptr);
+    L.jobs[i].xf = x[i];
+    L.jobs[i].signs = signs ? signs[i] : nullptr;
+    L.jobs[i].had_block = blk;
+    L.jobs[i].had_scale = blk ? 1.0f / std::sqrt((float)blk) : 1.0f;
+    maxK = w[i]->K > maxK ? w[i]->K : maxK;
+  }
+  L.fmt = w[0]->fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
+  if (B > kGemvMaxB || !gemv_fits(ctx, L))
+    return fail(ctx, OUROQ_ERR_UNSUPPORTED,
+                "B=%d, K=%d: activations do not fit the fused GEMV (use quantize + gemm_group)",
+                B, maxK);
+  DeviceGuard g(ctx->device);
+  return run_gemv(ctx, L, static_cast<cudaStream_t>(stream));
+}
+
 ouroq_status ouroq_gemm_f32act(ouroq_ctx* ctx, const ouroq_weight* w, const float* x, int B,
                                const float* signs, int hadamard_block, float* y, void* stream) {
   if (!ctx || !w) return fail(ctx, OUROQ_ERR_BAD_ARG, "null handle");
@@ -494,11 +551,26 @@ ouroq_status ouroq_gemm_f32act(ouroq_ctx* ctx, const ouroq_weight* w, const floa
   if (st != OUROQ_OK) return st;
   if (!aligned16(x)) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "x not 16-byte aligned");
   DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int dfmt = w->fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
+  if (B <= kGemvMaxB && (hadamard_block == 0 || (hadamard_block >= 32 && hadamard_block <= 128))) {
+    // one launch: rotate + quantise in the GEMV prologue
+    GemvLaunch L{};
+    L.njobs = 1;
+    L.B = B;
+    L.fmt = dfmt;
+    L.fused = 1;
+    L.jobs[0] = make_job(w, nullptr, nullptr, y, nullptr);
+    L.jobs[0].xf = x;
+    L.jobs[0].signs = signs;
+    L.jobs[0].had_block = hadamard_block;
+    L.jobs[0].had_scale = hadamard_block ? 1.0f / std::sqrt((float)hadamard_block) : 1.0f;
+    if (gemv_fits(ctx, L)) return run_gemv(ctx, L, s);
+  }
   st = grow(ctx, ctx->q_scratch, ctx->q_cap, (size_t)B * w->K, "q scratch");
   if (st != OUROQ_OK) return st;
   st = grow(ctx, ctx->s_scratch, ctx->s_cap, (size_t)B, "s scratch");
   if (st != OUROQ_OK) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   st = quantize_impl(ctx, x, B, w->K, signs, hadamard_block, ctx->q_scratch, ctx->s_scratch, s);
   if (st != OUROQ_OK) return st;
   return gemm_impl(ctx, w, ctx->q_scratch, ctx->s_scratch, B, y, nullptr, s);

@@ -147,7 +147,12 @@ inline cudaError_t ensure_max_smem() {
   int optin = 0;
   e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(Func, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+  cudaFuncAttributes fa;
+  e = cudaFuncGetAttributes(&fa, Func);
+  if (e != cudaSuccess) return e;
+  // the dynamic limit excludes the kernel's static shared memory
+  e = cudaFuncSetAttribute(Func, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           optin - (int)fa.sharedSizeBytes);
   if (e == cudaSuccess && dev < 64) done[dev] = 1;
   return e;
 }

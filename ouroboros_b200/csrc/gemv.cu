@@ -1,94 +1,110 @@
 // gemv.cu -- K2 / K3: packed ternary (2-bit) and 1-bit-sign weight x int8
 // activation GEMV for small token batches (B <= 8), grouped over up to eight
-// matrices per launch.
+// matrices per launch, optionally with the activation quantisation (and the
+// blockwise Hadamard rotation) fused into the prologue.
 //
 // Reference operator: ops::matvec_q / matmul_q (cluster/src/infer/ops.rs:76-84,
 // 219-230), called per named tensor by Stage::wm / wmat_batched
 // (cluster/src/infer/mod.rs:138-167). The arithmetic follows north_star
-// (int8 activations, int32 accumulation, fp32 epilogue) as fixed in
-// oracle/oracle.h.
+// (int8 activations, int32 accumulation, fp32 epilogue) with the conventions
+// fixed by the CPU oracle (oracle/oracle.h).
 //
 // Design (sm_100a):
 //  * Work unit = tile of 32 weight rows x all of K. A CTA (one per SM) walks a
-//    contiguous range of tiles across the job list, so a CTA changes job at
-//    most a few times.
-//  * Weights stream HBM -> shared memory with 1-D bulk copies (one per row
-//    per K-slice) into an NS-stage ring tracked by mbarriers. A dedicated
-//    producer warp issues them; rows are padded by 16 B so that consumer lanes
-//    (one lane per row) read 16-byte chunks without bank conflicts.
-//  * Programmatic dependent launch: the producer issues the first NS weight
-//    stages BEFORE griddepcontrol.wait (weights never depend on the previous
-//    kernel); only the activation copy waits. Successor kernels are released
-//    at entry, so their weight prefetch overlaps this kernel's tail.
-//  * Activations (int8 [B][K]) sit in shared memory (double-buffered per job
-//    switch) and are read as warp-wide broadcasts.
+//    contiguous range of tiles; the host balances the ranges by weight bytes.
+//  * Weights stream HBM -> shared memory through a ring of up to 13 stages
+//    tracked by mbarriers, one 1-D bulk copy per stage (a K-slice of a 32-row
+//    tile is contiguous in the tiled device layout: 8-16 KB per copy; small
+//    copies are limited by the copy engine's op rate, large ones run at HBM
+//    speed). A producer warp issues them and never waits for the previous
+//    grid: weights do not depend on it.
+//  * 15 consumer warps. Before touching weights they wait for the previous
+//    grid (programmatic dependent launch), then load the activations of every
+//    job of the CTA with ordinary loads (not through the copy queue, where
+//    they would sit behind the weight prefetch), optionally rotate them
+//    (blockwise Walsh-Hadamard), take the per-token absmax, quantise to int8
+//    and keep them in shared memory with their per-group sums.
+//  * Consumer lanes (one per row) read chunk c of rows 0..31 = 512 contiguous
+//    bytes of a stage: no bank conflicts. Activations are read as broadcasts.
+//  * The job table is copied from the kernel parameters into shared memory
+//    once: dependent lookups into the parameter bank miss the constant cache
+//    one after another.
 //  * Math: with the device layout of kernels.h, masking a weight word with
 //    0x03030303 << 2j (ternary) or 0x01010101 << j (sign) gives four byte
-//    lanes = code * 2^(2j) (or bit * 2^j) for four consecutive k, and one
+//    lanes = code * 4^j (or bit * 2^j) for four consecutive k, and one
 //    dp4a.u32.s32 against the matching int8 word accumulates them. Separate
 //    accumulators per mask are shifted back exactly at the end:
 //      ternary: acc = sum_j (A_j >> 2j) - sum(q)            (c = w + 1)
 //      sign:    acc_g = 2 * sum_j (A_j >> j) - sum_{k in g}(q)
+//    The integer pipe (half the issue rate) bounds this loop at about 64
+//    packed-ternary bytes per clock per SM, 1.4x the SM's share of HBM.
 //  * Epilogues in fp32 with explicit _rn intrinsics (no contraction), in the
 //    oracle's order, so y is bit-identical to the CPU oracle.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "hadamard.cuh"
 #include "kernels.h"
 
 namespace ouroq {
 namespace {
 
-constexpr int kRows = 32;           // rows per tile (one per consumer lane)
-constexpr int kCWarps = 8;          // consumer warps
-constexpr int kThreads = (kCWarps + 1) * 32;
-constexpr int kStages = 4;          // ring depth
-constexpr int kTernSliceChunks = 32;  // 16-B chunks per row per stage (512 B)
-constexpr int kSignSliceChunks = 16;  // 256 B per row per stage (16 groups)
+constexpr int kRows = kTileRows;      // rows per tile (one per consumer lane)
+// 15 consumer warps + 1 producer warp = 16 warps: four per SM sub-partition,
+// which leaves each thread 128 registers (a 17th warp would cap them at 96).
+constexpr int kCWarps = 15;
+constexpr int kCThreads = kCWarps * 32;
+constexpr int kThreads = kCThreads + 32;
+constexpr int kMaxStages = kMaxGemvStages;
+constexpr int kTernSliceChunks = 32;  // 16-B chunks per row per stage (16 KB stage)
+constexpr int kSignSliceChunks = 16;  // 16 groups per row per stage (8 KB + 1 KB scales)
 
-// Stage row pitch: ternary rows are 512 B of weights + 16 B pad (132 words,
-// = 4 mod 32 banks); sign rows are 256 B of weights + 32 B of fp16 group
-// scales + 16 B pad (76 words, = 12 mod 32). Both make the eight lanes of a
-// quarter-warp hit disjoint banks with 16-byte loads.
+// Stage layout: weights [chunk][32 rows][16 B]; sign stages append the fp16
+// group scales of the slice as [group][32 rows].
 template <int FMT>
 struct Fmt;
 template <>
 struct Fmt<kTern2> {
   static constexpr int kSliceChunks = kTernSliceChunks;
   static constexpr int kWeightsPerChunk = 64;
-  static constexpr int kPitch = kTernSliceChunks * 16 + 16;
-  __device__ static int row_bytes(int K) { return K / 4; }
+  static constexpr int kStageBytes = kTernSliceChunks * 512;
 };
 template <>
 struct Fmt<kSign1> {
   static constexpr int kSliceChunks = kSignSliceChunks;
   static constexpr int kWeightsPerChunk = 128;
-  static constexpr int kPitch = kSignSliceChunks * 16 + 32 + 16;
-  __device__ static int row_bytes(int K) { return K / 8; }
+  static constexpr int kStageBytes = kSignSliceChunks * (512 + 64);
 };
 
-// Shared-memory plan (dynamic), all offsets 16-byte aligned:
-//   [0, 64)                          mbarriers: full[kStages], empty[kStages], xfull[2], xempty[2]
-//   stage ring                       kStages * kRows * pitch
-//   x buffers                        2 * B * maxK bytes
-//   qsum                             2 * B * maxG ints   (ternary: maxG = 1)
-//   red / terms                      ternary: kCWarps*B*32 ints; sign: B*slice*32 floats
+__host__ __device__ constexpr uint32_t align128(uint32_t v) { return (v + 127u) & ~127u; }
+
+// Shared-memory plan (dynamic), every region 128-byte aligned:
+//   job table   copy of the GemvLaunch parameters
+//   barriers    full[13], empty[13]
+//   ring        stages * stage bytes
+//   xwork       xcap bytes: int8 activations [job][B][K] of the CTA's jobs
+//   qg          gcap ints: per-(token, 128-group) activation sums
+//   sx / qtot   [8 jobs][8 tokens] per-token scales / sums
+//   red         ternary: kCWarps*B*32 ints; sign: B*slice*32 floats
 struct Plan {
-  uint32_t ring, xbuf, qsum, red, total;
+  uint32_t bars, ring, xwork, qg, sx, qtot, red, total;
 };
 
-__host__ __device__ inline Plan make_plan(int fmt, int B, int maxK) {
+__host__ __device__ inline Plan make_plan(int fmt, int B, int stages, int xcap, int gcap) {
   Plan p;
-  const int slice = fmt == kTern2 ? kTernSliceChunks : kSignSliceChunks;
-  const int pitch = fmt == kTern2 ? Fmt<kTern2>::kPitch : Fmt<kSign1>::kPitch;
-  const int maxG = fmt == kTern2 ? 1 : maxK / 128;
-  p.ring = 128;
-  p.xbuf = p.ring + kStages * kRows * pitch;
-  p.qsum = p.xbuf + 2 * B * maxK;
-  p.red = p.qsum + ((2 * B * maxG * 4 + 15) / 16) * 16;
-  const uint32_t red_bytes = fmt == kTern2 ? kCWarps * B * 32 * 4 : B * slice * 32 * 4;
-  p.total = p.red + red_bytes;
+  const uint32_t slice = fmt == kTern2 ? kTernSliceChunks : kSignSliceChunks;
+  const uint32_t stage = fmt == kTern2 ? Fmt<kTern2>::kStageBytes : Fmt<kSign1>::kStageBytes;
+  const uint32_t b = (uint32_t)B;
+  p.bars = align128(sizeof(GemvLaunch));
+  p.ring = p.bars + 256;
+  p.xwork = p.ring + (uint32_t)stages * stage;
+  p.qg = p.xwork + align128((uint32_t)xcap);
+  p.sx = p.qg + align128((uint32_t)gcap * 4u);
+  p.qtot = p.sx + 256;
+  p.red = p.qtot + 256;
+  const uint32_t red_bytes = fmt == kTern2 ? kCWarps * b * 32u * 4u : b * slice * 32u * 4u;
+  p.total = p.red + align128(red_bytes);
   return p;
 }
 
@@ -96,176 +112,351 @@ struct TileInfo {
   int job, row0, rows;
 };
 
-__device__ __forceinline__ TileInfo tile_info(const GemvLaunch& L, int t) {
+__host__ __device__ __forceinline__ TileInfo tile_info(const GemvLaunch& L, int t) {
   int j = 0;
-#pragma unroll 1
   while (j + 1 < L.njobs && t >= L.jobs[j + 1].tile_begin) ++j;
   TileInfo ti;
   ti.job = j;
   ti.row0 = (t - L.jobs[j].tile_begin) * kRows;
-  int r = L.jobs[j].M - ti.row0;
+  const int r = L.jobs[j].M - ti.row0;
   ti.rows = r < kRows ? r : kRows;
   return ti;
 }
 
 template <int FMT>
-__device__ __forceinline__ int nslices_of(int K) {
-  const int C = K / Fmt<FMT>::kWeightsPerChunk;
-  return (C + Fmt<FMT>::kSliceChunks - 1) / Fmt<FMT>::kSliceChunks;
+__device__ __forceinline__ int chunks_of(int K) {
+  return K / Fmt<FMT>::kWeightsPerChunk;
 }
 
-// Slice s covers chunks [c0, c1) of the row. Ternary slices are balanced;
-// sign slices start at multiples of 16 groups so that their fp16 scales
-// (32 B per full slice) stay 16-byte aligned for the bulk copy.
+template <int FMT>
+__device__ __forceinline__ int nslices_of(int K) {
+  return (chunks_of<FMT>(K) + Fmt<FMT>::kSliceChunks - 1) / Fmt<FMT>::kSliceChunks;
+}
+
+// Slice s covers chunks [c0, c1) of the row (balanced split).
 template <int FMT>
 __device__ __forceinline__ void slice_range(int K, int s, int ns, int& c0, int& c1) {
-  const int C = K / Fmt<FMT>::kWeightsPerChunk;
-  const int per = FMT == kTern2 ? (C + ns - 1) / ns : Fmt<FMT>::kSliceChunks;
+  const int C = chunks_of<FMT>(K);
+  const int per = (C + ns - 1) / ns;
   c0 = s * per;
   c1 = c0 + per < C ? c0 + per : C;
 }
 
+// Position in the weight ring: slot index and how many times it wrapped.
+struct RingPos {
+  int slot = 0, round = 0;
+  __device__ __forceinline__ void next(int ns) {
+    if (++slot == ns) {
+      slot = 0;
+      ++round;
+    }
+  }
+};
+
+// ---------------------------------------------------------------- prologue
+// The activations of a CTA's jobs are processed as "units" of 32*E = 128
+// consecutive values of one token row, E = 4 per lane; a unit holds whole
+// rotation blocks (block <= 128) and exactly one 128-group. Units of all (job, token) rows are numbered consecutively and
+// dealt to warps round-robin; each warp loads NB = max(1, 16/E) units before
+// using any of them, so a pass costs a few memory round trips, not one per
+// unit (in-order issue stalls at the first use of a load).
+struct Seg {
+  const float* x;     // fp32 row (global)
+  int8_t* q;          // int8 row (shared)
+  int* qg;            // per-128-group sums (shared)
+  int first_unit;     // global index of the row's first unit
+  int sidx;           // index into the per-token scale table
+};
+
+template <int E>
+__device__ __forceinline__ void load_unit(float* v, const float* src) {
+#pragma unroll
+  for (int i = 0; i < E; i += 4) {
+    const float4 t = *reinterpret_cast<const float4*>(src + i);
+    v[i] = t.x;
+    v[i + 1] = t.y;
+    v[i + 2] = t.z;
+    v[i + 3] = t.w;
+  }
+}
+
+// rotate_fwd of hadamard.rs:41-53 on one unit (block hb <= 32*E)
+template <int E>
+__device__ __forceinline__ void rotate_unit(float* v, const float* signs, int off, int hb,
+                                            float hscale, int lane) {
+  if (hb <= 0) return;
+  if (signs) {
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = __fmul_rn(v[i], signs[off + i]);
+  }
+  wht_span<E>(v, lane, hb);
+#pragma unroll
+  for (int i = 0; i < E; ++i) v[i] = __fmul_rn(v[i], hscale);
+}
+
+// Four int8 codes packed into a word; their sum is returned through *sum.
+// Kept out of line: the prologue runs once per CTA, and inlining two dozen
+// IEEE divisions bloats the code that every SM has to fetch cold.
+__device__ __noinline__ uint32_t quant4(float a, float b, float c, float d, float s, int* sum) {
+  const int c0 = quant_code(a, s), c1 = quant_code(b, s), c2 = quant_code(c, s),
+            c3 = quant_code(d, s);
+  *sum += c0 + c1 + c2 + c3;
+  return (uint32_t)(c0 & 0xFF) | ((uint32_t)(c1 & 0xFF) << 8) | ((uint32_t)(c2 & 0xFF) << 16) |
+         ((uint32_t)c3 << 24);
+}
+
+__device__ __forceinline__ int seg_of(const Seg* segs, int nseg, int unit) {
+  int s = 0;
+  while (s + 1 < nseg && unit >= segs[s + 1].first_unit) ++s;
+  return s;
+}
+
+// One warp's share of the prologue. Units u = warp, warp + kCWarps, ... of
+// the CTA. The first R = max(1, 24/E) of them are loaded (all loads issued before any
+// use), rotated and kept in registers across the absmax barrier, so a CTA
+// whose rows fit pays a single memory round trip; further units are loaded
+// again for the quantisation pass (shared memory leaves L1 too small to hold
+// them).
+template <int E>
+__device__ void prologue_units(const Seg* segs, int nseg, int nunits, const float* signs, int hb,
+                               float hscale, int* amax_bits, float* sx, int nscale, int B,
+                               int warp, int lane) {
+  constexpr int R = E >= 24 ? 1 : 24 / E;
+  constexpr int kLanesPerGroup = 128 / E;
+  float v[R][E];
+  int sg[R], off[R];
+  // ---- pass 1: load, rotate, absmax
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    const int u = warp + k * kCWarps;
+    sg[k] = -1;
+    if (u < nunits) {
+      sg[k] = seg_of(segs, nseg, u);
+      off[k] = (u - segs[sg[k]].first_unit) * 32 * E + lane * E;
+      load_unit<E>(v[k], segs[sg[k]].x + off[k]);
+    }
+  }
+  auto absmax_unit = [&](const float* w, int seg) {
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) m = fmaxf(m, fabsf(w[i]));
+    m = warp_max(m);
+    if (lane == 0) atomicMax(&amax_bits[segs[seg].sidx], __float_as_int(m));
+  };
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    if (sg[k] < 0) continue;  // warp-uniform
+    rotate_unit<E>(v[k], signs, off[k], hb, hscale, lane);
+    absmax_unit(v[k], sg[k]);
+  }
+  for (int u = warp + R * kCWarps; u < nunits; u += kCWarps) {
+    const int seg = seg_of(segs, nseg, u);
+    const int o = (u - segs[seg].first_unit) * 32 * E + lane * E;
+    float w[E];
+    load_unit<E>(w, segs[seg].x + o);
+    rotate_unit<E>(w, signs, o, hb, hscale, lane);
+    absmax_unit(w, seg);
+  }
+  named_bar_sync(1, kCThreads);
+  const int ctid = threadIdx.x;
+  if (ctid < nscale && (ctid & 7) < B) sx[ctid] = __fdiv_rn(__int_as_float(amax_bits[ctid]), 127.0f);
+  named_bar_sync(1, kCThreads);
+  // ---- pass 2: quantise, store int8 codes and 128-group sums
+  auto quant_unit = [&](const float* w, int seg, int o) {
+    const Seg& S = segs[seg];
+    const float sc = sx[S.sidx];
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < E; i += 4)
+      *reinterpret_cast<uint32_t*>(S.q + o + i) = quant4(w[i], w[i + 1], w[i + 2], w[i + 3], sc, &sum);
+#pragma unroll
+    for (int d = kLanesPerGroup / 2; d >= 1; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
+    if (lane % kLanesPerGroup == 0) S.qg[o / 128] = sum;
+  };
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    if (sg[k] < 0) continue;
+    quant_unit(v[k], sg[k], off[k]);
+  }
+  for (int u = warp + R * kCWarps; u < nunits; u += kCWarps) {
+    const int seg = seg_of(segs, nseg, u);
+    const int o = (u - segs[seg].first_unit) * 32 * E + lane * E;
+    float w[E];
+    load_unit<E>(w, segs[seg].x + o);
+    rotate_unit<E>(w, signs, o, hb, hscale, lane);
+    quant_unit(w, seg, o);
+  }
+}
+
+
 template <int FMT, int B>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvLaunch L) {
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvLaunch Lp) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int SC = Fmt<FMT>::kSliceChunks;
-  constexpr int PITCH = Fmt<FMT>::kPitch;
+  constexpr int STAGE = Fmt<FMT>::kStageBytes;
 
-  int maxK = 0;
-  for (int j = 0; j < L.njobs; ++j) maxK = L.jobs[j].K > maxK ? L.jobs[j].K : maxK;
-  const Plan P = make_plan(FMT, B, maxK);
-  const int maxG = FMT == kTern2 ? 1 : maxK / 128;
+  // ---- job table -> shared memory (one parallel load instead of serial parameter reads)
+  {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(&Lp);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(smem);
+    for (int i = threadIdx.x; i < (int)(sizeof(GemvLaunch) / 4); i += blockDim.x) dst[i] = src[i];
+  }
+  __syncthreads();
+  const GemvLaunch& L = *reinterpret_cast<const GemvLaunch*>(smem);
+  const int NS = L.stages;
+  const Plan P = make_plan(FMT, B, NS, L.xcap, L.gcap);
 
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + kStages;
-  uint64_t* xfull = empty + kStages;
-  uint64_t* xempty = xfull + 2;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.bars);
+  uint64_t* empty = full + kMaxStages;
   uint8_t* ring = smem + P.ring;
-  int8_t* xbuf = reinterpret_cast<int8_t*>(smem + P.xbuf);
-  int* qsum = reinterpret_cast<int*>(smem + P.qsum);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // contiguous tile range of this CTA
-  const int t_begin = (int)(((long long)blockIdx.x * L.ntiles) / gridDim.x);
-  const int t_end = (int)(((long long)(blockIdx.x + 1) * L.ntiles) / gridDim.x);
-
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kCWarps);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&xfull[i], 1);
-      mbar_init(&xempty[i], kCWarps);
     }
     fence_mbar_init();
   }
   __syncthreads();
   pdl_launch_dependents();
 
+  // this CTA's tile range (balanced by weight bytes on the host)
+  const int t_begin = L.cta_tile[blockIdx.x];
+  const int t_end = L.cta_tile[blockIdx.x + 1];
+  if (t_begin >= t_end) return;
+
   if (warp == kCWarps) {
-    // ---------------- producer warp ----------------
-    uint64_t pol = policy_evict_first();
-    // total stage count of this CTA (needed to size the pre-wait prefetch)
-    int total = 0;
-    for (int t = t_begin; t < t_end; ++t) total += nslices_of<FMT>(L.jobs[tile_info(L, t).job].K);
-    const int prefetch = total < kStages ? total : kStages;
-    bool waited = false;
-    int xi = 0;            // x copies issued
-    int x_next_tile = t_begin;  // first tile whose job's x copy is still pending
-    int last_job = -1;
+    // ---------------- producer warp: weights only ----------------
+    const uint64_t pol = policy_evict_first();
     int st = 0;
-
-    // issue the x copies for every job switch among tiles [x_next_tile, upto]
-    auto issue_x_upto = [&](int upto) {
-      for (; x_next_tile <= upto; ++x_next_tile) {
-        const int j = tile_info(L, x_next_tile).job;
-        if (j == last_job) continue;
-        last_job = j;
-        const int buf = xi & 1;
-        if (xi >= 2) {
-          if (!mbar_wait(&xempty[buf], ((xi >> 1) - 1) & 1, L.status)) return false;
-        }
-        const GemvJob& J = L.jobs[j];
-        const uint32_t bytes = (uint32_t)(B * J.K);
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&xfull[buf], bytes);
-          bulk_g2s(xbuf + (size_t)buf * B * maxK, J.q, bytes, &xfull[buf]);
-        }
-        __syncwarp();
-        ++xi;
-      }
-      return true;
-    };
-
+    RingPos rp;
     bool ok = true;
     for (int t = t_begin; t < t_end && ok; ++t) {
       const TileInfo ti = tile_info(L, t);
       const GemvJob& J = L.jobs[ti.job];
-      const int rb = Fmt<FMT>::row_bytes(J.K);
       const int ns = nslices_of<FMT>(J.K);
+      const int C = chunks_of<FMT>(J.K);
+      const size_t tile = (size_t)(ti.row0 / kRows);
       for (int s = 0; s < ns; ++s, ++st) {
-        if (st == prefetch && !waited) {
-          pdl_wait();
-          waited = true;
-          ok = issue_x_upto(t);
-          if (!ok) break;
-        } else if (waited) {
-          ok = issue_x_upto(t);
-          if (!ok) break;
+        const int slot = rp.slot;
+        if (rp.round > 0 && !mbar_wait(&empty[slot], (rp.round - 1) & 1, L.status)) {
+          ok = false;
+          break;
         }
-        const int slot = st % kStages;
-        if (st >= kStages) {
-          if (!mbar_wait(&empty[slot], ((st / kStages) - 1) & 1, L.status)) {
-            ok = false;
-            break;
-          }
-        }
+        rp.next(NS);
         int c0, c1;
         slice_range<FMT>(J.K, s, ns, c0, c1);
-        const uint32_t sb = (uint32_t)(c1 - c0) * 16;
-        // sign: fp16 scales of the slice, rounded up to 16 B (rows padded on upload)
-        const uint32_t scb = FMT == kSign1 ? (uint32_t)(((c1 - c0) * 2 + 15) / 16) * 16 : 0u;
-        if (lane == 0) mbar_arrive_expect_tx(&full[slot], (sb + scb) * ti.rows);
-        __syncwarp();
-        if (lane < ti.rows) {
-          uint8_t* dst = ring + (size_t)slot * kRows * PITCH + lane * PITCH;
-          const uint8_t* src = J.w + (size_t)(ti.row0 + lane) * rb + (size_t)c0 * 16;
-          bulk_g2s_stream(dst, src, sb, &full[slot], pol);
-          if (FMT == kSign1) {
-            const uint16_t* ssrc = J.scales + (size_t)(ti.row0 + lane) * J.gpad + c0;
-            bulk_g2s(dst + SC * 16, ssrc, scb, &full[slot]);
-          }
+        const uint32_t wb = (uint32_t)(c1 - c0) * 512;
+        const uint32_t sb = FMT == kSign1 ? (uint32_t)(c1 - c0) * 64 : 0u;
+        if (lane == 0) {
+          uint8_t* dst = ring + (size_t)slot * STAGE;
+          mbar_arrive_expect_tx(&full[slot], wb + sb);
+          bulk_g2s_stream(dst, J.w + (tile * C + c0) * 512, wb, &full[slot], pol);
+          if (FMT == kSign1)
+            bulk_g2s(dst + SC * 512, J.scales + (tile * C + c0) * kRows, sb, &full[slot]);
         }
         __syncwarp();
       }
     }
-    if (ok && !waited) {
-      pdl_wait();
-      ok = issue_x_upto(t_end - 1);
-    }
     // Drain: every bulk copy issued into this CTA's shared memory must land
     // before the CTA exits (consumers normally wait for all of them already;
     // this matters only after a timed-out wait).
-    for (int i = (st > kStages ? st - kStages : 0); i < st; ++i)
-      mbar_wait(&full[i % kStages], (i / kStages) & 1, L.status);
-    for (int i = (xi > 2 ? xi - 2 : 0); i < xi; ++i) mbar_wait(&xfull[i & 1], (i >> 1) & 1, L.status);
+    for (int i = (st > NS ? st - NS : 0); i < st; ++i)
+      mbar_wait(&full[i % NS], (i / NS) & 1, L.status);
     return;
   }
 
   // ---------------- consumer warps ----------------
+  const int ctid = threadIdx.x;
+  const int j_lo = tile_info(L, t_begin).job;
+  const int j_hi = tile_info(L, t_end - 1).job;
+  int8_t* xwork = reinterpret_cast<int8_t*>(smem + P.xwork);
+  int* qg_base = reinterpret_cast<int*>(smem + P.qg);
+  float* sx_s = reinterpret_cast<float*>(smem + P.sx);    // [job - j_lo][b]
+  int* qtot_s = reinterpret_cast<int*>(smem + P.qtot);    // [job - j_lo][b]
+
+  // activations of this CTA's jobs may be produced by the previous grid
   pdl_wait();
+
+  // ---- prologue: activations of jobs j_lo..j_hi -> int8 in shared memory
+  if (L.fused) {
+    // one segment per (job, token) row; all jobs of a fused launch share the
+    // rotation block (checked on the host), hence one unit size E
+    __shared__ Seg segs[kMaxGemvJobs * 8];
+    __shared__ int amax_bits[kMaxGemvJobs * 8];
+    // units of 128 values (the host routes rotation blocks above 128 through
+    // the stand-alone quantiser)
+    constexpr int e = 4;
+    int nseg = 0, nunits = 0;
+    {
+      int xoff = 0, goff = 0;
+      for (int jj = j_lo; jj <= j_hi; ++jj) {
+        const GemvJob& J = L.jobs[jj];
+        for (int b = 0; b < B; ++b, ++nseg) {
+          if (ctid == 0) {
+            segs[nseg].x = J.xf + (size_t)b * J.K;
+            segs[nseg].q = xwork + xoff + b * J.K;
+            segs[nseg].qg = qg_base + goff + b * (J.K / 128);
+            segs[nseg].first_unit = nunits;
+            segs[nseg].sidx = (jj - j_lo) * 8 + b;
+            amax_bits[(jj - j_lo) * 8 + b] = 0;
+          }
+          nunits += J.K / (32 * e);
+        }
+        xoff += B * J.K;
+        goff += B * (J.K / 128);
+      }
+    }
+    named_bar_sync(1, kCThreads);
+    const GemvJob& J0 = L.jobs[j_lo];
+    prologue_units<e>(segs, nseg, nunits, J0.signs, J0.had_block, J0.had_scale, amax_bits, sx_s,
+                      (j_hi - j_lo + 1) * 8, B, warp, lane);
+  } else {
+    int xoff = 0, goff = 0;
+    for (int jj = j_lo; jj <= j_hi; ++jj) {
+      const GemvJob& J = L.jobs[jj];
+      const int K = J.K, G = K / 128;
+      for (int b = 0; b < B; ++b) {
+        int8_t* q = xwork + xoff + b * K;
+        int* qg = qg_base + goff + b * G;
+        const int8_t* src = J.q + (size_t)b * K;
+        for (int g = warp; g < G; g += kCWarps) {
+          const uint32_t v = *reinterpret_cast<const uint32_t*>(src + g * 128 + lane * 4);
+          *reinterpret_cast<uint32_t*>(q + g * 128 + lane * 4) = v;
+          const int sum = warp_sum(__dp4a((int)v, 0x01010101, 0));
+          if (lane == 0) qg[g] = sum;
+        }
+        if (ctid == 0) sx_s[(jj - j_lo) * 8 + b] = J.s_x[b];
+      }
+      xoff += B * K;
+      goff += B * G;
+    }
+  }
+  named_bar_sync(1, kCThreads);
+  if (FMT == kTern2) {
+    // per-token sums of each job
+    int goff = 0;
+    for (int jj = j_lo; jj <= j_hi; ++jj) {
+      const int G = L.jobs[jj].K / 128;
+      if (ctid < B) {
+        int s = 0;
+        for (int g = 0; g < G; ++g) s += qg_base[goff + ctid * G + g];
+        qtot_s[(jj - j_lo) * 8 + ctid] = s;
+      }
+      goff += B * G;
+    }
+    named_bar_sync(1, kCThreads);
+  }
+
   int* red = reinterpret_cast<int*>(smem + P.red);
   float* terms = reinterpret_cast<float*>(smem + P.red);
-  const int nct = kCWarps * 32;
-  const int ctid = threadIdx.x;
-  int xc = 0;  // x buffers consumed
-  int cur_job = -1;
   int st = 0;
+  RingPos rp;
   bool ok = true;
-
+  int cur_job = -1, xoff = 0, goff = 0;
   // A failed (timed-out) wait clears `ok`: later waits are skipped but every
   // warp keeps walking the same sequence of named barriers, so the CTA always
   // terminates; the host sees the status word.
@@ -273,55 +464,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     const TileInfo ti = tile_info(L, t);
     const GemvJob& J = L.jobs[ti.job];
     const int K = J.K;
+    const int G = K / 128;
     const int ns = nslices_of<FMT>(K);
     if (ti.job != cur_job) {
       if (cur_job >= 0) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&xempty[(xc - 1) & 1]);
+        xoff += B * L.jobs[cur_job].K;
+        goff += B * (L.jobs[cur_job].K / 128);
       }
-      if (ok) ok = mbar_wait(&xfull[xc & 1], (xc >> 1) & 1, L.status);
       cur_job = ti.job;
-      ++xc;
-      // per-token (ternary) or per-group (sign) activation sums
-      const int8_t* xs = xbuf + (size_t)((xc - 1) & 1) * B * maxK;
-      int* qs = qsum + ((xc - 1) & 1) * B * maxG;
-      named_bar_sync(1, nct);  // previous users of this qsum buffer are done
-      if (FMT == kTern2) {
-        if (ctid < B) qs[ctid] = 0;
-        named_bar_sync(1, nct);
-        for (int b = 0; b < B; ++b) {
-          int part = 0;
-          for (int i = ctid * 16; i < K; i += nct * 16) {
-            uint4 v = *reinterpret_cast<const uint4*>(xs + (size_t)b * K + i);
-            part = __dp4a((int)v.x, 0x01010101, part);
-            part = __dp4a((int)v.y, 0x01010101, part);
-            part = __dp4a((int)v.z, 0x01010101, part);
-            part = __dp4a((int)v.w, 0x01010101, part);
-          }
-          part = warp_sum(part);
-          if (lane == 0) atomicAdd(&qs[b], part);
-        }
-      } else {
-        const int G = K / 128;
-        for (int p = ctid; p < B * G; p += nct) {
-          const int b = p / G, g = p % G;
-          const int8_t* src = xs + (size_t)b * K + g * 128;
-          int part = 0;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            uint4 v = *reinterpret_cast<const uint4*>(src + i * 16);
-            part = __dp4a((int)v.x, 0x01010101, part);
-            part = __dp4a((int)v.y, 0x01010101, part);
-            part = __dp4a((int)v.z, 0x01010101, part);
-            part = __dp4a((int)v.w, 0x01010101, part);
-          }
-          qs[b * maxG + g] = part;
-        }
-      }
-      named_bar_sync(1, nct);
     }
-    const int8_t* xs = xbuf + (size_t)((xc - 1) & 1) * B * maxK;
-    const int* qs = qsum + ((xc - 1) & 1) * B * maxG;
+    const int8_t* xs = xwork + xoff;
+    const int* qg = qg_base + goff;
+    const float* sx = sx_s + (ti.job - j_lo) * 8;
+    const int* qtot = qtot_s + (ti.job - j_lo) * 8;
     const int row = ti.row0 + lane;
     const bool row_ok = lane < ti.rows;
 
@@ -333,24 +488,41 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         for (int j = 0; j < 4; ++j) A[b][j] = 0;
 
       for (int s = 0; s < ns; ++s, ++st) {
-        const int slot = st % kStages;
-        if (ok) ok = mbar_wait(&full[slot], (st / kStages) & 1, L.status);
+        const int slot = rp.slot;
+        if (ok) ok = mbar_wait(&full[slot], rp.round & 1, L.status);
+        rp.next(NS);
         int c0, c1;
         slice_range<FMT>(K, s, ns, c0, c1);
-        const uint8_t* wrow = ring + (size_t)slot * kRows * PITCH + lane * PITCH;
-        for (int kc = warp; kc < c1 - c0; kc += kCWarps) {
-          const uint4 wv = *reinterpret_cast<const uint4*>(wrow + kc * 16);
-          const uint32_t wl[4] = {wv.x, wv.y, wv.z, wv.w};
+        const uint8_t* stg = ring + (size_t)slot * STAGE + lane * 16;
+        const int nck = c1 - c0;
+        // chunk kc belongs to warp (kc + st) % kCWarps: the remainder chunks of
+        // a stage land on different warps from stage to stage
+        const int first = ((warp - st) % kCWarps + kCWarps) % kCWarps;
+        const int8_t* xrow = xs + (size_t)c0 * 64;
+        for (int kc = first; kc < nck; kc += 2 * kCWarps) {
+          // two chunks per iteration: every shared load is issued before the math
+          const bool two = kc + kCWarps < nck;
+          const int kd = two ? kc + kCWarps : kc;
+          const uint4 wa = *reinterpret_cast<const uint4*>(stg + kc * 512);
+          const uint4 wb = *reinterpret_cast<const uint4*>(stg + kd * 512);
+          const uint32_t wl[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
           for (int b = 0; b < B; ++b) {
-            const uint4* xp = reinterpret_cast<const uint4*>(xs + (size_t)b * K + (size_t)(c0 + kc) * 64);
+            const uint4* xa = reinterpret_cast<const uint4*>(xrow + (size_t)b * K + kc * 64);
+            const uint4* xb = reinterpret_cast<const uint4*>(xrow + (size_t)b * K + kd * 64);
+            uint4 xv[8];
 #pragma unroll
             for (int t4 = 0; t4 < 4; ++t4) {
-              const uint4 xv = xp[t4];
-              A[b][0] = dp4a_us(wl[t4] & 0x03030303u, xv.x, A[b][0]);
-              A[b][1] = dp4a_us(wl[t4] & 0x0C0C0C0Cu, xv.y, A[b][1]);
-              A[b][2] = dp4a_us(wl[t4] & 0x30303030u, xv.z, A[b][2]);
-              A[b][3] = dp4a_us(wl[t4] & 0xC0C0C0C0u, xv.w, A[b][3]);
+              xv[t4] = xa[t4];
+              xv[4 + t4] = xb[t4];
+            }
+#pragma unroll
+            for (int t4 = 0; t4 < 8; ++t4) {
+              if (t4 >= 4 && !two) break;  // odd chunk count: the second chunk is absent
+              A[b][0] = dp4a_us(wl[t4] & 0x03030303u, xv[t4].x, A[b][0]);
+              A[b][1] = dp4a_us(wl[t4] & 0x0C0C0C0Cu, xv[t4].y, A[b][1]);
+              A[b][2] = dp4a_us(wl[t4] & 0x30303030u, xv[t4].z, A[b][2]);
+              A[b][3] = dp4a_us(wl[t4] & 0xC0C0C0C0u, xv[t4].w, A[b][3]);
             }
           }
         }
@@ -361,35 +533,36 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
 #pragma unroll
       for (int b = 0; b < B; ++b)
         red[(warp * B + b) * 32 + lane] = A[b][0] + (A[b][1] >> 2) + (A[b][2] >> 4) + (A[b][3] >> 6);
-      named_bar_sync(2, nct);
+      named_bar_sync(2, kCThreads);
       for (int b = warp; b < B; b += kCWarps) {
-        int acc = -qs[b];
+        int acc = -qtot[b];
 #pragma unroll
         for (int w = 0; w < kCWarps; ++w) acc += red[(w * B + b) * 32 + lane];
         if (row_ok) {
-          const float y = __fmul_rn(__fmul_rn(__int2float_rn(acc), J.w_scale), J.s_x[b]);
+          const float y = __fmul_rn(__fmul_rn(__int2float_rn(acc), J.w_scale), sx[b]);
           J.y[(size_t)b * J.ldy + row] = y;
           if (J.acc) J.acc[(size_t)b * J.M + row] = acc;
         }
       }
-      named_bar_sync(2, nct);
+      named_bar_sync(2, kCThreads);
     } else {
-      const int G = K / 128;
       float sum[B];
 #pragma unroll
       for (int b = 0; b < B; ++b) sum[b] = 0.0f;
       for (int s = 0; s < ns; ++s, ++st) {
-        const int slot = st % kStages;
-        if (ok) ok = mbar_wait(&full[slot], (st / kStages) & 1, L.status);
+        const int slot = rp.slot;
+        if (ok) ok = mbar_wait(&full[slot], rp.round & 1, L.status);
+        rp.next(NS);
         int c0, c1;
         slice_range<FMT>(K, s, ns, c0, c1);
-        const uint8_t* wrow = ring + (size_t)slot * kRows * PITCH + lane * PITCH;
-        for (int kc = warp; kc < c1 - c0; kc += kCWarps) {
-          const uint4 wv = *reinterpret_cast<const uint4*>(wrow + kc * 16);
+        const uint8_t* stg = ring + (size_t)slot * STAGE;
+        const int first = ((warp - st) % kCWarps + kCWarps) % kCWarps;
+        for (int kc = first; kc < c1 - c0; kc += kCWarps) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(stg + kc * 512 + lane * 16);
           const uint32_t wl[4] = {wv.x, wv.y, wv.z, wv.w};
           const int g = c0 + kc;
-          const float sc = __half2float(
-              __ushort_as_half(*reinterpret_cast<const uint16_t*>(wrow + SC * 16 + kc * 2)));
+          const float sc = __half2float(__ushort_as_half(
+              *reinterpret_cast<const uint16_t*>(stg + SC * 512 + kc * 64 + lane * 2)));
 #pragma unroll
           for (int b = 0; b < B; ++b) {
             const uint4* xp = reinterpret_cast<const uint4*>(xs + (size_t)b * K + (size_t)g * 128);
@@ -411,14 +584,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             }
             const int sb = a[0] + (a[1] >> 1) + (a[2] >> 2) + (a[3] >> 3) + (a[4] >> 4) +
                            (a[5] >> 5) + (a[6] >> 6) + (a[7] >> 7);
-            const int accg = 2 * sb - qs[b * maxG + g];
+            const int accg = 2 * sb - qg[b * G + g];
             terms[(b * SC + kc) * 32 + lane] = __fmul_rn(__int2float_rn(accg), sc);
             if (J.acc && row_ok) J.acc[((size_t)b * J.M + row) * G + g] = accg;
           }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
-        named_bar_sync(2, nct);
+        named_bar_sync(2, kCThreads);
         // ordered (ascending g) fp32 accumulation by the owner warp of each token
 #pragma unroll
         for (int b = 0; b < B; ++b) {
@@ -427,11 +600,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
           for (int kc = 0; kc < c1 - c0; ++kc) v = __fadd_rn(v, terms[(b * SC + kc) * 32 + lane]);
           sum[b] = v;
         }
-        named_bar_sync(2, nct);
+        named_bar_sync(2, kCThreads);
       }
 #pragma unroll
       for (int b = 0; b < B; ++b) {
-        if (b % kCWarps == warp && row_ok) J.y[(size_t)b * J.ldy + row] = __fmul_rn(sum[b], J.s_x[b]);
+        if (b % kCWarps == warp && row_ok) J.y[(size_t)b * J.ldy + row] = __fmul_rn(sum[b], sx[b]);
       }
     }
   }
@@ -471,14 +644,72 @@ cudaError_t launch_fmt(const GemvLaunch& L, int grid, size_t smem, cudaStream_t 
 
 }  // namespace
 
-size_t gemv_smem_bytes(int fmt, int B, int maxK) { return make_plan(fmt, B, maxK).total; }
+bool gemv_prepare(GemvLaunch& L, int num_sms, int smem_optin, int* grid_out, size_t* smem_out) {
+  const int wpc = L.fmt == kTern2 ? 64 : 128;
+  int tiles = 0;
+  long long total = 0;
+  for (int j = 0; j < L.njobs; ++j) {
+    L.jobs[j].tile_begin = tiles;
+    const int nt = (L.jobs[j].M + kRows - 1) / kRows;
+    tiles += nt;
+    total += (long long)nt * (L.jobs[j].K / wpc);
+  }
+  L.ntiles = tiles;
+  *grid_out = 0;
+  *smem_out = 0;
+  if (tiles <= 0) return true;
+  if (tiles > 65535 || L.B < 1 || L.B > kGemvMaxB) return false;
+  int grid = tiles < num_sms ? tiles : num_sms;
+  if (grid > kMaxGemvCtas) grid = kMaxGemvCtas;
+  // CTA c starts at the first tile whose cumulative weight reaches c * total / grid
+  {
+    int j = 0, t = 0;
+    long long w = 0;  // weight of tiles [0, t)
+    for (int c = 0; c <= grid; ++c) {
+      const long long target = total * c / grid;
+      while (t < tiles && w < target) {
+        while (j + 1 < L.njobs && t >= L.jobs[j + 1].tile_begin) ++j;
+        w += L.jobs[j].K / wpc;
+        ++t;
+      }
+      L.cta_tile[c] = (uint16_t)t;
+    }
+    L.cta_tile[grid] = (uint16_t)tiles;
+  }
+  // activations one CTA keeps resident: the jobs its tile range touches
+  int xcap = 0, gcap = 0;
+  for (int c = 0; c < grid; ++c) {
+    if (L.cta_tile[c] >= L.cta_tile[c + 1]) continue;
+    const int jlo = tile_info(L, L.cta_tile[c]).job;
+    const int jhi = tile_info(L, L.cta_tile[c + 1] - 1).job;
+    int x = 0, g = 0;
+    for (int j = jlo; j <= jhi; ++j) {
+      x += L.B * L.jobs[j].K;
+      g += L.B * (L.jobs[j].K / 128);
+    }
+    xcap = x > xcap ? x : xcap;
+    gcap = g > gcap ? g : gcap;
+  }
+  L.xcap = xcap;
+  L.gcap = gcap;
+  // deepest ring that fits next to the activations (4 KB are left for the
+  // kernel's static shared memory)
+  const uint32_t budget = (uint32_t)smem_optin - 4096u;
+  int stages = kMaxStages;
+  while (stages > 2 && make_plan(L.fmt, L.B, stages, xcap, gcap).total > budget) --stages;
+  L.stages = stages;
+  const size_t smem = make_plan(L.fmt, L.B, stages, xcap, gcap).total;
+  if (smem > budget) return false;
+  *grid_out = grid;
+  *smem_out = smem;
+  return true;
+}
 
-cudaError_t launch_gemv(const GemvLaunch& L, int num_sms, cudaStream_t s, bool pdl) {
-  if (L.ntiles <= 0) return cudaSuccess;
-  int maxK = 0;
-  for (int j = 0; j < L.njobs; ++j) maxK = L.jobs[j].K > maxK ? L.jobs[j].K : maxK;
-  const size_t smem = gemv_smem_bytes(L.fmt, L.B, maxK);
-  const int grid = L.ntiles < num_sms ? L.ntiles : num_sms;
+cudaError_t launch_gemv(GemvLaunch& L, int num_sms, int smem_optin, cudaStream_t s, bool pdl) {
+  int grid = 0;
+  size_t smem = 0;
+  if (!gemv_prepare(L, num_sms, smem_optin, &grid, &smem)) return cudaErrorInvalidValue;
+  if (grid == 0) return cudaSuccess;
   if (L.fmt == kTern2) return launch_fmt<kTern2>(L, grid, smem, s, pdl);
   if (L.fmt == kSign1) return launch_fmt<kSign1>(L, grid, smem, s, pdl);
   return cudaErrorInvalidValue;

@@ -10,32 +10,46 @@ namespace ouroq {
 
 // Device weight layouts (produced by the repack kernels at upload time).
 //
-// kTern2: one 32-bit word per 16 weights of a row (k = 16t .. 16t+15); in
-//   word t, byte b, bits (2j, 2j+1) hold code c = w + 1 of k = 16t + 4j + b.
-//   Masking a word with 0x03030303 << 2j therefore yields four bytes whose
-//   values are c * 4^j for four consecutive k, ready for dp4a against four
-//   consecutive int8 activations.
-// kSign1: one 32-bit word per 32 weights (k = 32t .. 32t+31); in word t,
-//   byte b, bit j holds the sign bit of k = 32t + 4j + b. Group scales stay
-//   fp16, stored [M][gpad] with gpad = K/128 rounded up to a multiple of 16
-//   (zero padding) so every 16-group slice of a row starts 16-byte aligned.
+// Rows are grouped in tiles of kTileRows = 32. A row is cut into 16-byte
+// chunks (64 ternary or 128 sign weights each), and a tile is stored
+// chunk-major: byte offset of (tile t, chunk c, row r) =
+//   (t * C + c) * 512 + r * 16,     C = row_bytes / 16.
+// Any run of chunks of a tile is therefore one contiguous block (one large
+// bulk copy per pipeline stage), and 32 lanes reading chunk c of rows 0..31
+// touch 512 contiguous bytes of shared memory (no bank conflicts).
+// Rows past M in the last tile are zero.
+//
+// Within each 32-bit word the bits are permuted so that one mask exposes four
+// consecutive k in the four byte lanes:
+// kTern2: word t of a row covers k = 16t .. 16t+15; byte b, bits (2j, 2j+1)
+//   hold code c = w + 1 of k = 16t + 4j + b. Masking with 0x03030303 << 2j
+//   yields four bytes c * 4^j for k = 16t+4j .. 16t+4j+3, ready for dp4a.
+// kSign1: word t covers k = 32t .. 32t+31; byte b, bit j holds the sign bit
+//   of k = 32t + 4j + b. fp16 group scales are tiled the same way:
+//   [tile][group][32 rows].
 enum DevFormat : int { kTern2 = 1, kSign1 = 2 };
+constexpr int kTileRows = 32;
 
 // One matrix-times-activations job of a (possibly grouped) GEMV launch.
 struct GemvJob {
-  const uint8_t* w;         // device layout, [M][row_bytes]
-  const uint16_t* scales;   // kSign1: fp16 [M][gpad] (rows padded to 16 groups); else null
-  const int8_t* q;          // [B][K] int8 activations (16-byte aligned)
-  const float* s_x;         // [B] per-token scales
+  const uint8_t* w;         // tiled device layout
+  const uint16_t* scales;   // kSign1: tiled fp16 group scales; else null
+  const int8_t* q;          // [B][K] int8 activations (16-byte aligned), unfused mode
+  const float* s_x;         // [B] per-token scales, unfused mode
+  const float* xf;          // [B][K] fp32 activations (16-byte aligned), fused mode
+  const float* signs;       // fused mode: rotation signs [K] or null (all +1)
   float* y;                 // [B][ldy] fp32 outputs, row b at y + b*ldy
   int32_t* acc;             // optional debug: tern [B][M]; sign [B][M][K/128]
   float w_scale;            // kTern2 per-tensor scale
+  float had_scale;          // fused mode: 1/sqrt(had_block)
   int M, K, ldy;
-  int gpad;                 // kSign1: scale row pitch in fp16 elements (multiple of 16)
+  int had_block;            // fused mode: Hadamard block, 0 = no rotation
   int tile_begin;           // first global tile index of this job
 };
 
 constexpr int kMaxGemvJobs = 8;
+constexpr int kMaxGemvCtas = 160;  // >= SM count of the device (148 on B200)
+constexpr int kMaxGemvStages = 13;
 
 struct GemvLaunch {
   GemvJob jobs[kMaxGemvJobs];
@@ -43,7 +57,14 @@ struct GemvLaunch {
   int ntiles;               // total 32-row tiles over all jobs
   int B;                    // tokens (same for all jobs)
   int fmt;                  // DevFormat (same for all jobs)
+  int fused;                // 1: jobs carry fp32 activations and quantise in the prologue
+  int stages;               // weight ring depth (2..kMaxGemvStages), sized to shared memory
+  int xcap;                 // bytes of int8 activations one CTA keeps resident (its jobs)
+  int gcap;                 // per-group activation sums one CTA keeps resident (ints)
   unsigned* status;         // device status word
+  // CTA c owns tiles [cta_tile[c], cta_tile[c+1]): ranges balanced by weight
+  // bytes on the host, so the kernel does no 64-bit division at start-up.
+  uint16_t cta_tile[kMaxGemvCtas + 1];
 };
 
 // One activation-quantisation job (fp32 [B][K] -> int8 [B][K] + s_x[B]).
@@ -70,10 +91,15 @@ struct QuantLaunch {
 cudaError_t launch_quantize(const QuantLaunch& L, cudaStream_t s, bool pdl);
 cudaError_t launch_rotate(const float* x, float* out, const float* signs, int B, int K,
                           int block, float scale, int inverse, cudaStream_t s);
-cudaError_t launch_gemv(const GemvLaunch& L, int num_sms, cudaStream_t s, bool pdl);
-size_t gemv_smem_bytes(int fmt, int B, int maxK);
-cudaError_t launch_repack_tern2(const uint8_t* canon, uint8_t* dev, int M, int K, cudaStream_t s);
-cudaError_t launch_repack_sign1(const uint8_t* canon, uint8_t* dev, int M, int K, cudaStream_t s);
+// Fills L.ntiles, tile_begin, the CTA ranges, xcap/gcap and stages; returns
+// false when the activations of one CTA's jobs cannot be kept in shared memory.
+bool gemv_prepare(GemvLaunch& L, int num_sms, int smem_optin, int* grid, size_t* smem);
+cudaError_t launch_gemv(GemvLaunch& L, int num_sms, int smem_optin, cudaStream_t s, bool pdl);
+size_t tiled_weight_bytes(int fmt, int M, int K);
+size_t tiled_scale_bytes(int M, int K);
+cudaError_t launch_repack(int fmt, const uint8_t* canon, uint8_t* dev, int M, int K, cudaStream_t s);
+cudaError_t launch_repack_scales(const uint16_t* canon, uint16_t* dev, int M, int K,
+                                 cudaStream_t s);
 
 // Limits of the small-batch GEMV path.
 constexpr int kGemvMaxB = 8;

@@ -205,6 +205,54 @@ def test_gemm_group_c2_layer(ctx, oracle):
         w.free()
 
 
+@pytest.mark.parametrize("B", [1, 2])
+def test_gemm_group_f32act_c2_layer(ctx, oracle, B):
+    # one fused launch: fp32 activations quantised in the GEMV prologue
+    import torch
+    shapes = [(3840, 2560), (2560, 2560), (6912, 2560), (6912, 2560), (2560, 6912)]
+    inputs = [oracle.normals(400 + i, B * k).reshape(B, k) for i, k in enumerate([2560, 2560, 2560, 6912])]
+    input_of = [0, 1, 2, 2, 3]
+    ws_, xs, ys, want = [], [], [], []
+    for i, (M, K) in enumerate(shapes):
+        packed, wsc, _ = tern_case(oracle, M, K, 1, seed=500 + i)
+        x = inputs[input_of[i]]
+        qr, sr = oracle.quantize_act(x)
+        want.append(oracle.gemm_tern2(packed, M, K, wsc, qr, sr)[1])
+        ws_.append(ctx.upload(oq.TERNARY2, packed, M, K, w_scale=wsc))
+        xs.append(dev(x))
+        ys.append(torch.empty((B, M), dtype=torch.float32, device="cuda"))
+    ctx.gemm_group_f32act(ws_, xs, ys)
+    for y, yr in zip(ys, want):
+        assert np.array_equal(host(y), yr)
+    for w in ws_:
+        w.free()
+
+
+@pytest.mark.parametrize("block", [64, 128, 1024])
+@pytest.mark.parametrize("M,K,B", [(4096, 4096, 1), (11008, 4096, 1), (300, 2048, 3)])
+def test_fused_hadamard_sign_gemv(ctx, oracle, M, K, B, block):
+    packed, sc, x = sign_case(oracle, M, K, B, seed=M + block)
+    sg = oracle.signs(77, K).astype(np.float32)
+    qr, sr = oracle.quantize_act(x, sg, block)
+    _, yr = oracle.gemm_sign1(packed, sc, M, K, qr, sr)
+    w = ctx.upload(oq.SIGN1G128, packed, M, K, scales=sc)
+    y = ctx.gemm_f32act(w, dev(x), signs=dev(sg), hadamard_block=block)
+    assert np.array_equal(host(y), yr)
+    w.free()
+
+
+def test_fused_group_rejects_oversized_activations(ctx, oracle):
+    import torch
+    packed, wsc, _ = tern_case(oracle, 64, 28672, 1, seed=3)
+    w = ctx.upload(oq.TERNARY2, packed, 64, 28672, w_scale=wsc)
+    x = torch.zeros((8, 28672), device="cuda")
+    y = torch.empty((8, 64), device="cuda")
+    with pytest.raises(oq.OuroqError) as e:
+        ctx.gemm_group_f32act([w], [x], [y])
+    assert e.value.status == 6
+    w.free()
+
+
 def test_host_mirrors_matvec_matmul(ctx, oracle):
     M, K = 1000, 2560
     packed, ws, x = tern_case(oracle, M, K, 5, seed=42)
