@@ -25,6 +25,7 @@ struct ouroq_ctx {
   int num_sms = 0;
   int smem_optin = 0;  // opt-in shared memory per block (bytes)
   bool pdl = true;
+  bool use_tc = true;  // tensor-core path for batches >= 16
   std::string err;
   unsigned* d_status = nullptr;
   uint64_t launches = 0;
@@ -163,8 +164,29 @@ ouroq_status run_gemv(ouroq_ctx* ctx, GemvLaunch& L, cudaStream_t s) {
   return OUROQ_OK;
 }
 
+// Token batches from this size up run on the tensor cores (ternary weights).
+constexpr int kTcMinBatch = 16;
+
 ouroq_status gemm_impl(ouroq_ctx* ctx, const ouroq_weight* w, const int8_t* q, const float* s_x,
                        int B, float* y, int32_t* acc, cudaStream_t s) {
+  const int dfmt = w->fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
+  if (B >= kTcMinBatch && ctx->use_tc && gemm_tc_supported(dfmt, w->M, w->K, B)) {
+    TcLaunch L{};
+    L.w = w->w;
+    L.y = y;
+    L.acc = acc;
+    L.s_x = s_x;
+    L.w_scale = w->w_scale;
+    L.M = w->M;
+    L.K = w->K;
+    L.ldy = w->M;
+    L.tok0 = 0;
+    L.nvalid = B;
+    L.status = ctx->d_status;
+    CU(ctx, launch_gemm_tc(L, q, B, ctx->smem_optin, s), "tensor-core gemm launch");
+    ctx->launches += (B + 255) / 256;
+    return OUROQ_OK;
+  }
   const int chunk = gemv_chunk(w->K);
   if (chunk < 1) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "K=%d too wide for the GEMV path", w->K);
   const int G = w->K / 128;

@@ -1,0 +1,428 @@
+// gemm_tc.cu -- K4: batched packed-ternary x int8 GEMM on the 5th-generation
+// tensor cores (tcgen05.mma kind::i8, accumulators in tensor memory).
+//
+// Reference operator: ops::matmul_q / matmul_tl1 (cluster/src/infer/ops.rs:
+// 162-230): K activation columns share each weight row, the output is
+// [k][out_len]. Here the arithmetic is north_star's: int8 activations, exact
+// int32 accumulation, y = ((float)acc * w_scale) * s_x, identical to the CPU
+// oracle (oracle/oracle.h).
+//
+// Tiling ("swap AB"): the MMA's M = 128 weight rows (operand A: 2-bit codes
+// expanded to u8 c = w + 1 and written straight into tensor memory), N = up
+// to 256 tokens (operand B: the int8 activations, TMA-loaded into shared
+// memory with the 128-byte swizzle), K = 32 per instruction. One CTA owns 128
+// rows of W and N tokens and walks all of K:
+//   warp 0      producer: per stage, bulk copies of the packed weight slice
+//               (four 32-row tiles of the tiled device layout) + TMA tensor
+//               loads of the activation slice
+//   warp 1      allocates tensor memory; one lane issues the MMAs (A from
+//               tensor memory, B from shared memory) and commits them to
+//               mbarriers
+//   warps 2-5   expand 2-bit codes to bytes (tcgen05.st into 4 rotating A
+//               buffers), sum each token's activations (the correction for
+//               c = w + 1), then run the epilogue out of tensor memory
+// Keeping A out of shared memory matters: expanding in shared memory would
+// cost a 4x write plus a 4x MMA read per packed byte, more shared-memory
+// bandwidth than the HBM stream feeds.
+// The accumulator is D[row][token] = sum_k c * q; acc = D - sum_k q.
+// Every wait is bounded and reports through the status word.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ouroq {
+namespace {
+
+constexpr int kTcRows = 128;     // weight rows per CTA = MMA M
+constexpr int kSliceK = 128;     // k per A buffer = 4 MMAs of K = 32
+constexpr int kTcThreads = 192;  // 6 warps
+constexpr int kMaxTcStages = 6;
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// mbarrier arrives once all previously issued MMAs of this thread are done
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 2-D TMA tile load (no multicast) completing on an mbarrier
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor (sm_100 format): start address, leading and
+// stride byte offsets in 16-byte units, version 1, layout type in bits 61-63.
+__device__ __forceinline__ uint64_t smem_desc(const void* p, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
+  const uint32_t a = smem_u32(p);
+  uint64_t d = 0;
+  d |= (uint64_t)((a >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;  // descriptor version for sm_100
+  d |= (uint64_t)(layout & 7u) << 61;
+  return d;
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc], u8 x s8 -> s32 (A read from tensor memory)
+__device__ __forceinline__ void mma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// this thread's lane, 32 consecutive 32-bit columns
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Tensor memory (512 columns x 128 lanes, 32 bit): accumulator D[row][token]
+// in columns [0, 256); expanded weight blocks A (128 rows x 128 k = 32
+// columns each, 4 int8 per column) in kTmemABufs buffers from column 256.
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemA0 = 256;
+constexpr int kTmemABufs = 4;
+
+struct TcPlan {
+  uint32_t bars, tmem, qsum, stage0, stage_bytes, act_off, total;
+  int ks;  // k per TMA stage (multiple of 128)
+};
+
+// Stage = the packed weights of 128 rows x ks k (four 32-row tiles, ks*8 B
+// each) followed by the activations (ks/128 swizzled 128-byte column blocks
+// of N rows). Larger k slices for small N keep enough weight bytes in flight.
+__host__ __device__ inline TcPlan tc_plan(int N, int stages) {
+  TcPlan p;
+  p.ks = N <= 64 ? 512 : (N <= 128 ? 256 : 128);
+  p.bars = 0;    // full[6], sfree[6], afull[4], afree[4], accfull
+  p.tmem = 256;  // allocated tensor-memory address
+  p.qsum = 512;  // int [256]
+  p.stage0 = 2048;
+  p.act_off = (uint32_t)p.ks * 32;  // 4 tiles x ks*8 B of packed weights
+  p.stage_bytes = ((p.act_off + (uint32_t)N * (uint32_t)p.ks + 1023) / 1024) * 1024;
+  p.total = p.stage0 + (uint32_t)stages * p.stage_bytes + 1024;  // + alignment slack
+  return p;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap act_map, const __grid_constant__ TcLaunch P) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzled activation tiles
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const TcPlan pl = tc_plan(P.N, P.stages);
+  const int S = P.stages;
+  const int KS = pl.ks;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + pl.bars);
+  uint64_t* sfree = full + kMaxTcStages;
+  uint64_t* afull = sfree + kMaxTcStages;
+  uint64_t* afree = afull + kTmemABufs;
+  uint64_t* accfull = afree + kTmemABufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + pl.tmem);
+  int* qsum = reinterpret_cast<int*>(smem + pl.qsum);
+  uint8_t* stages = smem + pl.stage0;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * kTcRows;
+  const int nstages = (P.K + KS - 1) / KS;  // the last stage may be shorter
+  const int C = P.K / 64;  // 16-byte chunks per packed row
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&sfree[i], 1);
+    }
+    for (int i = 0; i < kTmemABufs; ++i) {
+      mbar_init(&afull[i], 4);
+      mbar_init(&afree[i], 1);
+    }
+    mbar_init(accfull, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) qsum[i] = 0;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      // 32-row tiles of this CTA that exist (the last CTA may cover fewer)
+      const int ntiles = (P.M + kTileRows - 1) / kTileRows - row0 / kTileRows;
+      const int vt = ntiles < 4 ? ntiles : 4;
+      bool waited = false;
+      for (int s = 0; s < nstages; ++s) {
+        const int slot = s % S;
+        if (s >= S && !mbar_wait(&sfree[slot], ((s / S) - 1) & 1, P.status)) break;
+        const int ks = P.K - s * KS < KS ? P.K - s * KS : KS;
+        const int SUB = ks / kSliceK;
+        const uint32_t wbytes = (uint32_t)ks * 8u;  // per 32-row tile
+        uint8_t* st = stages + (size_t)slot * pl.stage_bytes;
+        mbar_arrive_expect_tx(&full[slot], wbytes * (uint32_t)vt + (uint32_t)(P.N * ks));
+        for (int t = 0; t < vt; ++t) {
+          const size_t tile = (size_t)(row0 / kTileRows + t);
+          bulk_g2s_stream(st + t * (KS * 8), P.w + (tile * C + (size_t)s * (KS / 64)) * 512, wbytes,
+                          &full[slot], pol);
+        }
+        if (!waited) {
+          pdl_wait();  // activations may come from the previous grid
+          waited = true;
+        }
+        for (int u = 0; u < SUB; ++u)
+          tma_load_2d(st + pl.act_off + (uint32_t)u * (uint32_t)P.N * 128u, &act_map,
+                      s * KS + u * kSliceK, P.tok0, &full[slot]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issue (one lane) ----------------
+    if (lane == 0) {
+      // instruction descriptor: D s32, A u8, B s8, both K-major, N, M = 128
+      const uint32_t idesc = (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(P.N >> 3) << 17) |
+                             ((uint32_t)(kTcRows >> 4) << 24);
+      bool ok = true;
+      int g = 0;
+      for (int s = 0; s < nstages && ok; ++s) {
+        const int slot = s % S;
+        ok = mbar_wait(&full[slot], (s / S) & 1, P.status);
+        uint8_t* st = stages + (size_t)slot * pl.stage_bytes;
+        const int SUB = (P.K - s * KS < KS ? P.K - s * KS : KS) / kSliceK;
+        for (int u = 0; u < SUB && ok; ++u, ++g) {
+          const int b = g % kTmemABufs;
+          ok = mbar_wait(&afull[b], (g / kTmemABufs) & 1, P.status);
+          if (!ok) break;
+          tc_fence_after();
+          const uint8_t* act = st + pl.act_off + (uint32_t)u * (uint32_t)P.N * 128u;
+#pragma unroll
+          for (int mb = 0; mb < 4; ++mb) {
+            // B: activations, 128-byte swizzle: rows 128 B apart, 8-row groups
+            //    1024 B apart (SBO); K block mb starts 32 B into the row
+            const uint64_t bd = smem_desc(act + mb * 32, 16, 1024, 2);
+            mma_i8_ts(tmem, tmem + kTmemA0 + (uint32_t)b * 32u + (uint32_t)mb * 8u, bd, idesc,
+                      (s > 0 || u > 0 || mb > 0) ? 1u : 0u);
+          }
+          mma_commit(&afree[b]);  // the A buffer may be refilled once these MMAs finished
+        }
+        mma_commit(&sfree[slot]);  // and the stage (weights + activations)
+      }
+      mma_commit(accfull);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- expansion + epilogue (warps 2..5) ----------------
+    const int q = warp & 3;           // tensor-memory lane quarter of this warp
+    const int r = q * 32 + lane;      // weight row within the CTA tile (= TMEM lane)
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    int qs0 = 0, qs1 = 0;             // running sum_k q for tokens e and e + 128
+    const int e = (warp - 2) * 32 + lane;
+    bool ok = true;
+    int g = 0;
+    for (int s = 0; s < nstages; ++s) {
+      const int slot = s % S;
+      if (ok) ok = mbar_wait(&full[slot], (s / S) & 1, P.status);
+      const uint8_t* st = stages + (size_t)slot * pl.stage_bytes;
+      const uint8_t* src = st + (r >> 5) * (KS * 8) + (r & 31) * 16;
+      const int SUB = (P.K - s * KS < KS ? P.K - s * KS : KS) / kSliceK;
+      for (int u = 0; u < SUB; ++u, ++g) {
+        const int b = g % kTmemABufs;
+        if (ok && g >= kTmemABufs) ok = mbar_wait(&afree[b], ((g / kTmemABufs) - 1) & 1, P.status);
+        // expand this row's two 64-k chunks of the sub-block into 32 columns
+        uint32_t a[32];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(src + (2 * u + c) * 512);
+          const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            a[c * 16 + t * 4 + 0] = w4[t] & 0x03030303u;
+            a[c * 16 + t * 4 + 1] = (w4[t] >> 2) & 0x03030303u;
+            a[c * 16 + t * 4 + 2] = (w4[t] >> 4) & 0x03030303u;
+            a[c * 16 + t * 4 + 3] = (w4[t] >> 6) & 0x03030303u;
+          }
+        }
+        tmem_st32(tmem + lane_base + kTmemA0 + (uint32_t)b * 32u, a);
+        // activation sums of this sub-block: rows e and e + 128 of the swizzled tile
+        const uint8_t* act = st + pl.act_off + (uint32_t)u * (uint32_t)P.N * 128u;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int n = e + half * 128;
+          if (n < P.N) {
+            int sum = 0;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const uint4 v = *reinterpret_cast<const uint4*>(act + n * 128 + ((c ^ (n & 7)) * 16));
+              sum = __dp4a((int)v.x, 0x01010101, sum);
+              sum = __dp4a((int)v.y, 0x01010101, sum);
+              sum = __dp4a((int)v.z, 0x01010101, sum);
+              sum = __dp4a((int)v.w, 0x01010101, sum);
+            }
+            if (half == 0) qs0 += sum; else qs1 += sum;
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[b]);
+      }
+    }
+    if (e < P.N) qsum[e] = qs0;
+    if (e + 128 < P.N) qsum[e + 128] = qs1;
+    named_bar_sync(1, 128);
+    // ---- epilogue: D[row][token] from tensor memory
+    if (ok) ok = mbar_wait(accfull, 0, P.status);
+    tc_fence_after();
+    const int row = row0 + r;
+    for (int j0 = 0; j0 < P.N; j0 += 32) {
+      uint32_t d[32];
+      tmem_ld32(tmem + lane_base + (uint32_t)j0, d);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = j0 + j;
+        if (n < P.nvalid && row < P.M) {
+          const int tok = P.tok0 + n;
+          const int acc = (int)d[j] - qsum[n];
+          P.y[(size_t)tok * P.ldy + row] =
+              __fmul_rn(__fmul_rn(__int2float_rn(acc), P.w_scale), P.s_x[tok]);
+          if (P.acc) P.acc[(size_t)tok * P.M + row] = acc;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+size_t gemm_tc_smem_bytes(int N, int stages) { return tc_plan(N, stages).total; }
+
+bool gemm_tc_supported(int fmt, int M, int K, int B) {
+  return fmt == kTern2 && M > 0 && K % kSliceK == 0 && B >= 1;
+}
+
+cudaError_t launch_gemm_tc(const TcLaunch& L0, const int8_t* q, int Btot, int smem_optin,
+                           cudaStream_t s) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  cudaError_t e = ensure_max_smem<gemm_tc_kernel>();
+  if (e != cudaSuccess) return e;
+  for (int tok0 = 0; tok0 < L0.nvalid; tok0 += 256) {
+    TcLaunch L = L0;
+    const int nv = L0.nvalid - tok0 < 256 ? L0.nvalid - tok0 : 256;
+    L.tok0 = L0.tok0 + tok0;
+    L.nvalid = nv;
+    L.N = (nv + 15) / 16 * 16;
+    if (L.N < 16) L.N = 16;
+    int stages = kMaxTcStages;
+    while (stages > 2 && tc_plan(L.N, stages).total > (uint32_t)smem_optin - 2048u) --stages;
+    L.stages = stages;
+    const size_t smem = tc_plan(L.N, stages).total;
+    // activations [Btot][K] int8, box 128 B x N rows, 128-byte swizzle, zero fill
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)L.K, (cuuint64_t)Btot};
+    const cuuint64_t strides[1] = {(cuuint64_t)L.K};
+    const cuuint32_t box[2] = {128u, (cuuint32_t)L.N};
+    const cuuint32_t estr[2] = {1u, 1u};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+    const dim3 grid((L.M + kTcRows - 1) / kTcRows, 1, 1);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel, map, L);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace ouroq

@@ -101,6 +101,28 @@ cudaError_t launch_repack(int fmt, const uint8_t* canon, uint8_t* dev, int M, in
 cudaError_t launch_repack_scales(const uint16_t* canon, uint16_t* dev, int M, int K,
                                  cudaStream_t s);
 
+// One tensor-core GEMM launch (ternary): 128 weight rows per CTA x N tokens.
+struct TcLaunch {
+  const uint8_t* w;   // tiled device layout (kTern2)
+  float* y;           // [tokens][ldy]
+  int32_t* acc;       // optional debug [tokens][M]
+  const float* s_x;   // [tokens]
+  float w_scale;
+  int M, K, ldy;
+  int tok0;           // first token of this launch
+  int N;              // tokens per CTA pass (multiple of 16, 16..256), filled by the launcher
+  int nvalid;         // valid tokens from tok0
+  int stages;         // filled by the launcher
+  unsigned* status;
+};
+
+bool gemm_tc_supported(int fmt, int M, int K, int B);
+size_t gemm_tc_smem_bytes(int N, int stages);
+// q: int8 activations [Btot][K] (16-byte aligned rows). Splits tokens into
+// passes of at most 256.
+cudaError_t launch_gemm_tc(const TcLaunch& L, const int8_t* q, int Btot, int smem_optin,
+                           cudaStream_t s);
+
 // Limits of the small-batch GEMV path.
 constexpr int kGemvMaxB = 8;
 constexpr size_t kGemvMaxXBytes = 64 * 1024;  // B*K int8 resident in shared memory

@@ -137,6 +137,24 @@ def test_gemm_tern2_batched_c2(ctx, oracle, B):
     w.free()
 
 
+# B >= 16: tcgen05 tensor-core path (u8 codes x s8 activations, TMEM accumulators)
+@pytest.mark.parametrize("M,K,B", [(128, 128, 16), (256, 256, 17), (200, 384, 33), (96, 512, 64),
+                                   (6912, 2560, 64), (2560, 6912, 100), (3840, 2560, 256),
+                                   (1000, 1024, 300), (2560, 2560, 512)])
+def test_gemm_tern2_tensor_core(ctx, oracle, M, K, B):
+    import torch
+    packed, ws, x = tern_case(oracle, M, K, B, seed=M + 3 * K + B)
+    qr, sr = oracle.quantize_act(x)
+    accr, yr = oracle.gemm_tern2(packed, M, K, ws, qr, sr)
+    w = ctx.upload(oq.TERNARY2, packed, M, K, w_scale=ws)
+    acc = torch.empty((B, M), dtype=torch.int32, device="cuda")
+    y = ctx.gemm(w, dev(qr), dev(sr), acc=acc)
+    assert np.array_equal(host(acc), accr)
+    assert np.array_equal(host(y), yr)
+    w.free()
+    ctx.check_device()
+
+
 def test_gemm_tern2_zero_and_extreme_activations(ctx, oracle):
     M, K, B = 96, 512, 4
     packed, ws, x = tern_case(oracle, M, K, B, seed=77)
