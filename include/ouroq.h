@@ -146,6 +146,30 @@ ouroq_status ouroq_gemm_group_f32act(ouroq_ctx *ctx, int n, const ouroq_weight *
 ouroq_status ouroq_gemm_f32act(ouroq_ctx *ctx, const ouroq_weight *w, const float *x, int B,
                                const float *signs, int hadamard_block, float *y, void *stream);
 
+/* ouroq_gemm_f32act for callers that must not allocate device memory while
+ * they run. This entry point has no counterpart in the reference.
+ *
+ * Who needs it: ouroq_gemm_f32act quantises batches it cannot fuse (B > 8)
+ * into a context-owned buffer, and grows that buffer with cudaMalloc, freeing
+ * the old one, the first time a larger batch arrives. A serving loop that
+ * reserved the GPU's memory up front for weights and caches cannot take that
+ * (the late cudaMalloc can fail), nor can one on a latency budget (cudaFree
+ * waits for the whole device). This variant allocates nothing: it uses a
+ * fixed scratch area compiled into the library, one per device.
+ *
+ * Limits: B <= 4096 and B * K <= 4 MiB (4194304); larger batches return
+ * OUROQ_ERR_BAD_SHAPE with nothing launched; split them into calls that fit.
+ * The first call on a device does one-time set-up (loads this library's
+ * kernels on that device and looks up the scratch address); make it before
+ * any stream capture. All calls on one device share the one scratch area,
+ * whatever context or stream they use: two calls in flight at the same time
+ * overwrite each other's activations. Order them on one stream, or wait for
+ * one to finish before starting the next. Results are identical to
+ * ouroq_gemm_f32act's. */
+ouroq_status ouroq_gemm_f32act_noalloc(ouroq_ctx *ctx, const ouroq_weight *w, const float *x,
+                                       int B, const float *signs, int hadamard_block, float *y,
+                                       void *stream);
+
 /* ---- host-buffer mirrors of the reference operators (synchronous) ---- */
 
 /* ops::matvec_q (ops.rs:76-84): x_host [K] fp32 -> y_host [M] fp32. */

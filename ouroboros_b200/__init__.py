@@ -66,6 +66,7 @@ ABI_FUNCTIONS = {
     "ouroq_gemm_group": (_i, [_p, _i, _p, _p, _p, _i, _p, _p]),
     "ouroq_gemm_group_f32act": (_i, [_p, _i, _p, _p, _i, _p, _p, _p, _p]),
     "ouroq_gemm_f32act": (_i, [_p, _p, _p, _i, _p, _i, _p, _p]),
+    "ouroq_gemm_f32act_noalloc": (_i, [_p, _p, _p, _i, _p, _i, _p, _p]),
     "ouroq_matvec_q": (_i, [_p, _p, _p, _p]),
     "ouroq_matmul_q": (_i, [_p, _p, _p, _i, _p]),
     "ouroq_rotate_fwd": (_i, [_p, _p, _p, _sz, _sz]),
@@ -274,6 +275,19 @@ class Context:
             y = torch.empty((B, w.M), dtype=torch.float32, device=x.device)
         self._check(self.lib.ouroq_gemm_f32act(self.ctx, w.handle, _ptr(x), B, _ptr(signs),
                                                hadamard_block, _ptr(y), _stream_ptr(stream)))
+        return y
+
+    def gemm_f32act_noalloc(self, w: Weight, x, y, signs=None, hadamard_block: int = 0, stream=None):
+        """gemm_f32act for callers that must not allocate device memory mid-run
+        (memory reserved up front, or no room for cudaFree's device-wide wait).
+        The library allocates nothing here, and neither does this wrapper: the
+        caller passes the output y [B][M] fp32. Limits B <= 4096, B*K <= 4 MiB;
+        all calls on one device share one scratch area, so two calls in flight at
+        once race. The first call on a device does set-up: make it before any
+        stream capture."""
+        B = x.shape[0]
+        self._check(self.lib.ouroq_gemm_f32act_noalloc(self.ctx, w.handle, _ptr(x), B, _ptr(signs),
+                                                       hadamard_block, _ptr(y), _stream_ptr(stream)))
         return y
 
     # -- host-buffer mirrors of the reference operators (numpy in, numpy out) --

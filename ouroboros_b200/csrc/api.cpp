@@ -13,6 +13,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 
@@ -596,6 +597,69 @@ ouroq_status ouroq_gemm_f32act(ouroq_ctx* ctx, const ouroq_weight* w, const floa
   st = quantize_impl(ctx, x, B, w->K, signs, hadamard_block, ctx->q_scratch, ctx->s_scratch, s);
   if (st != OUROQ_OK) return st;
   return gemm_impl(ctx, w, ctx->q_scratch, ctx->s_scratch, B, y, nullptr, s);
+}
+
+// Address of the fixed scratch on each device, looked up the first time a call
+// runs there (with that device current) and reused afterwards.
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[64] = {};
+
+static ouroq_status noalloc_scratch(ouroq_ctx* ctx, uint8_t** out) {
+  if (ctx->device < 0 || ctx->device >= 64)
+    return fail(ctx, OUROQ_ERR_UNSUPPORTED, "device %d: fixed scratch covers devices 0..63",
+                ctx->device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[ctx->device]) {
+    void* p = nullptr;
+    CU(ctx, noalloc_scratch_address(&p), "fixed scratch address");
+    g_noalloc_addr[ctx->device] = p;
+  }
+  *out = static_cast<uint8_t*>(g_noalloc_addr[ctx->device]);
+  return OUROQ_OK;
+}
+
+// Same result as ouroq_gemm_f32act, for callers that must not allocate device
+// memory mid-run; the activation codes go to the library's fixed per-device
+// scratch instead of a buffer grown with cudaMalloc / cudaFree.
+ouroq_status ouroq_gemm_f32act_noalloc(ouroq_ctx* ctx, const ouroq_weight* w, const float* x,
+                                       int B, const float* signs, int hadamard_block, float* y,
+                                       void* stream) {
+  if (!ctx || !w) return fail(ctx, OUROQ_ERR_BAD_ARG, "null handle");
+  if (B < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d", B);
+  if (B == 0) return OUROQ_OK;
+  if (!x || !y) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  ouroq_status st = check_quant_args(ctx, B, w->K, hadamard_block);
+  if (st != OUROQ_OK) return st;
+  if (!aligned16(x)) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "x not 16-byte aligned");
+  if (B > kNoAllocMaxTokens || (size_t)B * w->K > kNoAllocQBytes)
+    return fail(ctx, OUROQ_ERR_BAD_SHAPE,
+                "B=%d, K=%d: the fixed scratch holds at most %d tokens and B*K <= %zu "
+                "(split the batch, or use ouroq_gemm_f32act)",
+                B, w->K, kNoAllocMaxTokens, kNoAllocQBytes);
+  DeviceGuard g(ctx->device);
+  uint8_t* scratch = nullptr;
+  st = noalloc_scratch(ctx, &scratch);
+  if (st != OUROQ_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (B <= kGemvMaxB && (hadamard_block == 0 || (hadamard_block >= 32 && hadamard_block <= 128))) {
+    // one launch, no scratch: rotate + quantise in the GEMV prologue
+    GemvLaunch L{};
+    L.njobs = 1;
+    L.B = B;
+    L.fmt = w->fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
+    L.fused = 1;
+    L.jobs[0] = make_job(w, nullptr, nullptr, y, nullptr);
+    L.jobs[0].xf = x;
+    L.jobs[0].signs = signs;
+    L.jobs[0].had_block = hadamard_block;
+    L.jobs[0].had_scale = hadamard_block ? 1.0f / std::sqrt((float)hadamard_block) : 1.0f;
+    if (gemv_fits(ctx, L)) return run_gemv(ctx, L, s);
+  }
+  int8_t* q = reinterpret_cast<int8_t*>(scratch);
+  float* s_x = reinterpret_cast<float*>(scratch + kNoAllocQBytes);
+  st = quantize_impl(ctx, x, B, w->K, signs, hadamard_block, q, s_x, s);
+  if (st != OUROQ_OK) return st;
+  return gemm_impl(ctx, w, q, s_x, B, y, nullptr, s);
 }
 
 ouroq_status ouroq_matmul_q(ouroq_ctx* ctx, const ouroq_weight* w, const float* x_host, int k,

@@ -127,4 +127,13 @@ cudaError_t launch_gemm_tc(const TcLaunch& L, const int8_t* q, int Btot, int sme
 constexpr int kGemvMaxB = 8;
 constexpr size_t kGemvMaxXBytes = 64 * 1024;  // B*K int8 resident in shared memory
 
+// Fixed scratch of ouroq_gemm_f32act_noalloc (one copy per device): int8
+// codes for up to 4 MiB of B*K, then fp32 scales for up to 4096 tokens.
+constexpr size_t kNoAllocQBytes = 4u << 20;
+constexpr int kNoAllocMaxTokens = 4096;
+constexpr size_t kNoAllocScratchBytes = kNoAllocQBytes + (size_t)kNoAllocMaxTokens * sizeof(float);
+// Device address of that scratch on the current device (first use per device
+// loads this library's kernels there).
+cudaError_t noalloc_scratch_address(void** ptr);
+
 }  // namespace ouroq
