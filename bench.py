@@ -1,22 +1,30 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 packed-weight matmul path (one JSON line on rank 0).
 
-Default workload (BASELINE.json configs[1] at batch 1): all ternary
+Default workload (the headline configuration, at batch 1): all ternary
 projections of one BitNet b1.58 2B-class decoder layer -- fused QKV
 3840x2560, O 2560x2560, gate 6912x2560, up 6912x2560, down 2560x6912 --
 on synthetic data (ternary p = .25/.5/.25, fp32 N(0,1) activations).
 
-One step = one layer's projections at batch B: quantise the four distinct
-fp32 inputs (one grouped K1 launch) and run the five products (one grouped
-GEMV launch). Consecutive steps use 30 different layer copies (521 MB of
-weights, > 2x the 126 MB L2), so every step streams its weights from HBM.
+One step = one pass of the path over one batch: fp32 activations in, fp32
+outputs out. At B <= 8 that is ONE launch (grouped GEMV with the per-token
+quantisation fused into its prologue); at larger B it is one grouped
+quantisation launch followed by one matmul launch per matrix (tcgen05
+tensor-core GEMM for ternary weights from B = 16). Consecutive steps cycle
+through enough weight copies to exceed twice the 126 MB L2, so every step
+streams its weights from HBM.
+
+Other workloads (--workload): c1 (6912x2560), c5-up (28672x8192), c5-down
+(8192x28672), c3-4096 / c3-11008 (1-bit sign weights, fp16 group scales,
+Walsh-Hadamard block 128 on the activations).
 
 Arms:
   (default)          the CUDA library (ouroboros_b200 / libouroq.so)
-  --impl reference   the reference path on the host CPU: the oracle's
+  --impl reference   the reference arithmetic on the host CPU: the oracle's
                      threaded restatement, same config / metric / unit
 Launch: python bench.py [--gpus N --steps K --warmup W]; N > 1 under
-torch.distributed.run (one rank per GPU, NCCL), every rank a replica.
+torch.distributed.run (one rank per GPU, NCCL), every rank a replica with
+its own weights (no data-path collective: weak scaling).
 """
 from __future__ import annotations
 
@@ -35,16 +43,25 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+TERN, SIGN = 1, 2  # OUROQ_FMT_TERNARY2, OUROQ_FMT_SIGN1G128
 HIDDEN, FFN = 2560, 6912
-LAYER_SHAPES = [("attn_qkv", 3840, HIDDEN), ("attn_output", HIDDEN, HIDDEN),
-                ("ffn_gate", FFN, HIDDEN), ("ffn_up", FFN, HIDDEN), ("ffn_down", HIDDEN, FFN)]
-# which activation each projection reads: qkv <- attn input, o <- attn out,
-# gate/up <- ffn input, down <- ffn hidden
-INPUT_OF = [0, 1, 2, 2, 3]
-INPUT_K = [HIDDEN, HIDDEN, HIDDEN, FFN]
-N_LAYERS = 30
-WEIGHT_BYTES_PER_LAYER = sum(m * k // 4 for _, m, k in LAYER_SHAPES)  # 17,367,040
+L2_BYTES = 126 * 2**20
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+# workload -> (description, format, [(name, M, K, input index)], [input widths], hadamard block)
+WORKLOADS = {
+    "layer": ("bitnet2b-layer-projections", TERN,
+              [("attn_qkv", 3840, HIDDEN, 0), ("attn_output", HIDDEN, HIDDEN, 1),
+               ("ffn_gate", FFN, HIDDEN, 2), ("ffn_up", FFN, HIDDEN, 2),
+               ("ffn_down", HIDDEN, FFN, 3)],
+              [HIDDEN, HIDDEN, HIDDEN, FFN], 0),
+    "c1": ("ternary-6912x2560", TERN, [("w", 6912, 2560, 0)], [2560], 0),
+    "c5-up": ("ternary-28672x8192", TERN, [("ffn_up", 28672, 8192, 0)], [8192], 0),
+    "c5-down": ("ternary-8192x28672", TERN, [("ffn_down", 8192, 28672, 0)], [28672], 0),
+    "c3-4096": ("sign1-wht128-4096x4096", SIGN, [("w", 4096, 4096, 0)], [4096], 128),
+    "c3-11008": ("sign1-wht128-11008x4096", SIGN, [("w", 11008, 4096, 0)], [4096], 128),
+}
 
 
 def parse():
@@ -53,28 +70,44 @@ def parse():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=30)
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--workload", default="layer", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ouroq", choices=["ouroq", "reference"])
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="bound of the CPU-baseline sample (0 = skip)")
     return ap.parse_args()
 
 
-def step_bytes(B: int) -> dict:
-    """Algorithmic bytes of one step: what an ideal implementation moves once."""
-    w = WEIGHT_BYTES_PER_LAYER
-    x_f32 = B * sum(INPUT_K) * 4
-    y = B * sum(m for _, m, _ in LAYER_SHAPES) * 4
-    return {"step": w + x_f32 + y, "gemv": w + x_f32 + y, "weights": w}
+def weight_bytes(fmt: int, M: int, K: int) -> int:
+    return M * K // 4 if fmt == TERN else M * K // 8 + M * (K // 128) * 2
 
 
-def measured_peak():
+def step_bytes(wl, B: int) -> dict:
+    """Algorithmic bytes of one step: what an ideal implementation moves once
+    (weights + scales, the fp32 activations read once, the fp32 outputs)."""
+    _, fmt, mats, widths, _ = wl
+    w = sum(weight_bytes(fmt, M, K) for _, M, K, _ in mats)
+    x_f32 = B * sum(widths) * 4
+    x_i8 = B * sum(widths) + 4 * B * len(widths)
+    y = B * sum(M for _, M, _, _ in mats) * 4
+    ops = 2 * B * sum(M * K for _, M, K, _ in mats)
+    return {"step": w + x_f32 + y, "gemm": w + x_i8 + y, "weights": w, "ops": ops}
+
+
+def n_copies(wl) -> int:
+    w = step_bytes(wl, 1)["weights"]
+    return max(2, -(-2 * L2_BYTES // w))
+
+
+def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         try:
             d = json.loads(p.read_text())
-            return float(d["hbm_gbs"]), "measured"
+            return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
         except Exception:
             pass
-    return FALLBACK_HBM_GBS, "fallback"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
 
 
 def profiled_traffic(key: str):
@@ -136,32 +169,47 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- data
-def make_layer(torch, ctx, oq, gen, device):
-    """Random ternary layer packed on the device, uploaded through the C ABI."""
-    ws = []
-    for _, M, K in LAYER_SHAPES:
-        r = torch.randint(0, 4, (M, K), generator=gen, device=device, dtype=torch.uint8)
-        codes = (r == 3).to(torch.uint8) * 2 + ((r == 1) | (r == 2)).to(torch.uint8)
-        c = codes.view(M, K // 4, 4)
-        packed = (c[..., 0] | (c[..., 1] << 2) | (c[..., 2] << 4) | (c[..., 3] << 6)).contiguous()
-        nz = torch.count_nonzero(codes != 1).item()
-        w_scale = 0.02 * nz / (M * K)  # absmean of W_fp = ternary * 0.02
-        ws.append((ctx.upload_device(oq.TERNARY2, packed, M, K, None, w_scale), packed))
-    return ws
+def make_copy(torch, ctx, oq, wl, gen, device):
+    """One random copy of the workload's matrices, uploaded through the C ABI.
+    Returns [(Weight, packed codes, fp16 scales or None)]."""
+    _, fmt, mats, _, _ = wl
+    out = []
+    for _, M, K, _ in mats:
+        if fmt == TERN:
+            r = torch.randint(0, 4, (M, K), generator=gen, device=device, dtype=torch.uint8)
+            codes = (r == 3).to(torch.uint8) * 2 + ((r == 1) | (r == 2)).to(torch.uint8)
+            c = codes.view(M, K // 4, 4)
+            packed = (c[..., 0] | (c[..., 1] << 2) | (c[..., 2] << 4) | (c[..., 3] << 6)).contiguous()
+            nz = torch.count_nonzero(codes != 1).item()
+            del r, codes, c
+            w_scale = 0.02 * nz / (M * K)  # absmean of W_fp = ternary * 0.02
+            out.append((ctx.upload_device(oq.TERNARY2, packed, M, K, None, w_scale), packed, None))
+        else:
+            packed = torch.randint(0, 256, (M, K // 8), generator=gen, device=device,
+                                   dtype=torch.int32).to(torch.uint8)
+            sc = (torch.randn((M, K // 128), generator=gen, device=device) * 0.02).abs()
+            sc = sc.to(torch.float16).view(torch.int16).contiguous()
+            out.append((ctx.upload_device(oq.SIGN1G128, packed, M, K, sc, 1.0), packed, sc))
+    return out
 
 
-def cpu_reference_gbs(layer_host, B: int, seconds: float, threads: int):
-    """Oracle (threaded restatement) on one layer at batch B; returns GB/s and the sample."""
+def cpu_oracle_gbs(wl, host_mats, host_signs, B: int, seconds: float, threads: int):
+    """Oracle (threaded int8 restatement) on one copy at batch B, looping until
+    `seconds` have passed (at least one pass). Returns GB/s, passes, seconds."""
     from oracle import pyoracle as O
+    _, fmt, mats, widths, block = wl
     rng = np.random.default_rng(7)
-    xs = [rng.standard_normal((B, k), dtype=np.float32) for k in INPUT_K]
-    qs = [O.quantize_act(x) for x in xs]
-    nb = step_bytes(B)["step"]
+    xs = [rng.standard_normal((B, k), dtype=np.float32) for k in widths]
+    nb = step_bytes(wl, B)["step"]
     steps, t0 = 0, time.perf_counter()
     while True:
-        for (name, M, K), (packed, ws) in zip(LAYER_SHAPES, layer_host):
-            q, s = qs[INPUT_OF[[n for n, _, _ in LAYER_SHAPES].index(name)]]
-            O.gemm_tern2_mt(packed, M, K, ws, q, s, threads)
+        qs = [O.quantize_act(x, host_signs[i] if block else None, block) for i, x in enumerate(xs)]
+        for (_, M, K, xi), (packed, aux) in zip(mats, host_mats):
+            q, s = qs[xi]
+            if fmt == TERN:
+                O.gemm_tern2_mt(packed, M, K, aux, q, s, threads)
+            else:
+                O.gemm_sign1_mt(packed, aux, M, K, q, s, threads)
         steps += 1
         dt = time.perf_counter() - t0
         if dt >= seconds:
@@ -169,41 +217,65 @@ def cpu_reference_gbs(layer_host, B: int, seconds: float, threads: int):
     return nb * steps / dt / 1e9, steps, dt
 
 
+def host_copy(wl, seed: int):
+    """A host-side copy of the workload's matrices for the CPU arms."""
+    from oracle import pyoracle as O
+    _, fmt, mats, widths, block = wl
+    out = []
+    for i, (_, M, K, _) in enumerate(mats):
+        if fmt == TERN:
+            w = O.ternary(seed + i, M * K).reshape(M, K)
+            out.append((O.pack_tern2(w), float(O.absmean_scale(w, 0.02))))
+        else:
+            w = O.signs(seed + i, M * K).reshape(M, K)
+            out.append((O.pack_sign1(w), O.group_scales(seed + 50 + i, M * (K // 128), 0.02)))
+    signs = [O.signs(seed + 100 + j, k).astype(np.float32) for j, k in enumerate(widths)]
+    return out, signs
+
+
+def workload_config(args, wl, world):
+    desc, fmt, mats, widths, block = wl
+    return {"workload": f"{desc}-b{args.batch}", "batch": args.batch,
+            "format": "ternary2" if fmt == TERN else "sign1g128",
+            "shapes": [[M, K] for _, M, K, _ in mats], "hadamard_block": block,
+            "weight_copies_rotated": n_copies(wl),
+            "l2": f"inputs larger than L2: {n_copies(wl)} weight copies = "
+                  f"{n_copies(wl) * step_bytes(wl, 1)['weights'] / 1e6:.0f} MB rotated",
+            "parallelism": f"replicas x{world}"}
+
+
 # ---------------------------------------------------------------- arms
 def run_reference(args, rank):
     if rank != 0:
         return
     from oracle import pyoracle as O
+    wl = WORKLOADS[args.workload]
     B = args.batch
     threads = O.hw_threads()
-    rng = np.random.default_rng(11)
-    layer = []
-    for _, M, K in LAYER_SHAPES:
-        w = rng.integers(0, 4, size=(M, K), dtype=np.int8)
-        w = np.where(w == 0, -1, np.where(w == 3, 1, 0)).astype(np.int8)
-        layer.append((O.pack_tern2(w), 0.01))
-    # bounded sample: each timed step is one layer pass; steps capped so the run ends in minutes
-    per = []
-    for _ in range(max(args.warmup, 1)):
-        cpu_reference_gbs(layer, B, 0.0, threads)
+    host_mats, host_signs = host_copy(wl, 11)
+    for _ in range(max(min(args.warmup, 3), 1)):
+        cpu_oracle_gbs(wl, host_mats, host_signs, B, 0.0, threads)
     total_t, total_steps = 0.0, 0
-    for _ in range(max(1, min(args.steps, 50))):
-        g, st, dt = cpu_reference_gbs(layer, B, 0.0, threads)
+    budget = 60.0  # the whole run stays within minutes
+    for _ in range(max(1, args.steps)):
+        _, st, dt = cpu_oracle_gbs(wl, host_mats, host_signs, B, 0.0, threads)
         total_t += dt
         total_steps += st
-        per.append(dt)
-    gbs = step_bytes(B)["step"] * total_steps / total_t / 1e9
+        if total_t >= budget:
+            break
+    gbs = step_bytes(wl, B)["step"] * total_steps / total_t / 1e9
+    cfg = workload_config(args, wl, 1)
+    cfg["host_cpu"] = True
     line = {
-        "impl": "reference", "metric": "packed-weight GEMV HBM GB/s (BitNet-2B layer projections)",
+        "impl": "reference", "metric": "packed-weight GEMV HBM GB/s",
         "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": total_steps,
         "warmup": args.warmup, "ms_per_step": round(1e3 * total_t / total_steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-        "data": "synthetic",
-        "config": {"workload": f"bitnet2b-layer-projections-b{B}", "batch": B,
-                   "shapes": [[m, k] for _, m, k in LAYER_SHAPES], "host_cpu": True},
+        "data": "synthetic", "config": cfg,
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{total_steps} layer passes at batch {B} (oracle int8 GEMV, "
-                                   f"{threads} threads, rows chunked as ops.rs:104-105)"},
+                         "sample": f"{total_steps} steps at batch {B} (oracle int8 quantise + "
+                                   f"GEMV, {threads} threads, rows chunked as ops.rs:104-105; "
+                                   f"capped at {budget:.0f} s)"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -215,6 +287,8 @@ def run_ouroq(args, rank, world, local_rank):
     import torch.distributed as dist
     import ouroboros_b200 as oq
 
+    wl = WORKLOADS[args.workload]
+    desc, fmt, mats, widths, block = wl
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     ctx = oq.Context(local_rank)
@@ -223,42 +297,56 @@ def run_ouroq(args, rank, world, local_rank):
     B = args.batch
     gen = torch.Generator(device=device)
     gen.manual_seed(1234 + rank)
-    layers = [make_layer(torch, ctx, oq, gen, device) for _ in range(N_LAYERS)]
-    wts = [[w for w, _ in L] for L in layers]
+    ncop = n_copies(wl)
+    copies = [make_copy(torch, ctx, oq, wl, gen, device) for _ in range(ncop)]
+    wts = [[w for w, _, _ in c] for c in copies]
+    signs = [torch.where(torch.rand(k, generator=gen, device=device) < 0.5, -1.0, 1.0)
+             for k in widths] if block else None
 
-    # device-resident fp32 inputs per layer (independent synthetic activations)
-    xs = [[torch.randn((B, k), generator=gen, device=device) for k in INPUT_K] for _ in range(N_LAYERS)]
-    ys = [[torch.empty((B, m), dtype=torch.float32, device=device) for _, m, _ in LAYER_SHAPES]
+    # device-resident fp32 inputs per copy (independent synthetic activations)
+    xs = [[torch.randn((B, k), generator=gen, device=device) for k in widths] for _ in range(ncop)]
+    ys = [[torch.empty((B, M), dtype=torch.float32, device=device) for _, M, _, _ in mats]
           for _ in range(2)]
+    qs = [[torch.empty((B, k), dtype=torch.int8, device=device) for k in widths] for _ in range(2)]
+    sxs = [[torch.empty((B,), dtype=torch.float32, device=device) for _ in widths] for _ in range(2)]
     stream = torch.cuda.Stream(device=device)
-    def gemv_group(l, slot):
-        # one launch: the four fp32 inputs are quantised in the GEMV prologue
-        ctx.gemm_group_f32act(wts[l], [xs[l][INPUT_OF[i]] for i in range(5)], ys[slot],
-                              stream=stream)
+    fused = B <= 8
+    mat_signs = [signs[xi] for _, _, _, xi in mats] if block else None
+    mat_blocks = [block] * len(mats) if block else None
+
+    def run_step(wl_, xin, yout, qbuf, sbuf):
+        if fused:
+            # one launch: the fp32 inputs are quantised in the GEMV prologue
+            if len(mats) > 1:
+                ctx.gemm_group_f32act(wl_, [xin[xi] for _, _, _, xi in mats], yout,
+                                      signs=mat_signs, blocks=mat_blocks, stream=stream)
+            else:
+                ctx.gemm_f32act(wl_[0], xin[0], signs=signs[0] if block else None,
+                                hadamard_block=block, y=yout[0], stream=stream)
+        else:
+            ctx.quantize_group(xin, qbuf, sbuf, signs=signs if block else None,
+                               blocks=[block] * len(widths) if block else None, stream=stream)
+            for j, (_, _, _, xi) in enumerate(mats):
+                ctx.gemm(wl_[j], qbuf[xi], sbuf[xi], y=yout[j], stream=stream)
 
     def step(i):
-        gemv_group(i % N_LAYERS, i % 2)
+        run_step(wts[i % ncop], xs[i % ncop], ys[i % 2], qs[i % 2], sxs[i % 2])
 
-    # CUDA graph of one pass over the 30 layers (launch-bound loop -> graph replay)
-    with torch.cuda.stream(stream):
-        for i in range(max(args.warmup, 3)):
-            step(i)
-    stream.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for i in range(N_LAYERS):
-            step(i)
-    def replay(n_passes):
-        for _ in range(n_passes):
-            graph.replay()
+    def gemm_only(i):
+        for j, (_, _, _, xi) in enumerate(mats):
+            ctx.gemm(wts[i % ncop][j], qs[0][xi], sxs[0][xi], y=ys[i % 2][j], stream=stream)
 
-    with torch.cuda.stream(stream):
-        replay(max(1, args.warmup // N_LAYERS) + 1)
-    stream.synchronize()
-
-    passes = max(1, args.steps // N_LAYERS)
-    steps = passes * N_LAYERS
-    launches_per_step = 1  # one grouped GEMV launch with the quantisation fused in
+    def capture(fn):
+        with torch.cuda.stream(stream):
+            for i in range(max(args.warmup, 3)):
+                fn(i)
+        stream.synchronize()
+        n0 = ctx.launch_count()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(ncop):
+                fn(i)
+        return g, (ctx.launch_count() - n0) / ncop
 
     def timed(fn, n):
         if world > 1:
@@ -278,82 +366,116 @@ def run_ouroq(args, rank, world, local_rank):
             ms = float(t.item())
         return ms
 
+    # CUDA graph of one pass over the copies (launch-bound loop -> graph replay)
+    graph, launches_per_step = capture(step)
+    def replay(n_passes, g=graph):
+        for _ in range(n_passes):
+            g.replay()
+
+    with torch.cuda.stream(stream):
+        replay(max(1, args.warmup // ncop) + 1)
+    stream.synchronize()
+    passes = max(1, args.steps // ncop)
+    steps = passes * ncop
+
     with ClockSampler(local_rank) as clk:
         with torch.cuda.stream(stream):
             ms = timed(replay, passes)
     clocks = clk.summary()
 
-    nb = step_bytes(B)
+    nb = step_bytes(wl, B)
     value = nb["step"] * steps * world / (ms / 1e3) / 1e9
-    # the fused grouped GEMV is the only kernel of a step: its average launch
-    # duration is the timed region (CUDA events on its stream) / launches
-    gemv_avg_s = ms / 1e3 / steps
-    achieved = nb["gemv"] / gemv_avg_s / 1e9
-    peak, peak_kind = measured_peak()
+    hbm_peak, bf16_peak, peak_kind = peaks()
+    tensor_bound = fmt == TERN and B >= 64
+    if fused:
+        # the fused grouped GEMV is the only kernel of a step: its average launch
+        # duration is the timed region (CUDA events on its stream) / launches
+        kern_s = ms / 1e3 / steps
+        kern_bytes = nb["step"]
+        kernel = f"gemv_kernel<{'kTern2' if fmt == TERN else 'kSign1'},B={B}> (fused quantisation)"
+    else:
+        # matmul launches alone, on pre-quantised activations, timed the same way
+        g2, _ = capture(gemm_only)
+        with torch.cuda.stream(stream):
+            replay(1, g2)
+            kms = timed(lambda n: replay(n, g2), passes)
+        kern_s = kms / 1e3 / steps
+        kern_bytes = nb["gemm"]
+        kernel = ("gemm_tc_kernel (tcgen05 kind::i8)" if fmt == TERN and B >= 16
+                  else "gemv_kernel (8-token chunks)")
+        del g2
+    if tensor_bound:
+        int8_peak = 2.0 * bf16_peak
+        achieved = nb["ops"] / kern_s / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1),
+                "unit": "TOPS", "frac": round(achieved / int8_peak, 4),
+                "peak_kind": f"int8 dense = 2 x {peak_kind} bf16_tflops",
+                "ops_per_step": nb["ops"]}
+    else:
+        achieved = kern_bytes / kern_s / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4), "peak_kind": f"{peak_kind} (hbm_gbs)",
+                "bytes_per_step": kern_bytes}
+    roof["traffic"] = profiled_traffic(f"{args.workload}_b{B}")
+    roof["kernel"] = kernel
 
     # ---- e2e through the public API with host buffers (pinned), eager calls
-    xh = [[x.cpu().pin_memory() for x in xl] for xl in xs[:4]]
-    yh = [torch.empty((B, m), dtype=torch.float32).pin_memory() for _, m, _ in LAYER_SHAPES]
-    xd = [torch.empty((B, k), device=device) for k in INPUT_K]
+    xh = [[x.cpu().pin_memory() for x in xl] for xl in xs[:2]]
+    yh = [torch.empty((B, M), dtype=torch.float32).pin_memory() for _, M, _, _ in mats]
+    xd = [torch.empty((B, k), device=device) for k in widths]
     e2e_steps = min(steps, 600)
-    h2d = B * sum(INPUT_K) * 4
-    d2h = B * sum(m for _, m, _ in LAYER_SHAPES) * 4
+    h2d = B * sum(widths) * 4
+    d2h = B * sum(M for _, M, _, _ in mats) * 4
 
     def e2e(n):
         for i in range(n):
-            l = i % N_LAYERS
-            for j in range(4):
-                xd[j].copy_(xh[i % 4][j], non_blocking=True)
-            ctx.gemm_group_f32act(wts[l], [xd[INPUT_OF[k]] for k in range(5)], ys[0],
-                                  stream=stream)
-            for j in range(5):
+            for j in range(len(widths)):
+                xd[j].copy_(xh[i % 2][j], non_blocking=True)
+            run_step(wts[i % ncop], xd, ys[0], qs[0], sxs[0])
+            for j in range(len(mats)):
                 yh[j].copy_(ys[0][j], non_blocking=True)
 
     with torch.cuda.stream(stream):
-        e2e(10)
+        e2e(5)
         stream.synchronize()
         e2e_ms = timed(e2e, e2e_steps)
     e2e_value = nb["step"] * e2e_steps * world / (e2e_ms / 1e3) / 1e9
 
     # ---- CPU baseline (rank 0, N = 1 only), bounded sample of the same workload
     cpu = None
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
         from oracle import pyoracle as O
-        layer_host = [(p.cpu().numpy(), float(w.w_scale)) for (w, p) in layers[0]]
+        host_mats = []
+        for w, p, sc in copies[0]:
+            aux = float(w.w_scale) if fmt == TERN else sc.cpu().numpy().view(np.uint16)
+            host_mats.append((p.cpu().numpy(), aux))
+        host_signs = [s.cpu().numpy() for s in signs] if block else None
         threads = O.hw_threads()
-        gbs, st, dt = cpu_reference_gbs(layer_host, B, 10.0, threads)
+        gbs, st, dt = cpu_oracle_gbs(wl, host_mats, host_signs, B, args.cpu_seconds, threads)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{st} layer passes ({dt:.1f} s) at batch {B}: oracle int8 GEMV, "
+               "sample": f"{st} steps ({dt:.1f} s) at batch {B}: oracle int8 quantise + GEMV, "
                          f"{threads} threads"}
 
     if rank == 0:
-        traffic = profiled_traffic(f"gemv_group_b{B}")
+        cfg = workload_config(args, wl, world)
+        cfg.update({"pdl": not args.no_pdl, "launch": f"CUDA graph of {ncop} steps"})
         line = {
-            "metric": "packed-weight GEMV HBM GB/s (BitNet-2B layer projections)",
+            "metric": "packed-weight GEMV HBM GB/s",
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(ms / steps, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic (ternary p=.25/.5/.25, fp32 N(0,1) activations, random init)",
-            "config": {"workload": f"bitnet2b-layer-projections-b{B}", "batch": B,
-                       "shapes": [[m, k] for _, m, k in LAYER_SHAPES],
-                       "layers_rotated": N_LAYERS,
-                       "l2": f"inputs larger than L2: {N_LAYERS} layer copies = "
-                             f"{N_LAYERS * WEIGHT_BYTES_PER_LAYER / 1e6:.0f} MB rotated",
-                       "parallelism": f"replicas x{world}", "pdl": not args.no_pdl,
-                       "launch": "CUDA graph of 30 steps"},
-            "decode_tokens_per_s_ternary_only": round(B * world / (ms / 1e3 / steps * N_LAYERS), 1),
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic, "peak_kind": f"{peak_kind} (hbm_gbs)",
-                         "kernel": "gemv_kernel<kTern2,B> (grouped, 5 jobs, fused quantisation)",
-                         "bytes_per_launch": nb["gemv"]},
+            "data": "synthetic (random init weights, fp32 N(0,1) activations)",
+            "config": cfg,
+            "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
                     "how": "eager Python calls of the public API, pinned host buffers"},
-            "gpu_launches": launches_per_step * steps,
+            "gpu_launches": int(round(launches_per_step * steps)),
             "clocks": clocks,
         }
+        if args.workload == "layer":
+            line["decode_tokens_per_s_ternary_only"] = round(B * world / (ms / 1e3 / steps * 30), 1)
         print(json.dumps(line), flush=True)
     del graph
     ctx.close()

@@ -76,7 +76,7 @@ int orc_rotate_inv(float *x, const float *signs, size_t n, size_t block);
 int orc_quantize_act(const float *x, int B, int K, const float *signs, int had_block,
                      int8_t *q, float *s_x, float *x_rot /* nullable, [B][K] */);
 
-/* ---- int8-activation GEMM on the BASELINE formats ---- */
+/* ---- int8-activation GEMM on the TERNARY2 / SIGN1G128 formats ---- */
 int orc_gemm_tern2(const uint8_t *packed, int M, int K, float w_scale, const int8_t *q,
                    const float *s_x, int B, int32_t *acc /* nullable [B][M] */, float *y);
 int orc_gemm_sign1(const uint8_t *packed, const uint16_t *scales, int M, int K,
