@@ -75,6 +75,9 @@ def parse():
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="bound of the CPU-baseline sample (0 = skip)")
+    ap.add_argument("--shard", action="store_true",
+                    help="row-shard each matrix over the ranks (NCCL all-gather); "
+                         "single-matrix workloads only")
     return ap.parse_args()
 
 
@@ -481,6 +484,125 @@ def run_ouroq(args, rank, world, local_rank):
     ctx.close()
 
 
+def run_sharded(args, rank, world, local_rank):
+    """Strong scaling of one large matrix: rank r holds rows [r*M/N, (r+1)*M/N),
+    every step computes the local rows and all-gathers the full y on every rank."""
+    import torch
+    import torch.distributed as dist
+    import ouroboros_b200 as oq
+    from ouroboros_b200 import shard
+
+    wl = WORKLOADS[args.workload]
+    desc, fmt, mats, widths, block = wl
+    if len(mats) != 1 or fmt != TERN:
+        raise SystemExit("--shard takes a single ternary matrix workload (c1, c5-up, c5-down)")
+    _, M, K, _ = mats[0]
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    ctx = oq.Context(local_rank)
+    if world > 1:
+        shard.join(ctx)
+    else:
+        ctx.shard_init(oq.shard_unique_id(), 1, 0)
+    B = args.batch
+    ncop = n_copies(wl)
+    rng = np.random.default_rng(4321)
+    copies = []
+    for _ in range(ncop):  # identical full matrices on every rank (same seed)
+        codes = rng.integers(0, 4, size=(M, K), dtype=np.uint8)
+        codes[codes == 3] = 1  # p(-1, 0, +1) = .25, .5, .25 as codes 0, 1, 2
+        c = codes.reshape(M, K // 4, 4)
+        packed = (c[..., 0] | (c[..., 1] << 2) | (c[..., 2] << 4) | (c[..., 3] << 6)).astype(np.uint8)
+        w_scale = 0.02 * float(np.count_nonzero(codes != 1)) / (M * K)
+        copies.append(ctx.upload_shard(oq.TERNARY2, packed, M, K, None, w_scale))
+        del codes, c, packed
+    gen = torch.Generator(device=device)
+    gen.manual_seed(99)
+    xs = [torch.randn((B, K), generator=gen, device=device) for _ in range(ncop)]
+    ys = [torch.empty((B, M), dtype=torch.float32, device=device) for _ in range(2)]
+    ylocal = torch.empty((B, M // world), dtype=torch.float32, device=device)
+    stream = torch.cuda.Stream(device=device)
+
+    def step(i):
+        ctx.gemm_sharded(copies[i % ncop], xs[i % ncop], y=ys[i % 2], stream=stream)
+
+    def local(i):
+        ctx.gemm_f32act(copies[i % ncop], xs[i % ncop], y=ylocal, stream=stream)
+
+    def capture(fn):
+        with torch.cuda.stream(stream):
+            for i in range(max(args.warmup, 3)):
+                fn(i)
+        ctx.shard_sync(stream, timeout_ms=60000)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(ncop):
+                fn(i)
+        return g
+
+    def timed(g, n):
+        dist.barrier() if world > 1 else None
+        torch.cuda.synchronize(device)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(n):
+                g.replay()
+            e1.record(stream)
+        ctx.shard_sync(stream, timeout_ms=120000)
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    g_step = capture(step)
+    g_local = capture(local)
+    passes = max(1, args.steps // ncop)
+    steps = passes * ncop
+    timed(g_step, 1)
+    with ClockSampler(local_rank) as clk:
+        ms = timed(g_step, passes)
+    clocks = clk.summary()
+    timed(g_local, 1)
+    lms = timed(g_local, passes)
+
+    nb = step_bytes(wl, B)
+    value = nb["step"] * steps / (ms / 1e3) / 1e9  # the full matrix once per step, all ranks
+    hbm_peak, bf16_peak, peak_kind = peaks()
+    local_bytes = nb["weights"] // world + B * K * 4 + B * (M // world) * 4
+    achieved = local_bytes / (lms / 1e3 / steps) / 1e9
+    if rank == 0:
+        line = {
+            "metric": "packed-weight GEMV HBM GB/s", "value": round(value, 2), "unit": "GB/s",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / steps, 5), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (random init ternary weights, fp32 N(0,1) activations)",
+            "config": {"workload": f"{desc}-b{B}-rowsharded", "batch": B, "shapes": [[M, K]],
+                       "rows_per_rank": M // world, "weight_copies_rotated": ncop,
+                       "parallelism": f"row-sharded x{world}, in-place NCCL all-gather",
+                       "launch": f"CUDA graph of {ncop} steps"},
+            "local_product_us": round(1e3 * lms / steps, 3),
+            "gather_and_sync_us": round(1e3 * (ms - lms) / steps, 3),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
+                         "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                         "peak_kind": f"{peak_kind} (hbm_gbs)", "traffic": None,
+                         "kernel": "per-rank local product (fused GEMV / tensor-core GEMM)",
+                         "bytes_per_rank_step": local_bytes},
+            "cpu_baseline": None,
+            "gpu_launches": None,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    del g_step, g_local
+    ctx.shard_finalize()
+    ctx.close()
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -497,7 +619,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ouroq(args, rank, world, local_rank)
+        if args.shard:
+            run_sharded(args, rank, world, local_rank)
+        else:
+            run_ouroq(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -170,6 +170,38 @@ ouroq_status ouroq_gemm_f32act_noalloc(ouroq_ctx *ctx, const ouroq_weight *w, co
                                        int B, const float *signs, int hadamard_block, float *y,
                                        void *stream);
 
+/* ---- row-sharded matmul across the GPUs of one node (one process per GPU) ----
+ * New: the reference runs each matrix on one host. The rows of a large matrix
+ * (e.g. 28672x8192 / 8192x28672) are split evenly over G ranks; every rank
+ * computes its rows and an in-place NCCL all-gather over NVLink assembles the
+ * full y on every rank. NCCL is loaded at run time (libnccl.so.2). */
+#define OUROQ_SHARD_ID_BYTES 128
+/* Rank 0 makes the group id (OUROQ_SHARD_ID_BYTES bytes) and the caller hands
+ * the bytes to every rank over any channel it has. */
+ouroq_status ouroq_shard_unique_id(void *id_out);
+/* Join the group as `rank` of `world` on the context's device. Collective:
+ * every rank calls it with the same id. */
+ouroq_status ouroq_shard_init(ouroq_ctx *ctx, const void *id, int world, int rank);
+/* Leave the group (aborts it instead if a sync timed out or NCCL failed). */
+ouroq_status ouroq_shard_finalize(ouroq_ctx *ctx);
+/* Rows [*row0, *row0 + *rows) of an M-row matrix that `rank` owns; M must
+ * divide evenly (OUROQ_ERR_BAD_SHAPE otherwise). Host-only, no device needed. */
+ouroq_status ouroq_shard_rows(int M, int world, int rank, int *row0, int *rows);
+/* Upload this rank's rows of a full matrix given in the canonical host layout
+ * (same arguments as ouroq_weight_upload, full M). */
+ouroq_status ouroq_weight_upload_shard(ouroq_ctx *ctx, ouroq_format fmt, const void *packed_full,
+                                       int M, int K, const void *scales_full, float w_scale,
+                                       ouroq_weight **out);
+/* y [B][M] (full M, on every rank) = W . quant(rotate(x)), x fp32 [B][K]
+ * identical on every rank. Every rank must make the same sequence of calls. */
+ouroq_status ouroq_gemm_sharded(ouroq_ctx *ctx, const ouroq_weight *w_shard, const float *x,
+                                int B, const float *signs, int hadamard_block, float *y,
+                                void *stream);
+/* Wait until `stream` has finished, at most timeout_ms (< 0: no bound).
+ * OUROQ_ERR_TIMEOUT or OUROQ_ERR_NCCL marks the group failed: later sharded
+ * calls return OUROQ_ERR_NCCL and finalize aborts the communicator. */
+ouroq_status ouroq_shard_sync(ouroq_ctx *ctx, void *stream, int timeout_ms);
+
 /* ---- host-buffer mirrors of the reference operators (synchronous) ---- */
 
 /* ops::matvec_q (ops.rs:76-84): x_host [K] fp32 -> y_host [M] fp32. */

@@ -25,13 +25,14 @@ import numpy as np
 
 __all__ = [
     "OuroqError", "Context", "Weight", "TERNARY2", "SIGN1G128", "load_library", "LIB_PATH",
-    "ABI_FUNCTIONS",
+    "ABI_FUNCTIONS", "SHARD_ID_BYTES", "shard_unique_id", "shard_rows",
 ]
 
 LIB_PATH = Path(__file__).resolve().parent / "libouroq.so"
 
 TERNARY2 = 1
 SIGN1G128 = 2
+SHARD_ID_BYTES = 128
 
 OK = 0
 _STATUS = {
@@ -67,6 +68,13 @@ ABI_FUNCTIONS = {
     "ouroq_gemm_group_f32act": (_i, [_p, _i, _p, _p, _i, _p, _p, _p, _p]),
     "ouroq_gemm_f32act": (_i, [_p, _p, _p, _i, _p, _i, _p, _p]),
     "ouroq_gemm_f32act_noalloc": (_i, [_p, _p, _p, _i, _p, _i, _p, _p]),
+    "ouroq_shard_unique_id": (_i, [_p]),
+    "ouroq_shard_init": (_i, [_p, _p, _i, _i]),
+    "ouroq_shard_finalize": (_i, [_p]),
+    "ouroq_shard_rows": (_i, [_i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
+    "ouroq_weight_upload_shard": (_i, [_p, _i, _p, _i, _i, _p, _f, ctypes.POINTER(_p)]),
+    "ouroq_gemm_sharded": (_i, [_p, _p, _p, _i, _p, _i, _p, _p]),
+    "ouroq_shard_sync": (_i, [_p, _p, _i]),
     "ouroq_matvec_q": (_i, [_p, _p, _p, _p]),
     "ouroq_matmul_q": (_i, [_p, _p, _p, _i, _p]),
     "ouroq_rotate_fwd": (_i, [_p, _p, _p, _sz, _sz]),
@@ -116,6 +124,26 @@ def _stream_ptr(stream) -> int | None:
     if isinstance(stream, int):
         return stream
     return stream.cuda_stream
+
+
+def shard_unique_id() -> bytes:
+    """A new shard-group id (rank 0 makes it; every rank passes it to shard_init)."""
+    lib = load_library()
+    buf = ctypes.create_string_buffer(SHARD_ID_BYTES)
+    st = lib.ouroq_shard_unique_id(ctypes.cast(buf, _p))
+    if st != OK:
+        raise OuroqError(st, "ouroq_shard_unique_id")
+    return buf.raw
+
+
+def shard_rows(M: int, world: int, rank: int) -> tuple[int, int]:
+    """(first row, row count) of an M-row matrix owned by `rank` of `world`."""
+    lib = load_library()
+    r0, n = _i(), _i()
+    st = lib.ouroq_shard_rows(M, world, rank, ctypes.byref(r0), ctypes.byref(n))
+    if st != OK:
+        raise OuroqError(st, f"ouroq_shard_rows(M={M}, world={world}, rank={rank})")
+    return r0.value, n.value
 
 
 class Weight:
@@ -289,6 +317,42 @@ class Context:
         self._check(self.lib.ouroq_gemm_f32act_noalloc(self.ctx, w.handle, _ptr(x), B, _ptr(signs),
                                                        hadamard_block, _ptr(y), _stream_ptr(stream)))
         return y
+
+    # -- row-sharded matmul (one process per GPU, NCCL all-gather) --
+    def shard_init(self, group_id: bytes, world: int, rank: int) -> None:
+        """Join the shard group; `group_id` comes from shard_unique_id() on rank 0."""
+        buf = ctypes.create_string_buffer(bytes(group_id), SHARD_ID_BYTES)
+        self._check(self.lib.ouroq_shard_init(self.ctx, ctypes.cast(buf, _p), world, rank))
+
+    def shard_finalize(self) -> None:
+        self._check(self.lib.ouroq_shard_finalize(self.ctx))
+
+    def upload_shard(self, fmt: int, packed_full: np.ndarray, M: int, K: int,
+                     scales_full: np.ndarray | None = None, w_scale: float = 1.0) -> Weight:
+        """Upload this rank's rows of a full matrix (canonical host layout, full M)."""
+        packed_full = np.ascontiguousarray(packed_full, dtype=np.uint8)
+        if scales_full is not None:
+            scales_full = np.ascontiguousarray(scales_full, dtype=np.uint16)
+        h = _p()
+        self._check(self.lib.ouroq_weight_upload_shard(self.ctx, fmt, _ptr(packed_full), M, K,
+                                                       _ptr(scales_full), float(w_scale),
+                                                       ctypes.byref(h)))
+        w = Weight(self, h.value, fmt, M, K)
+        w.w_scale = float(w_scale)
+        return w
+
+    def gemm_sharded(self, w: Weight, x, y=None, signs=None, hadamard_block: int = 0, stream=None):
+        """y [B][M] (full M, every rank) from this rank's rows + an all-gather."""
+        import torch
+        B = x.shape[0]
+        if y is None:
+            y = torch.empty((B, w.M), dtype=torch.float32, device=x.device)
+        self._check(self.lib.ouroq_gemm_sharded(self.ctx, w.handle, _ptr(x), B, _ptr(signs),
+                                                hadamard_block, _ptr(y), _stream_ptr(stream)))
+        return y
+
+    def shard_sync(self, stream=None, timeout_ms: int = 10000) -> None:
+        self._check(self.lib.ouroq_shard_sync(self.ctx, _stream_ptr(stream), int(timeout_ms)))
 
     # -- host-buffer mirrors of the reference operators (numpy in, numpy out) --
     def matvec_q(self, w: Weight, x: np.ndarray) -> np.ndarray:

@@ -8,7 +8,10 @@
 #include "ouroq.h"
 
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
+#include <chrono>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -16,6 +19,7 @@
 #include <mutex>
 #include <new>
 #include <string>
+#include <thread>
 
 #include "kernels.h"
 
@@ -43,6 +47,12 @@ struct ouroq_ctx {
   size_t y_cap = 0;
   float* sign_stage = nullptr;
   size_t sign_cap = 0;
+  // row-sharded group (NCCL communicator, opaque here)
+  void* comm = nullptr;
+  int shard_world = 1, shard_rank = 0;
+  bool comm_failed = false;
+  float* gather = nullptr;
+  size_t gather_cap = 0;
 };
 
 struct ouroq_weight {
@@ -52,6 +62,8 @@ struct ouroq_weight {
   uint16_t* scales = nullptr;  // sign: tiled fp16 group scales
   float w_scale = 0.0f;
   size_t bytes = 0;
+  int shard_M = 0;     // full row count of a row-sharded matrix (0 = not sharded)
+  int shard_row0 = 0;  // first full-matrix row held here
 };
 
 namespace {
@@ -310,6 +322,80 @@ ouroq_status upload_impl(ouroq_ctx* ctx, ouroq_format fmt, const void* packed, i
   return cleanup(OUROQ_OK);
 }
 
+// ---- NCCL, resolved at run time: the library does not link it, so a process
+// that never shards needs no NCCL at all, and one that imported PyTorch first
+// shares the copy PyTorch already loaded.
+struct NcclApi {
+  bool ok = false;
+  std::string why;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+const NcclApi& nccl() {
+  static NcclApi api = [] {
+    NcclApi a;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!h) {
+      const char* e = dlerror();
+      a.why = std::string("libnccl.so.2 not loadable: ") + (e ? e : "?");
+      return a;
+    }
+    auto sym = [&](const char* name) { return dlsym(h, name); };
+    a.GetUniqueId = reinterpret_cast<decltype(a.GetUniqueId)>(sym("ncclGetUniqueId"));
+    a.CommInitRank = reinterpret_cast<decltype(a.CommInitRank)>(sym("ncclCommInitRank"));
+    a.AllGather = reinterpret_cast<decltype(a.AllGather)>(sym("ncclAllGather"));
+    a.CommDestroy = reinterpret_cast<decltype(a.CommDestroy)>(sym("ncclCommDestroy"));
+    a.CommAbort = reinterpret_cast<decltype(a.CommAbort)>(sym("ncclCommAbort"));
+    a.CommGetAsyncError =
+        reinterpret_cast<decltype(a.CommGetAsyncError)>(sym("ncclCommGetAsyncError"));
+    a.GetErrorString = reinterpret_cast<decltype(a.GetErrorString)>(sym("ncclGetErrorString"));
+    a.ok = a.GetUniqueId && a.CommInitRank && a.AllGather && a.CommDestroy && a.CommAbort &&
+           a.CommGetAsyncError && a.GetErrorString;
+    if (!a.ok) a.why = "libnccl.so.2 lacks a required symbol";
+    return a;
+  }();
+  return api;
+}
+
+ouroq_status nccl_fail(ouroq_ctx* ctx, ncclResult_t r, const char* what) {
+  return fail(ctx, OUROQ_ERR_NCCL, "%s: %s", what, nccl().GetErrorString(r));
+}
+
+void shard_release(ouroq_ctx* ctx) {
+  if (ctx->comm) {
+    ncclComm_t c = static_cast<ncclComm_t>(ctx->comm);
+    if (ctx->comm_failed)
+      nccl().CommAbort(c);
+    else
+      nccl().CommDestroy(c);
+    ctx->comm = nullptr;
+  }
+  cudaFree(ctx->gather);
+  ctx->gather = nullptr;
+  ctx->gather_cap = 0;
+  ctx->shard_world = 1;
+  ctx->shard_rank = 0;
+  ctx->comm_failed = false;
+}
+
+ouroq_status shard_rows_impl(ouroq_ctx* ctx, int M, int world, int rank, int* row0, int* rows) {
+  if (world < 1 || rank < 0 || rank >= world)
+    return fail(ctx, OUROQ_ERR_BAD_ARG, "rank %d of world %d", rank, world);
+  if (M <= 0 || M % world)
+    return fail(ctx, OUROQ_ERR_BAD_SHAPE, "M=%d rows do not split evenly over %d ranks", M, world);
+  *rows = M / world;
+  *row0 = rank * *rows;
+  return OUROQ_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -369,6 +455,7 @@ ouroq_status ouroq_ctx_destroy(ouroq_ctx* ctx) {
   cudaFree(ctx->x_stage);
   cudaFree(ctx->y_stage);
   cudaFree(ctx->sign_stage);
+  shard_release(ctx);
   delete ctx;
   return OUROQ_OK;
 }
@@ -738,6 +825,144 @@ ouroq_status ouroq_rotate_fwd(ouroq_ctx* ctx, float* x_host, const float* signs_
 ouroq_status ouroq_rotate_inv(ouroq_ctx* ctx, float* x_host, const float* signs_host, size_t n,
                               size_t block) {
   return rotate_host(ctx, x_host, signs_host, n, block, 1);
+}
+
+// ---------------------------------------------------------------- row sharding
+// Output rows of a large matrix split evenly over the GPUs of one node, one
+// process per GPU; an in-place NCCL all-gather over NVLink assembles y on
+// every rank. Activations are identical on all ranks and each rank quantises
+// them itself (no extra collective).
+
+ouroq_status ouroq_shard_unique_id(void* id_out) {
+  if (!id_out) return OUROQ_ERR_BAD_ARG;
+  const NcclApi& n = nccl();
+  if (!n.ok) return OUROQ_ERR_NCCL;
+  ncclUniqueId id;
+  if (n.GetUniqueId(&id) != ncclSuccess) return OUROQ_ERR_NCCL;
+  std::memcpy(id_out, &id, sizeof id);
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_shard_init(ouroq_ctx* ctx, const void* id, int world, int rank) {
+  if (!ctx || !id) return fail(ctx, OUROQ_ERR_BAD_ARG, "null argument");
+  if (world < 1 || rank < 0 || rank >= world)
+    return fail(ctx, OUROQ_ERR_BAD_ARG, "rank %d of world %d", rank, world);
+  if (ctx->comm) return fail(ctx, OUROQ_ERR_BAD_ARG, "context already joined a shard group");
+  const NcclApi& n = nccl();
+  if (!n.ok) return fail(ctx, OUROQ_ERR_NCCL, "%s", n.why.c_str());
+  DeviceGuard g(ctx->device);
+  ncclUniqueId uid;
+  std::memcpy(&uid, id, sizeof uid);
+  ncclComm_t comm = nullptr;
+  const ncclResult_t r = n.CommInitRank(&comm, world, uid, rank);
+  if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclCommInitRank");
+  ctx->comm = comm;
+  ctx->shard_world = world;
+  ctx->shard_rank = rank;
+  ctx->comm_failed = false;
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_shard_finalize(ouroq_ctx* ctx) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  DeviceGuard g(ctx->device);
+  shard_release(ctx);
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_shard_rows(int M, int world, int rank, int* row0, int* rows) {
+  if (!row0 || !rows) return OUROQ_ERR_BAD_ARG;
+  return shard_rows_impl(nullptr, M, world, rank, row0, rows);
+}
+
+ouroq_status ouroq_weight_upload_shard(ouroq_ctx* ctx, ouroq_format fmt, const void* packed_full,
+                                       int M, int K, const void* scales_full, float w_scale,
+                                       ouroq_weight** out) {
+  if (!ctx || !packed_full || !out) return fail(ctx, OUROQ_ERR_BAD_ARG, "null argument");
+  if (!ctx->comm) return fail(ctx, OUROQ_ERR_BAD_ARG, "context has not joined a shard group");
+  ouroq_status st = check_weight_shape(ctx, fmt, M, K);
+  if (st != OUROQ_OK) return st;
+  int row0 = 0, rows = 0;
+  st = shard_rows_impl(ctx, M, ctx->shard_world, ctx->shard_rank, &row0, &rows);
+  if (st != OUROQ_OK) return st;
+  const size_t rb = fmt == OUROQ_FMT_TERNARY2 ? (size_t)K / 4 : (size_t)K / 8;
+  const uint8_t* p = static_cast<const uint8_t*>(packed_full) + (size_t)row0 * rb;
+  const uint16_t* sc =
+      scales_full ? static_cast<const uint16_t*>(scales_full) + (size_t)row0 * (K / 128) : nullptr;
+  st = upload_impl(ctx, fmt, p, rows, K, sc, w_scale, out, false);
+  if (st != OUROQ_OK) return st;
+  (*out)->shard_M = M;
+  (*out)->shard_row0 = row0;
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_gemm_sharded(ouroq_ctx* ctx, const ouroq_weight* w, const float* x, int B,
+                                const float* signs, int hadamard_block, float* y, void* stream) {
+  if (!ctx || !w) return fail(ctx, OUROQ_ERR_BAD_ARG, "null handle");
+  if (!ctx->comm) return fail(ctx, OUROQ_ERR_BAD_ARG, "context has not joined a shard group");
+  if (w->shard_M == 0) return fail(ctx, OUROQ_ERR_BAD_ARG, "weight was not uploaded as a shard");
+  if (w->shard_M != w->M * ctx->shard_world)
+    return fail(ctx, OUROQ_ERR_BAD_ARG, "weight shard belongs to another group size");
+  if (B < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d", B);
+  if (B == 0) return OUROQ_OK;
+  if (!x || !y) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  if (ctx->comm_failed) return fail(ctx, OUROQ_ERR_NCCL, "shard group failed earlier");
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int R = w->M, G = ctx->shard_world, r = ctx->shard_rank;
+  const ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
+  float* slot;
+  float* recv;
+  if (B == 1) {
+    // slot order is the output order: compute into y's own rows, gather in place
+    recv = y;
+    slot = y + (size_t)r * R;
+  } else {
+    ouroq_status st = grow(ctx, ctx->gather, ctx->gather_cap, (size_t)G * B * R, "gather buffer");
+    if (st != OUROQ_OK) return st;
+    recv = ctx->gather;
+    slot = ctx->gather + (size_t)r * B * R;
+  }
+  ouroq_status st = ouroq_gemm_f32act(ctx, w, x, B, signs, hadamard_block, slot, stream);
+  if (st != OUROQ_OK) return st;
+  const ncclResult_t nr = nccl().AllGather(slot, recv, (size_t)B * R, ncclFloat32, comm, s);
+  if (nr != ncclSuccess) {
+    ctx->comm_failed = true;
+    return nccl_fail(ctx, nr, "ncclAllGather");
+  }
+  if (B > 1) {
+    CU(ctx, launch_shard_interleave(ctx->gather, y, B, R, G, s), "interleave launch");
+    ctx->launches++;
+  }
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_shard_sync(ouroq_ctx* ctx, void* stream, int timeout_ms) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  if (!ctx->comm) return fail(ctx, OUROQ_ERR_BAD_ARG, "context has not joined a shard group");
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(s);
+    if (q == cudaSuccess) return OUROQ_OK;
+    if (q != cudaErrorNotReady) return cuda_fail(ctx, q, "stream query");
+    ncclResult_t ar = ncclSuccess;
+    if (nccl().CommGetAsyncError(comm, &ar) == ncclSuccess && ar != ncclSuccess &&
+        ar != ncclInProgress) {
+      ctx->comm_failed = true;
+      return nccl_fail(ctx, ar, "shard group");
+    }
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                        std::chrono::steady_clock::now() - t0)
+                        .count();
+    if (timeout_ms >= 0 && ms > timeout_ms) {
+      ctx->comm_failed = true;  // the group is aborted, not destroyed, on release
+      return fail(ctx, OUROQ_ERR_TIMEOUT, "sharded work not done after %d ms", timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
 }
 
 }  // extern "C"

@@ -197,9 +197,10 @@ __device__ __forceinline__ void rotate_unit(float* v, const float* signs, int of
 // Four int8 codes packed into a word; their sum is returned through *sum.
 // Kept out of line: the prologue runs once per CTA, and inlining two dozen
 // IEEE divisions bloats the code that every SM has to fetch cold.
-__device__ __noinline__ uint32_t quant4(float a, float b, float c, float d, float s, int* sum) {
-  const int c0 = quant_code(a, s), c1 = quant_code(b, s), c2 = quant_code(c, s),
-            c3 = quant_code(d, s);
+__device__ __noinline__ uint32_t quant4(float a, float b, float c, float d, float s, float rs,
+                                        int* sum) {
+  const int c0 = quant_code(a, s, rs), c1 = quant_code(b, s, rs), c2 = quant_code(c, s, rs),
+            c3 = quant_code(d, s, rs);
   *sum += c0 + c1 + c2 + c3;
   return (uint32_t)(c0 & 0xFF) | ((uint32_t)(c1 & 0xFF) << 8) | ((uint32_t)(c2 & 0xFF) << 16) |
          ((uint32_t)c3 << 24);
@@ -249,13 +250,27 @@ __device__ void prologue_units(const Seg* segs, int nseg, int nunits, const floa
     rotate_unit<E>(v[k], signs, off[k], hb, hscale, lane);
     absmax_unit(v[k], sg[k]);
   }
-  for (int u = warp + R * kCWarps; u < nunits; u += kCWarps) {
-    const int seg = seg_of(segs, nseg, u);
-    const int o = (u - segs[seg].first_unit) * 32 * E + lane * E;
-    float w[E];
-    load_unit<E>(w, segs[seg].x + o);
-    rotate_unit<E>(w, signs, o, hb, hscale, lane);
-    absmax_unit(w, seg);
+  // further units (large batches): R at a time, every load of a batch issued
+  // before its first use, so a warp pays one memory round trip per R units
+  for (int u0 = warp + R * kCWarps; u0 < nunits; u0 += R * kCWarps) {
+    float w[R][E];
+    int wsg[R], wo[R];
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const int u = u0 + k * kCWarps;
+      wsg[k] = -1;
+      if (u < nunits) {
+        wsg[k] = seg_of(segs, nseg, u);
+        wo[k] = (u - segs[wsg[k]].first_unit) * 32 * E + lane * E;
+        load_unit<E>(w[k], segs[wsg[k]].x + wo[k]);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      if (wsg[k] < 0) continue;
+      rotate_unit<E>(w[k], signs, wo[k], hb, hscale, lane);
+      absmax_unit(w[k], wsg[k]);
+    }
   }
   named_bar_sync(1, kCThreads);
   const int ctid = threadIdx.x;
@@ -265,10 +280,11 @@ __device__ void prologue_units(const Seg* segs, int nseg, int nunits, const floa
   auto quant_unit = [&](const float* w, int seg, int o) {
     const Seg& S = segs[seg];
     const float sc = sx[S.sidx];
+    const float rsc = __frcp_rn(sc);
     int sum = 0;
 #pragma unroll
     for (int i = 0; i < E; i += 4)
-      *reinterpret_cast<uint32_t*>(S.q + o + i) = quant4(w[i], w[i + 1], w[i + 2], w[i + 3], sc, &sum);
+      *reinterpret_cast<uint32_t*>(S.q + o + i) = quant4(w[i], w[i + 1], w[i + 2], w[i + 3], sc, rsc, &sum);
 #pragma unroll
     for (int d = kLanesPerGroup / 2; d >= 1; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
     if (lane % kLanesPerGroup == 0) S.qg[o / 128] = sum;
@@ -278,13 +294,25 @@ __device__ void prologue_units(const Seg* segs, int nseg, int nunits, const floa
     if (sg[k] < 0) continue;
     quant_unit(v[k], sg[k], off[k]);
   }
-  for (int u = warp + R * kCWarps; u < nunits; u += kCWarps) {
-    const int seg = seg_of(segs, nseg, u);
-    const int o = (u - segs[seg].first_unit) * 32 * E + lane * E;
-    float w[E];
-    load_unit<E>(w, segs[seg].x + o);
-    rotate_unit<E>(w, signs, o, hb, hscale, lane);
-    quant_unit(w, seg, o);
+  for (int u0 = warp + R * kCWarps; u0 < nunits; u0 += R * kCWarps) {
+    float w[R][E];
+    int wsg[R], wo[R];
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const int u = u0 + k * kCWarps;
+      wsg[k] = -1;
+      if (u < nunits) {
+        wsg[k] = seg_of(segs, nseg, u);
+        wo[k] = (u - segs[wsg[k]].first_unit) * 32 * E + lane * E;
+        load_unit<E>(w[k], segs[wsg[k]].x + wo[k]);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      if (wsg[k] < 0) continue;
+      rotate_unit<E>(w[k], signs, wo[k], hb, hscale, lane);
+      quant_unit(w[k], wsg[k], wo[k]);
+    }
   }
 }
 

@@ -93,10 +93,18 @@ __device__ __forceinline__ void rotate_dispatch(float* row, const float* signs, 
 }
 
 // Per-token absmax int8 code of one value (s_x = absmax / 127 computed by the caller):
-// q = clamp(rint(v / s), -127, 127); s == 0 -> 0.
-__device__ __forceinline__ int quant_code(float v, float s) {
+// q = clamp(rint(v / s), -127, 127); s == 0 -> 0. `rs` = __frcp_rn(s).
+// Fast path: t = v * rs differs from the exact quotient by less than 2^-16
+// (|v / s| <= 127, two correctly rounded operations), and the correctly
+// rounded quotient by less than 2^-15. Both therefore round to the same
+// integer unless t lies within 2^-14 of a half-integer; only then (or when rs
+// overflowed) is the IEEE division evaluated. The result is always
+// rint(__fdiv_rn(v, s)), bit for bit.
+__device__ __forceinline__ int quant_code(float v, float s, float rs) {
   if (s == 0.0f) return 0;
-  float r = rintf(__fdiv_rn(v, s));
+  const float t = __fmul_rn(v, rs);
+  float r = rintf(t);
+  if (!(fabsf(__fsub_rn(t, r)) < 0.5f - 0x1p-14f)) r = rintf(__fdiv_rn(v, s));
   r = fminf(fmaxf(r, -127.0f), 127.0f);
   return (int)r;
 }

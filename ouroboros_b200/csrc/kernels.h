@@ -127,6 +127,10 @@ cudaError_t launch_gemm_tc(const TcLaunch& L, const int8_t* q, int Btot, int sme
 constexpr int kGemvMaxB = 8;
 constexpr size_t kGemvMaxXBytes = 64 * 1024;  // B*K int8 resident in shared memory
 
+// Row-sharded matmul: gather [G][B][R] -> y [B][G*R].
+cudaError_t launch_shard_interleave(const float* gather, float* y, int B, int R, int G,
+                                    cudaStream_t s);
+
 // Fixed scratch of ouroq_gemm_f32act_noalloc (one copy per device): int8
 // codes for up to 4 MiB of B*K, then fp32 scales for up to 4096 tokens.
 constexpr size_t kNoAllocQBytes = 4u << 20;

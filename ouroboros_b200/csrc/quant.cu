@@ -61,6 +61,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const __grid_co
   }
   __syncthreads();
   const float s = __fdiv_rn(red[0], 127.0f);
+  const float rs = __frcp_rn(s);
   if (threadIdx.x == 0) J.s_x[b] = s;
 
   int8_t* q = J.q + (size_t)b * K;
@@ -68,7 +69,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_kernel(const __grid_co
     char4 o;
     int v[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = quant_code(row[i + e], s);
+    for (int e = 0; e < 4; ++e) v[e] = quant_code(row[i + e], s, rs);
     o.x = (signed char)v[0];
     o.y = (signed char)v[1];
     o.z = (signed char)v[2];
