@@ -76,8 +76,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="bound of the CPU-baseline sample (0 = skip)")
     ap.add_argument("--shard", action="store_true",
-                    help="row-shard each matrix over the ranks (NCCL all-gather); "
-                         "single-matrix workloads only")
+                    help="row-shard each matrix over the ranks; single-matrix workloads only")
+    ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
+                    help="how --shard moves rows between ranks")
     return ap.parse_args()
 
 
@@ -504,6 +505,7 @@ def run_sharded(args, rank, world, local_rank):
         shard.join(ctx)
     else:
         ctx.shard_init(oq.shard_unique_id(), 1, 0)
+    ctx.shard_set_transport(args.transport)
     B = args.batch
     ncop = n_copies(wl)
     rng = np.random.default_rng(4321)
@@ -584,7 +586,9 @@ def run_sharded(args, rank, world, local_rank):
             "data": "synthetic (random init ternary weights, fp32 N(0,1) activations)",
             "config": {"workload": f"{desc}-b{B}-rowsharded", "batch": B, "shapes": [[M, K]],
                        "rows_per_rank": M // world, "weight_copies_rotated": ncop,
-                       "parallelism": f"row-sharded x{world}, in-place NCCL all-gather",
+                       "parallelism": f"row-sharded x{world}, " + (
+                           "peer stores over NVLink" if args.transport == "peer"
+                           else "in-place NCCL all-gather"),
                        "launch": f"CUDA graph of {ncop} steps"},
             "local_product_us": round(1e3 * lms / steps, 3),
             "gather_and_sync_us": round(1e3 * (ms - lms) / steps, 3),

@@ -182,6 +182,15 @@ ouroq_status ouroq_shard_unique_id(void *id_out);
 /* Join the group as `rank` of `world` on the context's device. Collective:
  * every rank calls it with the same id. */
 ouroq_status ouroq_shard_init(ouroq_ctx *ctx, const void *id, int world, int rank);
+/* How ouroq_gemm_sharded moves the rows between ranks:
+ *   OUROQ_SHARD_PEER (default): one small kernel per call stores each rank's
+ *     rows straight into every rank's landing buffer over NVLink (CUDA IPC
+ *     mappings); each 64-bit word carries its step number, so readers wait on
+ *     the data itself. Every wait is bounded.
+ *   OUROQ_SHARD_NCCL: in-place ncclAllGather, then an interleave kernel. */
+#define OUROQ_SHARD_PEER 0
+#define OUROQ_SHARD_NCCL 1
+ouroq_status ouroq_shard_set_transport(ouroq_ctx *ctx, int transport);
 /* Leave the group (aborts it instead if a sync timed out or NCCL failed). */
 ouroq_status ouroq_shard_finalize(ouroq_ctx *ctx);
 /* Rows [*row0, *row0 + *rows) of an M-row matrix that `rank` owns; M must

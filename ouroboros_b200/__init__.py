@@ -70,6 +70,7 @@ ABI_FUNCTIONS = {
     "ouroq_gemm_f32act_noalloc": (_i, [_p, _p, _p, _i, _p, _i, _p, _p]),
     "ouroq_shard_unique_id": (_i, [_p]),
     "ouroq_shard_init": (_i, [_p, _p, _i, _i]),
+    "ouroq_shard_set_transport": (_i, [_p, _i]),
     "ouroq_shard_finalize": (_i, [_p]),
     "ouroq_shard_rows": (_i, [_i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     "ouroq_weight_upload_shard": (_i, [_p, _i, _p, _i, _i, _p, _f, ctypes.POINTER(_p)]),
@@ -323,6 +324,10 @@ class Context:
         """Join the shard group; `group_id` comes from shard_unique_id() on rank 0."""
         buf = ctypes.create_string_buffer(bytes(group_id), SHARD_ID_BYTES)
         self._check(self.lib.ouroq_shard_init(self.ctx, ctypes.cast(buf, _p), world, rank))
+
+    def shard_set_transport(self, transport: str) -> None:
+        """'peer' (stores into every rank's buffer over NVLink) or 'nccl' (all-gather)."""
+        self._check(self.lib.ouroq_shard_set_transport(self.ctx, {"peer": 0, "nccl": 1}[transport]))
 
     def shard_finalize(self) -> None:
         self._check(self.lib.ouroq_shard_finalize(self.ctx))

@@ -20,6 +20,7 @@
 #include <new>
 #include <string>
 #include <thread>
+#include <vector>
 
 #include "kernels.h"
 
@@ -51,8 +52,14 @@ struct ouroq_ctx {
   void* comm = nullptr;
   int shard_world = 1, shard_rank = 0;
   bool comm_failed = false;
-  float* gather = nullptr;
+  float* gather = nullptr;  // NCCL transport: [G][B][R]; peer transport: staging [B][R]
   size_t gather_cap = 0;
+  int transport = OUROQ_SHARD_PEER;
+  unsigned long long* landing = nullptr;  // peer transport: two parities of [G][B][R] words
+  size_t landing_words = 0;               // per parity
+  unsigned long long* peer_ptr[kShardMaxRanks] = {};
+  unsigned* shard_ctr = nullptr;  // step, done
+  unsigned long long peer_timeout_ns = 2000000000ull;
 };
 
 struct ouroq_weight {
@@ -370,6 +377,9 @@ ouroq_status nccl_fail(ouroq_ctx* ctx, ncclResult_t r, const char* what) {
 }
 
 void shard_release(ouroq_ctx* ctx) {
+  // The communicator goes first: aborting it ends any collective still
+  // waiting on a peer, so the frees below (which synchronise the device)
+  // cannot block on it. A peer-store gather ends by itself (bounded wait).
   if (ctx->comm) {
     ncclComm_t c = static_cast<ncclComm_t>(ctx->comm);
     if (ctx->comm_failed)
@@ -378,12 +388,125 @@ void shard_release(ouroq_ctx* ctx) {
       nccl().CommDestroy(c);
     ctx->comm = nullptr;
   }
+  if (ctx->landing) cudaDeviceSynchronize();
+  for (int g = 0; g < kShardMaxRanks; ++g) {
+    if (ctx->peer_ptr[g] && ctx->peer_ptr[g] != ctx->landing) cudaIpcCloseMemHandle(ctx->peer_ptr[g]);
+    ctx->peer_ptr[g] = nullptr;
+  }
+  cudaFree(ctx->landing);
+  ctx->landing = nullptr;
+  ctx->landing_words = 0;
+  cudaFree(ctx->shard_ctr);
+  ctx->shard_ctr = nullptr;
   cudaFree(ctx->gather);
   ctx->gather = nullptr;
   ctx->gather_cap = 0;
   ctx->shard_world = 1;
   ctx->shard_rank = 0;
   ctx->comm_failed = false;
+}
+
+// Wait for `s` with a bound, watching the communicator for asynchronous
+// errors. On expiry or an NCCL error the group is marked failed.
+ouroq_status stream_wait_bounded(ouroq_ctx* ctx, cudaStream_t s, int timeout_ms) {
+  const ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(s);
+    if (q == cudaSuccess) return OUROQ_OK;
+    if (q != cudaErrorNotReady) return cuda_fail(ctx, q, "stream query");
+    ncclResult_t ar = ncclSuccess;
+    if (comm && nccl().CommGetAsyncError(comm, &ar) == ncclSuccess && ar != ncclSuccess &&
+        ar != ncclInProgress) {
+      ctx->comm_failed = true;
+      return nccl_fail(ctx, ar, "shard group");
+    }
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                        std::chrono::steady_clock::now() - t0)
+                        .count();
+    if (timeout_ms >= 0 && ms > timeout_ms) {
+      ctx->comm_failed = true;  // the group is aborted, not destroyed, on release
+      return fail(ctx, OUROQ_ERR_TIMEOUT, "sharded work not done after %d ms", timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+// Bound of the set-up exchange (landing buffer handles) between ranks.
+constexpr int kShardSetupTimeoutMs = 60000;
+
+// (Re)allocate this rank's landing buffer for `words` per parity and open
+// every peer's through CUDA IPC. Collective: every rank reaches it on the same
+// call (all ranks make the same sequence of sharded calls with the same sizes).
+ouroq_status ensure_landing(ouroq_ctx* ctx, size_t words, cudaStream_t s) {
+  if (words <= ctx->landing_words) return OUROQ_OK;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  CU(ctx, cudaStreamIsCapturing(s, &cs), "capture query");
+  if (cs != cudaStreamCaptureStatusNone)
+    return fail(ctx, OUROQ_ERR_UNSUPPORTED,
+                "the first sharded call of a given size must come before stream capture");
+  const int G = ctx->shard_world, me = ctx->shard_rank;
+  CU(ctx, cudaDeviceSynchronize(), "landing sync");
+  for (int g = 0; g < kShardMaxRanks; ++g) {
+    if (ctx->peer_ptr[g] && ctx->peer_ptr[g] != ctx->landing) cudaIpcCloseMemHandle(ctx->peer_ptr[g]);
+    ctx->peer_ptr[g] = nullptr;
+  }
+  unsigned long long* old = ctx->landing;
+  ctx->landing = nullptr;
+  ctx->landing_words = 0;
+  const size_t bytes = 2 * words * sizeof(unsigned long long);
+  unsigned long long* buf = nullptr;
+  CU(ctx, cudaMalloc(reinterpret_cast<void**>(&buf), bytes), "landing alloc");
+  // zeroed in stream order before the exchange: peers store here only after it
+  cudaError_t e = cudaMemsetAsync(buf, 0, bytes, s);
+  cudaIpcMemHandle_t mine;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mine, buf);
+  uint8_t* dh = nullptr;
+  const size_t hb = sizeof(cudaIpcMemHandle_t);
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&dh), hb * G);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dh + hb * me, &mine, hb, cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) {
+    cudaFree(dh);
+    cudaFree(buf);
+    cudaFree(old);
+    return cuda_fail(ctx, e, "landing set-up");
+  }
+  const ncclResult_t nr = nccl().AllGather(dh + hb * me, dh, hb, ncclUint8,
+                                           static_cast<ncclComm_t>(ctx->comm), s);
+  if (nr != ncclSuccess) {
+    ctx->comm_failed = true;
+    return nccl_fail(ctx, nr, "landing handle exchange");  // freed with the group
+  }
+  const ouroq_status ws = stream_wait_bounded(ctx, s, kShardSetupTimeoutMs);
+  if (ws != OUROQ_OK) return ws;  // buffers stay allocated until the group is released
+  std::vector<cudaIpcMemHandle_t> all(G);
+  e = cudaMemcpy(all.data(), dh, hb * G, cudaMemcpyDeviceToHost);
+  cudaFree(dh);
+  cudaFree(old);  // every peer closed its mapping of it before joining the exchange above
+  if (e != cudaSuccess) {
+    cudaFree(buf);
+    return cuda_fail(ctx, e, "landing handle exchange");
+  }
+  for (int g = 0; g < G; ++g) {
+    if (g == me) {
+      ctx->peer_ptr[g] = buf;
+      continue;
+    }
+    void* p = nullptr;
+    e = cudaIpcOpenMemHandle(&p, all[g], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int h = 0; h < g; ++h)
+        if (h != me && ctx->peer_ptr[h]) cudaIpcCloseMemHandle(ctx->peer_ptr[h]);
+      for (int h = 0; h < kShardMaxRanks; ++h) ctx->peer_ptr[h] = nullptr;
+      cudaFree(buf);
+      ctx->comm_failed = true;  // the peers hold a mapping of nothing usable
+      return cuda_fail(ctx, e, "open peer landing buffer");
+    }
+    ctx->peer_ptr[g] = static_cast<unsigned long long*>(p);
+  }
+  ctx->landing = buf;
+  ctx->landing_words = words;
+  return OUROQ_OK;
 }
 
 ouroq_status shard_rows_impl(ouroq_ctx* ctx, int M, int world, int rank, int* row0, int* rows) {
@@ -848,6 +971,8 @@ ouroq_status ouroq_shard_init(ouroq_ctx* ctx, const void* id, int world, int ran
   if (world < 1 || rank < 0 || rank >= world)
     return fail(ctx, OUROQ_ERR_BAD_ARG, "rank %d of world %d", rank, world);
   if (ctx->comm) return fail(ctx, OUROQ_ERR_BAD_ARG, "context already joined a shard group");
+  if (world > kShardMaxRanks)
+    return fail(ctx, OUROQ_ERR_UNSUPPORTED, "at most %d ranks per shard group", kShardMaxRanks);
   const NcclApi& n = nccl();
   if (!n.ok) return fail(ctx, OUROQ_ERR_NCCL, "%s", n.why.c_str());
   DeviceGuard g(ctx->device);
@@ -856,6 +981,14 @@ ouroq_status ouroq_shard_init(ouroq_ctx* ctx, const void* id, int world, int ran
   ncclComm_t comm = nullptr;
   const ncclResult_t r = n.CommInitRank(&comm, world, uid, rank);
   if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclCommInitRank");
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&ctx->shard_ctr), 4 * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(ctx->shard_ctr, 0, 4 * sizeof(unsigned));
+  if (e != cudaSuccess) {
+    n.CommDestroy(comm);
+    cudaFree(ctx->shard_ctr);
+    ctx->shard_ctr = nullptr;
+    return cuda_fail(ctx, e, "shard counters");
+  }
   ctx->comm = comm;
   ctx->shard_world = world;
   ctx->shard_rank = rank;
@@ -910,6 +1043,30 @@ ouroq_status ouroq_gemm_sharded(ouroq_ctx* ctx, const ouroq_weight* w, const flo
   DeviceGuard g(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int R = w->M, G = ctx->shard_world, r = ctx->shard_rank;
+  if (G == 1) return ouroq_gemm_f32act(ctx, w, x, B, signs, hadamard_block, y, stream);
+  if (ctx->transport == OUROQ_SHARD_PEER) {
+    ouroq_status st = ensure_landing(ctx, (size_t)G * B * R, s);
+    if (st != OUROQ_OK) return st;
+    st = grow(ctx, ctx->gather, ctx->gather_cap, (size_t)B * R, "staging buffer");
+    if (st != OUROQ_OK) return st;
+    st = ouroq_gemm_f32act(ctx, w, x, B, signs, hadamard_block, ctx->gather, stream);
+    if (st != OUROQ_OK) return st;
+    ShardGather P{};
+    P.staging = ctx->gather;
+    for (int i = 0; i < G; ++i) P.peers[i] = ctx->peer_ptr[i];
+    P.y = y;
+    P.step = ctx->shard_ctr;
+    P.done = ctx->shard_ctr + 1;
+    P.status = ctx->d_status;
+    P.rank = r;
+    P.G = G;
+    P.B = B;
+    P.R = R;
+    P.timeout_ns = ctx->peer_timeout_ns;
+    CU(ctx, launch_shard_gather(P, s, ctx->pdl), "peer gather launch");
+    ctx->launches++;
+    return OUROQ_OK;
+  }
   const ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
   float* slot;
   float* recv;
@@ -937,32 +1094,30 @@ ouroq_status ouroq_gemm_sharded(ouroq_ctx* ctx, const ouroq_weight* w, const flo
   return OUROQ_OK;
 }
 
+ouroq_status ouroq_shard_set_transport(ouroq_ctx* ctx, int transport) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  if (transport != OUROQ_SHARD_PEER && transport != OUROQ_SHARD_NCCL)
+    return fail(ctx, OUROQ_ERR_BAD_ARG, "unknown transport %d", transport);
+  ctx->transport = transport;
+  return OUROQ_OK;
+}
+
 ouroq_status ouroq_shard_sync(ouroq_ctx* ctx, void* stream, int timeout_ms) {
   if (!ctx) return OUROQ_ERR_BAD_ARG;
   if (!ctx->comm) return fail(ctx, OUROQ_ERR_BAD_ARG, "context has not joined a shard group");
   DeviceGuard g(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
-  const auto t0 = std::chrono::steady_clock::now();
-  for (;;) {
-    const cudaError_t q = cudaStreamQuery(s);
-    if (q == cudaSuccess) return OUROQ_OK;
-    if (q != cudaErrorNotReady) return cuda_fail(ctx, q, "stream query");
-    ncclResult_t ar = ncclSuccess;
-    if (nccl().CommGetAsyncError(comm, &ar) == ncclSuccess && ar != ncclSuccess &&
-        ar != ncclInProgress) {
-      ctx->comm_failed = true;
-      return nccl_fail(ctx, ar, "shard group");
-    }
-    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
-                        std::chrono::steady_clock::now() - t0)
-                        .count();
-    if (timeout_ms >= 0 && ms > timeout_ms) {
-      ctx->comm_failed = true;  // the group is aborted, not destroyed, on release
-      return fail(ctx, OUROQ_ERR_TIMEOUT, "sharded work not done after %d ms", timeout_ms);
-    }
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  ouroq_status st = stream_wait_bounded(ctx, s, timeout_ms);
+  if (st != OUROQ_OK) return st;
+  unsigned v = 0;
+  CU(ctx, cudaMemcpyAsync(&v, ctx->d_status, sizeof v, cudaMemcpyDeviceToHost, s), "status read");
+  CU(ctx, cudaStreamSynchronize(s), "status read");
+  if (v == kDevPeerTimeout) {
+    CU(ctx, cudaMemsetAsync(ctx->d_status, 0, sizeof v, s), "status clear");
+    ctx->comm_failed = true;
+    return fail(ctx, OUROQ_ERR_TIMEOUT, "a peer's rows did not arrive in time");
   }
+  return OUROQ_OK;
 }
 
 }  // extern "C"

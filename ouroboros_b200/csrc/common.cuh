@@ -10,14 +10,9 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
-namespace ouroq {
+#include "kernels.h"
 
-// Error codes written to the status word by a kernel that gave up waiting.
-enum : unsigned {
-  kDevOk = 0,
-  kDevWaitTimeout = 1,  // an mbarrier wait ran past its iteration limit
-  kDevBadTile = 2,      // a tile index outside the job table (never expected)
-};
+namespace ouroq {
 
 // Iteration limit for mbarrier polls (each try_wait blocks for a short
 // hardware-defined interval, so this is seconds of wall time at most).

@@ -28,6 +28,15 @@ namespace ouroq {
 //   of k = 32t + 4j + b. fp16 group scales are tiled the same way:
 //   [tile][group][32 rows].
 enum DevFormat : int { kTern2 = 1, kSign1 = 2 };
+
+// Error codes written to the status word by a kernel that gave up waiting.
+enum : unsigned {
+  kDevOk = 0,
+  kDevWaitTimeout = 1,  // an mbarrier wait ran past its iteration limit
+  kDevBadTile = 2,      // a tile index outside the job table (never expected)
+  kDevPeerTimeout = 3,  // a sharded gather waited too long for a peer's rows
+};
+
 constexpr int kTileRows = 32;
 
 // One matrix-times-activations job of a (possibly grouped) GEMV launch.
@@ -127,7 +136,24 @@ cudaError_t launch_gemm_tc(const TcLaunch& L, const int8_t* q, int Btot, int sme
 constexpr int kGemvMaxB = 8;
 constexpr size_t kGemvMaxXBytes = 64 * 1024;  // B*K int8 resident in shared memory
 
-// Row-sharded matmul: gather [G][B][R] -> y [B][G*R].
+// Row-sharded matmul, peer-store transport. Each rank's landing buffer (one
+// cudaMalloc, opened by every peer through CUDA IPC) holds two parities of
+// [G][B][R] 64-bit words, each (step << 32 | fp32 bits).
+constexpr int kShardMaxRanks = 8;
+constexpr int kShardGatherCtas = 64;
+struct ShardGather {
+  const float* staging;                       // this rank's rows [B][R]
+  unsigned long long* peers[kShardMaxRanks];  // landing buffer of every rank (own included)
+  float* y;                                   // [B][G*R]
+  unsigned* step;                             // this rank's step counter (device, starts at 0)
+  unsigned* done;                             // last-CTA counter (device, starts at 0)
+  unsigned* status;
+  int rank, G, B, R;
+  unsigned long long timeout_ns;
+};
+cudaError_t launch_shard_gather(const ShardGather& P, cudaStream_t s, bool pdl);
+
+// Row-sharded matmul, NCCL transport: gather [G][B][R] -> y [B][G*R].
 cudaError_t launch_shard_interleave(const float* gather, float* y, int B, int R, int G,
                                     cudaStream_t s);
 

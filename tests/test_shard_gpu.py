@@ -52,7 +52,7 @@ def _case_data(O, fmt, M, K, B, block, seed):
     return O.pack_sign1(w), sc, 1.0, x, sg
 
 
-def _worker(rank, world, port, mode, out_q):
+def _worker(rank, world, port, mode, out_q, transport="peer"):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -67,6 +67,7 @@ def _worker(rank, world, port, mode, out_q):
     ctx = oq.Context(rank)
     try:
         shard.join(ctx)
+        ctx.shard_set_transport(transport)
         if mode == "cases":
             for i, (fmt, M, K, B, block) in enumerate(CASES):
                 packed, sc, ws, x, sg = _case_data(O, fmt, M, K, B, block, 100 + i)
@@ -80,7 +81,7 @@ def _worker(rank, world, port, mode, out_q):
             ctx.shard_finalize()
         else:
             # rank 1 leaves between steps: it never enters the second product.
-            # Rank 0's all-gather cannot complete; its bounded sync must report
+            # Rank 0's gather cannot complete; its bounded sync must report
             # a timeout and mark the group failed, and finalize then aborts it.
             fmt, M, K, B, block = CASES[0]
             packed, sc, ws, x, sg = _case_data(O, fmt, M, K, B, block, 100)
@@ -112,12 +113,13 @@ def _worker(rank, world, port, mode, out_q):
         dist.destroy_process_group()
 
 
-def _run(world, mode):
+def _run(world, mode, transport="peer"):
     import torch.multiprocessing as mp
     mctx = mp.get_context("spawn")
     q = mctx.Queue()
     port = _free_port()
-    procs = [mctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    procs = [mctx.Process(target=_worker, args=(r, world, port, mode, q, transport))
+             for r in range(world)]
     for p in procs:
         p.start()
     n_expected = world * len(CASES) if mode == "cases" else world
@@ -128,9 +130,10 @@ def _run(world, mode):
     return out
 
 
-def test_sharded_matches_oracle_on_two_gpus(oracle):
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
+def test_sharded_matches_oracle_on_two_gpus(oracle, transport):
     _need_gpus(2)
-    out = _run(2, "cases")
+    out = _run(2, "cases", transport)
     for i, (fmt, M, K, B, block) in enumerate(CASES):
         packed, sc, ws, x, sg = _case_data(oracle, fmt, M, K, B, block, 100 + i)
         q, s = oracle.quantize_act(x, sg, block)
@@ -144,9 +147,10 @@ def test_sharded_matches_oracle_on_two_gpus(oracle):
             assert np.array_equal(y, want), f"case {i}"
 
 
-def test_sharded_sync_times_out_when_a_rank_leaves(oracle):
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
+def test_sharded_sync_times_out_when_a_rank_leaves(oracle, transport):
     _need_gpus(2)
-    out = _run(2, "timeout")
+    out = _run(2, "timeout", transport)
     r0 = [o for o in out if o[1] == 0][0]
     assert r0[2] == 5  # OUROQ_ERR_TIMEOUT
     assert r0[3] == 4  # later calls: OUROQ_ERR_NCCL (group marked failed)
