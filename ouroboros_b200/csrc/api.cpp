@@ -203,8 +203,8 @@ ouroq_status gemm_impl(ouroq_ctx* ctx, const ouroq_weight* w, const int8_t* q, c
     L.tok0 = 0;
     L.nvalid = B;
     L.status = ctx->d_status;
-    CU(ctx, launch_gemm_tc(L, q, B, ctx->smem_optin, s), "tensor-core gemm launch");
-    ctx->launches += (B + 255) / 256;
+    CU(ctx, launch_gemm_tc(L, q, B, ctx->smem_optin, ctx->num_sms, s), "tensor-core gemm launch");
+    ctx->launches++;
     return OUROQ_OK;
   }
   const int chunk = gemv_chunk(w->K);

@@ -11,16 +11,19 @@
 // expanded to u8 c = w + 1 and written straight into tensor memory), N = up
 // to 256 tokens (operand B: the int8 activations, TMA-loaded into shared
 // memory with the 128-byte swizzle), K = 32 per instruction. One CTA owns 128
-// rows of W and N tokens and walks all of K:
+// rows of W and one tile of N tokens (the grid covers row tiles x token tiles,
+// N chosen on the host so that the grid fills the SMs) and walks all of K:
 //   warp 0      producer: per stage, bulk copies of the packed weight slice
 //               (four 32-row tiles of the tiled device layout) + TMA tensor
 //               loads of the activation slice
 //   warp 1      allocates tensor memory; one lane issues the MMAs (A from
 //               tensor memory, B from shared memory) and commits them to
 //               mbarriers
-//   warps 2-5   expand 2-bit codes to bytes (tcgen05.st into 4 rotating A
-//               buffers), sum each token's activations (the correction for
-//               c = w + 1), then run the epilogue out of tensor memory
+//   warps 2-9   expand 2-bit codes to bytes (tcgen05.st into 8 rotating A
+//               buffers; two warps per tensor-memory lane quarter take
+//               alternate 128-k sub-blocks), sum each token's activations (the
+//               correction for c = w + 1), then run the epilogue out of tensor
+//               memory
 // Keeping A out of shared memory matters: expanding in shared memory would
 // cost a 4x write plus a 4x MMA read per packed byte, more shared-memory
 // bandwidth than the HBM stream feeds.
@@ -37,7 +40,8 @@ namespace {
 
 constexpr int kTcRows = 128;     // weight rows per CTA = MMA M
 constexpr int kSliceK = 128;     // k per A buffer = 4 MMAs of K = 32
-constexpr int kTcThreads = 192;  // 6 warps
+constexpr int kXWarps = 8;       // expansion warps: two per tensor-memory lane quarter
+constexpr int kTcThreads = 64 + kXWarps * 32;  // producer, MMA issuer, expansion
 constexpr int kMaxTcStages = 6;
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
@@ -141,7 +145,7 @@ __device__ __forceinline__ void tmem_wait_st() {
 // columns each, 4 int8 per column) in kTmemABufs buffers from column 256.
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA0 = 256;
-constexpr int kTmemABufs = 4;
+constexpr int kTmemABufs = 8;  // even buffers: sub-blocks of half 0, odd: half 1
 
 struct TcPlan {
   uint32_t bars, tmem, qsum, stage0, stage_bytes, act_off, total;
@@ -154,7 +158,7 @@ struct TcPlan {
 __host__ __device__ inline TcPlan tc_plan(int N, int stages) {
   TcPlan p;
   p.ks = N <= 64 ? 512 : (N <= 128 ? 256 : 128);
-  p.bars = 0;    // full[6], sfree[6], afull[4], afree[4], accfull
+  p.bars = 0;    // full[6], sfree[6], afull[8], afree[8], accfull
   p.tmem = 256;  // allocated tensor-memory address
   p.qsum = 512;  // int [256]
   p.stage0 = 2048;
@@ -184,6 +188,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * kTcRows;
+  // token tile of this CTA: [tok_base, tok_base + nv), at most P.N tokens
+  const int tok_base = P.tok0 + blockIdx.y * P.N;
+  const int nv = P.nvalid - blockIdx.y * P.N < P.N ? P.nvalid - blockIdx.y * P.N : P.N;
   const int nstages = (P.K + KS - 1) / KS;  // the last stage may be shorter
   const int C = P.K / 64;  // 16-byte chunks per packed row
 
@@ -234,7 +241,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         for (int u = 0; u < SUB; ++u)
           tma_load_2d(st + pl.act_off + (uint32_t)u * (uint32_t)P.N * 128u, &act_map,
-                      s * KS + u * kSliceK, P.tok0, &full[slot]);
+                      s * KS + u * kSliceK, tok_base, &full[slot]);
       }
     }
     __syncwarp();
@@ -273,21 +280,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- expansion + epilogue (warps 2..5) ----------------
-    const int q = warp & 3;           // tensor-memory lane quarter of this warp
+    // ---------------- expansion + epilogue (warps 2..9) ----------------
+    // Warp w may only touch tensor-memory lanes 32*(w%4) .. +31, so the lane
+    // quarter is w%4; the two warps of a quarter take alternate 128-k
+    // sub-blocks (half h takes g with g%2 == h) so that one expands while the
+    // other waits on its tensor-memory store.
+    const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
     const int r = q * 32 + lane;      // weight row within the CTA tile (= TMEM lane)
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    int qs0 = 0, qs1 = 0;             // running sum_k q for tokens e and e + 128
-    const int e = (warp - 2) * 32 + lane;
+    int qs0 = 0, qs1 = 0;             // partial sum_k q for tokens e and e + 128
+    const int e = ((warp - 2) & 3) * 32 + lane;
     bool ok = true;
     int g = 0;
     for (int s = 0; s < nstages; ++s) {
       const int slot = s % S;
+      const int SUB = (P.K - s * KS < KS ? P.K - s * KS : KS) / kSliceK;
+      // a stage holds a sub-block of this half unless it has one sub-block of the other
+      if (SUB == 1 && ((g & 1) != h)) {
+        ++g;
+        continue;
+      }
       if (ok) ok = mbar_wait(&full[slot], (s / S) & 1, P.status);
       const uint8_t* st = stages + (size_t)slot * pl.stage_bytes;
       const uint8_t* src = st + (r >> 5) * (KS * 8) + (r & 31) * 16;
-      const int SUB = (P.K - s * KS < KS ? P.K - s * KS : KS) / kSliceK;
       for (int u = 0; u < SUB; ++u, ++g) {
+        if ((g & 1) != h) continue;
         const int b = g % kTmemABufs;
         if (ok && g >= kTmemABufs) ok = mbar_wait(&afree[b], ((g / kTmemABufs) - 1) & 1, P.status);
         // expand this row's two 64-k chunks of the sub-block into 32 columns
@@ -329,21 +347,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) mbar_arrive(&afull[b]);
       }
     }
-    if (e < P.N) qsum[e] = qs0;
-    if (e + 128 < P.N) qsum[e + 128] = qs1;
-    named_bar_sync(1, 128);
-    // ---- epilogue: D[row][token] from tensor memory
+    if (e < P.N) atomicAdd(&qsum[e], qs0);
+    if (e + 128 < P.N) atomicAdd(&qsum[e + 128], qs1);
+    named_bar_sync(1, kXWarps * 32);
+    // ---- epilogue: D[row][token] from tensor memory, 32-column chunks split by half
     if (ok) ok = mbar_wait(accfull, 0, P.status);
     tc_fence_after();
     const int row = row0 + r;
-    for (int j0 = 0; j0 < P.N; j0 += 32) {
+    for (int j0 = h * 32; j0 < P.N; j0 += 64) {
       uint32_t d[32];
       tmem_ld32(tmem + lane_base + (uint32_t)j0, d);
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const int n = j0 + j;
-        if (n < P.nvalid && row < P.M) {
-          const int tok = P.tok0 + n;
+        if (n < nv && row < P.M) {
+          const int tok = tok_base + n;
           const int acc = (int)d[j] - qsum[n];
           P.y[(size_t)tok * P.ldy + row] =
               __fmul_rn(__fmul_rn(__int2float_rn(acc), P.w_scale), P.s_x[tok]);
@@ -386,43 +404,48 @@ bool gemm_tc_supported(int fmt, int M, int K, int B) {
   return fmt == kTern2 && M > 0 && K % kSliceK == 0 && B >= 1;
 }
 
+int gemm_tc_tile_n(int M, int B, int num_sms) {
+  // Largest token tile (multiple of 16, <= 256) that still gives the grid
+  // about one CTA per SM; each halving doubles the expansion work per MMA, so
+  // stop at 32.
+  const int mt = (M + kTcRows - 1) / kTcRows;
+  int N = (B < 256 ? B : 256);
+  N = (N + 15) / 16 * 16;
+  while (N > 32 && (long)mt * ((B + N - 1) / N) < (long)num_sms * 4 / 5) N = ((N / 2) + 15) / 16 * 16;
+  return N < 16 ? 16 : N;
+}
+
 cudaError_t launch_gemm_tc(const TcLaunch& L0, const int8_t* q, int Btot, int smem_optin,
-                           cudaStream_t s) {
+                           int num_sms, cudaStream_t s) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   cudaError_t e = ensure_max_smem<gemm_tc_kernel>();
   if (e != cudaSuccess) return e;
-  for (int tok0 = 0; tok0 < L0.nvalid; tok0 += 256) {
-    TcLaunch L = L0;
-    const int nv = L0.nvalid - tok0 < 256 ? L0.nvalid - tok0 : 256;
-    L.tok0 = L0.tok0 + tok0;
-    L.nvalid = nv;
-    L.N = (nv + 15) / 16 * 16;
-    if (L.N < 16) L.N = 16;
-    int stages = kMaxTcStages;
-    while (stages > 2 && tc_plan(L.N, stages).total > (uint32_t)smem_optin - 2048u) --stages;
-    L.stages = stages;
-    const size_t smem = tc_plan(L.N, stages).total;
-    // activations [Btot][K] int8, box 128 B x N rows, 128-byte swizzle, zero fill
-    CUtensorMap map;
-    const cuuint64_t dims[2] = {(cuuint64_t)L.K, (cuuint64_t)Btot};
-    const cuuint64_t strides[1] = {(cuuint64_t)L.K};
-    const cuuint32_t box[2] = {128u, (cuuint32_t)L.N};
-    const cuuint32_t estr[2] = {1u, 1u};
-    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return cudaErrorInvalidValue;
-    const dim3 grid((L.M + kTcRows - 1) / kTcRows, 1, 1);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(kTcThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel, map, L);
-    if (e != cudaSuccess) return e;
-  }
-  return cudaSuccess;
+  if (L0.nvalid <= 0) return cudaSuccess;
+  TcLaunch L = L0;
+  L.N = gemm_tc_tile_n(L.M, L.nvalid, num_sms);
+  int stages = kMaxTcStages;
+  while (stages > 2 && tc_plan(L.N, stages).total > (uint32_t)smem_optin - 2048u) --stages;
+  L.stages = stages;
+  const size_t smem = tc_plan(L.N, stages).total;
+  // activations [Btot][K] int8, box 128 B x N rows, 128-byte swizzle, zero fill
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)L.K, (cuuint64_t)Btot};
+  const cuuint64_t strides[1] = {(cuuint64_t)L.K};
+  const cuuint32_t box[2] = {128u, (cuuint32_t)L.N};
+  const cuuint32_t estr[2] = {1u, 1u};
+  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  // one CTA per (128-row tile, token tile)
+  const dim3 grid((L.M + kTcRows - 1) / kTcRows, (L.nvalid + L.N - 1) / L.N, 1);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, map, L);
 }
 
 }  // namespace ouroq

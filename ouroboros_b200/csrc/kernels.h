@@ -119,18 +119,19 @@ struct TcLaunch {
   float w_scale;
   int M, K, ldy;
   int tok0;           // first token of this launch
-  int N;              // tokens per CTA pass (multiple of 16, 16..256), filled by the launcher
-  int nvalid;         // valid tokens from tok0
+  int N;              // tokens per CTA tile (multiple of 16, 16..256), filled by the launcher
+  int nvalid;         // valid tokens from tok0 (all token tiles)
   int stages;         // filled by the launcher
   unsigned* status;
 };
 
 bool gemm_tc_supported(int fmt, int M, int K, int B);
 size_t gemm_tc_smem_bytes(int N, int stages);
-// q: int8 activations [Btot][K] (16-byte aligned rows). Splits tokens into
-// passes of at most 256.
+// q: int8 activations [Btot][K] (16-byte aligned rows). One launch; the grid
+// covers (128-row tiles) x (token tiles of gemm_tc_tile_n tokens).
+int gemm_tc_tile_n(int M, int B, int num_sms);
 cudaError_t launch_gemm_tc(const TcLaunch& L, const int8_t* q, int Btot, int smem_optin,
-                           cudaStream_t s);
+                           int num_sms, cudaStream_t s);
 
 // Limits of the small-batch GEMV path.
 constexpr int kGemvMaxB = 8;
