@@ -43,7 +43,9 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-TERN, SIGN = 1, 2  # OUROQ_FMT_TERNARY2, OUROQ_FMT_SIGN1G128
+TERN, SIGN, TL1, TQ1 = 1, 2, 3, 4  # OUROQ_FMT_TERNARY2, _SIGN1G128, _PTQ1_0, _TQ1_0
+FMT_NAME = {TERN: "ternary2", SIGN: "sign1g128", TL1: "ptq1_0", TQ1: "tq1_0"}
+REF_FMTS = (TL1, TQ1)
 HIDDEN, FFN = 2560, 6912
 L2_BYTES = 126 * 2**20
 FALLBACK_HBM_GBS = 6650.0
@@ -61,6 +63,18 @@ WORKLOADS = {
     "c5-down": ("ternary-8192x28672", TERN, [("ffn_down", 8192, 28672, 0)], [28672], 0),
     "c3-4096": ("sign1-wht128-4096x4096", SIGN, [("w", 4096, 4096, 0)], [4096], 128),
     "c3-11008": ("sign1-wht128-11008x4096", SIGN, [("w", 11008, 4096, 0)], [4096], 128),
+    # the BitNet-2B layer in the reference's own shard formats (fp32 activations,
+    # no quantisation): the path the reference runs today
+    "layer-tq1": ("bitnet2b-layer-projections-tq1_0", TQ1,
+                  [("attn_qkv", 3840, HIDDEN, 0), ("attn_output", HIDDEN, HIDDEN, 1),
+                   ("ffn_gate", FFN, HIDDEN, 2), ("ffn_up", FFN, HIDDEN, 2),
+                   ("ffn_down", HIDDEN, 6912, 3)],
+                  [HIDDEN, HIDDEN, HIDDEN, FFN], 0),
+    "layer-tl1": ("bitnet2b-layer-projections-ptq1_0", TL1,
+                  [("attn_qkv", 3840, HIDDEN, 0), ("attn_output", HIDDEN, HIDDEN, 1),
+                   ("ffn_gate", FFN, HIDDEN, 2), ("ffn_up", FFN, HIDDEN, 2),
+                   ("ffn_down", HIDDEN, 6912, 3)],
+                  [HIDDEN, HIDDEN, HIDDEN, FFN], 0),
 }
 
 
@@ -83,6 +97,10 @@ def parse():
 
 
 def weight_bytes(fmt: int, M: int, K: int) -> int:
+    if fmt == TL1:
+        return M * (K // 128) * 28
+    if fmt == TQ1:
+        return M * (K // 256) * 54
     return M * K // 4 if fmt == TERN else M * K // 8 + M * (K // 128) * 2
 
 
@@ -179,6 +197,17 @@ def make_copy(torch, ctx, oq, wl, gen, device):
     _, fmt, mats, _, _ = wl
     out = []
     for _, M, K, _ in mats:
+        if fmt in REF_FMTS:
+            # random code bytes (every byte is a valid set of trits), finite f16 scales
+            gb = 28 if fmt == TL1 else 54
+            ng = M * K // (128 if fmt == TL1 else 256)
+            p = torch.randint(0, 256, (ng, gb), generator=gen, device=device,
+                              dtype=torch.int32).to(torch.uint8)
+            sc = (torch.randn((ng,), generator=gen, device=device) * 0.02).abs().to(torch.float16)
+            p[:, gb - 2:] = sc.view(torch.uint8).view(ng, 2)
+            p = p.reshape(-1).contiguous()
+            out.append((ctx.upload_device(fmt, p, M, K, None, 1.0), p, None))
+            continue
         if fmt == TERN:
             r = torch.randint(0, 4, (M, K), generator=gen, device=device, dtype=torch.uint8)
             codes = (r == 3).to(torch.uint8) * 2 + ((r == 1) | (r == 2)).to(torch.uint8)
@@ -207,6 +236,19 @@ def cpu_oracle_gbs(wl, host_mats, host_signs, B: int, seconds: float, threads: i
     nb = step_bytes(wl, B)["step"]
     steps, t0 = 0, time.perf_counter()
     while True:
+        if fmt in REF_FMTS:
+            # the reference's own algorithm for these formats, restated (threaded like it)
+            for (_, M, K, xi), (packed, _) in zip(mats, host_mats):
+                for b in range(B):
+                    if fmt == TL1:
+                        O.matvec_tl1_sse(packed, M, K, xs[xi][b], threads)
+                    else:
+                        O.matvec_tq1(packed, M, K, xs[xi][b], threads)
+            steps += 1
+            dt = time.perf_counter() - t0
+            if dt >= seconds:
+                break
+            continue
         qs = [O.quantize_act(x, host_signs[i] if block else None, block) for i, x in enumerate(xs)]
         for (_, M, K, xi), (packed, aux) in zip(mats, host_mats):
             q, s = qs[xi]
@@ -227,6 +269,12 @@ def host_copy(wl, seed: int):
     _, fmt, mats, widths, block = wl
     out = []
     for i, (_, M, K, _) in enumerate(mats):
+        if fmt in REF_FMTS:
+            gb = 28 if fmt == TL1 else 54
+            p = O.lcg_bytes(seed + i, M * K // (128 if fmt == TL1 else 256) * gb).reshape(-1, gb)
+            p[:, gb - 1] = 0x24  # f16 scales ~ 0.02
+            out.append((p.reshape(-1), None))
+            continue
         if fmt == TERN:
             w = O.ternary(seed + i, M * K).reshape(M, K)
             out.append((O.pack_tern2(w), float(O.absmean_scale(w, 0.02))))
@@ -240,7 +288,7 @@ def host_copy(wl, seed: int):
 def workload_config(args, wl, world):
     desc, fmt, mats, widths, block = wl
     return {"workload": f"{desc}-b{args.batch}", "batch": args.batch,
-            "format": "ternary2" if fmt == TERN else "sign1g128",
+            "format": FMT_NAME[fmt],
             "shapes": [[M, K] for _, M, K, _ in mats], "hadamard_block": block,
             "weight_copies_rotated": n_copies(wl),
             "l2": f"inputs larger than L2: {n_copies(wl)} weight copies = "
@@ -274,11 +322,14 @@ def run_reference(args, rank):
         "impl": "reference", "metric": "packed-weight GEMV HBM GB/s",
         "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": total_steps,
         "warmup": args.warmup, "ms_per_step": round(1e3 * total_t / total_steps, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if wl[1] in REF_FMTS else "int8",
         "data": "synthetic", "config": cfg,
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{total_steps} steps at batch {B} (oracle int8 quantise + "
-                                   f"GEMV, {threads} threads, rows chunked as ops.rs:104-105; "
+                         "sample": f"{total_steps} steps at batch {B} (" + (
+                             "the reference's own fp32 algorithm for this format, restated"
+                             if wl[1] in REF_FMTS else "oracle int8 quantise + GEMV") +
+                                   f", {threads} threads, rows chunked as ops.rs:104-105; "
                                    f"capped at {budget:.0f} s)"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -314,11 +365,16 @@ def run_ouroq(args, rank, world, local_rank):
     qs = [[torch.empty((B, k), dtype=torch.int8, device=device) for k in widths] for _ in range(2)]
     sxs = [[torch.empty((B,), dtype=torch.float32, device=device) for _ in widths] for _ in range(2)]
     stream = torch.cuda.Stream(device=device)
-    fused = B <= 8
+    fused = B <= 8 or fmt in REF_FMTS
     mat_signs = [signs[xi] for _, _, _, xi in mats] if block else None
     mat_blocks = [block] * len(mats) if block else None
 
     def run_step(wl_, xin, yout, qbuf, sbuf):
+        if fmt in REF_FMTS:
+            # fp32 activations straight into the reference-format kernels, one per matrix
+            for j, (_, _, _, xi) in enumerate(mats):
+                ctx.gemm_f32act(wl_[j], xin[xi], y=yout[j], stream=stream)
+            return
         if fused:
             # one launch: the fp32 inputs are quantised in the GEMV prologue
             if len(mats) > 1:
@@ -392,11 +448,13 @@ def run_ouroq(args, rank, world, local_rank):
     hbm_peak, bf16_peak, peak_kind = peaks()
     tensor_bound = fmt == TERN and B >= 64
     if fused:
-        # the fused grouped GEMV is the only kernel of a step: its average launch
-        # duration is the timed region (CUDA events on its stream) / launches
+        # the step's kernels are the product itself (the fused grouped GEMV, or one
+        # reference-format kernel per matrix): bytes of the step / the timed region
         kern_s = ms / 1e3 / steps
         kern_bytes = nb["step"]
-        kernel = f"gemv_kernel<{'kTern2' if fmt == TERN else 'kSign1'},B={B}> (fused quantisation)"
+        kernel = (f"{'tl1' if fmt == TL1 else 'tq1'}_matvec_kernel (reference order)"
+                  if fmt in REF_FMTS else
+                  f"gemv_kernel<{'kTern2' if fmt == TERN else 'kSign1'},B={B}> (fused quantisation)")
     else:
         # matmul launches alone, on pre-quantised activations, timed the same way
         g2, _ = capture(gemm_only)
@@ -451,14 +509,17 @@ def run_ouroq(args, rank, world, local_rank):
         from oracle import pyoracle as O
         host_mats = []
         for w, p, sc in copies[0]:
-            aux = float(w.w_scale) if fmt == TERN else sc.cpu().numpy().view(np.uint16)
+            aux = (float(w.w_scale) if fmt == TERN else
+                   None if fmt in REF_FMTS else sc.cpu().numpy().view(np.uint16))
             host_mats.append((p.cpu().numpy(), aux))
         host_signs = [s.cpu().numpy() for s in signs] if block else None
         threads = O.hw_threads()
         gbs, st, dt = cpu_oracle_gbs(wl, host_mats, host_signs, B, args.cpu_seconds, threads)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{st} steps ({dt:.1f} s) at batch {B}: oracle int8 quantise + GEMV, "
-                         f"{threads} threads"}
+               "sample": f"{st} steps ({dt:.1f} s) at batch {B}: " + (
+                   "the reference's own fp32 algorithm for this format (matvec_tl1 x86 order / "
+                   "matvec_qblock), restated" if fmt in REF_FMTS else
+                   "oracle int8 quantise + GEMV") + f", {threads} threads"}
 
     if rank == 0:
         cfg = workload_config(args, wl, world)
@@ -467,7 +528,8 @@ def run_ouroq(args, rank, world, local_rank):
             "metric": "packed-weight GEMV HBM GB/s",
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(ms / steps, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32" if fmt in REF_FMTS else "int8",
             "data": "synthetic (random init weights, fp32 N(0,1) activations)",
             "config": cfg,
             "roofline": roof,

@@ -54,7 +54,18 @@ typedef enum {
 
 typedef enum {
   OUROQ_FMT_TERNARY2 = 1,
-  OUROQ_FMT_SIGN1G128 = 2
+  OUROQ_FMT_SIGN1G128 = 2,
+  /* The reference's own shard formats, uploaded byte for byte (no scales
+   * argument, w_scale ignored) and used with fp32 activations only
+   * (ouroq_gemm_f32act, ouroq_matvec_q, ouroq_matmul_q, ouroq_gemm_sharded):
+   *   PTQ1_0 ("Tl1", QuantKind::Tl1, dequant.rs:123-171): per 128 weights
+   *     28 bytes qs[24] | qh[2] | f16 d; K multiple of 128. Results are
+   *     bit-identical to matvec_tl1's x86 order (ops.rs:499-584), per token.
+   *   TQ1_0 (QuantKind::Tq1_0, dequant.rs:50-105): per 256 weights 54 bytes
+   *     qs[48] | qh[4] | f16 d; K multiple of 256. Results are bit-identical
+   *     to matvec_qblock (dequantise, then dot in element order, ops.rs:53-60). */
+  OUROQ_FMT_PTQ1_0 = 3,
+  OUROQ_FMT_TQ1_0 = 4
 } ouroq_format;
 
 typedef struct ouroq_ctx ouroq_ctx;

@@ -24,7 +24,8 @@ from pathlib import Path
 import numpy as np
 
 __all__ = [
-    "OuroqError", "Context", "Weight", "TERNARY2", "SIGN1G128", "load_library", "LIB_PATH",
+    "OuroqError", "Context", "Weight", "TERNARY2", "SIGN1G128", "PTQ1_0", "TQ1_0", "load_library",
+    "LIB_PATH",
     "ABI_FUNCTIONS", "SHARD_ID_BYTES", "shard_unique_id", "shard_rows",
 ]
 
@@ -32,6 +33,8 @@ LIB_PATH = Path(__file__).resolve().parent / "libouroq.so"
 
 TERNARY2 = 1
 SIGN1G128 = 2
+PTQ1_0 = 3  # the reference's Tl1 shard format (28 B per 128 weights), fp32 activations
+TQ1_0 = 4   # the reference's TQ1_0 shard format (54 B per 256 weights), fp32 activations
 SHARD_ID_BYTES = 128
 
 OK = 0

@@ -48,6 +48,9 @@ struct ouroq_ctx {
   size_t y_cap = 0;
   float* sign_stage = nullptr;
   size_t sign_cap = 0;
+  // rotated fp32 activations for the reference formats (hadamard_block != 0)
+  float* rot_scratch = nullptr;
+  size_t rot_cap = 0;
   // row-sharded group (NCCL communicator, opaque here)
   void* comm = nullptr;
   int shard_world = 1, shard_rank = 0;
@@ -245,11 +248,70 @@ ouroq_status quantize_impl(ouroq_ctx* ctx, const float* x, int B, int K, const f
   return OUROQ_OK;
 }
 
+bool is_ref_format(int fmt) { return fmt == OUROQ_FMT_PTQ1_0 || fmt == OUROQ_FMT_TQ1_0; }
+
+// Bytes of one row of a reference-format payload (dequant.rs:123-130, 50-53).
+size_t ref_row_bytes(int fmt, int K) {
+  return fmt == OUROQ_FMT_PTQ1_0 ? (size_t)K / 128 * 28 : (size_t)K / 256 * 54;
+}
+
 ouroq_status check_weight_shape(ouroq_ctx* ctx, ouroq_format fmt, int M, int K) {
-  if (fmt != OUROQ_FMT_TERNARY2 && fmt != OUROQ_FMT_SIGN1G128)
+  if (fmt != OUROQ_FMT_TERNARY2 && fmt != OUROQ_FMT_SIGN1G128 && !is_ref_format(fmt))
     return fail(ctx, OUROQ_ERR_BAD_ARG, "unknown format %d", (int)fmt);
   if (M <= 0 || K <= 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "M=%d K=%d", M, K);
   if (K % 128) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "K=%d not a multiple of 128", K);
+  if (fmt == OUROQ_FMT_TQ1_0 && K % 256)
+    return fail(ctx, OUROQ_ERR_BAD_SHAPE, "TQ1_0: K=%d not a multiple of 256", K);
+  return OUROQ_OK;
+}
+
+// Reference formats are kept on the device byte for byte as in the shard.
+ouroq_status upload_ref(ouroq_ctx* ctx, ouroq_format fmt, const void* packed, int M, int K,
+                        ouroq_weight** out, bool from_device) {
+  ouroq_weight* w = new (std::nothrow) ouroq_weight;
+  if (!w) return fail(ctx, OUROQ_ERR_OOM, "host allocation");
+  w->fmt = fmt;
+  w->M = M;
+  w->K = K;
+  const size_t bytes = ref_row_bytes(fmt, K) * (size_t)M;
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&w->w), bytes);
+  if (e != cudaSuccess) {
+    delete w;
+    return cuda_fail(ctx, e, "weight alloc");
+  }
+  e = cudaMemcpyAsync(w->w, packed, bytes,
+                      from_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                      ctx->host_stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->host_stream);
+  if (e != cudaSuccess) {
+    cudaFree(w->w);
+    delete w;
+    return cuda_fail(ctx, e, "weight upload");
+  }
+  w->bytes = bytes;
+  *out = w;
+  return OUROQ_OK;
+}
+
+// fp32 x [B][K] -> y [B][M] for the reference formats (no quantisation).
+ouroq_status ref_matvec(ouroq_ctx* ctx, const ouroq_weight* w, const float* x, int B, float* y,
+                        cudaStream_t s) {
+  RefLaunch P{};
+  P.fmt = w->fmt == OUROQ_FMT_PTQ1_0 ? kPtq1 : kTq1;
+  P.w = w->w;
+  P.x = x;
+  P.y = y;
+  P.M = w->M;
+  P.K = w->K;
+  P.B = B;
+  P.ldy = w->M;
+  const size_t smem = P.fmt == kPtq1 ? tl1_smem_bytes(w->K, tl1_rows_per_cta(w->K))
+                                     : tq1_smem_bytes(w->K);
+  if (smem > (size_t)ctx->smem_optin)
+    return fail(ctx, OUROQ_ERR_UNSUPPORTED, "K=%d too wide for the reference-format kernels", w->K);
+  if ((size_t)B > 65535) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d (max 65535)", B);
+  CU(ctx, launch_refmt_matvec(P, s), "reference-format matvec launch");
+  ctx->launches++;
   return OUROQ_OK;
 }
 
@@ -264,6 +326,7 @@ ouroq_status upload_impl(ouroq_ctx* ctx, ouroq_format fmt, const void* packed, i
   DeviceGuard g(ctx->device);
   // device-side inputs may still be in flight on the caller's streams
   if (from_device) CU(ctx, cudaDeviceSynchronize(), "upload input sync");
+  if (is_ref_format(fmt)) return upload_ref(ctx, fmt, packed, M, K, out, from_device);
   ouroq_weight* w = new (std::nothrow) ouroq_weight;
   if (!w) return fail(ctx, OUROQ_ERR_OOM, "host allocation");
   w->fmt = fmt;
@@ -578,6 +641,7 @@ ouroq_status ouroq_ctx_destroy(ouroq_ctx* ctx) {
   cudaFree(ctx->x_stage);
   cudaFree(ctx->y_stage);
   cudaFree(ctx->sign_stage);
+  cudaFree(ctx->rot_scratch);
   shard_release(ctx);
   delete ctx;
   return OUROQ_OK;
@@ -704,6 +768,8 @@ ouroq_status ouroq_gemm(ouroq_ctx* ctx, const ouroq_weight* w, const int8_t* q, 
   if (B < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d", B);
   if (B == 0) return OUROQ_OK;
   if (!q || !s_x || !y) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  if (is_ref_format(w->fmt))
+    return fail(ctx, OUROQ_ERR_UNSUPPORTED, "PTQ1_0 / TQ1_0 weights take fp32 activations");
   if (!aligned16(q)) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "q not 16-byte aligned");
   DeviceGuard g(ctx->device);
   return gemm_impl(ctx, w, q, s_x, B, y, acc_debug, static_cast<cudaStream_t>(stream));
@@ -722,6 +788,8 @@ ouroq_status ouroq_gemm_group(ouroq_ctx* ctx, int n, const ouroq_weight* const* 
   L.B = B;
   for (int i = 0; i < n; ++i) {
     if (!w[i] || !q[i] || !s_x[i] || !y[i]) return fail(ctx, OUROQ_ERR_BAD_ARG, "null entry %d", i);
+    if (is_ref_format(w[i]->fmt))
+      return fail(ctx, OUROQ_ERR_UNSUPPORTED, "grouped calls take TERNARY2 / SIGN1G128 weights");
     if (w[i]->fmt != w[0]->fmt) return fail(ctx, OUROQ_ERR_UNSUPPORTED, "mixed formats in a group");
     if ((size_t)B * w[i]->K > kGemvMaxXBytes)
       return fail(ctx, OUROQ_ERR_UNSUPPORTED, "B*K=%d exceeds the grouped GEMV limit", B * w[i]->K);
@@ -749,6 +817,8 @@ ouroq_status ouroq_gemm_group_f32act(ouroq_ctx* ctx, int n, const ouroq_weight* 
   int maxK = 0;
   for (int i = 0; i < n; ++i) {
     if (!w[i] || !x[i] || !y[i]) return fail(ctx, OUROQ_ERR_BAD_ARG, "null entry %d", i);
+    if (is_ref_format(w[i]->fmt))
+      return fail(ctx, OUROQ_ERR_UNSUPPORTED, "grouped calls take TERNARY2 / SIGN1G128 weights");
     if (w[i]->fmt != w[0]->fmt) return fail(ctx, OUROQ_ERR_UNSUPPORTED, "mixed formats in a group");
     const int blk = blocks ? blocks[i] : 0;
     ouroq_status st = check_quant_args(ctx, B, w[i]->K, blk);
@@ -785,6 +855,21 @@ ouroq_status ouroq_gemm_f32act(ouroq_ctx* ctx, const ouroq_weight* w, const floa
   if (!aligned16(x)) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "x not 16-byte aligned");
   DeviceGuard g(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (is_ref_format(w->fmt)) {
+    // the reference rotates x first (Qwen35Stage::wh, qwen35.rs:683-692), then matvec_q
+    const float* xin = x;
+    if (hadamard_block) {
+      st = grow(ctx, ctx->rot_scratch, ctx->rot_cap, (size_t)B * w->K, "rotation scratch");
+      if (st != OUROQ_OK) return st;
+      CU(ctx,
+         launch_rotate(x, ctx->rot_scratch, signs, B, w->K, hadamard_block,
+                       1.0f / std::sqrt((float)hadamard_block), 0, s),
+         "rotate launch");
+      ctx->launches++;
+      xin = ctx->rot_scratch;
+    }
+    return ref_matvec(ctx, w, xin, B, y, s);
+  }
   const int dfmt = w->fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
   if (B <= kGemvMaxB && (hadamard_block == 0 || (hadamard_block >= 32 && hadamard_block <= 128))) {
     // one launch: rotate + quantise in the GEMV prologue
@@ -847,6 +932,13 @@ ouroq_status ouroq_gemm_f32act_noalloc(ouroq_ctx* ctx, const ouroq_weight* w, co
                 "(split the batch, or use ouroq_gemm_f32act)",
                 B, w->K, kNoAllocMaxTokens, kNoAllocQBytes);
   DeviceGuard g(ctx->device);
+  if (is_ref_format(w->fmt)) {
+    // no quantisation, so no scratch; the rotation would need a buffer
+    if (hadamard_block)
+      return fail(ctx, OUROQ_ERR_UNSUPPORTED,
+                  "PTQ1_0 / TQ1_0 with a rotation needs scratch: rotate first, or use ouroq_gemm_f32act");
+    return ref_matvec(ctx, w, x, B, y, static_cast<cudaStream_t>(stream));
+  }
   uint8_t* scratch = nullptr;
   st = noalloc_scratch(ctx, &scratch);
   if (st != OUROQ_OK) return st;
@@ -1018,7 +1110,8 @@ ouroq_status ouroq_weight_upload_shard(ouroq_ctx* ctx, ouroq_format fmt, const v
   int row0 = 0, rows = 0;
   st = shard_rows_impl(ctx, M, ctx->shard_world, ctx->shard_rank, &row0, &rows);
   if (st != OUROQ_OK) return st;
-  const size_t rb = fmt == OUROQ_FMT_TERNARY2 ? (size_t)K / 4 : (size_t)K / 8;
+  const size_t rb = is_ref_format(fmt) ? ref_row_bytes(fmt, K)
+                                       : (fmt == OUROQ_FMT_TERNARY2 ? (size_t)K / 4 : (size_t)K / 8);
   const uint8_t* p = static_cast<const uint8_t*>(packed_full) + (size_t)row0 * rb;
   const uint16_t* sc =
       scales_full ? static_cast<const uint16_t*>(scales_full) + (size_t)row0 * (K / 128) : nullptr;

@@ -27,7 +27,7 @@ namespace ouroq {
 // kSign1: word t covers k = 32t .. 32t+31; byte b, bit j holds the sign bit
 //   of k = 32t + 4j + b. fp16 group scales are tiled the same way:
 //   [tile][group][32 rows].
-enum DevFormat : int { kTern2 = 1, kSign1 = 2 };
+enum DevFormat : int { kTern2 = 1, kSign1 = 2, kPtq1 = 3, kTq1 = 4 };
 
 // Error codes written to the status word by a kernel that gave up waiting.
 enum : unsigned {
@@ -132,6 +132,20 @@ size_t gemm_tc_smem_bytes(int N, int stages);
 int gemm_tc_tile_n(int M, int B, int num_sms);
 cudaError_t launch_gemm_tc(const TcLaunch& L, const int8_t* q, int Btot, int smem_optin,
                            int num_sms, cudaStream_t s);
+
+// The reference's own shard formats (PTQ1_0 "Tl1", TQ1_0), stored on the device
+// exactly as in the shard (row-major, no repack): fp32 x [B][K] -> y [B][ldy].
+struct RefLaunch {
+  int fmt;            // kPtq1 or kTq1
+  const uint8_t* w;   // payload, rows of K/128*28 (kPtq1) or K/256*54 (kTq1) bytes
+  const float* x;
+  float* y;
+  int M, K, B, ldy;
+};
+size_t tl1_smem_bytes(int K, int R);
+int tl1_rows_per_cta(int K);
+size_t tq1_smem_bytes(int K);
+cudaError_t launch_refmt_matvec(const RefLaunch& P, cudaStream_t s);
 
 // Limits of the small-batch GEMV path.
 constexpr int kGemvMaxB = 8;
