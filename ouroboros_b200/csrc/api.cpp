@@ -841,7 +841,52 @@ ouroq_status ouroq_gemm_group_f32act(ouroq_ctx* ctx, int n, const ouroq_weight* 
                 "B=%d, K=%d: activations do not fit the fused GEMV (use quantize + gemm_group)",
                 B, maxK);
   DeviceGuard g(ctx->device);
-  return run_gemv(ctx, L, static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (B <= kFusedMaxB) return run_gemv(ctx, L, s);
+  // Larger batches: every CTA would quantise all tokens of its matrices again,
+  // so quantise each distinct activation set once (one launch) into scratch
+  // and run the grouped GEMV on the int8 codes.
+  QuantLaunch Q{};
+  Q.B = B;
+  int set_of[kMaxGemvJobs];
+  size_t qoff[kMaxQuantJobs], soff[kMaxQuantJobs], qtot = 0, stot = 0;
+  for (int i = 0; i < n; ++i) {
+    int k = 0;
+    while (k < Q.njobs && !(Q.jobs[k].x == x[i] && Q.jobs[k].signs == L.jobs[i].signs &&
+                            Q.jobs[k].had_block == L.jobs[i].had_block && Q.jobs[k].K == w[i]->K))
+      ++k;
+    if (k == Q.njobs) {
+      QuantJob& J = Q.jobs[Q.njobs++];
+      J.x = x[i];
+      J.signs = L.jobs[i].signs;
+      J.x_rot = nullptr;
+      J.K = w[i]->K;
+      J.had_block = L.jobs[i].had_block;
+      J.had_scale = L.jobs[i].had_scale;
+      qoff[k] = qtot;
+      soff[k] = stot;
+      qtot += ((size_t)B * w[i]->K + 15) / 16 * 16;
+      stot += (size_t)B;
+    }
+    set_of[i] = k;
+  }
+  ouroq_status st = grow(ctx, ctx->q_scratch, ctx->q_cap, qtot, "q scratch");
+  if (st != OUROQ_OK) return st;
+  st = grow(ctx, ctx->s_scratch, ctx->s_cap, stot, "s scratch");
+  if (st != OUROQ_OK) return st;
+  for (int k = 0; k < Q.njobs; ++k) {
+    Q.jobs[k].q = ctx->q_scratch + qoff[k];
+    Q.jobs[k].s_x = ctx->s_scratch + soff[k];
+  }
+  CU(ctx, launch_quantize(Q, s, ctx->pdl), "quantize launch");
+  ctx->launches++;
+  L.fused = 0;
+  for (int i = 0; i < n; ++i) {
+    L.jobs[i].q = Q.jobs[set_of[i]].q;
+    L.jobs[i].s_x = Q.jobs[set_of[i]].s_x;
+    L.jobs[i].xf = nullptr;
+  }
+  return run_gemv(ctx, L, s);
 }
 
 ouroq_status ouroq_gemm_f32act(ouroq_ctx* ctx, const ouroq_weight* w, const float* x, int B,
@@ -871,7 +916,7 @@ ouroq_status ouroq_gemm_f32act(ouroq_ctx* ctx, const ouroq_weight* w, const floa
     return ref_matvec(ctx, w, xin, B, y, s);
   }
   const int dfmt = w->fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
-  if (B <= kGemvMaxB && (hadamard_block == 0 || (hadamard_block >= 32 && hadamard_block <= 128))) {
+  if (B <= kFusedMaxB && (hadamard_block == 0 || (hadamard_block >= 32 && hadamard_block <= 128))) {
     // one launch: rotate + quantise in the GEMV prologue
     GemvLaunch L{};
     L.njobs = 1;

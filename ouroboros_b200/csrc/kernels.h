@@ -149,6 +149,9 @@ cudaError_t launch_refmt_matvec(const RefLaunch& P, cudaStream_t s);
 
 // Limits of the small-batch GEMV path.
 constexpr int kGemvMaxB = 8;
+// Above this batch the fp32-activation entry points quantise once in a separate
+// launch instead of in every GEMV CTA's prologue (which repeats it per CTA).
+constexpr int kFusedMaxB = 2;
 constexpr size_t kGemvMaxXBytes = 64 * 1024;  // B*K int8 resident in shared memory
 
 // Row-sharded matmul, peer-store transport. Each rank's landing buffer (one

@@ -29,14 +29,18 @@
 namespace ouroq {
 namespace {
 
-__device__ __forceinline__ int ptq1_digit(uint32_t byte, uint32_t pow3) {
-  const uint32_t q = (byte * pow3) & 0xFFu;
-  return (int)((q * 3u) >> 8);
+// Next digit of a byte: with q = byte * 3^n mod 256 in *q, returns digit n
+// ((q * 3) >> 8) and leaves byte * 3^(n+1) mod 256 in *q.
+__device__ __forceinline__ uint32_t next_digit(uint32_t* q) {
+  const uint32_t q3 = *q * 3u;
+  *q = q3 & 0xFFu;
+  return q3 >> 8;
 }
 
-// ((float)t * d) * x, t = digit - 1
-__device__ __forceinline__ float term(uint32_t byte, uint32_t pow3, float d, float x) {
-  const float t = (float)(ptq1_digit(byte, pow3) - 1);
+// ((float)(digit - 1) * d) * x, exactly as the reference rounds it (the digit
+// is 0, 1 or 2, so the trit is selected rather than converted).
+__device__ __forceinline__ float term(uint32_t digit, float d, float x) {
+  const float t = digit == 0u ? -1.0f : (digit == 1u ? 0.0f : 1.0f);
   return __fmul_rn(__fmul_rn(t, d), x);
 }
 
@@ -44,7 +48,7 @@ constexpr int kTl1Threads = 256;
 constexpr int kTl1XStride = 129;  // padded group stride of x in shared memory (bank spread)
 
 // grid (row blocks, tokens). R rows per CTA; work item = (row, group).
-__global__ void __launch_bounds__(kTl1Threads) tl1_matvec_kernel(const __grid_constant__ RefLaunch P,
+__global__ void __launch_bounds__(kTl1Threads, 2) tl1_matvec_kernel(const __grid_constant__ RefLaunch P,
                                                                 int R) {
   extern __shared__ float sm[];
   const int G = P.K / 128;
@@ -55,36 +59,50 @@ __global__ void __launch_bounds__(kTl1Threads) tl1_matvec_kernel(const __grid_co
   const float* x = P.x + (size_t)b * P.K;
   for (int i = threadIdx.x; i < P.K; i += blockDim.x) xs[(i >> 7) * kTl1XStride + (i & 127)] = x[i];
   __syncthreads();
-  const uint32_t pw[5] = {1u, 3u, 9u, 27u, 81u};
+  // the next work item's 28 bytes are fetched while the current one is decoded
+  uint32_t nwd[7];
+  auto fetch = [&](int p, uint32_t* out) {
+    const int r = p / G, g = p - (p / G) * G;
+    const int row = row0 + r < P.M ? row0 + r : P.M - 1;
+    const uint32_t* gw = reinterpret_cast<const uint32_t*>(P.w + ((size_t)row * G + g) * 28);
+#pragma unroll
+    for (int i = 0; i < 7; ++i) out[i] = __ldg(gw + i);
+  };
+  if (threadIdx.x < R * G) fetch(threadIdx.x, nwd);
   for (int p = threadIdx.x; p < R * G; p += blockDim.x) {
     const int r = p / G, g = p - (p / G) * G;
     const int row = row0 + r;
-    if (row >= P.M) continue;
-    const uint32_t* gw = reinterpret_cast<const uint32_t*>(P.w + ((size_t)row * G + g) * 28);
     uint32_t wd[7];
 #pragma unroll
-    for (int i = 0; i < 7; ++i) wd[i] = __ldg(gw + i);
+    for (int i = 0; i < 7; ++i) wd[i] = nwd[i];
+    if (p + (int)blockDim.x < R * G) fetch(p + blockDim.x, nwd);
+    if (row >= P.M) continue;
     const float d = __half2float(__ushort_as_half((unsigned short)(wd[6] >> 16)));
     const float* xg = xs + g * kTl1XStride;
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    uint32_t q[24];  // byte * 3^n mod 256 of qs[0..24], advanced one digit per n
 #pragma unroll
+    for (int i = 0; i < 24; ++i) q[i] = (wd[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+#pragma unroll 1
     for (int n = 0; n < 5; ++n) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int sh = 8 * j;
-        acc[j] = __fadd_rn(term((wd[0] >> sh) & 0xFFu, pw[n], d, xg[n * 16 + j]), acc[j]);
-        acc[j] = __fadd_rn(term((wd[1] >> sh) & 0xFFu, pw[n], d, xg[n * 16 + 4 + j]), acc[j]);
-        acc[j] = __fadd_rn(term((wd[2] >> sh) & 0xFFu, pw[n], d, xg[n * 16 + 8 + j]), acc[j]);
-        acc[j] = __fadd_rn(term((wd[3] >> sh) & 0xFFu, pw[n], d, xg[n * 16 + 12 + j]), acc[j]);
-        acc[j] = __fadd_rn(term((wd[4] >> sh) & 0xFFu, pw[n], d, xg[80 + n * 8 + j]), acc[j]);
-        acc[j] = __fadd_rn(term((wd[5] >> sh) & 0xFFu, pw[n], d, xg[80 + n * 8 + 4 + j]), acc[j]);
+        // lane j: bytes j, 4+j, 8+j, 12+j, 16+j, 20+j (three digits8 calls of ops.rs:553-557)
+        acc[j] = __fadd_rn(term(next_digit(&q[j]), d, xg[n * 16 + j]), acc[j]);
+        acc[j] = __fadd_rn(term(next_digit(&q[4 + j]), d, xg[n * 16 + 4 + j]), acc[j]);
+        acc[j] = __fadd_rn(term(next_digit(&q[8 + j]), d, xg[n * 16 + 8 + j]), acc[j]);
+        acc[j] = __fadd_rn(term(next_digit(&q[12 + j]), d, xg[n * 16 + 12 + j]), acc[j]);
+        acc[j] = __fadd_rn(term(next_digit(&q[16 + j]), d, xg[80 + n * 8 + j]), acc[j]);
+        acc[j] = __fadd_rn(term(next_digit(&q[20 + j]), d, xg[80 + n * 8 + 4 + j]), acc[j]);
       }
     }
     float* out = part + (size_t)p * 9;
+    uint32_t qh[2] = {wd[6] & 0xFFu, (wd[6] >> 8) & 0xFFu};
 #pragma unroll
     for (int n = 0; n < 4; ++n)
 #pragma unroll
-      for (int m = 0; m < 2; ++m) out[n * 2 + m] = term((wd[6] >> (8 * m)) & 0xFFu, pw[n], d, xg[120 + n * 2 + m]);
+      for (int m = 0; m < 2; ++m)
+        out[n * 2 + m] = term(next_digit(&qh[m]), d, xg[120 + n * 2 + m]);
     out[8] = __fadd_rn(__fadd_rn(acc[0], acc[2]), __fadd_rn(acc[1], acc[3]));
   }
   __syncthreads();
@@ -102,67 +120,101 @@ __global__ void __launch_bounds__(kTl1Threads) tl1_matvec_kernel(const __grid_co
   }
 }
 
-// TQ1_0: a team of 8 lanes per row. Per 256-element block the team decodes
-// the weights times x into shared memory (element order), then the team's
-// first lane adds them up in order -- the running sum is the only serial part.
-constexpr int kTq1Threads = 256;
-constexpr int kTq1Rows = kTq1Threads / 8;   // 32 rows per CTA
-constexpr int kTq1ProdStride = 257;         // padded row stride of the product buffer
+// TQ1_0: 32 rows per CTA, four warps. Warps 1-3 decode the weights of a
+// 256-element block times x into a double-buffered product tile [32 rows][256];
+// warp 0 (lane = row) adds each row's products in element order -- the one
+// serial chain of the reference's dot. Named barriers hand the buffers over.
+constexpr int kTq1Warps = 4;
+constexpr int kTq1Threads = kTq1Warps * 32;
+constexpr int kTq1Rows = 32;
+constexpr int kTq1ProdStride = 257;  // padded row stride: lanes of a warp hit distinct banks
 
-__device__ __forceinline__ int tq1_byte_of(int e, int* n) {
-  if (e < 160) {
-    *n = e >> 5;
-    return e & 31;
-  }
-  if (e < 240) {
-    const int f = e - 160;
-    *n = f >> 4;
-    return 32 + (f & 15);
-  }
-  const int f = e - 240;
-  *n = f >> 2;
-  return 48 + (f & 3);
+__device__ __forceinline__ void bar_sync(unsigned id, unsigned n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(unsigned id, unsigned n) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// element index of digit n of code byte m in a TQ1_0 block (dequant.rs:61-79)
+__device__ __forceinline__ int tq1_elem(int m, int n) {
+  return m < 32 ? n * 32 + m : (m < 48 ? 160 + n * 16 + (m - 32) : 240 + n * 4 + (m - 48));
 }
 
 __global__ void __launch_bounds__(kTq1Threads) tq1_matvec_kernel(const __grid_constant__ RefLaunch P) {
   extern __shared__ float sm[];
-  float* xs = sm;                                   // [K]
-  float* prod = sm + P.K;                           // [32 rows][257]
+  float* xs = sm;                  // [K]
+  float* prod = sm + P.K;          // [2][32][257]
   const int b = blockIdx.y;
   const float* x = P.x + (size_t)b * P.K;
   for (int i = threadIdx.x; i < P.K; i += blockDim.x) xs[i] = x[i];
   __syncthreads();
-  const int team = threadIdx.x >> 3, k = threadIdx.x & 7;
-  const int row = blockIdx.x * kTq1Rows + team;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kTq1Rows + lane;
   const bool live = row < P.M;
   const int nblk = P.K / 256;
-  const size_t rb = (size_t)nblk * 54;
-  const uint8_t* wr = P.w + (size_t)(live ? row : 0) * rb;
-  float* pr = prod + team * kTq1ProdStride;
-  const uint32_t pw[5] = {1u, 3u, 9u, 27u, 81u};
-  // the 8 lanes of a team sit in one warp: team lanes = 8 consecutive lanes
-  const unsigned team_mask = 0xFFu << ((threadIdx.x & 31) & ~7);
-  float sum = 0.0f;
-  for (int blk = 0; blk < nblk; ++blk) {
-    const uint8_t* bb = wr + (size_t)blk * 54;
-    if (live) {
-      const float d =
-          __half2float(__ushort_as_half((unsigned short)(bb[52] | ((unsigned)bb[53] << 8))));
-      const float* xb = xs + blk * 256;
-      for (int e = k; e < 256; e += 8) {
-        int n;
-        const int byte_idx = tq1_byte_of(e, &n);
-        const float w = __fmul_rn(__fsub_rn((float)ptq1_digit(bb[byte_idx], pw[n]), 1.0f), d);
-        pr[e] = __fmul_rn(w, xb[e]);
+  const uint8_t* wr = P.w + (size_t)(live ? row : 0) * ((size_t)nblk * 54);
+  // barrier ids: 1 + buf = "products of buf ready", 3 + buf = "buf free"
+  if (warp == 0) {
+    float sum = 0.0f;
+    for (int blk = 0; blk < nblk; ++blk) {
+      const int buf = blk & 1;
+      bar_sync(1 + buf, kTq1Threads);
+      const float* src = prod + (size_t)buf * kTq1Rows * kTq1ProdStride + lane * kTq1ProdStride;
+      for (int e = 0; e < 256; e += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = src[e + j];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sum = __fadd_rn(sum, v[j]);
       }
+      if (blk + 2 < nblk) bar_arrive(3 + buf, kTq1Threads);  // the decoders refill buf
     }
-    __syncwarp(team_mask);
-    if (k == 0 && live) {
-      for (int e = 0; e < 256; ++e) sum = __fadd_rn(sum, pr[e]);
+    if (live) P.y[(size_t)b * P.ldy + row] = sum;
+  } else {
+    const int dw = warp - 1;  // decode warp 0..2: code bytes m = dw, dw + 3, ...
+    constexpr int kSlots = (52 + kTq1Warps - 2) / (kTq1Warps - 1);  // 18 bytes per lane per block
+    // this lane's code bytes and scale of a block, all loads issued together;
+    // the next block's are fetched while the current one is decoded
+    auto fetch = [&](int blk, uint32_t* by, float* d) {
+      const uint8_t* bb = wr + (size_t)blk * 54;
+#pragma unroll
+      for (int i = 0; i < kSlots; ++i) {
+        const int m = dw + (kTq1Warps - 1) * i;
+        by[i] = m < 52 ? (uint32_t)__ldg(bb + m) : 0u;
+      }
+      *d = __half2float(__ushort_as_half((unsigned short)(__ldg(bb + 52) | ((unsigned)__ldg(bb + 53) << 8))));
+    };
+    uint32_t cur[kSlots], nxt[kSlots];
+    float dcur = 0.0f, dnxt = 0.0f;
+    fetch(0, cur, &dcur);
+    for (int blk = 0; blk < nblk; ++blk) {
+      const int buf = blk & 1;
+      if (blk + 1 < nblk) fetch(blk + 1, nxt, &dnxt);
+      if (blk >= 2) bar_sync(3 + buf, kTq1Threads);
+      float* dst = prod + (size_t)buf * kTq1Rows * kTq1ProdStride + lane * kTq1ProdStride;
+      const float* xb = xs + blk * 256;
+#pragma unroll
+      for (int i = 0; i < kSlots; ++i) {
+        const int m = dw + (kTq1Warps - 1) * i;
+        if (m >= 52) continue;
+        uint32_t q = cur[i];
+        const int nd = m < 48 ? 5 : 4;
+        for (int n = 0; n < nd; ++n) {
+          const uint32_t q3 = q * 3u;
+          q = q3 & 0xFFu;
+          const int e = tq1_elem(m, n);
+          // w = ((float)digit - 1) * d, then w * x (the dot's product)
+          const float w = __fmul_rn((float)(q3 >> 8) - 1.0f, dcur);
+          dst[e] = __fmul_rn(w, xb[e]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kSlots; ++i) cur[i] = nxt[i];
+      dcur = dnxt;
+      bar_arrive(1 + buf, kTq1Threads);
     }
-    __syncwarp(team_mask);
   }
-  if (k == 0 && live) P.y[(size_t)b * P.ldy + row] = sum;
 }
 
 }  // namespace
@@ -178,7 +230,9 @@ int tl1_rows_per_cta(int K) {
   return R < 1 ? 1 : R;
 }
 
-size_t tq1_smem_bytes(int K) { return ((size_t)K + (size_t)kTq1Rows * kTq1ProdStride) * sizeof(float); }
+size_t tq1_smem_bytes(int K) {
+  return ((size_t)K + 2 * (size_t)kTq1Rows * kTq1ProdStride) * sizeof(float);
+}
 
 cudaError_t launch_refmt_matvec(const RefLaunch& P, cudaStream_t s) {
   if (P.M <= 0 || P.B <= 0) return cudaSuccess;

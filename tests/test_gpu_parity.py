@@ -223,12 +223,14 @@ def test_gemm_group_c2_layer(ctx, oracle):
         w.free()
 
 
-@pytest.mark.parametrize("B", [1, 2])
+@pytest.mark.parametrize("B", [1, 2, 4, 8])
 def test_gemm_group_f32act_c2_layer(ctx, oracle, B):
-    # one fused launch: fp32 activations quantised in the GEMV prologue
+    # B <= 2: one fused launch (fp32 activations quantised in the GEMV prologue);
+    # larger B: each distinct input quantised once, then the grouped GEMV
     import torch
     shapes = [(3840, 2560), (2560, 2560), (6912, 2560), (6912, 2560), (2560, 6912)]
     inputs = [oracle.normals(400 + i, B * k).reshape(B, k) for i, k in enumerate([2560, 2560, 2560, 6912])]
+    dev_inputs = [dev(x) for x in inputs]  # gate and up share one input buffer
     input_of = [0, 1, 2, 2, 3]
     ws_, xs, ys, want = [], [], [], []
     for i, (M, K) in enumerate(shapes):
@@ -237,7 +239,7 @@ def test_gemm_group_f32act_c2_layer(ctx, oracle, B):
         qr, sr = oracle.quantize_act(x)
         want.append(oracle.gemm_tern2(packed, M, K, wsc, qr, sr)[1])
         ws_.append(ctx.upload(oq.TERNARY2, packed, M, K, w_scale=wsc))
-        xs.append(dev(x))
+        xs.append(dev_inputs[input_of[i]])
         ys.append(torch.empty((B, M), dtype=torch.float32, device="cuda"))
     ctx.gemm_group_f32act(ws_, xs, ys)
     for y, yr in zip(ys, want):
