@@ -305,12 +305,12 @@ ouroq_status ref_matvec(ouroq_ctx* ctx, const ouroq_weight* w, const float* x, i
   P.K = w->K;
   P.B = B;
   P.ldy = w->M;
-  const size_t smem = P.fmt == kPtq1 ? tl1_smem_bytes(w->K, tl1_rows_per_cta(w->K))
+  const size_t smem = P.fmt == kPtq1 ? tl1_smem_bytes(w->K, tl1_rows_per_cta(w->K, w->M, ctx->num_sms))
                                      : tq1_smem_bytes(w->K);
   if (smem > (size_t)ctx->smem_optin)
     return fail(ctx, OUROQ_ERR_UNSUPPORTED, "K=%d too wide for the reference-format kernels", w->K);
   if ((size_t)B > 65535) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d (max 65535)", B);
-  CU(ctx, launch_refmt_matvec(P, s), "reference-format matvec launch");
+  CU(ctx, launch_refmt_matvec(P, ctx->num_sms, s), "reference-format matvec launch");
   ctx->launches++;
   return OUROQ_OK;
 }

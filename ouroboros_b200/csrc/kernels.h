@@ -143,9 +143,9 @@ struct RefLaunch {
   int M, K, B, ldy;
 };
 size_t tl1_smem_bytes(int K, int R);
-int tl1_rows_per_cta(int K);
+int tl1_rows_per_cta(int K, int M, int num_sms);
 size_t tq1_smem_bytes(int K);
-cudaError_t launch_refmt_matvec(const RefLaunch& P, cudaStream_t s);
+cudaError_t launch_refmt_matvec(const RefLaunch& P, int num_sms, cudaStream_t s);
 
 // Limits of the small-batch GEMV path.
 constexpr int kGemvMaxB = 8;

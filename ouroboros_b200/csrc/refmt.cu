@@ -224,20 +224,24 @@ size_t tl1_smem_bytes(int K, int R) {
   return ((size_t)G * kTl1XStride + (size_t)R * G * 9) * sizeof(float);
 }
 
-int tl1_rows_per_cta(int K) {
+int tl1_rows_per_cta(int K, int M, int num_sms) {
+  // at most ~1024 (row, group) items per CTA, and at least two CTAs per SM
   const int G = K / 128;
-  int R = 1024 / G;
-  return R < 1 ? 1 : R;
+  int cap = 1024 / G;
+  if (cap < 1) cap = 1;
+  int R = (M + 2 * num_sms - 1) / (2 * num_sms);
+  if (R < 1) R = 1;
+  return R < cap ? R : cap;
 }
 
 size_t tq1_smem_bytes(int K) {
   return ((size_t)K + 2 * (size_t)kTq1Rows * kTq1ProdStride) * sizeof(float);
 }
 
-cudaError_t launch_refmt_matvec(const RefLaunch& P, cudaStream_t s) {
+cudaError_t launch_refmt_matvec(const RefLaunch& P, int num_sms, cudaStream_t s) {
   if (P.M <= 0 || P.B <= 0) return cudaSuccess;
   if (P.fmt == kPtq1) {
-    const int R = tl1_rows_per_cta(P.K);
+    const int R = tl1_rows_per_cta(P.K, P.M, num_sms);
     const size_t smem = tl1_smem_bytes(P.K, R);
     cudaError_t e = ensure_max_smem<tl1_matvec_kernel>();
     if (e != cudaSuccess) return e;
