@@ -222,6 +222,31 @@ ouroq_status ouroq_gemm_sharded(ouroq_ctx *ctx, const ouroq_weight *w_shard, con
  * calls return OUROQ_ERR_NCCL and finalize aborts the communicator. */
 ouroq_status ouroq_shard_sync(ouroq_ctx *ctx, void *stream, int timeout_ms);
 
+/* ---- BMTS v1 shard files (cluster/src/bmts.rs:1-14, 171-209) ----
+ * BmtsShard::open: the file is memory-mapped and its header and JSON tensor
+ * table parsed; version 2 (Cap'n Proto meta) is refused. Spans are views into
+ * the mapping, valid until ouroq_bmts_close. `err` (nullable, err_len bytes)
+ * receives the reason of a failure. */
+typedef struct ouroq_bmts ouroq_bmts;
+ouroq_status ouroq_bmts_open(const char *path, ouroq_bmts **out, char *err, size_t err_len);
+ouroq_status ouroq_bmts_close(ouroq_bmts *f);
+/* node, tensor count, data-section file offset, sum of declared tensor lengths (data_len) */
+ouroq_status ouroq_bmts_info(const ouroq_bmts *f, int *node, int *n_tensors, uint64_t *data_start,
+                             uint64_t *data_len);
+/* Entry i of the tensor table; shape4 receives up to four dimensions. */
+ouroq_status ouroq_bmts_tensor(const ouroq_bmts *f, int i, const char **name, int *rank,
+                               uint64_t *shape4, uint32_t *dtype, uint64_t *offset,
+                               uint64_t *length);
+/* read_span (bmts.rs:286-309): bytes [offset, offset + length) of tensor
+ * `name`; a span past the tensor's declared length is refused, never cut. */
+ouroq_status ouroq_bmts_span(const ouroq_bmts *f, const char *name, uint64_t offset,
+                             uint64_t length, const void **out, char *err, size_t err_len);
+/* Stage::from_shard for one tensor (infer/mod.rs:110-123) plus the device
+ * upload: dtype 143 (Tl1) -> OUROQ_FMT_PTQ1_0, 34 (TQ1_0) -> OUROQ_FMT_TQ1_0,
+ * GGUF shape [in, out] -> K = shape[0], M = shape[1]. */
+ouroq_status ouroq_bmts_upload(ouroq_ctx *ctx, const ouroq_bmts *f, const char *name,
+                               ouroq_weight **out, char *err, size_t err_len);
+
 /* ---- host-buffer mirrors of the reference operators (synchronous) ---- */
 
 /* ops::matvec_q (ops.rs:76-84): x_host [K] fp32 -> y_host [M] fp32. */

@@ -79,6 +79,16 @@ ABI_FUNCTIONS = {
     "ouroq_weight_upload_shard": (_i, [_p, _i, _p, _i, _i, _p, _f, ctypes.POINTER(_p)]),
     "ouroq_gemm_sharded": (_i, [_p, _p, _p, _i, _p, _i, _p, _p]),
     "ouroq_shard_sync": (_i, [_p, _p, _i]),
+    "ouroq_bmts_open": (_i, [ctypes.c_char_p, ctypes.POINTER(_p), ctypes.c_char_p, _sz]),
+    "ouroq_bmts_close": (_i, [_p]),
+    "ouroq_bmts_info": (_i, [_p, ctypes.POINTER(_i), ctypes.POINTER(_i),
+                             ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
+    "ouroq_bmts_tensor": (_i, [_p, _i, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_i),
+                               ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint32),
+                               ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
+    "ouroq_bmts_span": (_i, [_p, ctypes.c_char_p, ctypes.c_uint64, ctypes.c_uint64,
+                             ctypes.POINTER(_p), ctypes.c_char_p, _sz]),
+    "ouroq_bmts_upload": (_i, [_p, _p, ctypes.c_char_p, ctypes.POINTER(_p), ctypes.c_char_p, _sz]),
     "ouroq_matvec_q": (_i, [_p, _p, _p, _p]),
     "ouroq_matmul_q": (_i, [_p, _p, _p, _i, _p]),
     "ouroq_rotate_fwd": (_i, [_p, _p, _p, _sz, _sz]),

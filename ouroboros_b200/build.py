@@ -25,7 +25,7 @@ NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompil
               "-Xptxas", "-warn-spills", "--threads", "0", "-I", str(ROOT / "include"),
               "-I", str(CSRC)]
 CU_SOURCES = ["quant.cu", "gemv.cu", "repack.cu", "gemm_tc.cu", "noalloc.cu", "shard.cu", "refmt.cu"]
-CPP_SOURCES = ["api.cpp"]
+CPP_SOURCES = ["api.cpp", "bmts.cpp"]
 
 
 def nvcc() -> str:
