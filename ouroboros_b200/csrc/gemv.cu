@@ -14,7 +14,7 @@
 //    contiguous range of tiles; the host balances the ranges by weight bytes.
 //  * Weights stream HBM -> shared memory through a ring of up to 13 stages
 //    tracked by mbarriers, one 1-D bulk copy per stage (a K-slice of a 32-row
-//    tile is contiguous in the tiled device layout: 8-16 KB per copy; small
+//    tile is contiguous in the tiled device layout: 8-32 KB per copy; small
 //    copies are limited by the copy engine's op rate, large ones run at HBM
 //    speed). A producer warp issues them and never waits for the previous
 //    grid: weights do not depend on it.
@@ -57,7 +57,7 @@ constexpr int kCWarps = 15;
 constexpr int kCThreads = kCWarps * 32;
 constexpr int kThreads = kCThreads + 32;
 constexpr int kMaxStages = kMaxGemvStages;
-constexpr int kTernSliceChunks = 32;  // 16-B chunks per row per stage (16 KB stage)
+constexpr int kTernSliceChunks = 64;  // 16-B chunks per row per stage (32 KB stage)
 constexpr int kSignSliceChunks = 16;  // 16 groups per row per stage (8 KB + 1 KB scales)
 
 // Stage layout: weights [chunk][32 rows][16 B]; sign stages append the fp16
@@ -86,7 +86,7 @@ __host__ __device__ constexpr uint32_t align128(uint32_t v) { return (v + 127u) 
 //   xwork       xcap bytes: int8 activations [job][B][K] of the CTA's jobs
 //   qg          gcap ints: per-(token, 128-group) activation sums
 //   sx / qtot   [8 jobs][8 tokens] per-token scales / sums
-//   red         ternary: kCWarps*B*32 ints; sign: B*slice*32 floats
+//   red         ternary: 2 x kCWarps*B*32 ints; sign: B*slice*32 floats
 struct Plan {
   uint32_t bars, ring, xwork, qg, sx, qtot, red, total;
 };
@@ -103,7 +103,8 @@ __host__ __device__ inline Plan make_plan(int fmt, int B, int stages, int xcap, 
   p.sx = p.qg + align128((uint32_t)gcap * 4u);
   p.qtot = p.sx + 256;
   p.red = p.qtot + 256;
-  const uint32_t red_bytes = fmt == kTern2 ? kCWarps * b * 32u * 4u : b * slice * 32u * 4u;
+  // ternary: two buffers of per-warp partials (one barrier per tile)
+  const uint32_t red_bytes = fmt == kTern2 ? 2u * kCWarps * b * 32u * 4u : b * slice * 32u * 4u;
   p.total = p.red + align128(red_bytes);
   return p;
 }
@@ -465,16 +466,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   }
   named_bar_sync(1, kCThreads);
   if (FMT == kTern2) {
-    // per-token sums of each job
-    int goff = 0;
-    for (int jj = j_lo; jj <= j_hi; ++jj) {
-      const int G = L.jobs[jj].K / 128;
-      if (ctid < B) {
-        int s = 0;
-        for (int g = 0; g < G; ++g) s += qg_base[goff + ctid * G + g];
-        qtot_s[(jj - j_lo) * 8 + ctid] = s;
-      }
-      goff += B * G;
+    // per-token sums of each job: one warp per (job, token), lanes over groups
+    const int npairs = (j_hi - j_lo + 1) * B;
+    for (int pr = warp; pr < npairs; pr += kCWarps) {
+      const int jl = pr / B, b = pr - (pr / B) * B;
+      int goff = 0;
+      for (int jj = j_lo; jj < j_lo + jl; ++jj) goff += B * (L.jobs[jj].K / 128);
+      const int G = L.jobs[j_lo + jl].K / 128;
+      int s = 0;
+      for (int g = lane; g < G; g += 32) s += qg_base[goff + b * G + g];
+      s = warp_sum(s);
+      if (lane == 0) qtot_s[jl * 8 + b] = s;
     }
     named_bar_sync(1, kCThreads);
   }
@@ -482,6 +484,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   int* red = reinterpret_cast<int*>(smem + P.red);
   float* terms = reinterpret_cast<float*>(smem + P.red);
   int st = 0;
+  int first = warp;  // chunk rotation: chunk kc of stage st belongs to warp (kc + st) % kCWarps
+  int tpar = 0;      // parity of the ternary partial-sum buffer
   RingPos rp;
   bool ok = true;
   int cur_job = -1, xoff = 0, goff = 0;
@@ -515,17 +519,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
 #pragma unroll
         for (int j = 0; j < 4; ++j) A[b][j] = 0;
 
+      const int C = chunks_of<FMT>(K);
+      const int per = (C + ns - 1) / ns;  // slice_range's split, computed once per tile
       for (int s = 0; s < ns; ++s, ++st) {
         const int slot = rp.slot;
         if (ok) ok = mbar_wait(&full[slot], rp.round & 1, L.status);
         rp.next(NS);
-        int c0, c1;
-        slice_range<FMT>(K, s, ns, c0, c1);
+        const int c0 = s * per;
+        const int c1 = c0 + per < C ? c0 + per : C;
         const uint8_t* stg = ring + (size_t)slot * STAGE + lane * 16;
         const int nck = c1 - c0;
         // chunk kc belongs to warp (kc + st) % kCWarps: the remainder chunks of
         // a stage land on different warps from stage to stage
-        const int first = ((warp - st) % kCWarps + kCWarps) % kCWarps;
         const int8_t* xrow = xs + (size_t)c0 * 64;
         for (int kc = first; kc < nck; kc += 2 * kCWarps) {
           // two chunks per iteration: every shared load is issued before the math
@@ -556,23 +561,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
+        first = first == 0 ? kCWarps - 1 : first - 1;
       }
-      // cross-warp reduction of the exact per-warp partials
+      // cross-warp reduction of the exact per-warp partials. Two buffers: a
+      // buffer is rewritten two tiles later, after every warp has passed the
+      // next tile's barrier, so its readers are done -- one barrier per tile.
+      int* rb = red + tpar * (kCWarps * B * 32);
+      tpar ^= 1;
 #pragma unroll
       for (int b = 0; b < B; ++b)
-        red[(warp * B + b) * 32 + lane] = A[b][0] + (A[b][1] >> 2) + (A[b][2] >> 4) + (A[b][3] >> 6);
+        rb[(warp * B + b) * 32 + lane] = A[b][0] + (A[b][1] >> 2) + (A[b][2] >> 4) + (A[b][3] >> 6);
       named_bar_sync(2, kCThreads);
       for (int b = warp; b < B; b += kCWarps) {
         int acc = -qtot[b];
 #pragma unroll
-        for (int w = 0; w < kCWarps; ++w) acc += red[(w * B + b) * 32 + lane];
+        for (int w = 0; w < kCWarps; ++w) acc += rb[(w * B + b) * 32 + lane];
         if (row_ok) {
           const float y = __fmul_rn(__fmul_rn(__int2float_rn(acc), J.w_scale), sx[b]);
           J.y[(size_t)b * J.ldy + row] = y;
           if (J.acc) J.acc[(size_t)b * J.M + row] = acc;
         }
       }
-      named_bar_sync(2, kCThreads);
     } else {
       float sum[B];
 #pragma unroll
@@ -584,8 +593,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         int c0, c1;
         slice_range<FMT>(K, s, ns, c0, c1);
         const uint8_t* stg = ring + (size_t)slot * STAGE;
-        const int first = ((warp - st) % kCWarps + kCWarps) % kCWarps;
-        for (int kc = first; kc < c1 - c0; kc += kCWarps) {
+        const int sfirst = ((warp - st) % kCWarps + kCWarps) % kCWarps;
+        for (int kc = sfirst; kc < c1 - c0; kc += kCWarps) {
           const uint4 wv = *reinterpret_cast<const uint4*>(stg + kc * 512 + lane * 16);
           const uint32_t wl[4] = {wv.x, wv.y, wv.z, wv.w};
           const int g = c0 + kc;
