@@ -70,6 +70,9 @@ WORKLOADS = {
                    ("ffn_gate", FFN, HIDDEN, 2), ("ffn_up", FFN, HIDDEN, 2),
                    ("ffn_down", HIDDEN, 6912, 3)],
                   [HIDDEN, HIDDEN, HIDDEN, FFN], 0),
+    # the whole BitNet-2B decode step (configuration 4): 30 layers, KV context
+    # 1024, lm_head, greedy sampling; metric: decode tokens/s
+    "decode": ("bitnet2b-decode", TERN, [], [], 0),
     "layer-tl1": ("bitnet2b-layer-projections-ptq1_0", TL1,
                   [("attn_qkv", 3840, HIDDEN, 0), ("attn_output", HIDDEN, HIDDEN, 1),
                    ("ffn_gate", FFN, HIDDEN, 2), ("ffn_up", FFN, HIDDEN, 2),
@@ -93,6 +96,8 @@ def parse():
                     help="row-shard each matrix over the ranks; single-matrix workloads only")
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="how --shard moves rows between ranks")
+    ap.add_argument("--tokens", type=int, default=256,
+                    help="decode workload: tokens generated per sequence in the timed region")
     return ap.parse_args()
 
 
@@ -301,6 +306,23 @@ def run_reference(args, rank):
     if rank != 0:
         return
     from oracle import pyoracle as O
+    if args.workload == "decode":
+        threads = O.hw_threads()
+        v, n, dt = cpu_decode_tokens_per_s(args.batch, 20.0, threads)
+        line = {"impl": "reference", "metric": "decode tokens/s", "value": round(v, 3),
+                "unit": "tokens/s", "n_gpus": args.gpus, "steps": n, "warmup": 0,
+                "ms_per_step": round(1e3 * args.batch / v, 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+                "config": {"workload": f"bitnet2b-decode-b{args.batch}-ctx1024-gen256",
+                           "batch": args.batch, "host_cpu": True},
+                "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": threads,
+                                 "kind": "port",
+                                 "sample": f"{n} single-layer passes scaled to 30 layers plus "
+                                           f"the lm_head, {threads} threads"},
+                "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     wl = WORKLOADS[args.workload]
     B = args.batch
     threads = O.hw_threads()
@@ -547,6 +569,177 @@ def run_ouroq(args, rank, world, local_rank):
     ctx.close()
 
 
+def cpu_decode_tokens_per_s(B: int, seconds: float, threads: int):
+    """The same decode step on the host cores, bounded: one layer's seven
+    ternary projections with the oracle's threaded int8 quantise + GEMV, its
+    norms and attention over the 1024-token context in numpy, scaled to 30
+    layers, plus one lm_head product (f16 weights as fp32)."""
+    from oracle import pyoracle as O
+    rng = np.random.default_rng(5)
+    shapes = [(2560, 2560), (640, 2560), (640, 2560), (2560, 2560), (6912, 2560), (6912, 2560),
+              (2560, 6912)]
+    mats = []
+    for i, (M, K) in enumerate(shapes):
+        w = O.ternary(900 + i, M * K).reshape(M, K)
+        mats.append((O.pack_tern2(w), M, K, float(O.absmean_scale(w, 0.02))))
+    kc = rng.standard_normal((B, 5, 1024, 128), dtype=np.float32)
+    vc = rng.standard_normal((B, 5, 1024, 128), dtype=np.float32)
+    emb = (0.02 * rng.standard_normal((128256, 2560))).astype(np.float16)
+    x = rng.standard_normal((B, 2560), dtype=np.float32)
+
+    kv_head = np.arange(20) // 4  # GQA: query head h reads KV head h // 4
+
+    def rms(v):
+        return (v / np.sqrt((v * v).mean(-1, keepdims=True) + 1e-5)).astype(np.float32)
+
+    def layer():
+        q, s = O.quantize_act(rms(x))
+        qkv = [O.gemm_tern2_mt(p, M, K, ws, q, s, threads) for p, M, K, ws in mats[:3]]
+        qh = qkv[0].reshape(B, 20, 128)
+        att = np.einsum("bhd,bhtd->bht", qh, kc[:, kv_head]) / np.sqrt(128.0)
+        pr = np.exp(att - att.max(-1, keepdims=True))
+        pr /= pr.sum(-1, keepdims=True)
+        o = np.einsum("bht,bhtd->bhd", pr, vc[:, kv_head]).reshape(B, 2560)
+        q2, s2 = O.quantize_act(rms(o))
+        h1 = x + O.gemm_tern2_mt(mats[3][0], 2560, 2560, mats[3][3], q2, s2, threads)
+        q3, s3 = O.quantize_act(rms(h1))
+        g_, u_ = [O.gemm_tern2_mt(p, M, K, ws, q3, s3, threads) for p, M, K, ws in mats[4:6]]
+        q4, s4 = O.quantize_act(rms(g_ / (1 + np.exp(-g_)) * u_))
+        O.gemm_tern2_mt(mats[6][0], 2560, 6912, mats[6][3], q4, s4, threads)
+
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        layer()
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    t_layer = (time.perf_counter() - t0) / n
+    head = emb[:16384].astype(np.float32)  # an eighth of the lm_head, as fp32
+    t1 = time.perf_counter()
+    _ = x @ head.T
+    t_head = (time.perf_counter() - t1) * (128256 / 16384)
+    return B / (30 * t_layer + t_head), n, 30 * t_layer + t_head
+
+
+def run_decode(args, rank, world, local_rank):
+    """Configuration 4: BitNet-2B-class decode, 30 layers, KV context 1024,
+    256 generated tokens per sequence (the timed region; --tokens), greedy sampling.
+    Every rank decodes its own batch (replicas, weak scaling)."""
+    import torch
+    import torch.distributed as dist
+    import ouroboros_b200 as oq
+    from ouroboros_b200.decode import Decoder
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    ctx = oq.Context(local_rank)
+    B, gen = args.batch, args.tokens
+    dec = Decoder(ctx, batch=B, context=1024, generate=gen, device=device, seed=17 + rank)
+    n0 = ctx.launch_count()
+    g_full = dec.capture(dec.step)  # two eager steps, then the captured one
+    launches_per_token = (ctx.launch_count() - n0) / 3
+    dec.lm_head = False
+    g_body = dec.capture(dec.step)
+    dec.lm_head = True
+    g_tern = dec.capture(dec.ternary_only_step)
+
+    def timed(g, n):
+        if world > 1:
+            dist.barrier()
+        dec.pos.fill_(1024)
+        torch.cuda.synchronize(device)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(dec.stream):
+            e0.record(dec.stream)
+            for _ in range(n):
+                g.replay()
+            e1.record(dec.stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    timed(g_full, max(3, min(args.warmup, gen)))
+    with ClockSampler(local_rank) as clk:
+        ms_full = timed(g_full, gen)
+    clocks = clk.summary()
+    ms_body = timed(g_body, gen)
+    ms_tern = timed(g_tern, gen)
+    tok_s = B * world * gen / (ms_full / 1e3)
+    tok_s_body = B * world * gen / (ms_body / 1e3)
+    # ternary weight bytes streamed per token step (all 30 layers)
+    tern_bytes = 30 * (2 * 2560 * 2560 + 2 * 640 * 2560 + 3 * 6912 * 2560) // 4
+    achieved = tern_bytes / (ms_tern / 1e3 / gen) / 1e9
+    hbm_peak, _, peak_kind = peaks()
+
+    # e2e: the same step with the sampled token ids read back to the host and
+    # fed in again from pinned host memory every step
+    tok_h = torch.empty((B,), dtype=torch.long).pin_memory()
+    def e2e(n):
+        for _ in range(n):
+            g_full.replay()
+            tok_h.copy_(dec.tokens, non_blocking=True)
+            dec.tokens.copy_(tok_h, non_blocking=True)
+    if world > 1:
+        dist.barrier()
+    dec.pos.fill_(1024)
+    torch.cuda.synchronize(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(dec.stream):
+        e0.record(dec.stream)
+        e2e(gen)
+        e1.record(dec.stream)
+    e1.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    e2e_tok_s = B * world * gen / (e2e_ms / 1e3)
+
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        from oracle import pyoracle as O
+        threads = O.hw_threads()
+        v, n, dt = cpu_decode_tokens_per_s(B, args.cpu_seconds, threads)
+        cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"{n} single-layer passes at batch {B} (oracle int8 GEMV, numpy norms and "
+                         f"attention over 1024 tokens) scaled to 30 layers, plus the lm_head; "
+                         f"{threads} threads"}
+    if rank == 0:
+        line = {
+            "metric": "decode tokens/s", "value": round(tok_s, 2), "unit": "tokens/s",
+            "n_gpus": world, "steps": gen, "warmup": max(3, min(args.warmup, gen)),
+            "ms_per_step": round(ms_full / gen, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (random init BitNet-2B-class weights, random 1024-token KV context)",
+            "config": {"workload": f"bitnet2b-decode-b{B}-ctx1024-gen256", "batch": B,
+                       "layers": 30, "hidden": 2560, "heads": "20/5x128", "ffn": 6912,
+                       "vocab": 128256, "kv": "fp32", "parallelism": f"replicas x{world}",
+                       "launch": "one CUDA graph per decode step"},
+            "tokens_per_s_without_lm_head": round(tok_s_body, 2),
+            "ternary_matmul_share": round(ms_tern / ms_full, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
+                         "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                         "peak_kind": f"{peak_kind} (hbm_gbs)", "traffic": None,
+                         "kernel": "ternary projections of one decode step (30 layers)",
+                         "bytes_per_step": tern_bytes},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8 * B,
+                    "d2h_bytes_per_step": 8 * B,
+                    "how": "graph replay per token with the sampled ids copied to pinned host "
+                           "memory and back"},
+            "gpu_launches": int(round(launches_per_token * gen)),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    del g_full, g_body, g_tern
+    dec.free()
+    ctx.close()
+
+
 def run_sharded(args, rank, world, local_rank):
     """Strong scaling of one large matrix: rank r holds rows [r*M/N, (r+1)*M/N),
     every step computes the local rows and all-gathers the full y on every rank."""
@@ -685,7 +878,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.shard:
+        if args.workload == "decode":
+            run_decode(args, rank, world, local_rank)
+        elif args.shard:
             run_sharded(args, rank, world, local_rank)
         else:
             run_ouroq(args, rank, world, local_rank)

@@ -80,8 +80,10 @@ ouroq_status ouroq_ctx_create(int device, ouroq_ctx **out);
 ouroq_status ouroq_ctx_destroy(ouroq_ctx *ctx);
 /* Text of the last error on this context ("" if none). Valid until the next call. */
 const char *ouroq_last_error(const ouroq_ctx *ctx);
-/* Read and clear the device status word that bounded in-kernel waits write on
- * expiry (synchronises the device). OUROQ_ERR_TIMEOUT if a wait gave up. */
+/* Read and clear the device status word that kernels write on a fault they
+ * refuse to act on (synchronises the device). OUROQ_ERR_TIMEOUT if a bounded
+ * wait gave up, OUROQ_ERR_BAD_SHAPE if a decode position lay outside the KV
+ * cache. */
 ouroq_status ouroq_check_device(ouroq_ctx *ctx);
 /* Number of kernels this context has launched (for bench accounting). */
 uint64_t ouroq_launch_count(const ouroq_ctx *ctx);
@@ -221,6 +223,39 @@ ouroq_status ouroq_gemm_sharded(ouroq_ctx *ctx, const ouroq_weight *w_shard, con
  * OUROQ_ERR_TIMEOUT or OUROQ_ERR_NCCL marks the group failed: later sharded
  * calls return OUROQ_ERR_NCCL and finalize aborts the communicator. */
 ouroq_status ouroq_shard_sync(ouroq_ctx *ctx, void *stream, int timeout_ms);
+
+/* ---- the decode step either side of the path (infer/mod.rs:298-336) ----
+ * fp32, stream-ordered, device buffers. These replace the reference's host
+ * ops around the projections so that a decode step stays on the GPU.
+ * rmsnorm (ops.rs:12-17): h = x + r (r, h nullable: no residual / not
+ * stored), y[b] = h[b] / sqrt(mean(h[b]^2) + eps) * w, B rows of n. */
+ouroq_status ouroq_rmsnorm(ouroq_ctx *ctx, const float *x, const float *r, float *h, const float *w,
+                           float *y, int B, int n, float eps, void *stream);
+/* y = rmsnorm(silu(gate) * up) * w (ops.rs:34-36, the FFN sub-norm). */
+ouroq_status ouroq_swiglu_rmsnorm(ouroq_ctx *ctx, const float *gate, const float *up,
+                                  const float *w, float *y, int B, int n, float eps, void *stream);
+/* NeoX RoPE (ops.rs:21-33, rot = head_dim = 128) of q [B][n_head][128] in
+ * place and of k [B][n_kv][128] at position *pos (a device int64), then k and
+ * v appended to the caches [B][n_kv][tmax][128] at *pos. */
+ouroq_status ouroq_rope_kv_append(ouroq_ctx *ctx, float *q, const float *k, const float *v,
+                                  float *kcache, float *vcache, const int64_t *pos, int B,
+                                  int n_head, int n_kv, int tmax, float rope_base, void *stream);
+/* Causal GQA attention of q [B][n_head][128] over cache positions 0..*pos
+ * (mod.rs:337-365, scale 1/sqrt(128)): out [B][n_head][128]. n_head a
+ * multiple of n_kv, at most 8 query heads per KV head; every buffer 16-byte
+ * aligned. A *pos outside [0, tmax) writes zeros to out, leaves the caches
+ * alone and leaves a code in the status word. The slice partials live in
+ * the context: calls on one context must not overlap in time. */
+ouroq_status ouroq_attention_decode(ouroq_ctx *ctx, const float *q, const float *kcache,
+                                    const float *vcache, const int64_t *pos, float *out, int B,
+                                    int n_head, int n_kv, int tmax, void *stream);
+/* ouroq_rope_kv_append followed by ouroq_attention_decode, in one launch: q
+ * and k arrive un-rotated (q is left as it is), k and v are written to the
+ * caches at *pos, and out is the attention of the rotated q. */
+ouroq_status ouroq_rope_attention_decode(ouroq_ctx *ctx, const float *q, const float *k,
+                                         const float *v, float *kcache, float *vcache,
+                                         const int64_t *pos, float *out, int B, int n_head,
+                                         int n_kv, int tmax, float rope_base, void *stream);
 
 /* ---- BMTS v1 shard files (cluster/src/bmts.rs:1-14, 171-209) ----
  * BmtsShard::open: the file is memory-mapped and its header and JSON tensor

@@ -79,6 +79,12 @@ ABI_FUNCTIONS = {
     "ouroq_weight_upload_shard": (_i, [_p, _i, _p, _i, _i, _p, _f, ctypes.POINTER(_p)]),
     "ouroq_gemm_sharded": (_i, [_p, _p, _p, _i, _p, _i, _p, _p]),
     "ouroq_shard_sync": (_i, [_p, _p, _i]),
+    "ouroq_rmsnorm": (_i, [_p, _p, _p, _p, _p, _p, _i, _i, _f, _p]),
+    "ouroq_swiglu_rmsnorm": (_i, [_p, _p, _p, _p, _p, _i, _i, _f, _p]),
+    "ouroq_rope_kv_append": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _f, _p]),
+    "ouroq_attention_decode": (_i, [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p]),
+    "ouroq_rope_attention_decode": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i,
+                                         ctypes.c_float, _p]),
     "ouroq_bmts_open": (_i, [ctypes.c_char_p, ctypes.POINTER(_p), ctypes.c_char_p, _sz]),
     "ouroq_bmts_close": (_i, [_p]),
     "ouroq_bmts_info": (_i, [_p, ctypes.POINTER(_i), ctypes.POINTER(_i),
@@ -371,6 +377,58 @@ class Context:
 
     def shard_sync(self, stream=None, timeout_ms: int = 10000) -> None:
         self._check(self.lib.ouroq_shard_sync(self.ctx, _stream_ptr(stream), int(timeout_ms)))
+
+    # -- the decode step around the projections (fp32 device tensors) --
+    def rmsnorm(self, x, w, y=None, residual=None, h=None, eps: float = 1e-5, stream=None):
+        """y = rmsnorm(x + residual) * w; h (optional) receives x + residual."""
+        import torch
+        B, n = x.shape
+        if y is None:
+            y = torch.empty_like(x)
+        self._check(self.lib.ouroq_rmsnorm(self.ctx, _ptr(x), _ptr(residual), _ptr(h), _ptr(w), _ptr(y),
+                                           B, n, eps, _stream_ptr(stream)))
+        return y
+
+    def swiglu_rmsnorm(self, gate, up, w, y=None, eps: float = 1e-5, stream=None):
+        import torch
+        B, n = gate.shape
+        if y is None:
+            y = torch.empty_like(gate)
+        self._check(self.lib.ouroq_swiglu_rmsnorm(self.ctx, _ptr(gate), _ptr(up), _ptr(w), _ptr(y),
+                                                  B, n, eps, _stream_ptr(stream)))
+        return y
+
+    def rope_kv_append(self, q, k, v, kcache, vcache, pos, n_head: int, n_kv: int,
+                       rope_base: float = 500000.0, stream=None):
+        B = q.shape[0]
+        tmax = kcache.shape[-2]
+        self._check(self.lib.ouroq_rope_kv_append(self.ctx, _ptr(q), _ptr(k), _ptr(v), _ptr(kcache),
+                                                  _ptr(vcache), _ptr(pos), B, n_head, n_kv, tmax,
+                                                  rope_base, _stream_ptr(stream)))
+
+    def attention_decode(self, q, kcache, vcache, pos, n_head: int, n_kv: int, out=None, stream=None):
+        import torch
+        B = q.shape[0]
+        tmax = kcache.shape[-2]
+        if out is None:
+            out = torch.empty((B, n_head * 128), dtype=torch.float32, device=q.device)
+        self._check(self.lib.ouroq_attention_decode(self.ctx, _ptr(q), _ptr(kcache), _ptr(vcache),
+                                                    _ptr(pos), _ptr(out), B, n_head, n_kv, tmax,
+                                                    _stream_ptr(stream)))
+        return out
+
+    def rope_attention_decode(self, q, k, v, kcache, vcache, pos, n_head: int, n_kv: int,
+                              rope_base: float = 500000.0, out=None, stream=None):
+        """rope_kv_append + attention_decode in one launch; q is not modified."""
+        import torch
+        B = q.shape[0]
+        tmax = kcache.shape[-2]
+        if out is None:
+            out = torch.empty((B, n_head * 128), dtype=torch.float32, device=q.device)
+        self._check(self.lib.ouroq_rope_attention_decode(
+            self.ctx, _ptr(q), _ptr(k), _ptr(v), _ptr(kcache), _ptr(vcache), _ptr(pos), _ptr(out),
+            B, n_head, n_kv, tmax, rope_base, _stream_ptr(stream)))
+        return out
 
     # -- host-buffer mirrors of the reference operators (numpy in, numpy out) --
     def matvec_q(self, w: Weight, x: np.ndarray) -> np.ndarray:

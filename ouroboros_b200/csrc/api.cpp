@@ -51,6 +51,11 @@ struct ouroq_ctx {
   // rotated fp32 activations for the reference formats (hadamard_block != 0)
   float* rot_scratch = nullptr;
   size_t rot_cap = 0;
+  // slice partials of the decode attention
+  float* attn_part = nullptr;
+  size_t attn_cap = 0;
+  unsigned* attn_ctr = nullptr;  // zeroed on allocation; each launch leaves it zero
+  size_t attn_ctr_cap = 0;
   // row-sharded group (NCCL communicator, opaque here)
   void* comm = nullptr;
   int shard_world = 1, shard_rank = 0;
@@ -642,6 +647,8 @@ ouroq_status ouroq_ctx_destroy(ouroq_ctx* ctx) {
   cudaFree(ctx->y_stage);
   cudaFree(ctx->sign_stage);
   cudaFree(ctx->rot_scratch);
+  cudaFree(ctx->attn_part);
+  cudaFree(ctx->attn_ctr);
   shard_release(ctx);
   delete ctx;
   return OUROQ_OK;
@@ -665,7 +672,16 @@ ouroq_status ouroq_check_device(ouroq_ctx* ctx) {
   CU(ctx, cudaMemcpy(&v, ctx->d_status, sizeof v, cudaMemcpyDeviceToHost), "status read");
   if (v != 0) {
     CU(ctx, cudaMemset(ctx->d_status, 0, sizeof v), "status clear");
-    return fail(ctx, OUROQ_ERR_TIMEOUT, "device wait expired (code %u)", v);
+    switch (v) {
+      case kDevBadTile:
+        return fail(ctx, OUROQ_ERR_CUDA, "tile index outside the job table (code %u)", v);
+      case kDevBadPosition:
+        return fail(ctx, OUROQ_ERR_BAD_SHAPE, "decode position outside the KV cache (code %u)", v);
+      case kDevPeerTimeout:
+        return fail(ctx, OUROQ_ERR_TIMEOUT, "peer rows did not arrive in time (code %u)", v);
+      default:
+        return fail(ctx, OUROQ_ERR_TIMEOUT, "device wait expired (code %u)", v);
+    }
   }
   return OUROQ_OK;
 }
@@ -1256,6 +1272,142 @@ ouroq_status ouroq_shard_sync(ouroq_ctx* ctx, void* stream, int timeout_ms) {
     return fail(ctx, OUROQ_ERR_TIMEOUT, "a peer's rows did not arrive in time");
   }
   return OUROQ_OK;
+}
+
+
+// ---------------------------------------------------------------- decode step
+ouroq_status ouroq_rmsnorm(ouroq_ctx* ctx, const float* x, const float* r, float* h, const float* w,
+                           float* y, int B, int n, float eps, void* stream) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  if (B < 0 || n <= 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d n=%d", B, n);
+  if (B == 0) return OUROQ_OK;
+  if (!x || !w || !y) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  DeviceGuard g(ctx->device);
+  CU(ctx, launch_rmsnorm(x, r, h, w, y, B, n, eps, static_cast<cudaStream_t>(stream), ctx->pdl),
+     "rmsnorm launch");
+  ctx->launches++;
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_swiglu_rmsnorm(ouroq_ctx* ctx, const float* gate, const float* up,
+                                  const float* w, float* y, int B, int n, float eps, void* stream) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  if (B < 0 || n <= 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d n=%d", B, n);
+  if (B == 0) return OUROQ_OK;
+  if (!gate || !up || !w || !y) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  DeviceGuard g(ctx->device);
+  CU(ctx, launch_swiglu_norm(gate, up, w, y, B, n, eps, static_cast<cudaStream_t>(stream), ctx->pdl),
+     "swiglu launch");
+  ctx->launches++;
+  return OUROQ_OK;
+}
+
+static ouroq_status check_attn_shape(ouroq_ctx* ctx, int B, int n_head, int n_kv, int tmax) {
+  if (B < 0 || n_head <= 0 || n_kv <= 0 || tmax <= 0)
+    return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d n_head=%d n_kv=%d tmax=%d", B, n_head, n_kv, tmax);
+  if (n_head % n_kv || n_head / n_kv > 8)
+    return fail(ctx, OUROQ_ERR_UNSUPPORTED, "%d query heads over %d KV heads (group of at most 8)",
+                n_head, n_kv);
+  if (B > 65535 || n_kv > 65535) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "grid too large");
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_rope_kv_append(ouroq_ctx* ctx, float* q, const float* k, const float* v,
+                                  float* kcache, float* vcache, const int64_t* pos, int B,
+                                  int n_head, int n_kv, int tmax, float rope_base, void* stream) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  ouroq_status st = check_attn_shape(ctx, B, n_head, n_kv, tmax);
+  if (st != OUROQ_OK || B == 0) return st;
+  if (!q || !k || !v || !kcache || !vcache || !pos)
+    return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  DecodeAttn P{};
+  P.q = q;
+  P.k = k;
+  P.v = v;
+  P.kcache = kcache;
+  P.vcache = vcache;
+  P.pos = reinterpret_cast<const long long*>(pos);
+  P.status = ctx->d_status;
+  P.B = B;
+  P.n_head = n_head;
+  P.n_kv = n_kv;
+  P.tmax = tmax;
+  P.rope_base = rope_base;
+  DeviceGuard g(ctx->device);
+  CU(ctx, launch_rope_append(P, static_cast<cudaStream_t>(stream), ctx->pdl), "rope launch");
+  ctx->launches++;
+  return OUROQ_OK;
+}
+
+static ouroq_status attention_common(ouroq_ctx* ctx, DecodeAttn& P, bool rope, void* stream) {
+  if (!aligned16(P.q) || !aligned16(P.kcache) || !aligned16(P.vcache) || !aligned16(P.out) ||
+      (rope && (!aligned16(P.k) || !aligned16(P.v))))
+    return fail(ctx, OUROQ_ERR_BAD_ALIGN, "attention buffers not 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  P.status = ctx->d_status;
+  P.splits = attn_splits(P.B, P.n_kv, P.tmax, ctx->num_sms);
+  P.scale = 1.0f / std::sqrt(128.0f);
+  ouroq_status st = grow(ctx, ctx->attn_part, ctx->attn_cap,
+                         attn_part_floats(P.B, P.n_head, P.splits), "attention partials");
+  if (st != OUROQ_OK) return st;
+  const size_t nctr = (size_t)P.B * P.n_kv;
+  if (nctr > ctx->attn_ctr_cap) {
+    st = grow(ctx, ctx->attn_ctr, ctx->attn_ctr_cap, nctr, "attention counters");
+    if (st != OUROQ_OK) return st;
+    CU(ctx, cudaMemset(ctx->attn_ctr, 0, ctx->attn_ctr_cap * sizeof(unsigned)),
+       "attention counters");
+  }
+  P.part = ctx->attn_part;
+  P.counter = ctx->attn_ctr;
+  CU(ctx, launch_attention_decode(P, rope, static_cast<cudaStream_t>(stream), ctx->pdl),
+     "attention launch");
+  ctx->launches++;
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_attention_decode(ouroq_ctx* ctx, const float* q, const float* kcache,
+                                    const float* vcache, const int64_t* pos, float* out, int B,
+                                    int n_head, int n_kv, int tmax, void* stream) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  ouroq_status st = check_attn_shape(ctx, B, n_head, n_kv, tmax);
+  if (st != OUROQ_OK || B == 0) return st;
+  if (!q || !kcache || !vcache || !pos || !out) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  DecodeAttn P{};
+  P.q = const_cast<float*>(q);
+  P.kcache = const_cast<float*>(kcache);
+  P.vcache = const_cast<float*>(vcache);
+  P.pos = reinterpret_cast<const long long*>(pos);
+  P.out = out;
+  P.B = B;
+  P.n_head = n_head;
+  P.n_kv = n_kv;
+  P.tmax = tmax;
+  return attention_common(ctx, P, false, stream);
+}
+
+ouroq_status ouroq_rope_attention_decode(ouroq_ctx* ctx, const float* q, const float* k,
+                                         const float* v, float* kcache, float* vcache,
+                                         const int64_t* pos, float* out, int B, int n_head,
+                                         int n_kv, int tmax, float rope_base, void* stream) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  ouroq_status st = check_attn_shape(ctx, B, n_head, n_kv, tmax);
+  if (st != OUROQ_OK || B == 0) return st;
+  if (!q || !k || !v || !kcache || !vcache || !pos || !out)
+    return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  DecodeAttn P{};
+  P.q = const_cast<float*>(q);
+  P.k = k;
+  P.v = v;
+  P.kcache = kcache;
+  P.vcache = vcache;
+  P.pos = reinterpret_cast<const long long*>(pos);
+  P.out = out;
+  P.B = B;
+  P.n_head = n_head;
+  P.n_kv = n_kv;
+  P.tmax = tmax;
+  P.rope_base = rope_base;
+  return attention_common(ctx, P, true, stream);
 }
 
 }  // extern "C"

@@ -35,6 +35,7 @@ enum : unsigned {
   kDevWaitTimeout = 1,  // an mbarrier wait ran past its iteration limit
   kDevBadTile = 2,      // a tile index outside the job table (never expected)
   kDevPeerTimeout = 3,  // a sharded gather waited too long for a peer's rows
+  kDevBadPosition = 4,  // a decode position outside the KV cache (nothing written)
 };
 
 constexpr int kTileRows = 32;
@@ -174,6 +175,32 @@ cudaError_t launch_shard_gather(const ShardGather& P, cudaStream_t s, bool pdl);
 // Row-sharded matmul, NCCL transport: gather [G][B][R] -> y [B][G*R].
 cudaError_t launch_shard_interleave(const float* gather, float* y, int B, int R, int G,
                                     cudaStream_t s);
+
+// The decode step around the ternary path (decode.cu). Head dim 128; up to 8
+// query heads per KV head. KV cache [B][n_kv][tmax][128] fp32 per layer.
+struct DecodeAttn {
+  float* q;                  // [B][n_head][128] (rotated in place by rope_append)
+  const float* k;            // [B][n_kv][128] new keys (before RoPE)
+  const float* v;            // [B][n_kv][128] new values
+  float* kcache;             // [B][n_kv][tmax][128]
+  float* vcache;
+  const long long* pos;      // device: the position being decoded
+  float* out;                // [B][n_head][128]
+  float* part;               // [B][n_kv][splits][group][132] slice partials
+  unsigned* counter;         // [B][n_kv] slices finished (zero between launches)
+  unsigned* status;
+  int B, n_head, n_kv, tmax, splits;
+  float rope_base, scale;
+};
+cudaError_t launch_rmsnorm(const float* x, const float* r, float* h, const float* w, float* y,
+                           int B, int n, float eps, cudaStream_t s, bool pdl);
+cudaError_t launch_swiglu_norm(const float* g, const float* u, const float* w, float* y, int B,
+                               int n, float eps, cudaStream_t s, bool pdl);
+cudaError_t launch_rope_append(const DecodeAttn& P, cudaStream_t s, bool pdl);
+int attn_splits(int B, int n_kv, int tmax, int num_sms);
+size_t attn_part_floats(int B, int n_head, int splits);
+// rope: q, k un-rotated; k and v appended to the cache at pos in the same launch
+cudaError_t launch_attention_decode(const DecodeAttn& P, bool rope, cudaStream_t s, bool pdl);
 
 // Fixed scratch of ouroq_gemm_f32act_noalloc (one copy per device): int8
 // codes for up to 4 MiB of B*K, then fp32 scales for up to 4096 tokens.

@@ -1,0 +1,219 @@
+"""The decode step around the ternary path, against fp32/float64 torch references.
+
+These ops follow the reference's host code (cluster/src/infer/ops.rs:11-40,
+mod.rs:298-365) but sum in a different order than its sequential loops, so
+they are checked within tolerances written here: 1e-5 relative for the norms
+and RoPE, 1e-4 relative (1e-5 absolute) for attention (online softmax over
+slices). A fused layer is checked stage by stage on its own buffers, and the
+graph-captured step against the eager one bit for bit.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import ouroboros_b200 as oq
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref_rms(x, w, eps=1e-5):
+    x64 = x.double()
+    return (x64 / torch.sqrt((x64 * x64).mean(-1, keepdim=True) + eps) * w.double()).float()
+
+
+@pytest.mark.parametrize("B,n", [(1, 2560), (3, 6912), (32, 2560)])
+def test_rmsnorm_with_residual(ctx, B, n):
+    g = torch.Generator(device="cuda").manual_seed(n + B)
+    x = torch.randn((B, n), generator=g, device="cuda")
+    r = torch.randn((B, n), generator=g, device="cuda")
+    w = 1 + 0.02 * torch.randn(n, generator=g, device="cuda")
+    h = torch.empty_like(x)
+    y = ctx.rmsnorm(x, w, residual=r, h=h)
+    torch.cuda.synchronize()
+    assert torch.equal(h, x + r)
+    torch.testing.assert_close(y, _ref_rms(x + r, w), rtol=1e-5, atol=1e-6)
+    y2 = ctx.rmsnorm(x, w)
+    torch.testing.assert_close(y2, _ref_rms(x, w), rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("B", [1, 5])
+def test_swiglu_rmsnorm(ctx, B):
+    n = 6912
+    g = torch.Generator(device="cuda").manual_seed(B)
+    gate = 3 * torch.randn((B, n), generator=g, device="cuda")
+    up = torch.randn((B, n), generator=g, device="cuda")
+    w = 1 + 0.02 * torch.randn(n, generator=g, device="cuda")
+    y = ctx.swiglu_rmsnorm(gate, up, w)
+    a = gate.double() / (1 + torch.exp(-gate.double())) * up.double()
+    torch.testing.assert_close(y, _ref_rms(a.float(), w), rtol=1e-5, atol=1e-6)
+
+
+def _rope_ref(v, pos, base=500000.0):
+    # ops.rs:21-33 in float32: theta_i = 1 / base^(2i/128), angle = pos * theta_i
+    half = 64
+    i = torch.arange(half, dtype=torch.float32, device=v.device)
+    theta = 1.0 / torch.pow(torch.tensor(base, dtype=torch.float32), 2 * i / 128.0)
+    ang = torch.tensor(float(pos), dtype=torch.float32) * theta
+    c, s = torch.cos(ang.double()).float(), torch.sin(ang.double()).float()
+    a, b = v[..., :half], v[..., half:]
+    return torch.cat([a * c - b * s, b * c + a * s], dim=-1)
+
+
+@pytest.mark.parametrize("B,pos", [(1, 0), (2, 1023), (3, 1279)])
+def test_rope_kv_append(ctx, B, pos):
+    n_head, n_kv, tmax = 20, 5, 1280
+    g = torch.Generator(device="cuda").manual_seed(pos)
+    q = torch.randn((B, n_head * 128), generator=g, device="cuda")
+    k = torch.randn((B, n_kv * 128), generator=g, device="cuda")
+    v = torch.randn((B, n_kv * 128), generator=g, device="cuda")
+    kc = torch.zeros((B, n_kv, tmax, 128), device="cuda")
+    vc = torch.zeros((B, n_kv, tmax, 128), device="cuda")
+    p = torch.full((1,), pos, dtype=torch.long, device="cuda")
+    q0 = q.clone()
+    ctx.rope_kv_append(q, k, v, kc, vc, p, n_head, n_kv)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(q.view(B, n_head, 128), _rope_ref(q0.view(B, n_head, 128), pos),
+                               rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(kc[:, :, pos], _rope_ref(k.view(B, n_kv, 128), pos),
+                               rtol=1e-5, atol=1e-5)
+    assert torch.equal(vc[:, :, pos], v.view(B, n_kv, 128))
+    others = torch.ones(tmax, dtype=torch.bool, device="cuda")
+    others[pos] = False
+    assert torch.count_nonzero(kc[:, :, others]) == 0 and torch.count_nonzero(vc[:, :, others]) == 0
+
+
+def _attn_ref(q, kc, vc, pos, n_head, n_kv):
+    B = q.shape[0]
+    grp = n_head // n_kv
+    qh = q.view(B, n_head, 128).double()
+    k = kc[:, :, :pos + 1].double().repeat_interleave(grp, dim=1)
+    v = vc[:, :, :pos + 1].double().repeat_interleave(grp, dim=1)
+    sc = torch.einsum("bhd,bhtd->bht", qh, k) / math.sqrt(128.0)
+    return torch.einsum("bht,bhtd->bhd", torch.softmax(sc, -1), v).reshape(B, -1).float()
+
+
+@pytest.mark.parametrize("B,pos", [(1, 0), (1, 1024), (4, 700), (32, 1279)])
+def test_attention_decode(ctx, B, pos):
+    n_head, n_kv, tmax = 20, 5, 1280
+    g = torch.Generator(device="cuda").manual_seed(B * 7 + pos)
+    q = torch.randn((B, n_head * 128), generator=g, device="cuda")
+    kc = torch.randn((B, n_kv, tmax, 128), generator=g, device="cuda")
+    vc = torch.randn((B, n_kv, tmax, 128), generator=g, device="cuda")
+    p = torch.full((1,), pos, dtype=torch.long, device="cuda")
+    out = ctx.attention_decode(q, kc, vc, p, n_head, n_kv)
+    torch.testing.assert_close(out, _attn_ref(q, kc, vc, pos, n_head, n_kv), rtol=1e-4, atol=1e-5)
+
+
+def test_position_outside_the_cache_is_refused(ctx):
+    B, n_head, n_kv, tmax = 1, 20, 5, 64
+    q = torch.randn((B, n_head * 128), device="cuda")
+    k = torch.randn((B, n_kv * 128), device="cuda")
+    v = torch.randn((B, n_kv * 128), device="cuda")
+    kc = torch.zeros((B, n_kv, tmax, 128), device="cuda")
+    vc = torch.zeros((B, n_kv, tmax, 128), device="cuda")
+    p = torch.full((1,), tmax, dtype=torch.long, device="cuda")
+    ctx.rope_kv_append(q, k, v, kc, vc, p, n_head, n_kv)
+    with pytest.raises(oq.OuroqError):
+        ctx.check_device()
+    assert torch.count_nonzero(kc) == 0 and torch.count_nonzero(vc) == 0
+    for fused in (False, True):
+        if fused:
+            out = ctx.rope_attention_decode(q, k, v, kc, vc, p, n_head, n_kv)
+        else:
+            out = ctx.attention_decode(q, kc, vc, p, n_head, n_kv)
+        with pytest.raises(oq.OuroqError) as ei:
+            ctx.check_device()
+        assert ei.value.status == 1 and "position" in str(ei.value)
+        assert torch.count_nonzero(out) == 0
+        assert torch.count_nonzero(kc) == 0 and torch.count_nonzero(vc) == 0
+
+
+def _tern(dec, w, x):
+    """W x into a fresh buffer through the same library calls the decoder makes."""
+    import torch
+    y = torch.empty((x.shape[0], w.M), device=x.device)
+    if dec.B <= dec.oq_fused_max():
+        dec.ctx.gemm_group_f32act([w], [x], [y], stream=dec.stream)
+    else:
+        q, s = dec.ctx.quantize_act(x, stream=dec.stream)
+        dec.ctx.gemm(w, q, s, y=y, stream=dec.stream)
+    return y
+
+
+@pytest.mark.parametrize("B", [1, 3, 16])
+def test_fused_decode_layer_wiring(ctx, B):
+    """Every stage of a fused layer against its torch formula applied to the
+    fused path's own inputs of that stage. A whole step cannot be compared with
+    a tolerance: the int8 quantisation of each activation turns a last-bit
+    difference into a one-step code change that later layers amplify, so the
+    stages are checked one by one (the ternary products bit-exactly)."""
+    from ouroboros_b200.decode import (Decoder, HIDDEN, N_HEAD, N_KV, HEAD_DIM, EPS)
+    dec = Decoder(ctx, layers=2, batch=B, context=64, generate=4, vocab=512, seed=3)
+    bf = dec.buf
+    pos = int(dec.pos.item())
+    norm = dict(rtol=1e-5, atol=1e-5)
+    with torch.cuda.stream(dec.stream):
+        bf["x"].copy_(dec.tok_embd.index_select(0, dec.tokens).float())
+        for li in range(dec.L):
+            L = dec.layers[li]
+            x_in = bf["x"].clone() if li == 0 else bf["h1"] + bf["down"]
+            dec.layer_fused(li, li == 0)
+            dec.stream.synchronize()
+            assert torch.equal(bf["x"], x_in)
+            torch.testing.assert_close(bf["a"], _ref_rms(x_in, L["attn_norm"]), **norm)
+            q_raw, k_raw, v_raw = (_tern(dec, L[n], bf["a"]) for n in ("q", "k", "v"))
+            dec.stream.synchronize()
+            assert torch.equal(bf["q"], q_raw)
+            assert torch.equal(bf["k"], k_raw) and torch.equal(bf["v"], v_raw)
+            torch.testing.assert_close(dec.kc[li][:, :, pos],
+                                       _rope_ref(k_raw.view(B, N_KV, HEAD_DIM), pos), **norm)
+            assert torch.equal(dec.vc[li][:, :, pos], v_raw.view(B, N_KV, HEAD_DIM))
+            q_rot = _rope_ref(q_raw.view(B, N_HEAD, HEAD_DIM), pos).reshape(B, -1)
+            torch.testing.assert_close(
+                bf["attn"], _attn_ref(q_rot, dec.kc[li], dec.vc[li], pos, N_HEAD, N_KV),
+                rtol=1e-4, atol=1e-5)
+            torch.testing.assert_close(bf["b"], _ref_rms(bf["attn"], L["attn_sub_norm"]), **norm)
+            o = _tern(dec, L["o"], bf["b"])
+            dec.stream.synchronize()
+            assert torch.equal(bf["o"], o)
+            assert torch.equal(bf["h1"], x_in + o)
+            torch.testing.assert_close(bf["f"], _ref_rms(bf["h1"], L["ffn_norm"]), **norm)
+            gate, up = _tern(dec, L["gate"], bf["f"]), _tern(dec, L["up"], bf["f"])
+            dec.stream.synchronize()
+            assert torch.equal(bf["gate"], gate) and torch.equal(bf["up"], up)
+            act = (gate.double() / (1 + torch.exp(-gate.double())) * up.double()).float()
+            torch.testing.assert_close(bf["s"], _ref_rms(act, L["ffn_sub_norm"]), **norm)
+            down = _tern(dec, L["down"], bf["s"])
+            dec.stream.synchronize()
+            assert torch.equal(bf["down"], down)
+    dec.free()
+
+
+def test_decode_graph_replay_is_deterministic(ctx):
+    """The captured step, replayed, gives the eager step's tokens bit for bit."""
+    from ouroboros_b200.decode import Decoder
+    runs = []
+    for graph in (False, True):
+        dec = Decoder(ctx, layers=2, batch=4, context=64, generate=8, vocab=1024, seed=5)
+        toks = []
+        if graph:
+            g = dec.capture(dec.step)
+            for _ in range(3):
+                g.replay()
+                dec.stream.synchronize()
+                toks.append(dec.tokens.clone())
+        else:
+            with torch.cuda.stream(dec.stream):
+                for _ in range(3):
+                    dec.step()
+                    toks.append(dec.tokens.clone())
+            dec.stream.synchronize()
+        runs.append((torch.stack(toks), dec.buf["x"].clone(), dec.kc.clone()))
+        if graph:
+            del g
+        dec.free()
+    assert torch.equal(runs[0][0], runs[1][0])
+    assert torch.equal(runs[0][1], runs[1][1])
+    assert torch.equal(runs[0][2], runs[1][2])
