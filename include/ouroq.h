@@ -65,7 +65,14 @@ typedef enum {
    *     qs[48] | qh[4] | f16 d; K multiple of 256. Results are bit-identical
    *     to matvec_qblock (dequantise, then dot in element order, ops.rs:53-60). */
   OUROQ_FMT_PTQ1_0 = 3,
-  OUROQ_FMT_TQ1_0 = 4
+  OUROQ_FMT_TQ1_0 = 4,
+  /* 16-bit weights as stored in the shard, rows of K little-endian values,
+   * any K >= 1: F16 (QuantKind::F16, ops.rs:131-153) and BF16
+   * (QuantKind::Bf16, ops.rs:600-620). Each row is one fp32 chain in element
+   * order with every product and sum rounded, bit-identical to the
+   * reference (a NaN keeps its position, not necessarily its payload). */
+  OUROQ_FMT_F16 = 5,
+  OUROQ_FMT_BF16 = 6
 } ouroq_format;
 
 typedef struct ouroq_ctx ouroq_ctx;
@@ -256,6 +263,15 @@ ouroq_status ouroq_rope_attention_decode(ouroq_ctx *ctx, const float *q, const f
                                          const float *v, float *kcache, float *vcache,
                                          const int64_t *pos, float *out, int B, int n_head,
                                          int n_kv, int tmax, float rope_base, void *stream);
+
+/* argmax_token (infer/mod.rs:190-194): the tied lm_head of an F16 or BF16
+ * weight [vocab][K] applied to the final hidden states x [B][K] (device
+ * fp32), then finite_argmax (mod.rs:70-83: NaN skipped, first maximum wins,
+ * 0 when every logit is NaN) of each sequence, in one launch. tokens [B]
+ * device int64; logits [B][vocab] device fp32 or NULL. Calls on one context
+ * must not overlap in time (the reduction scratch lives in the context). */
+ouroq_status ouroq_argmax_token(ouroq_ctx *ctx, const ouroq_weight *w, const float *x, int B,
+                                float *logits, int64_t *tokens, void *stream);
 
 /* ---- BMTS v1 shard files (cluster/src/bmts.rs:1-14, 171-209) ----
  * BmtsShard::open: the file is memory-mapped and its header and JSON tensor

@@ -327,6 +327,8 @@ static void tl1_rows_sse(const uint8_t *payload, int r0, int r1, int in_len, con
                          float *y);
 static void tq1_rows(const uint8_t *payload, int r0, int r1, int in_len, const float *x,
                      float *y);
+static void half_rows(const uint8_t *payload, int r0, int r1, int in_len, const float *x,
+                      float *y, int bf16);
 
 static void *mt_worker(void *p) {
     mt_job *j = (mt_job *)p;
@@ -344,6 +346,10 @@ static void *mt_worker(void *p) {
             break;
         case 3:
             tq1_rows(j->packed, j->r0, j->r1, j->K, j->xf, j->y);
+            break;
+        case 4:
+        case 5:
+            half_rows(j->packed, j->r0, j->r1, j->K, j->xf, j->y, j->kind == 5);
             break;
     }
     return NULL;
@@ -607,4 +613,51 @@ int orc_matvec_tq1(const uint8_t *payload, int out_len, int in_len, const float 
     mt_job j = {0};
     j.kind = 3, j.packed = payload, j.M = out_len, j.K = in_len, j.xf = x, j.y = y;
     return run_mt(j, out_len, threads);
+}
+
+/* bf16_to_f32 (dequant.rs, test_bf16_known_values dequant.rs:680-690): the
+ * top 16 bits of an f32 */
+float orc_bf16_to_f32(uint16_t bits) {
+    uint32_t u = (uint32_t)bits << 16;
+    float r;
+    memcpy(&r, &u, 4);
+    return r;
+}
+
+/* matvec_f16 (ops.rs:131-153) and matvec_bf16 (ops.rs:600-620): each row one
+ * fp32 chain in element order, s = s + f32(w) * x[i] with the product and
+ * the sum rounded separately (this file is built with -ffp-contract=off). */
+static void half_rows(const uint8_t *payload, int r0, int r1, int in_len, const float *x,
+                      float *y, int bf16) {
+    for (int r = r0; r < r1; r++) {
+        const uint8_t *w = payload + (size_t)r * in_len * 2;
+        float s = 0.0f;
+        for (int i = 0; i < in_len; i++) {
+            uint16_t bits = (uint16_t)(w[2 * i] | (w[2 * i + 1] << 8));
+            float wf = bf16 ? orc_bf16_to_f32(bits) : orc_f16_to_f32(bits);
+            s = s + wf * x[i];
+        }
+        y[r] = s;
+    }
+}
+
+int orc_matvec_half(const uint8_t *payload, int out_len, int in_len, const float *x, float *y,
+                    int bf16, int threads) {
+    mt_job j = {0};
+    j.kind = bf16 ? 5 : 4, j.packed = payload, j.M = out_len, j.K = in_len, j.xf = x, j.y = y;
+    return run_mt(j, out_len, threads);
+}
+
+/* finite_argmax (infer/mod.rs:70-83): NaN skipped, the first maximum wins,
+ * 0 when every value is NaN */
+int orc_finite_argmax(const float *l, int n) {
+    int best = 0, found = 0;
+    for (int i = 0; i < n; i++) {
+        if (l[i] != l[i]) continue;
+        if (!found || l[i] > l[best]) {
+            best = i;
+            found = 1;
+        }
+    }
+    return best;
 }

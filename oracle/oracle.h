@@ -99,6 +99,11 @@ int orc_matmul_tl1_scalar(const uint8_t *payload, int out_len, int in_len, const
                           int k, float *y /* [k][out_len] */);
 int orc_matvec_tq1(const uint8_t *payload, int out_len, int in_len, const float *x, float *y,
                    int threads);
+/* 16-bit weights (QuantKind::F16 / Bf16) and the greedy pick */
+float orc_bf16_to_f32(uint16_t bits);
+int orc_matvec_half(const uint8_t *payload, int out_len, int in_len, const float *x, float *y,
+                    int bf16, int threads);
+int orc_finite_argmax(const float *l, int n);
 int orc_hw_threads(void);
 
 #ifdef __cplusplus

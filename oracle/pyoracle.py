@@ -69,6 +69,9 @@ def lib() -> ctypes.CDLL:
             "orc_matvec_tl1_sse": (_i, [_u8p, _i, _i, _f32p, _f32p, _i]),
             "orc_matmul_tl1_scalar": (_i, [_u8p, _i, _i, _f32p, _i, _f32p]),
             "orc_matvec_tq1": (_i, [_u8p, _i, _i, _f32p, _f32p, _i]),
+            "orc_bf16_to_f32": (ctypes.c_float, [ctypes.c_uint16]),
+            "orc_matvec_half": (_i, [_u8p, _i, _i, _f32p, _f32p, _i, _i]),
+            "orc_finite_argmax": (_i, [_f32p, _i]),
             "orc_hw_threads": (_i, []),
         }
         for name, (res, args) in sig.items():
@@ -281,6 +284,27 @@ def matvec_tq1(payload, out_len, in_len, x, threads=0):
     _chk(lib().orc_matvec_tq1(_p(payload, _u8p), out_len, in_len, _p(x, _f32p), _p(y, _f32p),
                               threads), "matvec_tq1")
     return y
+
+
+def bf16_to_f32(bits: int) -> float:
+    return float(lib().orc_bf16_to_f32(bits))
+
+
+def matvec_half(payload, out_len, in_len, x, bf16=False, threads=0):
+    """matvec_f16 / matvec_bf16 (ops.rs:131-153, 600-620) on the shard bytes."""
+    payload = np.ascontiguousarray(payload).view(np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    assert payload.size == out_len * in_len * 2 and x.size == in_len
+    y = np.empty(out_len, dtype=np.float32)
+    _chk(lib().orc_matvec_half(_p(payload, _u8p), out_len, in_len, _p(x, _f32p), _p(y, _f32p),
+                               int(bool(bf16)), threads), "matvec_half")
+    return y
+
+
+def finite_argmax(logits) -> int:
+    """infer/mod.rs:70-83."""
+    l = np.ascontiguousarray(logits, dtype=np.float32)
+    return int(lib().orc_finite_argmax(_p(l, _f32p), l.size))
 
 
 def hw_threads() -> int:

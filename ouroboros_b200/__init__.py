@@ -24,7 +24,8 @@ from pathlib import Path
 import numpy as np
 
 __all__ = [
-    "OuroqError", "Context", "Weight", "TERNARY2", "SIGN1G128", "PTQ1_0", "TQ1_0", "load_library",
+    "OuroqError", "Context", "Weight", "TERNARY2", "SIGN1G128", "PTQ1_0", "TQ1_0", "F16", "BF16",
+    "load_library",
     "LIB_PATH",
     "ABI_FUNCTIONS", "SHARD_ID_BYTES", "shard_unique_id", "shard_rows",
 ]
@@ -35,6 +36,8 @@ TERNARY2 = 1
 SIGN1G128 = 2
 PTQ1_0 = 3  # the reference's Tl1 shard format (28 B per 128 weights), fp32 activations
 TQ1_0 = 4   # the reference's TQ1_0 shard format (54 B per 256 weights), fp32 activations
+F16 = 5     # 16-bit shard weights (QuantKind::F16, e.g. the tied token_embd), fp32 activations
+BF16 = 6    # QuantKind::Bf16
 SHARD_ID_BYTES = 128
 
 OK = 0
@@ -85,6 +88,7 @@ ABI_FUNCTIONS = {
     "ouroq_attention_decode": (_i, [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p]),
     "ouroq_rope_attention_decode": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i,
                                          ctypes.c_float, _p]),
+    "ouroq_argmax_token": (_i, [_p, _p, _p, _i, _p, _p, _p]),
     "ouroq_bmts_open": (_i, [ctypes.c_char_p, ctypes.POINTER(_p), ctypes.c_char_p, _sz]),
     "ouroq_bmts_close": (_i, [_p]),
     "ouroq_bmts_info": (_i, [_p, ctypes.POINTER(_i), ctypes.POINTER(_i),
@@ -232,6 +236,8 @@ class Context:
     # -- weights --
     def upload(self, fmt: int, packed: np.ndarray, M: int, K: int, scales: np.ndarray | None = None,
                w_scale: float = 1.0) -> Weight:
+        if fmt in (F16, BF16) and np.asarray(packed).dtype.itemsize == 2:
+            packed = np.ascontiguousarray(packed).view(np.uint8)  # the shard's bytes
         packed = np.ascontiguousarray(packed, dtype=np.uint8)
         if scales is not None:
             scales = np.ascontiguousarray(scales, dtype=np.uint16)
@@ -416,6 +422,17 @@ class Context:
                                                     _ptr(pos), _ptr(out), B, n_head, n_kv, tmax,
                                                     _stream_ptr(stream)))
         return out
+
+    def argmax_token(self, w: Weight, x, tokens=None, logits=None, stream=None):
+        """Greedy next token of each row of x [B][K] through the F16 / BF16 head w
+        (the reference's argmax_token); logits [B][M] are written if given."""
+        import torch
+        B = x.shape[0]
+        if tokens is None:
+            tokens = torch.empty((B,), dtype=torch.long, device=x.device)
+        self._check(self.lib.ouroq_argmax_token(self.ctx, w.handle, _ptr(x), B, _ptr(logits),
+                                                _ptr(tokens), _stream_ptr(stream)))
+        return tokens
 
     def rope_attention_decode(self, q, k, v, kcache, vcache, pos, n_head: int, n_kv: int,
                               rope_base: float = 500000.0, out=None, stream=None):

@@ -20,12 +20,14 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from . import OuroqError, Weight, load_library, PTQ1_0, TQ1_0
+from . import OuroqError, Weight, load_library, PTQ1_0, TQ1_0, F16, BF16
 
 BMTS_MAGIC = 0x4F55524F
 BMTS_VERSION = 1
 DTYPE_TQ1_0 = 34   # QuantKind::Tq1_0 (dequant.rs:344)
 DTYPE_TL1 = 143    # QuantKind::Tl1 (dequant.rs:345)
+DTYPE_F16 = 1      # QuantKind::F16 (dequant.rs:337)
+DTYPE_BF16 = 30    # QuantKind::Bf16 (dequant.rs:338)
 
 
 @dataclass
@@ -106,7 +108,7 @@ class BmtsShard:
         return self.read_span(name, 0, t.length)
 
     def upload(self, ctx, name: str) -> Weight:
-        """Device copy of a Tl1 / TQ1_0 tensor, shape [in, out] -> (M = out, K = in)."""
+        """Device copy of a Tl1 / TQ1_0 / F16 / BF16 tensor, shape [in, out] -> (M = out, K = in)."""
         err = ctypes.create_string_buffer(512)
         h = ctypes.c_void_p()
         st = self.lib.ouroq_bmts_upload(ctx.ctx, self.handle, name.encode(), ctypes.byref(h), err,
@@ -114,5 +116,5 @@ class BmtsShard:
         if st != 0:
             raise OuroqError(st, err.value.decode())
         t = next(t for t in self.tensors if t.name == name)
-        fmt = PTQ1_0 if t.dtype == DTYPE_TL1 else TQ1_0
+        fmt = {DTYPE_TL1: PTQ1_0, DTYPE_TQ1_0: TQ1_0, DTYPE_F16: F16, DTYPE_BF16: BF16}[t.dtype]
         return Weight(ctx, h.value, fmt, int(t.shape[1]), int(t.shape[0]))

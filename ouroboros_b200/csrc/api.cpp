@@ -56,6 +56,8 @@ struct ouroq_ctx {
   size_t attn_cap = 0;
   unsigned* attn_ctr = nullptr;  // zeroed on allocation; each launch leaves it zero
   size_t attn_ctr_cap = 0;
+  unsigned long long* head_key = nullptr;  // argmax keys [B] + 1 counter word,
+  size_t head_key_cap = 0;                 // zeroed on allocation, left zero
   // row-sharded group (NCCL communicator, opaque here)
   void* comm = nullptr;
   int shard_world = 1, shard_rank = 0;
@@ -253,10 +255,15 @@ ouroq_status quantize_impl(ouroq_ctx* ctx, const float* x, int B, int K, const f
   return OUROQ_OK;
 }
 
-bool is_ref_format(int fmt) { return fmt == OUROQ_FMT_PTQ1_0 || fmt == OUROQ_FMT_TQ1_0; }
+bool is_half_format(int fmt) { return fmt == OUROQ_FMT_F16 || fmt == OUROQ_FMT_BF16; }
+bool is_ref_format(int fmt) {
+  return fmt == OUROQ_FMT_PTQ1_0 || fmt == OUROQ_FMT_TQ1_0 || is_half_format(fmt);
+}
 
-// Bytes of one row of a reference-format payload (dequant.rs:123-130, 50-53).
+// Bytes of one row of a reference-format payload (dequant.rs:123-130, 50-53;
+// 2 bytes per element for F16 / BF16).
 size_t ref_row_bytes(int fmt, int K) {
+  if (is_half_format(fmt)) return (size_t)K * 2;
   return fmt == OUROQ_FMT_PTQ1_0 ? (size_t)K / 128 * 28 : (size_t)K / 256 * 54;
 }
 
@@ -264,6 +271,7 @@ ouroq_status check_weight_shape(ouroq_ctx* ctx, ouroq_format fmt, int M, int K) 
   if (fmt != OUROQ_FMT_TERNARY2 && fmt != OUROQ_FMT_SIGN1G128 && !is_ref_format(fmt))
     return fail(ctx, OUROQ_ERR_BAD_ARG, "unknown format %d", (int)fmt);
   if (M <= 0 || K <= 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "M=%d K=%d", M, K);
+  if (is_half_format(fmt)) return OUROQ_OK;
   if (K % 128) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "K=%d not a multiple of 128", K);
   if (fmt == OUROQ_FMT_TQ1_0 && K % 256)
     return fail(ctx, OUROQ_ERR_BAD_SHAPE, "TQ1_0: K=%d not a multiple of 256", K);
@@ -301,6 +309,23 @@ ouroq_status upload_ref(ouroq_ctx* ctx, ouroq_format fmt, const void* packed, in
 // fp32 x [B][K] -> y [B][M] for the reference formats (no quantisation).
 ouroq_status ref_matvec(ouroq_ctx* ctx, const ouroq_weight* w, const float* x, int B, float* y,
                         cudaStream_t s) {
+  if (is_half_format(w->fmt)) {
+    if ((size_t)B > 65535 * 8) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d too large", B);
+    HeadLaunch L{};
+    L.w = reinterpret_cast<const uint16_t*>(w->w);
+    L.x = x;
+    L.y = y;
+    L.M = w->M;
+    L.K = w->K;
+    L.B = B;
+    L.ldy = w->M;
+    L.bf16 = w->fmt == OUROQ_FMT_BF16;
+    L.vec = w->K % 8 == 0 && aligned16(w->w) && aligned16(x);
+    L.num_sms = ctx->num_sms;
+    CU(ctx, launch_head(L, s, ctx->pdl), "16-bit matvec launch");
+    ctx->launches++;
+    return OUROQ_OK;
+  }
   RefLaunch P{};
   P.fmt = w->fmt == OUROQ_FMT_PTQ1_0 ? kPtq1 : kTq1;
   P.w = w->w;
@@ -649,6 +674,7 @@ ouroq_status ouroq_ctx_destroy(ouroq_ctx* ctx) {
   cudaFree(ctx->rot_scratch);
   cudaFree(ctx->attn_part);
   cudaFree(ctx->attn_ctr);
+  cudaFree(ctx->head_key);
   shard_release(ctx);
   delete ctx;
   return OUROQ_OK;
@@ -911,9 +937,12 @@ ouroq_status ouroq_gemm_f32act(ouroq_ctx* ctx, const ouroq_weight* w, const floa
   if (B < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d", B);
   if (B == 0) return OUROQ_OK;
   if (!x || !y) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
-  ouroq_status st = check_quant_args(ctx, B, w->K, hadamard_block);
+  // 16-bit weights read x element by element and need neither the
+  // quantiser's shape rules nor alignment, unless x is rotated first
+  const bool plain_half = is_half_format(w->fmt) && hadamard_block == 0;
+  ouroq_status st = plain_half ? OUROQ_OK : check_quant_args(ctx, B, w->K, hadamard_block);
   if (st != OUROQ_OK) return st;
-  if (!aligned16(x)) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "x not 16-byte aligned");
+  if (!plain_half && !aligned16(x)) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "x not 16-byte aligned");
   DeviceGuard g(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (is_ref_format(w->fmt)) {
@@ -984,6 +1013,10 @@ ouroq_status ouroq_gemm_f32act_noalloc(ouroq_ctx* ctx, const ouroq_weight* w, co
   if (B < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d", B);
   if (B == 0) return OUROQ_OK;
   if (!x || !y) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
+  if (is_half_format(w->fmt) && hadamard_block == 0) {
+    DeviceGuard g(ctx->device);  // no quantisation, no scratch
+    return ref_matvec(ctx, w, x, B, y, static_cast<cudaStream_t>(stream));
+  }
   ouroq_status st = check_quant_args(ctx, B, w->K, hadamard_block);
   if (st != OUROQ_OK) return st;
   if (!aligned16(x)) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "x not 16-byte aligned");
@@ -1408,6 +1441,43 @@ ouroq_status ouroq_rope_attention_decode(ouroq_ctx* ctx, const float* q, const f
   P.tmax = tmax;
   P.rope_base = rope_base;
   return attention_common(ctx, P, true, stream);
+}
+
+ouroq_status ouroq_argmax_token(ouroq_ctx* ctx, const ouroq_weight* w, const float* x, int B,
+                                float* logits, int64_t* tokens, void* stream) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  if (!w || !x || !tokens) return fail(ctx, OUROQ_ERR_BAD_ARG, "null argument");
+  if (!is_half_format(w->fmt))
+    return fail(ctx, OUROQ_ERR_UNSUPPORTED, "argmax_token needs an F16 or BF16 head (format %d)",
+                (int)w->fmt);
+  if (B < 0 || (size_t)B > 65535 * 8) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d", B);
+  if (B == 0) return OUROQ_OK;
+  DeviceGuard g(ctx->device);
+  const size_t need = (size_t)B + 1;  // keys, then the CTA counter
+  if (need > ctx->head_key_cap) {
+    ouroq_status st = grow(ctx, ctx->head_key, ctx->head_key_cap, need, "argmax scratch");
+    if (st != OUROQ_OK) return st;
+    CU(ctx, cudaMemset(ctx->head_key, 0, ctx->head_key_cap * sizeof(unsigned long long)),
+       "argmax scratch");
+  }
+  HeadLaunch L{};
+  L.w = reinterpret_cast<const uint16_t*>(w->w);
+  L.x = x;
+  L.y = logits;
+  L.M = w->M;
+  L.K = w->K;
+  L.B = B;
+  L.ldy = w->M;
+  L.bf16 = w->fmt == OUROQ_FMT_BF16;
+  L.vec = w->K % 8 == 0 && aligned16(w->w) && aligned16(x);
+  L.num_sms = ctx->num_sms;
+  // the counter word sits after the keys of the largest B seen so far
+  L.key = ctx->head_key;
+  L.counter = reinterpret_cast<unsigned*>(ctx->head_key + ctx->head_key_cap - 1);
+  L.tokens = reinterpret_cast<long long*>(tokens);
+  CU(ctx, launch_head(L, static_cast<cudaStream_t>(stream), ctx->pdl), "argmax_token launch");
+  ctx->launches++;
+  return OUROQ_OK;
 }
 
 }  // extern "C"

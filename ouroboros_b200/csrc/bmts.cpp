@@ -45,6 +45,8 @@ constexpr uint16_t kBmtsVersion = 1;
 constexpr size_t kBmtsHeaderLen = 16;
 constexpr uint32_t kDtypeTq1 = 34;   // QuantKind::Tq1_0 (dequant.rs:344)
 constexpr uint32_t kDtypeTl1 = 143;  // QuantKind::Tl1 (dequant.rs:345)
+constexpr uint32_t kDtypeF16 = 1;    // QuantKind::F16 (dequant.rs:337)
+constexpr uint32_t kDtypeBf16 = 30;  // QuantKind::Bf16 (dequant.rs:338)
 
 void set_err(char* err, size_t len, const char* fmt, ...) {
   if (!err || !len) return;
@@ -396,8 +398,13 @@ ouroq_status ouroq_bmts_upload(ouroq_ctx* ctx, const ouroq_bmts* f, const char* 
     fmt = OUROQ_FMT_PTQ1_0;
   } else if (t->dtype == kDtypeTq1) {
     fmt = OUROQ_FMT_TQ1_0;
+  } else if (t->dtype == kDtypeF16) {
+    fmt = OUROQ_FMT_F16;
+  } else if (t->dtype == kDtypeBf16) {
+    fmt = OUROQ_FMT_BF16;
   } else {
-    set_err(err, err_len, "tensor %s: dtype %u is not a ternary matmul format (34 TQ1_0, 143 Tl1)",
+    set_err(err, err_len,
+            "tensor %s: dtype %u is not a matmul format here (1 F16, 30 BF16, 34 TQ1_0, 143 Tl1)",
             name, t->dtype);
     return OUROQ_ERR_UNSUPPORTED;
   }
@@ -408,7 +415,9 @@ ouroq_status ouroq_bmts_upload(ouroq_ctx* ctx, const ouroq_bmts* f, const char* 
     return OUROQ_ERR_BAD_SHAPE;
   }
   const int K = (int)t->shape[0], M = (int)t->shape[1];
-  const uint64_t rb = fmt == OUROQ_FMT_PTQ1_0 ? (uint64_t)K / 128 * 28 : (uint64_t)K / 256 * 54;
+  const uint64_t rb = fmt == OUROQ_FMT_PTQ1_0 ? (uint64_t)K / 128 * 28
+                      : fmt == OUROQ_FMT_TQ1_0 ? (uint64_t)K / 256 * 54
+                                               : (uint64_t)K * 2;
   if (rb * (uint64_t)M != t->length) {
     set_err(err, err_len, "tensor %s: %llu bytes, %d x %d needs %llu", name,
             (unsigned long long)t->length, M, K, (unsigned long long)(rb * (uint64_t)M));

@@ -148,6 +148,23 @@ int tl1_rows_per_cta(int K, int M, int num_sms);
 size_t tq1_smem_bytes(int K);
 cudaError_t launch_refmt_matvec(const RefLaunch& P, int num_sms, cudaStream_t s);
 
+// 16-bit weights (F16 / BF16 shards, the tied lm_head): fp32 x [B][K] ->
+// y [B][ldy] in the reference's per-row order; with tokens set, also the
+// finite argmax of each sequence's logits (y may then be null).
+struct HeadLaunch {
+  const uint16_t* w;          // [M][K] as stored in the shard
+  const float* x;
+  float* y;                   // optional when tokens is set
+  int M, K, B, ldy;
+  int bf16;                   // 0: f16, 1: bf16
+  int vec;                    // K % 8 == 0, w and x 16-byte aligned
+  int num_sms;
+  unsigned long long* key;    // [B] argmax keys, zero between launches
+  unsigned* counter;          // CTAs finished, zero between launches
+  long long* tokens;          // [B] or null (no argmax)
+};
+cudaError_t launch_head(const HeadLaunch& L, cudaStream_t s, bool pdl);
+
 // Limits of the small-batch GEMV path.
 constexpr int kGemvMaxB = 8;
 // Above this batch the fp32-activation entry points quantise once in a separate

@@ -12,8 +12,8 @@ The layer follows the reference's run_layer (cluster/src/infer/mod.rs:298-336):
     s  = rmsnorm(silu(W_gate f) * (W_up f), ffn_sub_norm)   (ternary gate/up)
     x' = h1 + W_down s                                  (ternary)
 
-then the output norm and the tied embedding as the lm_head (f16), greedy
-next token. Configuration defaults of ArchConfig (mod.rs:45-55): hidden 2560,
+then the output norm and the tied embedding as the lm_head (an F16 weight),
+greedy next token (finite_argmax, fused into the lm_head launch). Configuration defaults of ArchConfig (mod.rs:45-55): hidden 2560,
 20 heads / 5 KV heads of 128, FFN 6912, eps 1e-5, RoPE base 500000.
 
 Every ternary projection runs through the C ABI (the path this library
@@ -22,7 +22,7 @@ rebuilds). The ops around it run either as this library's fused kernels
 KV append + split-sequence GQA attention in one launch -- ouroq_rmsnorm,
 ouroq_swiglu_rmsnorm, ouroq_rope_attention_decode) or as plain torch operations
 (`fused=False`, the unfused host path kept as a cross-check). fp32 throughout
-like the reference, KV cache included; the lm_head is a torch f16 product. A
+like the reference, KV cache included. A
 decode step has static shapes -- the position lives in a device tensor -- so it
 is captured as one CUDA graph. Weights are random (synthetic).
 """
@@ -72,6 +72,8 @@ class Decoder:
                 "ffn_norm": gain(HIDDEN), "ffn_sub_norm": gain(FFN),
             })
         self.tok_embd = (0.02 * torch.randn((vocab, HIDDEN), generator=g, device=dev)).half()
+        # the tied lm_head: token_embd as an F16 weight (the shard's dtype 1)
+        self.head = ctx.upload_device(oq.F16, self.tok_embd, vocab, HIDDEN)
         self.output_norm = gain(HIDDEN)
         B, T = batch, self.tmax
         # KV cache [layer][B, kv_head, T, dim], the first `context` positions filled
@@ -181,17 +183,17 @@ class Decoder:
             self.buf["x"].copy_(x)
             for li in range(self.L):
                 self.layer_fused(li, li == 0)
-            xo = self.buf["x"]  # scratch for the final residual sum
-            h = self.ctx.rmsnorm(self.buf["h1"], self.output_norm, residual=self.buf["down"], h=xo,
-                                 stream=self.stream)
+            xo = self.buf["x"]  # the final residual sum
+            h = self.ctx.rmsnorm(self.buf["h1"], self.output_norm, y=self.buf["a"],
+                                 residual=self.buf["down"], h=xo, stream=self.stream)
             x = xo
         else:
             for li in range(self.L):
                 x = self.layer(li, x)
             h = self.rmsnorm(x, self.output_norm)
         if self.lm_head:
-            logits = h.half() @ self.tok_embd.t()
-            self.tokens.copy_(logits.argmax(-1))
+            # tied lm_head + finite_argmax in one launch (mod.rs:190-194)
+            self.ctx.argmax_token(self.head, h, tokens=self.tokens, stream=self.stream)
         self.pos.add_(1)
         return x
 
@@ -232,3 +234,4 @@ class Decoder:
         for L in self.layers:
             for n in ("q", "k", "v", "o", "gate", "up", "down"):
                 L[n].free()
+        self.head.free()

@@ -7,7 +7,9 @@ inputs and tolerance, and runs it against oracle/oracle.c:
   dequant.rs:564-603   PTQ1_0 group decode vs an independent transcription
   dequant.rs:608-664   PTQ1_0 round trip vs the transcribed C quantiser (64 LCG groups)
   dequant.rs:667-677   PTQ1_0 trits in range
+  dequant.rs:680-690   bf16 known values
   dequant.rs:693-702   f16 known values (incl. subnormal)
+  ops.rs:782-798       F16 matmul_q == K x matvec_f16 (its payload restated)
   dequant.rs:705-726   TQ1_0 zero block and value set
   ops.rs:721-750       matmul_tl1 K=4 == K x matvec_tl1
   ops.rs:801-838       fused matvec_tl1 == decode-then-dot
@@ -207,6 +209,75 @@ def test_f16_decode_matches_numpy_for_all_finite_patterns(oracle):
     r = ref[::97]
     fin = np.isfinite(r)
     assert np.array_equal(got[fin], r[fin])
+
+
+def test_bf16_known_values(oracle):
+    # dequant.rs:680-690
+    f = oracle.bf16_to_f32
+    assert f(0x0000) == 0.0
+    assert f(0x3F80) == 1.0
+    assert f(0xBF80) == -1.0
+    assert f(0x7F80) == math.inf
+    assert f(0x4000) == 2.0
+    assert abs(np.float32(f(0x3EAA)) - np.float32(0.33203125)) < np.float32(1e-6)
+
+
+def _matvec_half_loop(payload, out_len, in_len, x, bf16):
+    """matvec_f16 / matvec_bf16 (ops.rs:131-153, 600-620) as plain float32
+    steps: s = s + w * x, the product and the sum rounded separately."""
+    bits = np.ascontiguousarray(payload).view(np.uint16).reshape(out_len, in_len)
+    if bf16:
+        w = (bits.astype(np.uint32) << 16).view(np.float32)
+    else:
+        w = bits.view(np.float16).astype(np.float32)
+    y = np.zeros(out_len, np.float32)
+    for r in range(out_len):
+        s = np.float32(0.0)
+        for i in range(in_len):
+            s = np.float32(s + np.float32(w[r, i] * np.float32(x[i])))
+        y[r] = s
+    return y
+
+
+def matmul_fallback_payload(out_len, in_len):
+    """ops.rs:785-790: the low two bytes of ((i % 17) - 8) * 0.25 as f32."""
+    v = ((np.arange(out_len * in_len) % 17).astype(np.float32) - 8.0) * np.float32(0.25)
+    return (v.view(np.uint32) & 0xFFFF).astype(np.uint16)
+
+
+def test_matmul_q_fallback_payload(oracle):
+    # ops.rs:782-798: x[i] = (i % 7) * 0.5 over two columns; each column is matvec_f16
+    out_len, in_len = 16, 32
+    payload = matmul_fallback_payload(out_len, in_len)
+    x = ((np.arange(2 * in_len) % 7) * 0.5).astype(np.float32)
+    for c in range(2):
+        xc = x[c * in_len:(c + 1) * in_len]
+        got = oracle.matvec_half(payload, out_len, in_len, xc)
+        assert np.array_equal(got, _matvec_half_loop(payload, out_len, in_len, xc, False))
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+def test_matvec_half_matches_loop(oracle, bf16):
+    out_len, in_len = 23, 70
+    payload = oracle.lcg_bytes(7 + bf16, out_len * in_len * 2).view(np.uint16).copy()
+    # keep exponents tame so the chain stays finite (no NaN or inf patterns)
+    payload = (payload & 0x807F) | 0x3F00 if bf16 else (payload & 0x83FF) | 0x3800
+    x = oracle.normals(9, in_len)
+    got = oracle.matvec_half(payload, out_len, in_len, x, bf16=bf16)
+    want = _matvec_half_loop(payload, out_len, in_len, x, bf16)
+    assert np.array_equal(got, want)
+
+
+def test_finite_argmax_rules(oracle):
+    # infer/mod.rs:70-83: NaN skipped, first maximum wins, 0 if all NaN
+    nan, inf = float("nan"), float("inf")
+    assert oracle.finite_argmax([1.0, 3.0, 2.0, 3.0]) == 1
+    assert oracle.finite_argmax([nan, 0.5, nan, 0.7]) == 3
+    assert oracle.finite_argmax([nan, nan, nan]) == 0
+    assert oracle.finite_argmax([-inf, -inf]) == 0
+    assert oracle.finite_argmax([-0.0, 0.0]) == 0
+    assert oracle.finite_argmax([0.0, -0.0, -1.0]) == 0
+    assert oracle.finite_argmax([-2.0, nan, inf, inf]) == 2
 
 
 def test_tq1_values_are_ternary_scaled(oracle):
