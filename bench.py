@@ -98,6 +98,8 @@ def parse():
                     help="how --shard moves rows between ranks")
     ap.add_argument("--tokens", type=int, default=256,
                     help="decode workload: tokens generated per sequence in the timed region")
+    ap.add_argument("--layers", type=int, default=30,
+                    help="decode workload: layers (30 = BitNet-2B; fewer only to profile a small case)")
     return ap.parse_args()
 
 
@@ -635,7 +637,8 @@ def run_decode(args, rank, world, local_rank):
     torch.cuda.set_device(device)
     ctx = oq.Context(local_rank)
     B, gen = args.batch, args.tokens
-    dec = Decoder(ctx, batch=B, context=1024, generate=gen, device=device, seed=17 + rank)
+    dec = Decoder(ctx, layers=args.layers, batch=B, context=1024, generate=gen, device=device,
+                  seed=17 + rank)
     n0 = ctx.launch_count()
     g_full = dec.capture(dec.step)  # two eager steps, then the captured one
     launches_per_token = (ctx.launch_count() - n0) / 3
@@ -673,7 +676,7 @@ def run_decode(args, rank, world, local_rank):
     tok_s = B * world * gen / (ms_full / 1e3)
     tok_s_body = B * world * gen / (ms_body / 1e3)
     # ternary weight bytes streamed per token step (all 30 layers)
-    tern_bytes = 30 * (2 * 2560 * 2560 + 2 * 640 * 2560 + 3 * 6912 * 2560) // 4
+    tern_bytes = args.layers * (2 * 2560 * 2560 + 2 * 640 * 2560 + 3 * 6912 * 2560) // 4
     achieved = tern_bytes / (ms_tern / 1e3 / gen) / 1e9
     hbm_peak, _, peak_kind = peaks()
 
@@ -715,8 +718,9 @@ def run_decode(args, rank, world, local_rank):
             "ms_per_step": round(ms_full / gen, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (random init BitNet-2B-class weights, random 1024-token KV context)",
-            "config": {"workload": f"bitnet2b-decode-b{B}-ctx1024-gen256", "batch": B,
-                       "layers": 30, "hidden": 2560, "heads": "20/5x128", "ffn": 6912,
+            "config": {"workload": f"bitnet2b-decode-b{B}-ctx1024-gen{gen}"
+                                   + ("" if args.layers == 30 else f"-{args.layers}layers"),
+                       "batch": B, "layers": args.layers, "hidden": 2560, "heads": "20/5x128", "ffn": 6912,
                        "vocab": 128256, "kv": "fp32", "parallelism": f"replicas x{world}",
                        "launch": "one CUDA graph per decode step"},
             "tokens_per_s_without_lm_head": round(tok_s_body, 2),
@@ -724,7 +728,7 @@ def run_decode(args, rank, world, local_rank):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
                          "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                          "peak_kind": f"{peak_kind} (hbm_gbs)", "traffic": None,
-                         "kernel": "ternary projections of one decode step (30 layers)",
+                         "kernel": f"ternary projections of one decode step ({args.layers} layers)",
                          "bytes_per_step": tern_bytes},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8 * B,

@@ -1378,10 +1378,10 @@ static ouroq_status attention_common(ouroq_ctx* ctx, DecodeAttn& P, bool rope, v
     return fail(ctx, OUROQ_ERR_BAD_ALIGN, "attention buffers not 16-byte aligned");
   DeviceGuard g(ctx->device);
   P.status = ctx->d_status;
-  P.splits = attn_splits(P.B, P.n_kv, P.tmax, ctx->num_sms);
+  P.splits = attn_splits(P.B, P.n_head, P.n_kv, P.tmax, ctx->num_sms);
   P.scale = 1.0f / std::sqrt(128.0f);
   ouroq_status st = grow(ctx, ctx->attn_part, ctx->attn_cap,
-                         attn_part_floats(P.B, P.n_head, P.splits), "attention partials");
+                         attn_part_floats(P.B, P.n_head, P.n_kv, P.splits), "attention partials");
   if (st != OUROQ_OK) return st;
   const size_t nctr = (size_t)P.B * P.n_kv;
   if (nctr > ctx->attn_ctr_cap) {

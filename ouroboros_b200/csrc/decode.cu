@@ -24,7 +24,6 @@ namespace {
 
 constexpr int kNormThreads = 256;
 constexpr int kHeadDim = 128;
-constexpr int kMaxGroup = 8;  // query heads per KV head
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
   v = warp_sum_f(v);
@@ -230,53 +229,90 @@ __global__ void rope_append_kernel(DecodeAttn P) {
 
 // ---- decode attention: one launch per layer ----
 //
-// grid (B, n_kv, S), block (G + 1) warps, G = n_head / n_kv query heads per
-// KV head. The CTA takes cache positions [t0, t1) of the causal range
-// [0, pos], cut into S equal slices from the device-side position. Warp G
-// (one lane) streams the slice's K and V rows into a ring of shared-memory
-// stages with bulk copies; warp g < G serves query head g. Per stage a lane
-// scores one position against the head's query (rows read at a rotated
-// float4 offset, so the 8 lanes of each shared-memory phase hit distinct
-// banks), the warp updates its online softmax (running max m, sum l), and
-// then lane l accumulates dims 4l..4l+3 of P.V. The slice's (m, l, acc) goes
-// to a partial record; the last CTA of the (sequence, KV head) to finish --
-// counted with an atomic -- merges the S records into the output and resets
-// the counter for the next launch.
+// grid (B, n_kv, S), block NW + 1 warps, where G = n_head / n_kv query heads
+// share a KV head, kG is G rounded up to a power of two (lanes of heads >= G
+// idle) and NW = 2 kG compute warps (kG for kG = 8). The CTA takes cache positions [t0, t1) of the causal range
+// [0, pos], cut into S equal slices from the device-side position. The last
+// warp (one lane) streams the slice in stages of 32 positions: K by a 2-D
+// tensor copy in four 32 x 32 boxes with the 128-byte swizzle (16-byte unit
+// u of row r lands at u ^ (r & 7)), V by a plain bulk copy.
 //
-// kRope: q and k arrive un-rotated; every CTA rotates its G query heads, and
-// the CTA whose slice holds pos rotates k and writes k and v to the cache at
-// pos. That CTA's staged copy of row pos may predate the write, so it scores
-// the new key from registers and substitutes the new value row in P.V.
-constexpr int kAttnP = 32;  // cache positions per stage
-constexpr int kAttnStages = 3;
-constexpr int kAttnRec = 132;  // floats per partial record: m, l, 2 unused, acc[128]
-constexpr int kAttnMaxSplits = 64;
+// Compute warp w takes positions w*PW .. w*PW + PW - 1 of every stage for all
+// heads at once: in the scores lane (g, p, h) forms half h of the 128-dim dot
+// of head g's query with row p (the whole dot when kG = 8), the halves added
+// with one shuffle. Lanes of one row read the same K address and lanes of one
+// head the same query address (query rows padded to 528 bytes, K swizzled,
+// the two halves a bank group apart), so each step reads one 128-byte
+// wavefront of each. For G = 4 that is 8 compute warps of 4 positions. Each head keeps an online softmax (max m,
+// sum l) over the warp's positions in its PW lanes; then every lane adds
+// dims 4l..4l+3 of P.V for all heads, V read once per warp with the
+// probabilities shuffled across. Each (warp, head) leaves one partial record
+// (m, l, acc); the last CTA of the (sequence, KV head) to finish -- counted
+// with an atomic -- merges the S * NW records of each head into the output
+// and resets the counter for the next launch.
+//
+// kRope: q and k arrive un-rotated; the CTA rotates its queries, and the CTA
+// whose slice holds pos rotates k and writes k and v to the cache at pos.
+// Its staged copy of row pos may predate that write, so the new row's score
+// and values are taken from registers instead.
+constexpr int kAttnP = 32;       // cache positions per stage
+constexpr int kAttnStages = 2;   // ~70 KB a CTA: three CTAs share an SM
+constexpr int kAttnRec = 132;    // floats per partial record: m, l, 2 unused, acc[128]
+constexpr int kAttnMaxRecs = 128;  // records per head: slices x compute warps
+constexpr int kAttnMaxG = 8;
+constexpr int kQPitch = kHeadDim + 4;  // floats: 528-byte query rows
+constexpr size_t kAttnKStage = (size_t)kAttnP * kHeadDim * sizeof(float);  // 16 KB
+constexpr size_t kAttnVStage = kAttnKStage;
 
-struct AttnShared {
-  float ring[kAttnStages][2][kAttnP][kHeadDim];  // K rows then V rows, 32 KB a stage
-  float q[kMaxGroup][kHeadDim];
-  float p[kMaxGroup][kAttnP];
+struct AttnTail {
+  float q[kAttnMaxG][kQPitch];
   uint64_t full[kAttnStages];
   uint64_t empty[kAttnStages];
+  uint64_t qready;
   int issued;
   int last;
 };
-// the merge's scratch reuses the ring once every stage is drained
-static_assert(kAttnMaxSplits * kMaxGroup * sizeof(float) <= sizeof(float) * kAttnP * kHeadDim,
-              "merge weights fit in one stage");
+// the stages (1024-byte aligned for the swizzled copies), then the tail;
+// +1024 for the alignment of the dynamic shared memory base
+constexpr size_t kAttnSmem = kAttnStages * (kAttnKStage + kAttnVStage) + sizeof(AttnTail) + 1024;
+// the merge weights reuse the V stages once every copy has landed
+static_assert(kAttnMaxRecs * kAttnMaxG * sizeof(float) <= kAttnStages * kAttnVStage,
+              "merge weights fit in the V stages");
 
-template <bool kRope>
-__global__ void __launch_bounds__((kMaxGroup + 1) * 32) attn_decode_kernel(DecodeAttn P) {
-  extern __shared__ __align__(128) unsigned char attn_smem[];
-  AttnShared& S = *reinterpret_cast<AttnShared*>(attn_smem);
+__host__ __device__ constexpr int attn_kg(int G) { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; }
+
+// lanes per dot product
+// (splitting a dot over two lanes doubles the warps but needs registers
+// beyond the three-CTAs-per-SM budget; one lane per dot measured faster)
+__host__ __device__ constexpr int attn_ds(int) { return 1; }
+__host__ __device__ constexpr int attn_nw(int kG) { return kG * attn_ds(kG); }
+
+template <bool kRope, int kG>
+__global__ void __launch_bounds__((attn_nw(kG) + 1) * 32, 3)
+    attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, DecodeAttn P) {
+  extern __shared__ __align__(16) unsigned char attn_smem[];
+  constexpr int kDS = attn_ds(kG);         // lanes per dot product
+  constexpr int NW = attn_nw(kG);          // compute warps
+  constexpr int PW = kAttnP / NW;          // positions per compute warp per stage
+  constexpr int kGL = PW * kDS;            // lanes per head in the score layout
+  constexpr int kUnits = kHeadDim / 4 / kDS;  // float4 units per lane per dot
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(attn_smem) + 1023) & ~uintptr_t(1023));
+  float* kst = reinterpret_cast<float*>(base);
+  float* vst = reinterpret_cast<float*>(base + kAttnStages * kAttnKStage);
+  AttnTail& S = *reinterpret_cast<AttnTail*>(base + kAttnStages * (kAttnKStage + kAttnVStage));
   const int b = blockIdx.x, kh = blockIdx.y, sidx = blockIdx.z;
   const int G = P.n_head / P.n_kv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_launch_dependents();
-  pdl_wait();
+  // The position and the cache rows before it were written by earlier decode
+  // steps, which completed before this step's first kernel started (the step
+  // begins with ordinary launches), so they are read before the wait for the
+  // previous kernel; q, k, v and every write come after it.
   const long long pos = *P.pos;
   float* out = P.out + ((size_t)b * P.n_head + (size_t)kh * G) * kHeadDim;
   if (pos < 0 || pos >= P.tmax) {
+    pdl_wait();
     if (threadIdx.x == 0 && kh == 0 && sidx == 0) atomicExch(P.status, kDevBadPosition);
     if (sidx == 0)
       for (int i = threadIdx.x; i < G * kHeadDim; i += blockDim.x) out[i] = 0.0f;
@@ -289,20 +325,20 @@ __global__ void __launch_bounds__((kMaxGroup + 1) * 32) attn_decode_kernel(Decod
   const int n = t1 - t0;
   const int nchunks = (n + kAttnP - 1) / kAttnP;
   const int pos_chunk = (kRope && pos >= t0 && pos < t1) ? (int)(pos - t0) / kAttnP : -1;
-  const size_t head_off = ((size_t)b * P.n_kv + kh) * P.tmax * kHeadDim;
-  const float* kbase = P.kcache + head_off;
-  const float* vbase = P.vcache + head_off;
+  const size_t head_row = ((size_t)b * P.n_kv + kh) * P.tmax;  // first cache row of this head
+  const float* vbase = P.vcache + head_row * kHeadDim;
   if (threadIdx.x == 0) {
     for (int st = 0; st < kAttnStages; ++st) {
       mbar_init(&S.full[st], 1);
-      mbar_init(&S.empty[st], G);
+      mbar_init(&S.empty[st], NW);
     }
+    mbar_init(&S.qready, NW);
     S.issued = 0;
     fence_mbar_init();
   }
   __syncthreads();
 
-  if (warp == G) {
+  if (warp == NW) {
     if (lane == 0) {
       int c = 0;
       for (; c < nchunks; ++c) {
@@ -310,27 +346,34 @@ __global__ void __launch_bounds__((kMaxGroup + 1) * 32) attn_decode_kernel(Decod
         if (c >= kAttnStages && !mbar_wait(&S.empty[st], ((c / kAttnStages) - 1) & 1, P.status))
           break;
         const int rows = min(kAttnP, n - c * kAttnP);
-        const uint32_t bytes = (uint32_t)rows * kHeadDim * sizeof(float);
-        const size_t at = (size_t)(t0 + c * kAttnP) * kHeadDim;
-        mbar_arrive_expect_tx(&S.full[st], 2 * bytes);
-        bulk_g2s(&S.ring[st][0][0][0], kbase + at, bytes, &S.full[st]);
-        bulk_g2s(&S.ring[st][1][0][0], vbase + at, bytes, &S.full[st]);
+        const int r0 = t0 + c * kAttnP;
+        mbar_arrive_expect_tx(&S.full[st], (uint32_t)kAttnKStage + (uint32_t)rows * kHeadDim * 4u);
+#pragma unroll
+        for (int db = 0; db < kHeadDim / 32; ++db)  // whole boxes; rows past the slice are unused
+          tma_load_2d(kst + (size_t)st * kAttnP * kHeadDim + db * kAttnP * 32, &kmap, db * 32,
+                      (int)(head_row + r0), &S.full[st]);
+        bulk_g2s(vst + (size_t)st * kAttnP * kHeadDim, vbase + (size_t)r0 * kHeadDim,
+                 (uint32_t)rows * kHeadDim * 4u, &S.full[st]);
       }
       S.issued = c;
     }
   } else {
-    const int g = warp;
-    const float* qg = P.q + ((size_t)b * P.n_head + (size_t)kh * G + g) * kHeadDim;
-    if (kRope) {
-      for (int i = lane; i < 64; i += 32) {
-        float c, s;
-        rope_cs(pos, i, P.rope_base, c, s);
-        const float x0 = qg[i], x1 = qg[i + 64];
-        S.q[g][i] = x0 * c - x1 * s;
-        S.q[g][i + 64] = x1 * c + x0 * s;
+    pdl_wait();  // q, k, v come from the previous kernel
+    // this CTA's queries, rotated (warp w takes head w)
+    if (warp < G) {
+      const float* qg = P.q + ((size_t)b * P.n_head + (size_t)kh * G + warp) * kHeadDim;
+      float* qw = S.q[warp];
+      if (kRope) {
+        for (int i = lane; i < 64; i += 32) {
+          float c, s;
+          rope_cs(pos, i, P.rope_base, c, s);
+          const float x0 = qg[i], x1 = qg[i + 64];
+          qw[i] = x0 * c - x1 * s;
+          qw[i + 64] = x1 * c + x0 * s;
+        }
+      } else {
+        reinterpret_cast<float4*>(qw)[lane] = reinterpret_cast<const float4*>(qg)[lane];
       }
-    } else {
-      reinterpret_cast<float4*>(S.q[g])[lane] = reinterpret_cast<const float4*>(qg)[lane];
     }
     // the new key and value rows, rotated, for the CTA that holds pos; lane l
     // keeps key dims l, l + 32, l + 64, l + 96 and value dims 4l..4l+3
@@ -347,126 +390,188 @@ __global__ void __launch_bounds__((kMaxGroup + 1) * 32) attn_decode_kernel(Decod
       kr1 = kn[lane + 32] * c - kn[lane + 96] * s;
       kr3 = kn[lane + 96] * c + kn[lane + 32] * s;
       vnew = reinterpret_cast<const float4*>(vn)[lane];
-      if (g == 0) {
-        float* kc = P.kcache + head_off + (size_t)pos * kHeadDim;
+      if (warp == 0) {
+        float* kc = P.kcache + (head_row + pos) * kHeadDim;
         kc[lane] = kr0;
         kc[lane + 32] = kr1;
         kc[lane + 64] = kr2;
         kc[lane + 96] = kr3;
-        reinterpret_cast<float4*>(P.vcache + head_off + (size_t)pos * kHeadDim)[lane] = vnew;
+        reinterpret_cast<float4*>(P.vcache + (head_row + pos) * kHeadDim)[lane] = vnew;
       }
     }
     __syncwarp();
-    // its score, taken here: the staged copy of row pos predates this write
+    if (lane == 0) mbar_arrive(&S.qready);
+    mbar_wait(&S.qready, 0, P.status);
+    const int my_g = lane / kGL;                 // score layout: lane = (g, p, dh)
+    const int p = (lane % kGL) / kDS, dh = lane % kDS;
+    const int row = warp * PW + p;               // this lane's row in every stage
+    // the new key's score for this lane's head, taken from registers: the
+    // staged copy of row pos predates the write above
     float s_new = 0.0f;
     if (pos_chunk >= 0) {
-      const float d = S.q[g][lane] * kr0 + S.q[g][lane + 32] * kr1 + S.q[g][lane + 64] * kr2 +
-                      S.q[g][lane + 96] * kr3;
-      s_new = warp_sum_f(d) * P.scale;
+#pragma unroll
+      for (int g = 0; g < kG; ++g) {
+        if (g < G) {
+          const float* qg = S.q[g];
+          const float d = warp_sum_f(qg[lane] * kr0 + qg[lane + 32] * kr1 + qg[lane + 64] * kr2 +
+                                     qg[lane + 96] * kr3);
+          if (g == my_g) s_new = d * P.scale;
+        }
+      }
     }
+    // swizzled K addresses of this lane's row: unit u of a box at (u ^ (row & 7))
+    const int rsw = row & 7;
+    const float* qrow = S.q[my_g < G ? my_g : 0];
     float m = -INFINITY, l = 0.0f;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    const float4* qr = reinterpret_cast<const float4*>(S.q[g]);
+    float acc[kG][4];
+#pragma unroll
+    for (int g = 0; g < kG; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.0f;
     for (int c = 0; c < nchunks; ++c) {
       const int st = c % kAttnStages;
       if (!mbar_wait(&S.full[st], (c / kAttnStages) & 1, P.status)) break;
       const int rows = min(kAttnP, n - c * kAttnP);
-      float(*Ks)[kHeadDim] = S.ring[st][0];
-      float(*Vs)[kHeadDim] = S.ring[st][1];
       const int rnew = c == pos_chunk ? (int)(pos - t0) - c * kAttnP : -1;
+      const float* kb = kst + (size_t)st * kAttnP * kHeadDim + row * 32;
       float sc = -INFINITY;
-      if (lane < rows) {
-        const float4* kr = reinterpret_cast<const float4*>(Ks[lane]);
+      if (my_g < G && row < rows) {
         float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
 #pragma unroll 8
-        for (int i = 0; i < kHeadDim / 4; ++i) {
-          const int j = (i + lane) & (kHeadDim / 4 - 1);
-          const float4 kk = kr[j], qq = qr[j];
+        for (int i = 0; i < kUnits; ++i) {
+          // the second half-lane walks its units 4 ahead, so the two halves
+          // of a row never read the same bank group
+          const int unit = kDS == 2 ? dh * kUnits + ((i + dh * 4) & (kUnits - 1)) : i;
+          const int db = unit >> 3, u = unit & 7;
+          const float4 kk = *reinterpret_cast<const float4*>(kb + db * kAttnP * 32 + ((u ^ rsw) << 2));
+          const float4 qq = *reinterpret_cast<const float4*>(qrow + unit * 4);
           d0 += qq.x * kk.x;
           d1 += qq.y * kk.y;
           d2 += qq.z * kk.z;
           d3 += qq.w * kk.w;
         }
-        sc = ((d0 + d1) + (d2 + d3)) * P.scale;
-        if (lane == rnew) sc = s_new;
+        sc = (d0 + d1) + (d2 + d3);
       }
-      const float mn = fmaxf(m, warp_max(sc));  // finite: lane 0 holds a position
-      const float corr = expf(m - mn);
-      const float p = lane < rows ? expf(sc - mn) : 0.0f;
-      l = l * corr + warp_sum_f(p);
+      if (kDS == 2) sc += __shfl_xor_sync(0xffffffffu, sc, 1);  // the other half of the dims
+      sc *= P.scale;
+      if (my_g < G && row < rows && row == rnew) sc = s_new;
+      // online softmax of each head over this warp's PW positions (kGL lanes)
+      float mx = sc;
+#pragma unroll
+      for (int o = 1; o < kGL; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mn = fmaxf(m, mx);
+      const float corr = mn == -INFINITY ? 1.0f : expf(m - mn);
+      const float pv = sc == -INFINITY ? 0.0f : expf(sc - mn);
+      float ps = dh == 0 ? pv : 0.0f;
+#pragma unroll
+      for (int o = 1; o < kGL; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      l = l * corr + ps;
       m = mn;
-      S.p[g][lane] = p;
-      __syncwarp();
-      a0 *= corr;
-      a1 *= corr;
-      a2 *= corr;
-      a3 *= corr;
-      const float4* vcol = reinterpret_cast<const float4*>(&Vs[0][0]) + lane;
-#pragma unroll 4
-      for (int t = 0; t < rows; ++t) {
-        const float pt = S.p[g][t];
-        const float4 vv = t == rnew ? vnew : vcol[t * (kHeadDim / 4)];
-        a0 += pt * vv.x;
-        a1 += pt * vv.y;
-        a2 += pt * vv.z;
-        a3 += pt * vv.w;
+      // P.V: lane holds dims 4*lane..4*lane+3 of every head
+#pragma unroll
+      for (int g = 0; g < kG; ++g) {
+        const float cg = __shfl_sync(0xffffffffu, corr, g * kGL);
+        acc[g][0] *= cg;
+        acc[g][1] *= cg;
+        acc[g][2] *= cg;
+        acc[g][3] *= cg;
+      }
+      const float* vb = vst + (size_t)st * kAttnP * kHeadDim + lane * 4;
+#pragma unroll
+      for (int q = 0; q < PW; ++q) {
+        const int r = warp * PW + q;
+        if (r >= rows) break;  // the stage holds only `rows` value rows
+        float4 vv;
+        if (r == rnew)
+          vv = vnew;
+        else
+          vv = *reinterpret_cast<const float4*>(vb + r * kHeadDim);
+#pragma unroll
+        for (int g = 0; g < kG; ++g) {
+          const float pg = __shfl_sync(0xffffffffu, pv, (g * PW + q) * kDS);
+          acc[g][0] += pg * vv.x;
+          acc[g][1] += pg * vv.y;
+          acc[g][2] += pg * vv.z;
+          acc[g][3] += pg * vv.w;
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.empty[st]);
     }
-    float* rec = P.part +
-                 ((((size_t)b * P.n_kv + kh) * P.splits + sidx) * G + g) * (size_t)kAttnRec;
-    if (lane == 0) {
-      rec[0] = m;
-      rec[1] = l;
+    // records [S][NW][G][132]: (m, l) from the head's first lane, acc from all
+    float* recs = P.part + (((size_t)b * P.n_kv + kh) * P.splits + sidx) * NW * G * (size_t)kAttnRec +
+                  (size_t)warp * G * kAttnRec;
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      if (g < G) {
+        float* rec = recs + (size_t)g * kAttnRec;
+        if (lane == g * kGL) {
+          rec[0] = m;
+          rec[1] = l;
+        }
+        reinterpret_cast<float4*>(rec + 4)[lane] =
+            make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+      }
     }
-    reinterpret_cast<float4*>(rec + 4)[lane] = make_float4(a0, a1, a2, a3);
   }
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    // no bulk copy may still be landing when the ring is reused or the CTA
+    // no copy may still be landing when the stages are reused or the CTA
     // exits: wait (bounded) for the last copy issued into each stage
     const int issued = S.issued;
     for (int st = 0; st < kAttnStages && st < issued; ++st) {
       const int c_last = st + ((issued - 1 - st) / kAttnStages) * kAttnStages;
       mbar_wait(&S.full[st], (c_last / kAttnStages) & 1, P.status);
     }
+    // one fence: it is cumulative, so it orders every record write of the CTA
+    // (ordered before it by the barrier) before the count
+    __threadfence();
     const unsigned prev = atomicAdd(&P.counter[(size_t)b * P.n_kv + kh], 1u);
     S.last = prev == (unsigned)P.splits - 1;
+    if (S.last) __threadfence();  // and the other CTAs' records before the reads below
   }
   __syncthreads();
   if (!S.last) return;
-  __threadfence();
-  // merge: out_g = sum_s acc_sg e^(m_sg - M_g) / sum_s l_sg e^(m_sg - M_g);
-  // warp g reduces head g's S (m, l) pairs, lane s taking slices s, s + 32
-  float* sm_e = &S.ring[0][0][0][0];  // [S][G] merge weights
-  const float* recs =
-      P.part + (((size_t)b * P.n_kv + kh) * P.splits) * G * (size_t)kAttnRec;
+  // merge: out_g = sum_j acc_j e^(m_j - M) / sum_j l_j e^(m_j - M) over the
+  // NR = S*NW records j of head g; warp g takes head g, lanes stride the records
+  const int NR = P.splits * NW;
+  float* sm_e = vst;  // [NR][G] merge weights
+  const float* hrecs = P.part + (((size_t)b * P.n_kv + kh) * P.splits) * NW * G * (size_t)kAttnRec;
   if (warp < G) {
     const int g = warp;
-    const bool h0 = lane < P.splits, h1 = lane + 32 < P.splits;
-    const float* r0 = recs + ((size_t)lane * G + g) * kAttnRec;
-    const float* r1 = recs + ((size_t)(lane + 32) * G + g) * kAttnRec;
-    const float m0 = h0 ? __ldcg(r0) : -INFINITY, l0 = h0 ? __ldcg(r0 + 1) : 0.0f;
-    const float m1 = h1 ? __ldcg(r1) : -INFINITY, l1 = h1 ? __ldcg(r1 + 1) : 0.0f;
-    const float M = warp_max(fmaxf(m0, m1));  // finite: slice 0 is never empty
-    const float e0 = m0 == -INFINITY ? 0.0f : expf(m0 - M);
-    const float e1 = m1 == -INFINITY ? 0.0f : expf(m1 - M);
-    const float L = warp_sum_f(l0 * e0 + l1 * e1);
+    constexpr int kPer = kAttnMaxRecs / 32;
+    float mj[kPer], lj[kPer];
+    float M = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      const int j = lane + 32 * q;
+      const float* r = hrecs + ((size_t)j * G + g) * kAttnRec;
+      mj[q] = j < NR ? __ldcg(r) : -INFINITY;
+      lj[q] = j < NR ? __ldcg(r + 1) : 0.0f;
+      M = fmaxf(M, mj[q]);
+    }
+    M = warp_max(M);  // finite: the first record holds position 0
+    float L = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      mj[q] = mj[q] == -INFINITY ? 0.0f : expf(mj[q] - M);
+      L += lj[q] * mj[q];
+    }
+    L = warp_sum_f(L);
     const float invL = L > 0.0f ? 1.0f / L : 0.0f;
-    if (h0) sm_e[lane * G + g] = e0 * invL;
-    if (h1) sm_e[(lane + 32) * G + g] = e1 * invL;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      const int j = lane + 32 * q;
+      if (j < NR) sm_e[j * G + g] = mj[q] * invL;
+    }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < G * (kHeadDim / 4); i += blockDim.x) {
     const int g = i / (kHeadDim / 4), c4 = i % (kHeadDim / 4);
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 16
-    for (int s = 0; s < P.splits; ++s) {
-      const float e = sm_e[s * G + g];
+    for (int j = 0; j < NR; ++j) {
+      const float e = sm_e[j * G + g];
       const float4 a =
-          __ldcg(reinterpret_cast<const float4*>(recs + (size_t)(s * G + g) * kAttnRec + 4) + c4);
+          __ldcg(reinterpret_cast<const float4*>(hrecs + ((size_t)j * G + g) * kAttnRec + 4) + c4);
       o.x += a.x * e;
       o.y += a.y * e;
       o.z += a.z * e;
@@ -545,32 +650,64 @@ cudaError_t launch_rope_append(const DecodeAttn& P, cudaStream_t s, bool pdl) {
                   P);
 }
 
-int attn_splits(int B, int n_kv, int tmax, int num_sms) {
-  // about one CTA per SM, at least one stage of positions per slice
-  int S = (num_sms + B * n_kv - 1) / (B * n_kv);
-  const int max_s = (tmax + kAttnP - 1) / kAttnP;
+int attn_splits(int B, int n_head, int n_kv, int tmax, int num_sms) {
+  // one resident wave (three CTAs per SM): longer slices stream better than
+  // more, shorter ones, whose fixed cost (launch, query, record, count) would
+  // be paid per wave; at least two stages of positions per slice, and at most
+  // kAttnMaxRecs records per head for the merge
+  const int slots = 3 * num_sms;
+  int S = slots / (B * n_kv);
+  const int max_s = (tmax + 2 * kAttnP - 1) / (2 * kAttnP);
   if (S > max_s) S = max_s;
-  if (S > kAttnMaxSplits) S = kAttnMaxSplits;
+  const int max_rec = kAttnMaxRecs / attn_nw(attn_kg(n_head / n_kv));
+  if (S > max_rec) S = max_rec;
   return S < 1 ? 1 : S;
 }
 
-size_t attn_part_floats(int B, int n_head, int splits) {
-  return (size_t)B * n_head * splits * kAttnRec;
+size_t attn_part_floats(int B, int n_head, int n_kv, int splits) {
+  return (size_t)B * n_kv * splits * attn_nw(attn_kg(n_head / n_kv)) * (n_head / n_kv) * kAttnRec;
 }
+
+namespace {
+template <bool kRope, int kG>
+cudaError_t launch_attn_t(const CUtensorMap& map, const DecodeAttn& P, cudaStream_t s, bool pdl) {
+  cudaError_t e = ensure_max_smem<attn_decode_kernel<kRope, kG>>();
+  if (e != cudaSuccess) return e;
+  return launch_k(attn_decode_kernel<kRope, kG>, dim3(P.B, P.n_kv, P.splits),
+                  dim3((attn_nw(kG) + 1) * 32), kAttnSmem, s, pdl, map, P);
+}
+template <int kG>
+cudaError_t launch_attn_g(const CUtensorMap& map, const DecodeAttn& P, bool rope, cudaStream_t s,
+                          bool pdl) {
+  return rope ? launch_attn_t<true, kG>(map, P, s, pdl) : launch_attn_t<false, kG>(map, P, s, pdl);
+}
+}  // namespace
 
 cudaError_t launch_attention_decode(const DecodeAttn& P, bool rope, cudaStream_t s, bool pdl) {
   if (P.B <= 0) return cudaSuccess;
-  if (P.splits < 1 || P.splits > kAttnMaxSplits || P.n_head % P.n_kv ||
-      P.n_head / P.n_kv > kMaxGroup)
-    return cudaErrorInvalidValue;
   const int G = P.n_head / P.n_kv;
-  const dim3 grid(P.B, P.n_kv, P.splits);
-  const size_t smem = sizeof(AttnShared);
-  cudaError_t e = rope ? ensure_max_smem<attn_decode_kernel<true>>()
-                        : ensure_max_smem<attn_decode_kernel<false>>();
-  if (e != cudaSuccess) return e;
-  return launch_k(rope ? attn_decode_kernel<true> : attn_decode_kernel<false>, grid,
-                  dim3((G + 1) * 32), smem, s, pdl, P);
+  if (P.n_head % P.n_kv || G > kAttnMaxG || P.splits < 1 ||
+      P.splits * attn_nw(attn_kg(G)) > kAttnMaxRecs)
+    return cudaErrorInvalidValue;
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return cudaErrorNotSupported;
+  // the K cache as rows of 128 floats, boxes of 32 rows x 32 floats (128 B),
+  // 128-byte swizzle
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)kHeadDim, (cuuint64_t)P.B * P.n_kv * P.tmax};
+  const cuuint64_t strides[1] = {(cuuint64_t)kHeadDim * sizeof(float)};
+  const cuuint32_t box[2] = {32u, (cuuint32_t)kAttnP};
+  const cuuint32_t estr[2] = {1u, 1u};
+  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, P.kcache, dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  switch (attn_kg(G)) {
+    case 1: return launch_attn_g<1>(map, P, rope, s, pdl);
+    case 2: return launch_attn_g<2>(map, P, rope, s, pdl);
+    case 4: return launch_attn_g<4>(map, P, rope, s, pdl);
+    default: return launch_attn_g<8>(map, P, rope, s, pdl);
+  }
 }
 
 }  // namespace ouroq

@@ -87,16 +87,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// 2-D TMA tile load (no multicast) completing on an mbarrier
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // Shared-memory matrix descriptor (sm_100 format): start address, leading and
 // stride byte offsets in 16-byte units, version 1, layout type in bits 61-63.
 __device__ __forceinline__ uint64_t smem_desc(const void* p, uint32_t lbo, uint32_t sbo,
@@ -378,24 +368,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
-}
-
 }  // namespace
 
 size_t gemm_tc_smem_bytes(int N, int stages) { return tc_plan(N, stages).total; }
@@ -417,7 +389,7 @@ int gemm_tc_tile_n(int M, int B, int num_sms) {
 
 cudaError_t launch_gemm_tc(const TcLaunch& L0, const int8_t* q, int Btot, int smem_optin,
                            int num_sms, cudaStream_t s) {
-  EncodeTiledFn enc = encode_fn();
+  EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return cudaErrorNotSupported;
   cudaError_t e = ensure_max_smem<gemm_tc_kernel>();
   if (e != cudaSuccess) return e;

@@ -109,12 +109,16 @@ __device__ __forceinline__ void argmax_finish(const HeadLaunch& L,
     for (int w = 0; w < kWarps; ++w) key = red[w][threadIdx.x] > key ? red[w][threadIdx.x] : key;
     if (key) atomicMax(L.key + b0 + threadIdx.x, key);
   }
-  __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(L.counter, 1u) == gridDim.x * gridDim.y - 1;
+  if (threadIdx.x == 0) {
+    // one fence: cumulative, it orders the CTA's atomicMax calls (ordered
+    // before it by the barrier) before the count
+    __threadfence();
+    last = atomicAdd(L.counter, 1u) == gridDim.x * gridDim.y - 1;
+    if (last) __threadfence();
+  }
   __syncthreads();
   if (last) {
-    __threadfence();
     for (int b = threadIdx.x; b < L.B; b += blockDim.x) {
       const unsigned long long key = atomicExch(L.key + b, 0ull);
       // every logit NaN: the reference's best stays 0

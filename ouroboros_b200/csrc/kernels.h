@@ -203,7 +203,7 @@ struct DecodeAttn {
   float* vcache;
   const long long* pos;      // device: the position being decoded
   float* out;                // [B][n_head][128]
-  float* part;               // [B][n_kv][splits][group][132] slice partials
+  float* part;               // [B][n_kv][splits][warps][group][132] partial records
   unsigned* counter;         // [B][n_kv] slices finished (zero between launches)
   unsigned* status;
   int B, n_head, n_kv, tmax, splits;
@@ -214,8 +214,8 @@ cudaError_t launch_rmsnorm(const float* x, const float* r, float* h, const float
 cudaError_t launch_swiglu_norm(const float* g, const float* u, const float* w, float* y, int B,
                                int n, float eps, cudaStream_t s, bool pdl);
 cudaError_t launch_rope_append(const DecodeAttn& P, cudaStream_t s, bool pdl);
-int attn_splits(int B, int n_kv, int tmax, int num_sms);
-size_t attn_part_floats(int B, int n_head, int splits);
+int attn_splits(int B, int n_head, int n_kv, int tmax, int num_sms);
+size_t attn_part_floats(int B, int n_head, int n_kv, int splits);
 // rope: q, k un-rotated; k and v appended to the cache at pos in the same launch
 cudaError_t launch_attention_decode(const DecodeAttn& P, bool rope, cudaStream_t s, bool pdl);
 
