@@ -315,8 +315,11 @@ cudaError_t launch_nb(const HeadLaunch& L, cudaStream_t s, bool pdl) {
     // resident CTAs per SM by shared memory (228 KB per SM, 1 KB reserved per CTA)
     const int per_sm = smem + 1024 <= 114 * 1024 ? 2 : 1;
     const int nsets = (L.M + kTileRows - 1) / kTileRows;
-    int grid = L.num_sms * per_sm;
-    if (grid > nsets) grid = nsets;
+    // the fewest row sets per CTA that fit one resident wave, and just enough
+    // CTAs for them, so that every CTA has the same number of sets
+    const int slots = L.num_sms * per_sm;
+    const int per_cta = (nsets + slots - 1) / slots;
+    const int grid = (nsets + per_cta - 1) / per_cta;
     cfg.gridDim = dim3((unsigned)grid, groups, 1);
     cfg.blockDim = dim3(kTileRows);
     cfg.dynamicSmemBytes = smem;
