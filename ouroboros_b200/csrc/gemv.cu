@@ -86,12 +86,18 @@ __host__ __device__ constexpr uint32_t align128(uint32_t v) { return (v + 127u) 
 //   xwork       xcap bytes: int8 activations [job][B][K] of the CTA's jobs
 //   qg          gcap ints: per-(token, 128-group) activation sums
 //   sx / qtot   [8 jobs][8 tokens] per-token scales / sums
-//   red         ternary: 2 x kCWarps*B*32 ints; sign: B*slice*32 floats
+//   red         ternary: max(2, defer) x kCWarps*B*32 ints; sign: B*slice*32 floats
 struct Plan {
   uint32_t bars, ring, xwork, qg, sx, qtot, red, total;
 };
 
-__host__ __device__ inline Plan make_plan(int fmt, int B, int stages, int xcap, int gcap) {
+// Deferred reduction (ternary): when the per-warp partials of all the CTA's
+// tiles fit in this many bytes, every warp runs through its tiles without a
+// CTA barrier and the tiles are reduced together at the end.
+constexpr uint32_t kDeferBudget = 48u * 1024u;
+
+__host__ __device__ inline Plan make_plan(int fmt, int B, int stages, int xcap, int gcap,
+                                          int defer = 0) {
   Plan p;
   const uint32_t slice = fmt == kTern2 ? kTernSliceChunks : kSignSliceChunks;
   const uint32_t stage = fmt == kTern2 ? Fmt<kTern2>::kStageBytes : Fmt<kSign1>::kStageBytes;
@@ -103,8 +109,10 @@ __host__ __device__ inline Plan make_plan(int fmt, int B, int stages, int xcap, 
   p.sx = p.qg + align128((uint32_t)gcap * 4u);
   p.qtot = p.sx + 256;
   p.red = p.qtot + 256;
-  // ternary: two buffers of per-warp partials (one barrier per tile)
-  const uint32_t red_bytes = fmt == kTern2 ? 2u * kCWarps * b * 32u * 4u : b * slice * 32u * 4u;
+  // ternary: two buffers of per-warp partials (one barrier per tile), or one
+  // slot per tile of the CTA (deferred reduction)
+  const uint32_t nbuf = defer > 2 ? (uint32_t)defer : 2u;
+  const uint32_t red_bytes = fmt == kTern2 ? nbuf * kCWarps * b * 32u * 4u : b * slice * 32u * 4u;
   p.total = p.red + align128(red_bytes);
   return p;
 }
@@ -333,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   __syncthreads();
   const GemvLaunch& L = *reinterpret_cast<const GemvLaunch*>(smem);
   const int NS = L.stages;
-  const Plan P = make_plan(FMT, B, NS, L.xcap, L.gcap);
+  const Plan P = make_plan(FMT, B, NS, L.xcap, L.gcap, L.defer);
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.bars);
   uint64_t* empty = full + kMaxStages;
@@ -563,6 +571,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         if (lane == 0) mbar_arrive(&empty[slot]);
         first = first == 0 ? kCWarps - 1 : first - 1;
       }
+      if (L.defer) {
+        // this warp's exact partials of the tile, reduced after the last tile
+        int* rb = red + ((t - t_begin) * kCWarps + warp) * B * 32;
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+          rb[b * 32 + lane] = A[b][0] + (A[b][1] >> 2) + (A[b][2] >> 4) + (A[b][3] >> 6);
+        continue;
+      }
       // cross-warp reduction of the exact per-warp partials. Two buffers: a
       // buffer is rewritten two tiles later, after every warp has passed the
       // next tile's barrier, so its readers are done -- one barrier per tile.
@@ -642,6 +658,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
 #pragma unroll
       for (int b = 0; b < B; ++b) {
         if (b % kCWarps == warp && row_ok) J.y[(size_t)b * J.ldy + row] = __fmul_rn(sum[b], sx[b]);
+      }
+    }
+  }
+  if (FMT == kTern2 && L.defer) {
+    // every tile's partials are in place: warp w reduces (tile, token) pairs
+    // w, w + kCWarps, ... and writes the outputs
+    named_bar_sync(2, kCThreads);
+    const int ntl = t_end - t_begin;
+    for (int i = warp; i < ntl * B; i += kCWarps) {
+      const int tl = i / B, b = i - tl * B;
+      const TileInfo ti = tile_info(L, t_begin + tl);
+      const GemvJob& J = L.jobs[ti.job];
+      const int* rb = red + (size_t)tl * kCWarps * B * 32 + b * 32 + lane;
+      int acc = -qtot_s[(ti.job - j_lo) * 8 + b];
+#pragma unroll
+      for (int w = 0; w < kCWarps; ++w) acc += rb[w * B * 32];
+      if (lane < ti.rows) {
+        const int row = ti.row0 + lane;
+        const float y =
+            __fmul_rn(__fmul_rn(__int2float_rn(acc), J.w_scale), sx_s[(ti.job - j_lo) * 8 + b]);
+        J.y[(size_t)b * J.ldy + row] = y;
+        if (J.acc) J.acc[(size_t)b * J.M + row] = acc;
       }
     }
   }
@@ -729,13 +767,20 @@ bool gemv_prepare(GemvLaunch& L, int num_sms, int smem_optin, int* grid_out, siz
   }
   L.xcap = xcap;
   L.gcap = gcap;
+  // most tiles one CTA owns: the deferred reduction keeps a slot per tile
+  int maxt = 0;
+  for (int c = 0; c < grid; ++c) {
+    const int nt = L.cta_tile[c + 1] - L.cta_tile[c];
+    maxt = nt > maxt ? nt : maxt;
+  }
+  L.defer = L.fmt == kTern2 && (uint32_t)maxt * kCWarps * L.B * 32u * 4u <= kDeferBudget ? maxt : 0;
   // deepest ring that fits next to the activations (4 KB are left for the
   // kernel's static shared memory)
   const uint32_t budget = (uint32_t)smem_optin - 4096u;
   int stages = kMaxStages;
-  while (stages > 2 && make_plan(L.fmt, L.B, stages, xcap, gcap).total > budget) --stages;
+  while (stages > 2 && make_plan(L.fmt, L.B, stages, xcap, gcap, L.defer).total > budget) --stages;
   L.stages = stages;
-  const size_t smem = make_plan(L.fmt, L.B, stages, xcap, gcap).total;
+  const size_t smem = make_plan(L.fmt, L.B, stages, xcap, gcap, L.defer).total;
   if (smem > budget) return false;
   *grid_out = grid;
   *smem_out = smem;

@@ -71,6 +71,7 @@ struct GemvLaunch {
   int stages;               // weight ring depth (2..kMaxGemvStages), sized to shared memory
   int xcap;                 // bytes of int8 activations one CTA keeps resident (its jobs)
   int gcap;                 // per-group activation sums one CTA keeps resident (ints)
+  int defer;                // ternary: > 0 = tile slots for the end-of-CTA reduction
   unsigned* status;         // device status word
   // CTA c owns tiles [cta_tile[c], cta_tile[c+1]): ranges balanced by weight
   // bytes on the host, so the kernel does no 64-bit division at start-up.
