@@ -92,6 +92,16 @@ const char *ouroq_last_error(const ouroq_ctx *ctx);
  * wait gave up, OUROQ_ERR_BAD_SHAPE if a decode position lay outside the KV
  * cache. */
 ouroq_status ouroq_check_device(ouroq_ctx *ctx);
+/* Where a buffer lives. Host-buffer entry points (ouroq_matvec_q,
+ * ouroq_matmul_q, ouroq_rotate_fwd/inv) and device-buffer entry points
+ * (ouroq_gemm*, ouroq_quantize_act, the decode ops) are separate; a caller
+ * holding a pointer of unknown origin asks here which one applies. */
+typedef enum {
+  OUROQ_PTR_HOST = 0,    /* pageable or pinned host memory */
+  OUROQ_PTR_DEVICE = 1,  /* device memory of some GPU */
+  OUROQ_PTR_MANAGED = 2  /* unified (managed) memory */
+} ouroq_ptr_kind_t;
+ouroq_status ouroq_ptr_kind(const void *p, int *kind, int *device);
 /* Number of kernels this context has launched (for bench accounting). */
 uint64_t ouroq_launch_count(const ouroq_ctx *ctx);
 /* 1 = launch GEMV kernels with programmatic dependent launch (default), 0 = off. */
@@ -263,6 +273,22 @@ ouroq_status ouroq_rope_attention_decode(ouroq_ctx *ctx, const float *q, const f
                                          const float *v, float *kcache, float *vcache,
                                          const int64_t *pos, float *out, int B, int n_head,
                                          int n_kv, int tmax, float rope_base, void *stream);
+
+/* The norm in front of a projection group, fused into it (infer/mod.rs:303-333:
+ * attn_norm before q/k/v, attn_sub_norm before o, ffn_norm before gate/up,
+ * ffn_sub_norm before down): y_i = W_i . (rmsnorm(v) * norm_w) for the n
+ * matrices w[i] (one format, one K), with v = x + residual (mode 0; residual
+ * may be NULL; h, if not NULL, receives v) or v = silu(x) * residual (mode 1:
+ * x the gate projection, residual the up projection, h NULL). x, residual,
+ * h: device [B][K] fp32; y[i]: device [B][M_i]. Up to 2 tokens with rows of
+ * up to 11520 values run as one launch (the norm in the GEMV prologue);
+ * otherwise the norm kernel writes a context scratch row and the grouped
+ * product reads it -- the same results either way up to the order of the sum
+ * of squares. */
+ouroq_status ouroq_gemm_norm_f32act(ouroq_ctx *ctx, int n, const ouroq_weight *const *w,
+                                    const float *x, const float *residual, int mode,
+                                    const float *norm_w, float eps, float *h, int B,
+                                    float *const *y, void *stream);
 
 /* argmax_token (infer/mod.rs:190-194): the tied lm_head of an F16 or BF16
  * weight [vocab][K] applied to the final hidden states x [B][K] (device

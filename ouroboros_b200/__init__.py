@@ -59,6 +59,7 @@ ABI_FUNCTIONS = {
     "ouroq_ctx_destroy": (_i, [_p]),
     "ouroq_last_error": (ctypes.c_char_p, [_p]),
     "ouroq_check_device": (_i, [_p]),
+    "ouroq_ptr_kind": (_i, [_p, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     "ouroq_launch_count": (ctypes.c_uint64, [_p]),
     "ouroq_set_pdl": (_i, [_p, _i]),
     "ouroq_weight_upload": (_i, [_p, _i, _p, _i, _i, _p, _f, ctypes.POINTER(_p)]),
@@ -89,6 +90,7 @@ ABI_FUNCTIONS = {
     "ouroq_rope_attention_decode": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i,
                                          ctypes.c_float, _p]),
     "ouroq_argmax_token": (_i, [_p, _p, _p, _i, _p, _p, _p]),
+    "ouroq_gemm_norm_f32act": (_i, [_p, _i, _p, _p, _p, _i, _p, ctypes.c_float, _p, _i, _p, _p]),
     "ouroq_bmts_open": (_i, [ctypes.c_char_p, ctypes.POINTER(_p), ctypes.c_char_p, _sz]),
     "ouroq_bmts_close": (_i, [_p]),
     "ouroq_bmts_info": (_i, [_p, ctypes.POINTER(_i), ctypes.POINTER(_i),
@@ -106,6 +108,20 @@ ABI_FUNCTIONS = {
 }
 
 _lib = None
+
+
+PTR_HOST, PTR_DEVICE, PTR_MANAGED = 0, 1, 2
+
+
+def ptr_kind(ptr: int) -> tuple[int, int]:
+    """(kind, device) of a raw pointer: PTR_HOST / PTR_DEVICE / PTR_MANAGED,
+    device -1 for host memory."""
+    lib = load_library()
+    kind, dev = ctypes.c_int(), ctypes.c_int()
+    st = lib.ouroq_ptr_kind(ctypes.c_void_p(ptr), ctypes.byref(kind), ctypes.byref(dev))
+    if st != OK:
+        raise OuroqError(st, "ptr_kind")
+    return kind.value, dev.value
 
 
 class OuroqError(RuntimeError):
@@ -422,6 +438,18 @@ class Context:
                                                     _ptr(pos), _ptr(out), B, n_head, n_kv, tmax,
                                                     _stream_ptr(stream)))
         return out
+
+    def gemm_norm_f32act(self, ws, x, norm_w, ys, residual=None, swiglu=False, h=None,
+                         eps: float = 1e-5, stream=None):
+        """ys[i] = W_i (rmsnorm(x + residual) * norm_w), or with swiglu=True
+        W_i (rmsnorm(silu(x) * residual) * norm_w); h receives x + residual."""
+        n = len(ws)
+        B = x.shape[0]
+        arr = lambda vals: (_p * n)(*vals)  # noqa: E731
+        self._check(self.lib.ouroq_gemm_norm_f32act(
+            self.ctx, n, arr([w.handle for w in ws]), _ptr(x), _ptr(residual), 1 if swiglu else 0,
+            _ptr(norm_w), eps, _ptr(h), B, arr([_ptr(y) for y in ys]), _stream_ptr(stream)))
+        return ys
 
     def argmax_token(self, w: Weight, x, tokens=None, logits=None, stream=None):
         """Greedy next token of each row of x [B][K] through the F16 / BF16 head w

@@ -50,6 +50,8 @@ struct ouroq_ctx {
   size_t sign_cap = 0;
   // rotated fp32 activations for the reference formats (hadamard_block != 0)
   float* rot_scratch = nullptr;
+  float* norm_scratch = nullptr;  // normalised activations when the norm is not fused
+  size_t norm_cap = 0;
   size_t rot_cap = 0;
   // slice partials of the decode attention
   float* attn_part = nullptr;
@@ -674,6 +676,7 @@ ouroq_status ouroq_ctx_destroy(ouroq_ctx* ctx) {
   cudaFree(ctx->rot_scratch);
   cudaFree(ctx->attn_part);
   cudaFree(ctx->attn_ctr);
+  cudaFree(ctx->norm_scratch);
   cudaFree(ctx->head_key);
   shard_release(ctx);
   delete ctx;
@@ -687,6 +690,23 @@ uint64_t ouroq_launch_count(const ouroq_ctx* ctx) { return ctx ? ctx->launches :
 ouroq_status ouroq_set_pdl(ouroq_ctx* ctx, int enable) {
   if (!ctx) return OUROQ_ERR_BAD_ARG;
   ctx->pdl = enable != 0;
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_ptr_kind(const void* p, int* kind, int* device) {
+  if (!p || !kind) return OUROQ_ERR_BAD_ARG;
+  cudaPointerAttributes a{};
+  const cudaError_t e = cudaPointerGetAttributes(&a, p);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();  // not a pointer CUDA knows: ordinary host memory
+    *kind = OUROQ_PTR_HOST;
+    if (device) *device = -1;
+    return OUROQ_OK;
+  }
+  *kind = a.type == cudaMemoryTypeDevice    ? OUROQ_PTR_DEVICE
+          : a.type == cudaMemoryTypeManaged ? OUROQ_PTR_MANAGED
+                                            : OUROQ_PTR_HOST;
+  if (device) *device = a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged ? a.device : -1;
   return OUROQ_OK;
 }
 
@@ -1477,6 +1497,76 @@ ouroq_status ouroq_argmax_token(ouroq_ctx* ctx, const ouroq_weight* w, const flo
   L.tokens = reinterpret_cast<long long*>(tokens);
   CU(ctx, launch_head(L, static_cast<cudaStream_t>(stream), ctx->pdl), "argmax_token launch");
   ctx->launches++;
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_gemm_norm_f32act(ouroq_ctx* ctx, int n, const ouroq_weight* const* w,
+                                    const float* x, const float* residual, int mode,
+                                    const float* norm_w, float eps, float* h, int B,
+                                    float* const* y, void* stream) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  if (n < 1 || n > kMaxGemvJobs)
+    return fail(ctx, OUROQ_ERR_BAD_SHAPE, "group size %d (1..%d)", n, kMaxGemvJobs);
+  if (B < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d", B);
+  if (B == 0) return OUROQ_OK;
+  if (!w || !x || !norm_w || !y) return fail(ctx, OUROQ_ERR_BAD_ARG, "null argument");
+  if (mode != 0 && mode != 1) return fail(ctx, OUROQ_ERR_BAD_ARG, "mode %d", mode);
+  if (mode == 1 && (!residual || h))
+    return fail(ctx, OUROQ_ERR_BAD_ARG, "mode 1 takes the up projection and no h");
+  for (int i = 0; i < n; ++i) {
+    if (!w[i] || !y[i]) return fail(ctx, OUROQ_ERR_BAD_ARG, "null entry %d", i);
+    if (is_ref_format(w[i]->fmt) || w[i]->fmt != w[0]->fmt)
+      return fail(ctx, OUROQ_ERR_UNSUPPORTED, "one TERNARY2 or SIGN1G128 format per group");
+    if (w[i]->K != w[0]->K) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "entries read one row width");
+  }
+  const int K = w[0]->K;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool aligned = aligned16(x) && (!residual || aligned16(residual)) && aligned16(norm_w) &&
+                       (!h || aligned16(h));
+  if (B <= kFusedMaxB && aligned && K % 128 == 0 && B * (K / 128) <= kNormFusedMaxUnits) {
+    GemvLaunch L{};
+    L.njobs = n;
+    L.B = B;
+    L.fused = 1;
+    L.fmt = w[0]->fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
+    for (int i = 0; i < n; ++i) {
+      L.jobs[i] = make_job(w[i], nullptr, nullptr, y[i], nullptr);
+      L.jobs[i].xf = x;
+    }
+    L.norm.x = x;
+    L.norm.r = residual;
+    L.norm.w = norm_w;
+    L.norm.h = h;
+    L.norm.eps = eps;
+    L.norm.mode = mode;
+    L.norm.K = K;
+    if (gemv_fits(ctx, L)) return run_gemv(ctx, L, s);
+  }
+  // not fused: the norm kernel into scratch, then the grouped product
+  ouroq_status st = grow(ctx, ctx->norm_scratch, ctx->norm_cap, (size_t)B * K, "norm scratch");
+  if (st != OUROQ_OK) return st;
+  float* a = ctx->norm_scratch;
+  if (mode == 0)
+    CU(ctx, launch_rmsnorm(x, residual, h, norm_w, a, B, K, eps, s, ctx->pdl), "rmsnorm launch");
+  else
+    CU(ctx, launch_swiglu_norm(x, residual, norm_w, a, B, K, eps, s, ctx->pdl), "swiglu launch");
+  ctx->launches++;
+  if (B <= kGemvMaxB) {
+    const float* xs[kMaxGemvJobs];
+    for (int i = 0; i < n; ++i) xs[i] = a;
+    return ouroq_gemm_group_f32act(ctx, n, w, xs, B, nullptr, nullptr, y, stream);
+  }
+  st = grow(ctx, ctx->q_scratch, ctx->q_cap, (size_t)B * K, "q scratch");
+  if (st != OUROQ_OK) return st;
+  st = grow(ctx, ctx->s_scratch, ctx->s_cap, (size_t)B, "s scratch");
+  if (st != OUROQ_OK) return st;
+  st = ouroq_quantize_act(ctx, a, B, K, nullptr, 0, ctx->q_scratch, ctx->s_scratch, stream);
+  if (st != OUROQ_OK) return st;
+  for (int i = 0; i < n; ++i) {
+    st = ouroq_gemm(ctx, w[i], ctx->q_scratch, ctx->s_scratch, B, y[i], nullptr, stream);
+    if (st != OUROQ_OK) return st;
+  }
   return OUROQ_OK;
 }
 

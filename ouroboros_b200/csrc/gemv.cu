@@ -326,6 +326,105 @@ __device__ void prologue_units(const Seg* segs, int nseg, int nunits, const floa
 }
 
 
+// Fused RMSNorm prologue: every job of the launch reads one activation row
+// per token. v = x + r (or silu(x) * r), h = v (CTA 0 only), a = v * inv * w
+// with inv = 1 / sqrt(mean(v^2) + eps) (ops.rs:12-17, a = (v * inv) * w), then
+// the per-token absmax quantisation of a, once for all the CTA's jobs: the
+// codes and group sums go to the first job's slots and every job reads them.
+// The whole row stays in registers (the host admits only rows of at most
+// kNormFusedMaxUnits units), and the sum of squares is combined across warps
+// in a fixed order, so every CTA computes the same codes.
+template <int B>
+__device__ void prologue_norm(const NormSpec& N, int8_t* xq, int* qg, float* sx, int njs,
+                              int* amax_bits, float* ssq, float* inv_s, int warp, int lane) {
+  constexpr int E = 4, R = 6;
+  static_assert(R * kCWarps == kNormFusedMaxUnits, "register budget of the fused norm");
+  const int K = N.K;
+  const int upt = K / (32 * E);  // units (128 values) per token
+  const int nunits = B * upt;
+  if (threadIdx.x < B) amax_bits[threadIdx.x] = 0;
+  float v[R][E];
+  float ssl[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) ssl[b] = 0.0f;
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    const int u = warp + k * kCWarps;
+    if (u < nunits) {
+      const int b = u / upt;
+      const size_t at = (size_t)b * K + (size_t)(u - b * upt) * 32 * E + lane * E;
+      load_unit<E>(v[k], N.x + at);
+      if (N.r) {
+        float r[E];
+        load_unit<E>(r, N.r + at);
+#pragma unroll
+        for (int i = 0; i < E; ++i)
+          v[k][i] = N.mode == 1 ? v[k][i] / (1.0f + expf(-v[k][i])) * r[i] : v[k][i] + r[i];
+      }
+      if (N.h && blockIdx.x == 0)
+        *reinterpret_cast<float4*>(N.h + at) = make_float4(v[k][0], v[k][1], v[k][2], v[k][3]);
+      float s = 0.0f;
+#pragma unroll
+      for (int i = 0; i < E; ++i) s += v[k][i] * v[k][i];
+#pragma unroll
+      for (int b2 = 0; b2 < B; ++b2)
+        if (b2 == b) ssl[b2] += s;
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    const float t = warp_sum_f(ssl[b]);
+    if (lane == 0) ssq[b * kCWarps + warp] = t;
+  }
+  named_bar_sync(1, kCThreads);
+  if (threadIdx.x < B) {
+    float t = 0.0f;
+    for (int w = 0; w < kCWarps; ++w) t += ssq[threadIdx.x * kCWarps + w];
+    inv_s[threadIdx.x] = 1.0f / sqrtf(t / (float)K + N.eps);
+  }
+  named_bar_sync(1, kCThreads);
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    const int u = warp + k * kCWarps;
+    if (u < nunits) {  // warp-uniform
+      const int b = u / upt;
+      const int o = (u - b * upt) * 32 * E + lane * E;
+      float wv[E];
+      load_unit<E>(wv, N.w + o);
+      const float iv = inv_s[b];
+      float m = 0.0f;
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        v[k][i] = v[k][i] * iv * wv[i];
+        m = fmaxf(m, fabsf(v[k][i]));
+      }
+      m = warp_max(m);
+      if (lane == 0) atomicMax(&amax_bits[b], __float_as_int(m));
+    }
+  }
+  named_bar_sync(1, kCThreads);
+  if (threadIdx.x < B) {
+    const float sc = __fdiv_rn(__int_as_float(amax_bits[threadIdx.x]), 127.0f);
+    for (int j = 0; j < njs; ++j) sx[j * 8 + threadIdx.x] = sc;
+  }
+  named_bar_sync(1, kCThreads);
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    const int u = warp + k * kCWarps;
+    if (u < nunits) {
+      const int b = u / upt, ut = u - b * upt;
+      const int o = ut * 32 * E + lane * E;
+      const float sc = sx[b];
+      const float rsc = __frcp_rn(sc);
+      int sum = 0;
+      *reinterpret_cast<uint32_t*>(xq + (size_t)b * K + o) =
+          quant4(v[k][0], v[k][1], v[k][2], v[k][3], sc, rsc, &sum);
+      sum = warp_sum(sum);
+      if (lane == 0) qg[b * (K / 128) + ut] = sum;
+    }
+  }
+}
+
 template <int FMT, int B>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvLaunch Lp) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -419,7 +518,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   pdl_wait();
 
   // ---- prologue: activations of jobs j_lo..j_hi -> int8 in shared memory
-  if (L.fused) {
+  const bool shared_x = L.norm.w != nullptr;  // every job reads the first job's codes
+  if (shared_x) {
+    __shared__ float ssq[2 * kCWarps];
+    __shared__ float inv_s[2];
+    __shared__ int amax_n[2];
+    if constexpr (B <= 2)
+      prologue_norm<B>(L.norm, xwork, qg_base, sx_s, j_hi - j_lo + 1, amax_n, ssq, inv_s, warp, lane);
+  } else if (L.fused) {
     // one segment per (job, token) row; all jobs of a fused launch share the
     // rotation block (checked on the host), hence one unit size E
     __shared__ Seg segs[kMaxGemvJobs * 8];
@@ -479,7 +585,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     for (int pr = warp; pr < npairs; pr += kCWarps) {
       const int jl = pr / B, b = pr - (pr / B) * B;
       int goff = 0;
-      for (int jj = j_lo; jj < j_lo + jl; ++jj) goff += B * (L.jobs[jj].K / 128);
+      if (!shared_x)
+        for (int jj = j_lo; jj < j_lo + jl; ++jj) goff += B * (L.jobs[jj].K / 128);
       const int G = L.jobs[j_lo + jl].K / 128;
       int s = 0;
       for (int g = lane; g < G; g += 32) s += qg_base[goff + b * G + g];
@@ -507,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     const int G = K / 128;
     const int ns = nslices_of<FMT>(K);
     if (ti.job != cur_job) {
-      if (cur_job >= 0) {
+      if (cur_job >= 0 && !shared_x) {
         xoff += B * L.jobs[cur_job].K;
         goff += B * (L.jobs[cur_job].K / 128);
       }
@@ -751,9 +858,17 @@ bool gemv_prepare(GemvLaunch& L, int num_sms, int smem_optin, int* grid_out, siz
     }
     L.cta_tile[grid] = (uint16_t)tiles;
   }
-  // activations one CTA keeps resident: the jobs its tile range touches
+  // activations one CTA keeps resident: the jobs its tile range touches (one
+  // row for all of them under a fused norm)
   int xcap = 0, gcap = 0;
-  for (int c = 0; c < grid; ++c) {
+  if (L.norm.w) {
+    if (L.B > 2 || L.norm.K % 128 || L.B * L.norm.K / 128 > kNormFusedMaxUnits) return false;
+    for (int j = 0; j < L.njobs; ++j)
+      if (L.jobs[j].K != L.norm.K || L.jobs[j].had_block) return false;
+    xcap = L.B * L.norm.K;
+    gcap = L.B * (L.norm.K / 128);
+  }
+  for (int c = 0; c < grid && !L.norm.w; ++c) {
     if (L.cta_tile[c] >= L.cta_tile[c + 1]) continue;
     const int jlo = tile_info(L, L.cta_tile[c]).job;
     const int jhi = tile_info(L, L.cta_tile[c + 1] - 1).job;
@@ -775,7 +890,8 @@ bool gemv_prepare(GemvLaunch& L, int num_sms, int smem_optin, int* grid_out, siz
   }
   L.defer = L.fmt == kTern2 && (uint32_t)maxt * kCWarps * L.B * 32u * 4u <= kDeferBudget ? maxt : 0;
   // deepest ring that fits next to the activations (4 KB are left for the
-  // kernel's static shared memory)
+  // kernel's static shared memory); capping it at the slices a CTA streams
+  // measured slower on the wide shapes and no faster in decode
   const uint32_t budget = (uint32_t)smem_optin - 4096u;
   int stages = kMaxStages;
   while (stages > 2 && make_plan(L.fmt, L.B, stages, xcap, gcap, L.defer).total > budget) --stages;

@@ -61,8 +61,26 @@ constexpr int kMaxGemvJobs = 8;
 constexpr int kMaxGemvCtas = 160;  // >= SM count of the device (148 on B200)
 constexpr int kMaxGemvStages = 13;
 
+// Fused RMSNorm ahead of a fused GEMV (infer/mod.rs:303-333): every job of the
+// launch reads the same K-wide row per token, v = x + r (mode 0, r nullable) or
+// v = silu(x) * r (mode 1), a = v * inv * w with inv = 1 / sqrt(mean(v^2) + eps),
+// quantised once per CTA; h (mode 0, nullable) receives v (written by CTA 0).
+// Disabled while w is null.
+struct NormSpec {
+  const float* x;
+  const float* r;
+  const float* w;
+  float* h;
+  float eps;
+  int mode;
+  int K;
+};
+// Rows the fused norm keeps entirely in registers: B * K / 128 units at most.
+constexpr int kNormFusedMaxUnits = 90;
+
 struct GemvLaunch {
   GemvJob jobs[kMaxGemvJobs];
+  NormSpec norm;
   int njobs;
   int ntiles;               // total 32-row tiles over all jobs
   int B;                    // tokens (same for all jobs)

@@ -18,9 +18,10 @@ greedy next token (finite_argmax, fused into the lm_head launch). Configuration 
 
 Every ternary projection runs through the C ABI (the path this library
 rebuilds). The ops around it run either as this library's fused kernels
-(`fused=True`, the default: residual + RMSNorm, SiLU·up + sub-norm, and RoPE +
-KV append + split-sequence GQA attention in one launch -- ouroq_rmsnorm,
-ouroq_swiglu_rmsnorm, ouroq_rope_attention_decode) or as plain torch operations
+(`fused=True`, the default: each RMSNorm -- with the residual add, or the
+SiLU·up product of the FFN sub-norm -- fused into the projection group that
+reads it, ouroq_gemm_norm_f32act; RoPE + KV append + split-sequence GQA
+attention in one launch, ouroq_rope_attention_decode) or as plain torch operations
 (`fused=False`, the unfused host path kept as a cross-check). fp32 throughout
 like the reference, KV cache included. A
 decode step has static shapes -- the position lives in a device tensor -- so it
@@ -156,24 +157,26 @@ class Decoder:
         return h1 + d
 
     def layer_fused(self, li, first):
-        """One layer on the library's kernels. On entry buf x holds the hidden
-        state (first layer) or h1 / down of the previous layer hold its two
-        residual terms; the residual add is fused into the first norm."""
+        """One layer on the library's kernels, each norm fused into the
+        projection group that reads it. On entry buf x holds the hidden state
+        (first layer) or h1 / down of the previous layer hold its two residual
+        terms, added inside the first launch."""
         c, bf, L = self.ctx, self.buf, self.layers[li]
         st = self.stream
+        qkv = [L[n] for n in ("q", "k", "v")]
+        out_qkv = [bf["q"], bf["k"], bf["v"]]
         if first:
-            c.rmsnorm(bf["x"], L["attn_norm"], y=bf["a"], stream=st)
+            c.gemm_norm_f32act(qkv, bf["x"], L["attn_norm"], out_qkv, eps=EPS, stream=st)
         else:
-            c.rmsnorm(bf["h1"], L["attn_norm"], y=bf["a"], residual=bf["down"], h=bf["x"], stream=st)
-        self.tern(("q", "k", "v"), L, bf["a"])
+            c.gemm_norm_f32act(qkv, bf["h1"], L["attn_norm"], out_qkv, residual=bf["down"],
+                               h=bf["x"], eps=EPS, stream=st)
         c.rope_attention_decode(bf["q"], bf["k"], bf["v"], self.kc[li], self.vc[li], self.pos,
                                 N_HEAD, N_KV, ROPE_BASE, out=bf["attn"], stream=st)
-        c.rmsnorm(bf["attn"], L["attn_sub_norm"], y=bf["b"], stream=st)
-        self.tern(("o",), L, bf["b"])
-        c.rmsnorm(bf["x"], L["ffn_norm"], y=bf["f"], residual=bf["o"], h=bf["h1"], stream=st)
-        self.tern(("gate", "up"), L, bf["f"])
-        c.swiglu_rmsnorm(bf["gate"], bf["up"], L["ffn_sub_norm"], y=bf["s"], stream=st)
-        self.tern(("down",), L, bf["s"])
+        c.gemm_norm_f32act([L["o"]], bf["attn"], L["attn_sub_norm"], [bf["o"]], eps=EPS, stream=st)
+        c.gemm_norm_f32act([L["gate"], L["up"]], bf["x"], L["ffn_norm"], [bf["gate"], bf["up"]],
+                           residual=bf["o"], h=bf["h1"], eps=EPS, stream=st)
+        c.gemm_norm_f32act([L["down"]], bf["gate"], L["ffn_sub_norm"], [bf["down"]],
+                           residual=bf["up"], swiglu=True, eps=EPS, stream=st)
 
     def step(self):
         """One token for every sequence: embed, 30 layers, lm_head, greedy pick."""

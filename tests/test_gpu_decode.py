@@ -142,13 +142,51 @@ def _tern(dec, w, x):
     return y
 
 
+def _close_q(got, want, w, x_normed):
+    """A product of a normalised row computed with a different order of the
+    sum of squares: equal up to 1e-5 relative (an ulp of 1/rms moves every
+    output) plus at most four int8 code flips per output, each worth
+    w_scale * s_x."""
+    s_x = x_normed.abs().amax(dim=1, keepdim=True) / 127.0
+    torch.testing.assert_close(got, want, rtol=1e-5, atol=0.0 + float((4 * w.w_scale * s_x).max()))
+
+
+@pytest.mark.parametrize("B", [1, 2, 3, 16])
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_gemm_norm_f32act(ctx, B, swiglu):
+    """y_i = W_i (rmsnorm(x + r) * w), or with the SwiGLU product, fused into the
+    GEMV prologue for B <= 2 (the norm kernel plus the grouped product above)."""
+    from ouroboros_b200.decode import Decoder, EPS
+    dec = Decoder(ctx, layers=1, batch=B, context=8, generate=2, vocab=64, seed=11)
+    L = dec.layers[0]
+    g = torch.Generator(device="cuda").manual_seed(B)
+    K = 6912 if swiglu else 2560
+    names = ("down",) if swiglu else ("q", "k", "v")
+    x = 2 * torch.randn((B, K), generator=g, device="cuda")
+    r = torch.randn((B, K), generator=g, device="cuda")
+    nw = L["ffn_sub_norm"] if swiglu else L["attn_norm"]
+    h = None if swiglu else torch.empty_like(x)
+    ys = [torch.empty((B, L[n].M), device="cuda") for n in names]
+    ctx.gemm_norm_f32act([L[n] for n in names], x, nw, ys, residual=r, swiglu=swiglu, h=h,
+                         eps=EPS, stream=dec.stream)
+    v = (x.double() / (1 + torch.exp(-x.double())) * r.double()).float() if swiglu else x + r
+    a = _ref_rms(v, nw)
+    refs = [_tern(dec, L[n], a) for n in names]
+    dec.stream.synchronize()
+    if h is not None:
+        assert torch.equal(h, x + r)
+    for n, y, ref in zip(names, ys, refs):
+        _close_q(y, ref, L[n], a)
+    dec.free()
+
+
 @pytest.mark.parametrize("B", [1, 3, 16])
 def test_fused_decode_layer_wiring(ctx, B):
     """Every stage of a fused layer against its torch formula applied to the
     fused path's own inputs of that stage. A whole step cannot be compared with
     a tolerance: the int8 quantisation of each activation turns a last-bit
     difference into a one-step code change that later layers amplify, so the
-    stages are checked one by one (the ternary products bit-exactly)."""
+    stages are checked one by one."""
     from ouroboros_b200.decode import (Decoder, HIDDEN, N_HEAD, N_KV, HEAD_DIM, EPS)
     dec = Decoder(ctx, layers=2, batch=B, context=64, generate=4, vocab=512, seed=3)
     bf = dec.buf
@@ -162,32 +200,34 @@ def test_fused_decode_layer_wiring(ctx, B):
             dec.layer_fused(li, li == 0)
             dec.stream.synchronize()
             assert torch.equal(bf["x"], x_in)
-            torch.testing.assert_close(bf["a"], _ref_rms(x_in, L["attn_norm"]), **norm)
-            q_raw, k_raw, v_raw = (_tern(dec, L[n], bf["a"]) for n in ("q", "k", "v"))
+            a = _ref_rms(x_in, L["attn_norm"])
+            q_raw, k_raw, v_raw = (_tern(dec, L[n], a) for n in ("q", "k", "v"))
             dec.stream.synchronize()
-            assert torch.equal(bf["q"], q_raw)
-            assert torch.equal(bf["k"], k_raw) and torch.equal(bf["v"], v_raw)
+            for n, ref in (("q", q_raw), ("k", k_raw), ("v", v_raw)):
+                _close_q(bf[n], ref, L[n], a)
             torch.testing.assert_close(dec.kc[li][:, :, pos],
-                                       _rope_ref(k_raw.view(B, N_KV, HEAD_DIM), pos), **norm)
-            assert torch.equal(dec.vc[li][:, :, pos], v_raw.view(B, N_KV, HEAD_DIM))
-            q_rot = _rope_ref(q_raw.view(B, N_HEAD, HEAD_DIM), pos).reshape(B, -1)
+                                       _rope_ref(bf["k"].view(B, N_KV, HEAD_DIM), pos), **norm)
+            assert torch.equal(dec.vc[li][:, :, pos], bf["v"].view(B, N_KV, HEAD_DIM))
+            q_rot = _rope_ref(bf["q"].view(B, N_HEAD, HEAD_DIM), pos).reshape(B, -1)
             torch.testing.assert_close(
                 bf["attn"], _attn_ref(q_rot, dec.kc[li], dec.vc[li], pos, N_HEAD, N_KV),
                 rtol=1e-4, atol=1e-5)
-            torch.testing.assert_close(bf["b"], _ref_rms(bf["attn"], L["attn_sub_norm"]), **norm)
-            o = _tern(dec, L["o"], bf["b"])
+            b = _ref_rms(bf["attn"], L["attn_sub_norm"])
+            o = _tern(dec, L["o"], b)
             dec.stream.synchronize()
-            assert torch.equal(bf["o"], o)
-            assert torch.equal(bf["h1"], x_in + o)
-            torch.testing.assert_close(bf["f"], _ref_rms(bf["h1"], L["ffn_norm"]), **norm)
-            gate, up = _tern(dec, L["gate"], bf["f"]), _tern(dec, L["up"], bf["f"])
+            _close_q(bf["o"], o, L["o"], b)
+            assert torch.equal(bf["h1"], x_in + bf["o"])
+            f = _ref_rms(bf["h1"], L["ffn_norm"])
+            gate, up = _tern(dec, L["gate"], f), _tern(dec, L["up"], f)
             dec.stream.synchronize()
-            assert torch.equal(bf["gate"], gate) and torch.equal(bf["up"], up)
-            act = (gate.double() / (1 + torch.exp(-gate.double())) * up.double()).float()
-            torch.testing.assert_close(bf["s"], _ref_rms(act, L["ffn_sub_norm"]), **norm)
-            down = _tern(dec, L["down"], bf["s"])
+            _close_q(bf["gate"], gate, L["gate"], f)
+            _close_q(bf["up"], up, L["up"], f)
+            act = (bf["gate"].double() / (1 + torch.exp(-bf["gate"].double())) *
+                   bf["up"].double()).float()
+            s_ = _ref_rms(act, L["ffn_sub_norm"])
+            down = _tern(dec, L["down"], s_)
             dec.stream.synchronize()
-            assert torch.equal(bf["down"], down)
+            _close_q(bf["down"], down, L["down"], s_)
     dec.free()
 
 

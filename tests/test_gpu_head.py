@@ -134,3 +134,13 @@ def test_argmax_token_rejects_other_formats(ctx, oracle):
     with pytest.raises(oq.OuroqError):
         ctx.argmax_token(w, _dev(oracle.normals(1, 256).reshape(1, 256)))
     w.free()
+
+
+def test_ptr_kind(ctx):
+    import torch
+    d = torch.empty(16, device="cuda")
+    pinned = torch.empty(16).pin_memory()
+    pageable = np.empty(16, np.float32)
+    assert oq.ptr_kind(d.data_ptr()) == (oq.PTR_DEVICE, 0)
+    assert oq.ptr_kind(pinned.data_ptr())[0] == oq.PTR_HOST
+    assert oq.ptr_kind(pageable.ctypes.data) == (oq.PTR_HOST, -1)
