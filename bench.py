@@ -84,7 +84,7 @@ WORKLOADS = {
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--steps", type=int, default=30000)
     ap.add_argument("--warmup", type=int, default=30)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--workload", default="layer", choices=sorted(WORKLOADS))
