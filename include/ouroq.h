@@ -280,7 +280,8 @@ ouroq_status ouroq_rope_attention_decode(ouroq_ctx *ctx, const float *q, const f
  * matrices w[i] (one format, one K), with v = x + residual (mode 0; residual
  * may be NULL; h, if not NULL, receives v) or v = silu(x) * residual (mode 1:
  * x the gate projection, residual the up projection, h NULL). x, residual,
- * h: device [B][K] fp32; y[i]: device [B][M_i]. Up to 2 tokens with rows of
+ * h: device [B][K] fp32, h overlapping neither x nor residual; y[i]: device
+ * [B][M_i]. Up to 2 tokens with rows of
  * up to 11520 values run as one launch (the norm in the GEMV prologue);
  * otherwise the norm kernel writes a context scratch row and the grouped
  * product reads it -- the same results either way up to the order of the sum

@@ -1520,6 +1520,15 @@ ouroq_status ouroq_gemm_norm_f32act(ouroq_ctx* ctx, int n, const ouroq_weight* c
     if (w[i]->K != w[0]->K) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "entries read one row width");
   }
   const int K = w[0]->K;
+  // one CTA writes h while the others still read x and the residual
+  const size_t row_bytes = (size_t)B * K * sizeof(float);
+  auto overlap = [&](const void* a, const void* b) {
+    const char* pa = static_cast<const char*>(a);
+    const char* pb = static_cast<const char*>(b);
+    return a && b && pa < pb + row_bytes && pb < pa + row_bytes;
+  };
+  if (h && (overlap(h, x) || overlap(h, residual)))
+    return fail(ctx, OUROQ_ERR_BAD_ARG, "h must not overlap x or the residual");
   DeviceGuard g(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool aligned = aligned16(x) && (!residual || aligned16(residual)) && aligned16(norm_w) &&

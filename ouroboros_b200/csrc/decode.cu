@@ -1,7 +1,9 @@
 // decode.cu -- the step either side of the ternary path in a decode layer
 // (cluster/src/infer/mod.rs:298-336), fused into a few kernels:
-//   rmsnorm_kernel        y = rmsnorm(x + r) * w, optionally h = x + r (residual)
-//   swiglu_norm_kernel    y = rmsnorm(silu(gate) * up) * w
+//   rmsnorm_vec_kernel    y = rmsnorm(x + r) * w, optionally h = x + r (residual);
+//                         rmsnorm_kernel for rows of any width or alignment
+//   swiglu_norm_vec_kernel  y = rmsnorm(silu(gate) * up) * w (swiglu_norm_kernel
+//                         for any width)
 //   rope_append_kernel    NeoX RoPE of q and k at the current position, k and v
 //                         appended to the layer's KV cache
 //   attn_decode_kernel    causal GQA attention, split over cache slices with
@@ -308,7 +310,7 @@ __global__ void __launch_bounds__((attn_nw(kG) + 1) * 32, 3)
   // The position and the cache rows before it were written by earlier decode
   // steps, which completed before this step's first kernel started (the step
   // begins with ordinary launches), so they are read before the wait for the
-  // previous kernel; q, k, v and every write come after it.
+  // previous kernel; q, k, v, the row at pos and every write come after it.
   const long long pos = *P.pos;
   float* out = P.out + ((size_t)b * P.n_head + (size_t)kh * G) * kHeadDim;
   if (pos < 0 || pos >= P.tmax) {
@@ -339,6 +341,11 @@ __global__ void __launch_bounds__((attn_nw(kG) + 1) * 32, 3)
   __syncthreads();
 
   if (warp == NW) {
+    // Without kRope the row at pos was appended by the caller, possibly by the
+    // launch just before this one: the slice holding it is fetched only after
+    // the dependency wait. (With kRope this kernel writes that row itself and
+    // takes it from registers, so every stage may be fetched early.)
+    if (!kRope) pdl_wait();
     if (lane == 0) {
       int c = 0;
       for (; c < nchunks; ++c) {

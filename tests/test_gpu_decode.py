@@ -106,6 +106,34 @@ def test_attention_decode(ctx, B, pos):
     torch.testing.assert_close(out, _attn_ref(q, kc, vc, pos, n_head, n_kv), rtol=1e-4, atol=1e-5)
 
 
+@pytest.mark.parametrize("B,pos", [(1, 31), (3, 700)])
+def test_append_then_attend_on_one_stream(ctx, B, pos):
+    """ouroq_rope_kv_append then ouroq_attention_decode back to back on one
+    stream (both with programmatic dependent launch): the attention must see
+    the row the append just wrote, and equal the fused call."""
+    n_head, n_kv, tmax = 20, 5, 1280
+    g = torch.Generator(device="cuda").manual_seed(pos + B)
+    q = torch.randn((B, n_head * 128), generator=g, device="cuda")
+    k = torch.randn((B, n_kv * 128), generator=g, device="cuda")
+    v = torch.randn((B, n_kv * 128), generator=g, device="cuda")
+    kc = torch.randn((B, n_kv, tmax, 128), generator=g, device="cuda")
+    vc = torch.randn((B, n_kv, tmax, 128), generator=g, device="cuda")
+    kc2, vc2 = kc.clone(), vc.clone()
+    p = torch.full((1,), pos, dtype=torch.long, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        fused = ctx.rope_attention_decode(q, k, v, kc2, vc2, p, n_head, n_kv, stream=s)
+        q2 = q.clone()
+        ctx.rope_kv_append(q2, k, v, kc, vc, p, n_head, n_kv, stream=s)
+        two = ctx.attention_decode(q2, kc, vc, p, n_head, n_kv, stream=s)
+    s.synchronize()
+    # the two kernels' RoPE may contract multiply-adds differently: last-bit tolerance
+    torch.testing.assert_close(kc, kc2, rtol=1e-6, atol=1e-6)
+    assert torch.equal(vc, vc2)
+    torch.testing.assert_close(two, fused, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(two, _attn_ref(q2, kc, vc, pos, n_head, n_kv), rtol=1e-4, atol=1e-5)
+
+
 def test_position_outside_the_cache_is_refused(ctx):
     B, n_head, n_kv, tmax = 1, 20, 5, 64
     q = torch.randn((B, n_head * 128), device="cuda")
@@ -177,6 +205,17 @@ def test_gemm_norm_f32act(ctx, B, swiglu):
         assert torch.equal(h, x + r)
     for n, y, ref in zip(names, ys, refs):
         _close_q(y, ref, L[n], a)
+    dec.free()
+
+
+def test_gemm_norm_refuses_aliased_h(ctx):
+    from ouroboros_b200.decode import Decoder
+    dec = Decoder(ctx, layers=1, batch=1, context=8, generate=2, vocab=64, seed=12)
+    L = dec.layers[0]
+    x = torch.randn((1, 2560), device="cuda")
+    y = torch.empty((1, L["q"].M), device="cuda")
+    with pytest.raises(oq.OuroqError):
+        ctx.gemm_norm_f32act([L["q"]], x, L["attn_norm"], [y], residual=x.clone(), h=x)
     dec.free()
 
 
