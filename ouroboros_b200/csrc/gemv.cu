@@ -229,8 +229,8 @@ __device__ __forceinline__ int seg_of(const Seg* segs, int nseg, int unit) {
 // them).
 template <int E>
 __device__ void prologue_units(const Seg* segs, int nseg, int nunits, const float* signs, int hb,
-                               float hscale, int* amax_bits, float* sx, int nscale, int B,
-                               int warp, int lane) {
+                               float hscale, int* amax_bits, float* sx, int* qtot, int nscale,
+                               int B, int warp, int lane) {
   constexpr int R = E >= 24 ? 1 : 24 / E;
   constexpr int kLanesPerGroup = 128 / E;
   float v[R][E];
@@ -285,8 +285,19 @@ __device__ void prologue_units(const Seg* segs, int nseg, int nunits, const floa
   const int ctid = threadIdx.x;
   if (ctid < nscale && (ctid & 7) < B) sx[ctid] = __fdiv_rn(__int_as_float(amax_bits[ctid]), 127.0f);
   named_bar_sync(1, kCThreads);
-  // ---- pass 2: quantise, store int8 codes and 128-group sums
+  // ---- pass 2: quantise, store int8 codes and 128-group sums; each warp adds
+  // the code sums of consecutive units of one row in a register and into the
+  // token's total once per row it leaves (integer sums: the order is free)
+  int run_seg = -1, run_sum = 0;
+  auto flush = [&]() {
+    if (run_seg >= 0 && lane % kLanesPerGroup == 0) atomicAdd(&qtot[segs[run_seg].sidx], run_sum);
+    run_sum = 0;
+  };
   auto quant_unit = [&](const float* w, int seg, int o) {
+    if (seg != run_seg) {  // warp-uniform
+      flush();
+      run_seg = seg;
+    }
     const Seg& S = segs[seg];
     const float sc = sx[S.sidx];
     const float rsc = __frcp_rn(sc);
@@ -296,7 +307,10 @@ __device__ void prologue_units(const Seg* segs, int nseg, int nunits, const floa
       *reinterpret_cast<uint32_t*>(S.q + o + i) = quant4(w[i], w[i + 1], w[i + 2], w[i + 3], sc, rsc, &sum);
 #pragma unroll
     for (int d = kLanesPerGroup / 2; d >= 1; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
-    if (lane % kLanesPerGroup == 0) S.qg[o / 128] = sum;
+    if (lane % kLanesPerGroup == 0) {
+      S.qg[o / 128] = sum;
+      run_sum += sum;
+    }
   };
 #pragma unroll
   for (int k = 0; k < R; ++k) {
@@ -323,6 +337,7 @@ __device__ void prologue_units(const Seg* segs, int nseg, int nunits, const floa
       quant_unit(w[k], wsg[k], wo[k]);
     }
   }
+  flush();
 }
 
 
@@ -335,14 +350,18 @@ __device__ void prologue_units(const Seg* segs, int nseg, int nunits, const floa
 // kNormFusedMaxUnits units), and the sum of squares is combined across warps
 // in a fixed order, so every CTA computes the same codes.
 template <int B>
-__device__ void prologue_norm(const NormSpec& N, int8_t* xq, int* qg, float* sx, int njs,
-                              int* amax_bits, float* ssq, float* inv_s, int warp, int lane) {
+__device__ void prologue_norm(const NormSpec& N, int8_t* xq, int* qg, float* sx, int* qtot,
+                              int njs, int* amax_bits, float* ssq, float* inv_s, int warp,
+                              int lane) {
   constexpr int E = 4, R = 6;
   static_assert(R * kCWarps == kNormFusedMaxUnits, "register budget of the fused norm");
   const int K = N.K;
   const int upt = K / (32 * E);  // units (128 values) per token
   const int nunits = B * upt;
-  if (threadIdx.x < B) amax_bits[threadIdx.x] = 0;
+  if (threadIdx.x < B) {
+    amax_bits[threadIdx.x] = 0;
+    qtot[threadIdx.x] = 0;  // token sums, in the first job's slots (read by every job)
+  }
   float v[R][E];
   float ssl[B];
 #pragma unroll
@@ -408,6 +427,9 @@ __device__ void prologue_norm(const NormSpec& N, int8_t* xq, int* qg, float* sx,
     for (int j = 0; j < njs; ++j) sx[j * 8 + threadIdx.x] = sc;
   }
   named_bar_sync(1, kCThreads);
+  int tsum[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) tsum[b] = 0;
 #pragma unroll
   for (int k = 0; k < R; ++k) {
     const int u = warp + k * kCWarps;
@@ -421,7 +443,15 @@ __device__ void prologue_norm(const NormSpec& N, int8_t* xq, int* qg, float* sx,
           quant4(v[k][0], v[k][1], v[k][2], v[k][3], sc, rsc, &sum);
       sum = warp_sum(sum);
       if (lane == 0) qg[b * (K / 128) + ut] = sum;
+#pragma unroll
+      for (int b2 = 0; b2 < B; ++b2)
+        if (b2 == b) tsum[b2] += sum;
     }
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int b = 0; b < B; ++b)
+      if (tsum[b]) atomicAdd(&qtot[b], tsum[b]);
   }
 }
 
@@ -524,7 +554,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     __shared__ float inv_s[2];
     __shared__ int amax_n[2];
     if constexpr (B <= 2)
-      prologue_norm<B>(L.norm, xwork, qg_base, sx_s, j_hi - j_lo + 1, amax_n, ssq, inv_s, warp, lane);
+      prologue_norm<B>(L.norm, xwork, qg_base, sx_s, qtot_s, j_hi - j_lo + 1, amax_n, ssq, inv_s,
+                       warp, lane);
   } else if (L.fused) {
     // one segment per (job, token) row; all jobs of a fused launch share the
     // rotation block (checked on the host), hence one unit size E
@@ -546,6 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             segs[nseg].first_unit = nunits;
             segs[nseg].sidx = (jj - j_lo) * 8 + b;
             amax_bits[(jj - j_lo) * 8 + b] = 0;
+            qtot_s[(jj - j_lo) * 8 + b] = 0;
           }
           nunits += J.K / (32 * e);
         }
@@ -556,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     named_bar_sync(1, kCThreads);
     const GemvJob& J0 = L.jobs[j_lo];
     prologue_units<e>(segs, nseg, nunits, J0.signs, J0.had_block, J0.had_scale, amax_bits, sx_s,
-                      (j_hi - j_lo + 1) * 8, B, warp, lane);
+                      qtot_s, (j_hi - j_lo + 1) * 8, B, warp, lane);
   } else {
     int xoff = 0, goff = 0;
     for (int jj = j_lo; jj <= j_hi; ++jj) {
@@ -579,8 +611,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     }
   }
   named_bar_sync(1, kCThreads);
-  if (FMT == kTern2) {
-    // per-token sums of each job: one warp per (job, token), lanes over groups
+  if (FMT == kTern2 && !L.fused) {
+    // per-token sums of each job (the fused prologues add them up as they
+    // quantise): one warp per (job, token), lanes over groups
     const int npairs = (j_hi - j_lo + 1) * B;
     for (int pr = warp; pr < npairs; pr += kCWarps) {
       const int jl = pr / B, b = pr - (pr / B) * B;
@@ -623,7 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     const int8_t* xs = xwork + xoff;
     const int* qg = qg_base + goff;
     const float* sx = sx_s + (ti.job - j_lo) * 8;
-    const int* qtot = qtot_s + (ti.job - j_lo) * 8;
+    const int* qtot = qtot_s + (shared_x ? 0 : (ti.job - j_lo) * 8);
     const int row = ti.row0 + lane;
     const bool row_ok = lane < ti.rows;
 
@@ -778,7 +811,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
       const TileInfo ti = tile_info(L, t_begin + tl);
       const GemvJob& J = L.jobs[ti.job];
       const int* rb = red + (size_t)tl * kCWarps * B * 32 + b * 32 + lane;
-      int acc = -qtot_s[(ti.job - j_lo) * 8 + b];
+      int acc = -qtot_s[(shared_x ? 0 : (ti.job - j_lo) * 8) + b];
 #pragma unroll
       for (int w = 0; w < kCWarps; ++w) acc += rb[w * B * 32];
       if (lane < ti.rows) {
