@@ -1,0 +1,37 @@
+"""bench.py's one-line JSON contract, checked on the host: the reference arm
+(the oracle on the host cores) runs without a GPU and must print every key
+the driver reads, with the reference arm's own additions."""
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _run(*args):
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), *args], cwd=ROOT,
+                         capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, out.stdout[-2000:]
+    return json.loads(lines[0])
+
+
+@pytest.mark.parametrize("workload", ["c1", "layer-tl1"])
+def test_reference_arm_line(workload):
+    d = _run("--impl", "reference", "--steps", "1", "--warmup", "1", "--workload", workload)
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+                "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference"
+    assert d["n_gpus"] == 1 and d["steps"] == 1 and d["warmup"] == 1
+    assert d["value"] > 0 and d["unit"] == "GB/s" and d["higher_is_better"] is True
+    assert d["config"]["workload"].endswith("-b1")
+    cb = d["cpu_baseline"]
+    assert cb["value"] == d["value"] and cb["cores"] >= 1 and cb["kind"] in ("port", "reference")
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
