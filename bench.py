@@ -139,6 +139,20 @@ def peaks():
     return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
 
 
+def sustained_bf16():
+    """The bf16 rate to hold a tensor-bound kernel against when it is timed
+    inside a seconds-long loop (the clocks settle under the power cap): the
+    measured sustained figure, else the burst figure of peaks()."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops_sustained"]), "measured bf16_tflops_sustained"
+        except Exception:
+            pass
+    _, bf16, kind = peaks()
+    return bf16, f"{kind} bf16_tflops"
+
+
 def profiled_traffic(key: str):
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
     p = ROOT / "profiles" / "traffic.json"
@@ -491,11 +505,13 @@ def run_ouroq(args, rank, world, local_rank):
                   else "gemv_kernel (8-token chunks)")
         del g2
     if tensor_bound:
-        int8_peak = 2.0 * bf16_peak
+        # the matmul launches run back to back for seconds: the sustained rate
+        bf16_rate, bf16_kind = sustained_bf16()
+        int8_peak = 2.0 * bf16_rate
         achieved = nb["ops"] / kern_s / 1e12
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1),
                 "unit": "TOPS", "frac": round(achieved / int8_peak, 4),
-                "peak_kind": f"int8 dense = 2 x {peak_kind} bf16_tflops",
+                "peak_kind": f"int8 dense = 2 x {bf16_kind}",
                 "ops_per_step": nb["ops"]}
     else:
         achieved = kern_bytes / kern_s / 1e9
