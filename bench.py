@@ -591,7 +591,8 @@ def cpu_decode_tokens_per_s(B: int, seconds: float, threads: int):
     """The same decode step on the host cores, bounded: one layer's seven
     ternary projections with the oracle's threaded int8 quantise + GEMV, its
     norms and attention over the 1024-token context in numpy, scaled to 30
-    layers, plus one lm_head product (f16 weights as fp32)."""
+    layers, plus the tied lm_head in the reference's own f16 order (an eighth
+    of the vocabulary, scaled)."""
     from oracle import pyoracle as O
     rng = np.random.default_rng(5)
     shapes = [(2560, 2560), (640, 2560), (640, 2560), (2560, 2560), (6912, 2560), (6912, 2560),
@@ -633,9 +634,12 @@ def cpu_decode_tokens_per_s(B: int, seconds: float, threads: int):
         if time.perf_counter() - t0 >= seconds:
             break
     t_layer = (time.perf_counter() - t0) / n
-    head = emb[:16384].astype(np.float32)  # an eighth of the lm_head, as fp32
+    # the tied lm_head as the reference computes it (matvec_f16: one fp32 chain
+    # per row, threaded over rows), on an eighth of the vocabulary, scaled
+    head = np.ascontiguousarray(emb[:16384]).view(np.uint16)
     t1 = time.perf_counter()
-    _ = x @ head.T
+    for b in range(B):
+        O.matvec_half(head, 16384, 2560, x[b], threads=threads)
     t_head = (time.perf_counter() - t1) * (128256 / 16384)
     return B / (30 * t_layer + t_head), n, 30 * t_layer + t_head
 
@@ -725,7 +729,8 @@ def run_decode(args, rank, world, local_rank):
         v, n, dt = cpu_decode_tokens_per_s(B, args.cpu_seconds, threads)
         cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
                "sample": f"{n} single-layer passes at batch {B} (oracle int8 GEMV, numpy norms and "
-                         f"attention over 1024 tokens) scaled to 30 layers, plus the lm_head; "
+                         f"attention over 1024 tokens) scaled to 30 layers, plus the lm_head in "
+                         f"the reference's matvec_f16 order (1/8 of the vocabulary, scaled); "
                          f"{threads} threads"}
     if rank == 0:
         line = {
