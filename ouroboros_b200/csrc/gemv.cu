@@ -590,24 +590,56 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     prologue_units<e>(segs, nseg, nunits, J0.signs, J0.had_block, J0.had_scale, amax_bits, sx_s,
                       qtot_s, (j_hi - j_lo + 1) * 8, B, warp, lane);
   } else {
-    int xoff = 0, goff = 0;
-    for (int jj = j_lo; jj <= j_hi; ++jj) {
-      const GemvJob& J = L.jobs[jj];
-      const int K = J.K, G = K / 128;
-      for (int b = 0; b < B; ++b) {
-        int8_t* q = xwork + xoff + b * K;
-        int* qg = qg_base + goff + b * G;
-        const int8_t* src = J.q + (size_t)b * K;
-        for (int g = warp; g < G; g += kCWarps) {
-          const uint32_t v = *reinterpret_cast<const uint32_t*>(src + g * 128 + lane * 4);
-          *reinterpret_cast<uint32_t*>(q + g * 128 + lane * 4) = v;
-          const int sum = warp_sum(__dp4a((int)v, 0x01010101, 0));
-          if (lane == 0) qg[g] = sum;
-        }
-        if (ctid == 0) sx_s[(jj - j_lo) * 8 + b] = J.s_x[b];
+    // Pre-quantised codes: every (job, token, 128-group) unit of the CTA's jobs
+    // is one 128-byte copy into shared memory plus its code sum. A job's units
+    // are contiguous in the source ([B][K] int8), in xwork and in qg, so unit
+    // u of job j is at offset (u - first unit of j) * 128 of each; a warp
+    // issues kCopyBatch units' loads before it uses any of them.
+    constexpr int kCopyBatch = 8;
+    __shared__ int ufirst[kMaxGemvJobs + 1], uxoff[kMaxGemvJobs], ugoff[kMaxGemvJobs];
+    const int njl = j_hi - j_lo + 1;
+    if (ctid == 0) {
+      int u = 0, xoff = 0, goff = 0;
+      for (int jl = 0; jl < njl; ++jl) {
+        const int K = L.jobs[j_lo + jl].K;
+        ufirst[jl] = u;
+        uxoff[jl] = xoff;
+        ugoff[jl] = goff;
+        u += B * (K / 128);
+        xoff += B * K;
+        goff += B * (K / 128);
       }
-      xoff += B * K;
-      goff += B * G;
+      ufirst[njl] = u;
+    }
+    if (ctid < njl * B) {
+      const int jl = ctid / B, b = ctid - (ctid / B) * B;
+      sx_s[jl * 8 + b] = L.jobs[j_lo + jl].s_x[b];
+    }
+    named_bar_sync(1, kCThreads);
+    const int nunits = ufirst[njl];
+    for (int u0 = warp; u0 < nunits; u0 += kCopyBatch * kCWarps) {
+      uint32_t v[kCopyBatch];
+      int jk[kCopyBatch];
+#pragma unroll
+      for (int k = 0; k < kCopyBatch; ++k) {
+        const int u = u0 + k * kCWarps;
+        jk[k] = -1;
+        if (u < nunits) {
+          int jl = 0;
+          while (u >= ufirst[jl + 1]) ++jl;
+          jk[k] = jl;
+          v[k] = *reinterpret_cast<const uint32_t*>(L.jobs[j_lo + jl].q +
+                                                    (size_t)(u - ufirst[jl]) * 128 + lane * 4);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kCopyBatch; ++k) {
+        if (jk[k] < 0) continue;  // warp-uniform
+        const int jl = jk[k], ul = u0 + k * kCWarps - ufirst[jl];
+        *reinterpret_cast<uint32_t*>(xwork + uxoff[jl] + ul * 128 + lane * 4) = v[k];
+        const int sum = warp_sum(__dp4a((int)v[k], 0x01010101, 0));
+        if (lane == 0) qg_base[ugoff[jl] + ul] = sum;
+      }
     }
   }
   named_bar_sync(1, kCThreads);
