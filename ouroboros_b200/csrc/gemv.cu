@@ -958,6 +958,8 @@ bool gemv_prepare(GemvLaunch& L, int num_sms, int smem_optin, int* grid_out, siz
   // kernel's static shared memory); capping it at the slices a CTA streams
   // measured slower on the wide shapes and no faster in decode
   const uint32_t budget = (uint32_t)smem_optin - 4096u;
+  // the deferred partials must leave room for a ring of at least four stages
+  if (L.defer && make_plan(L.fmt, L.B, 4, xcap, gcap, L.defer).total > budget) L.defer = 0;
   int stages = kMaxStages;
   while (stages > 2 && make_plan(L.fmt, L.B, stages, xcap, gcap, L.defer).total > budget) --stages;
   L.stages = stages;
