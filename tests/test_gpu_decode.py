@@ -208,6 +208,32 @@ def test_gemm_norm_f32act(ctx, B, swiglu):
     dec.free()
 
 
+@pytest.mark.parametrize("B", [1, 2, 4])
+def test_gemm_norm_f32act_sign_weights(ctx, oracle, B):
+    """The fused norm in front of 1-bit sign weights with fp16 group scales (the
+    sign epilogue reads the per-group code sums), against the library's own
+    product of the torch-normalised row: 1e-5 relative plus at most four code
+    steps, each worth the largest group scale times s_x."""
+    M, K = 1024, 4096
+    sg = oracle.signs(41, M * K).reshape(M, K)
+    sc = oracle.group_scales(42, M * (K // 128), 0.02)
+    w = ctx.upload(oq.SIGN1G128, oracle.pack_sign1(sg), M, K, scales=sc)
+    g = torch.Generator(device="cuda").manual_seed(43 + B)
+    x = torch.randn((B, K), generator=g, device="cuda")
+    r = torch.randn((B, K), generator=g, device="cuda")
+    nw = 1 + 0.02 * torch.randn(K, generator=g, device="cuda")
+    y = torch.empty((B, M), device="cuda")
+    ctx.gemm_norm_f32act([w], x, nw, [y], residual=r)
+    a = _ref_rms(x + r, nw)
+    ref = torch.empty((B, M), device="cuda")
+    ctx.gemm_group_f32act([w], [a], [ref])
+    torch.cuda.synchronize()
+    scale_max = float(np.abs(sc.view(np.float16).astype(np.float32)).max())
+    s_x = float((a.abs().amax() / 127.0).item())
+    torch.testing.assert_close(y, ref, rtol=1e-5, atol=4 * scale_max * s_x)
+    w.free()
+
+
 def test_gemm_norm_refuses_aliased_h(ctx):
     from ouroboros_b200.decode import Decoder
     dec = Decoder(ctx, layers=1, batch=1, context=8, generate=2, vocab=64, seed=12)
