@@ -660,11 +660,12 @@ cudaError_t launch_rope_append(const DecodeAttn& P, cudaStream_t s, bool pdl) {
 int attn_splits(int B, int n_head, int n_kv, int tmax, int num_sms) {
   // one resident wave (three CTAs per SM): longer slices stream better than
   // more, shorter ones, whose fixed cost (launch, query, record, count) would
-  // be paid per wave; at least two stages of positions per slice, and at most
+  // be paid per wave; at least four stages of positions per slice (fewer
+  // records for the merge; measured faster at B = 1 than two), and at most
   // kAttnMaxRecs records per head for the merge
   const int slots = 3 * num_sms;
   int S = slots / (B * n_kv);
-  const int max_s = (tmax + 2 * kAttnP - 1) / (2 * kAttnP);
+  const int max_s = (tmax + 4 * kAttnP - 1) / (4 * kAttnP);
   if (S > max_s) S = max_s;
   const int max_rec = kAttnMaxRecs / attn_nw(attn_kg(n_head / n_kv));
   if (S > max_rec) S = max_rec;
