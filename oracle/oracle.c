@@ -213,7 +213,7 @@ int orc_rotate_inv(float *x, const float *signs, size_t n, size_t block) {
 }
 
 /* ------------------------------------------------------------------ */
-/* activation quantisation (north_star K1; parity unpinned, fixed here) */
+/* activation quantisation (kernel K1; parity unpinned, fixed here)     */
 /* ------------------------------------------------------------------ */
 
 int orc_quantize_act(const float *x, int B, int K, const float *signs, int had_block, int8_t *q,

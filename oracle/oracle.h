@@ -21,8 +21,8 @@
  *       - matvec_qblock (TQ1_0)   cluster/src/infer/ops.rs:53-60,101-128
  *       - mt_threads chunking     cluster/src/infer/ops.rs:63-73,104-105
  *
- *  2. The int8-activation arithmetic that north_star names but the reference
- *     does not contain (it lives in the un-vendored bitnet-cpp submodule,
+ *  2. The int8-activation arithmetic of BitNet b1.58 that this library
+ *     targets but the reference does not contain (it lives in the un-vendored bitnet-cpp submodule,
  *     .gitmodules:1-3, commit unknown). PARITY UNPINNED: no reference test
  *     or golden vector covers it. Every free choice is fixed here in writing:
  *       - s_x = absmax / 127.0f (one fp32 divide); absmax == 0 -> s_x = 0, q = 0

@@ -3,7 +3,7 @@
 //
 // Reference operator: ops::matmul_q / matmul_tl1 (cluster/src/infer/ops.rs:
 // 162-230): K activation columns share each weight row, the output is
-// [k][out_len]. Here the arithmetic is north_star's: int8 activations, exact
+// [k][out_len]. Here the arithmetic is the BitNet b1.58 form: int8 activations, exact
 // int32 accumulation, y = ((float)acc * w_scale) * s_x, identical to the CPU
 // oracle (oracle/oracle.h).
 //

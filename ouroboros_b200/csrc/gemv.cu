@@ -5,8 +5,8 @@
 //
 // Reference operator: ops::matvec_q / matmul_q (cluster/src/infer/ops.rs:76-84,
 // 219-230), called per named tensor by Stage::wm / wmat_batched
-// (cluster/src/infer/mod.rs:138-167). The arithmetic follows north_star
-// (int8 activations, int32 accumulation, fp32 epilogue) with the conventions
+// (cluster/src/infer/mod.rs:138-167). The arithmetic is this library's BitNet
+// b1.58 form (per-token int8 activations, int32 accumulation, fp32 epilogue) with the conventions
 // fixed by the CPU oracle (oracle/oracle.h).
 //
 // Design (sm_100a):

@@ -7,7 +7,7 @@
 //   butterfly   cluster/src/infer/hadamard.rs:15-31  (h = 1, 2, 4, ...; lo = a+b, hi = a-b)
 // The rotation is bit-identical to the reference (see hadamard.cuh).
 //
-// Quantisation (north_star K1; not in the reference): s_x = absmax / 127,
+// Per-token absmax quantisation (kernel K1; not in the reference): s_x = absmax / 127,
 // q = clamp(rint(v / s_x), -127, 127), s_x == 0 -> q = 0.
 //
 // One CTA per (token, job). The token row is staged in shared memory and

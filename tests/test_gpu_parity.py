@@ -1,6 +1,6 @@
 """GPU parity: the CUDA path (through the C ABI) against the CPU oracle.
 
-Tolerances (north_star): int32 accumulators bit-exact; fp32 outputs and the
+Tolerances (the target's): int32 accumulators bit-exact; fp32 outputs and the
 Hadamard transform within 1e-5 relative. The kernels are built to reproduce
 the oracle's IEEE operation sequence, so every comparison below is exact
 equality, which implies both bounds; `assert_rel` states the 1e-5 bound
