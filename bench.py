@@ -328,13 +328,14 @@ def run_reference(args, rank):
         line = {"impl": "reference", "metric": "decode tokens/s", "value": round(v, 3),
                 "unit": "tokens/s", "n_gpus": args.gpus, "steps": n, "warmup": 0,
                 "ms_per_step": round(1e3 * args.batch / v, 3), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+                "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
                 "config": {"workload": f"bitnet2b-decode-b{args.batch}-ctx1024-gen256",
                            "batch": args.batch, "host_cpu": True},
                 "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": threads,
                                  "kind": "port",
-                                 "sample": f"{n} single-layer passes scaled to 30 layers plus "
-                                           f"the lm_head, {threads} threads"},
+                                 "sample": f"{n} single-layer passes (the reference's TQ1_0 "
+                                           f"matvec_qblock) scaled to 30 layers, plus the lm_head "
+                                           f"in the reference's matvec_f16 order, {threads} threads"},
                 "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
@@ -588,19 +589,23 @@ def run_ouroq(args, rank, world, local_rank):
 
 
 def cpu_decode_tokens_per_s(B: int, seconds: float, threads: int):
-    """The same decode step on the host cores, bounded: one layer's seven
-    ternary projections with the oracle's threaded int8 quantise + GEMV, its
-    norms and attention over the 1024-token context in numpy, scaled to 30
-    layers, plus the tied lm_head in the reference's own f16 order (an eighth
-    of the vocabulary, scaled)."""
+    """The same decode step on the host cores as the reference computes it,
+    bounded: one layer's seven projections as TQ1_0 shards through the
+    oracle's restatement of matvec_qblock (dequantise, then an fp32 dot in
+    element order, threaded over rows), its norms and attention over the
+    1024-token context in numpy, scaled to 30 layers, plus the tied lm_head in
+    the reference's f16 order (an eighth of the vocabulary, scaled)."""
     from oracle import pyoracle as O
     rng = np.random.default_rng(5)
     shapes = [(2560, 2560), (640, 2560), (640, 2560), (2560, 2560), (6912, 2560), (6912, 2560),
               (2560, 6912)]
     mats = []
     for i, (M, K) in enumerate(shapes):
-        w = O.ternary(900 + i, M * K).reshape(M, K)
-        mats.append((O.pack_tern2(w), M, K, float(O.absmean_scale(w, 0.02))))
+        pay = O.lcg_bytes(900 + i, M * (K // 256) * 54).reshape(-1, 54)
+        sc = (np.abs(rng.standard_normal(pay.shape[0])) * 0.02).astype(np.float16).view(np.uint16)
+        pay[:, 52] = sc & 0xFF
+        pay[:, 53] = sc >> 8
+        mats.append((pay.reshape(-1), M, K))
     kc = rng.standard_normal((B, 5, 1024, 128), dtype=np.float32)
     vc = rng.standard_normal((B, 5, 1024, 128), dtype=np.float32)
     emb = (0.02 * rng.standard_normal((128256, 2560))).astype(np.float16)
@@ -611,20 +616,22 @@ def cpu_decode_tokens_per_s(B: int, seconds: float, threads: int):
     def rms(v):
         return (v / np.sqrt((v * v).mean(-1, keepdims=True) + 1e-5)).astype(np.float32)
 
+    def proj(i, v):
+        pay, M, K = mats[i]
+        return np.stack([O.matvec_tq1(pay, M, K, v[b], threads) for b in range(B)])
+
     def layer():
-        q, s = O.quantize_act(rms(x))
-        qkv = [O.gemm_tern2_mt(p, M, K, ws, q, s, threads) for p, M, K, ws in mats[:3]]
-        qh = qkv[0].reshape(B, 20, 128)
+        a = rms(x)
+        q, _, _ = (proj(i, a) for i in range(3))
+        qh = q.reshape(B, 20, 128)
         att = np.einsum("bhd,bhtd->bht", qh, kc[:, kv_head]) / np.sqrt(128.0)
         pr = np.exp(att - att.max(-1, keepdims=True))
         pr /= pr.sum(-1, keepdims=True)
         o = np.einsum("bht,bhtd->bhd", pr, vc[:, kv_head]).reshape(B, 2560)
-        q2, s2 = O.quantize_act(rms(o))
-        h1 = x + O.gemm_tern2_mt(mats[3][0], 2560, 2560, mats[3][3], q2, s2, threads)
-        q3, s3 = O.quantize_act(rms(h1))
-        g_, u_ = [O.gemm_tern2_mt(p, M, K, ws, q3, s3, threads) for p, M, K, ws in mats[4:6]]
-        q4, s4 = O.quantize_act(rms(g_ / (1 + np.exp(-g_)) * u_))
-        O.gemm_tern2_mt(mats[6][0], 2560, 6912, mats[6][3], q4, s4, threads)
+        h1 = x + proj(3, rms(o))
+        f = rms(h1)
+        g_, u_ = proj(4, f), proj(5, f)
+        proj(6, rms(g_ / (1 + np.exp(-g_)) * u_))
 
     t0 = time.perf_counter()
     n = 0
@@ -728,10 +735,10 @@ def run_decode(args, rank, world, local_rank):
         threads = O.hw_threads()
         v, n, dt = cpu_decode_tokens_per_s(B, args.cpu_seconds, threads)
         cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"{n} single-layer passes at batch {B} (oracle int8 GEMV, numpy norms and "
-                         f"attention over 1024 tokens) scaled to 30 layers, plus the lm_head in "
-                         f"the reference's matvec_f16 order (1/8 of the vocabulary, scaled); "
-                         f"{threads} threads"}
+               "sample": f"{n} single-layer passes at batch {B} (the reference's TQ1_0 "
+                         f"matvec_qblock for the projections, numpy norms and attention over "
+                         f"1024 tokens) scaled to 30 layers, plus the lm_head in the reference's "
+                         f"matvec_f16 order (1/8 of the vocabulary, scaled); {threads} threads"}
     if rank == 0:
         line = {
             "metric": "decode tokens/s", "value": round(tok_s, 2), "unit": "tokens/s",
