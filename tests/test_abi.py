@@ -68,3 +68,11 @@ def test_product_package_does_not_load_the_oracle():
     for p in (ROOT / "ouroboros_b200").rglob("*"):
         if p.suffix in (".py", ".cpp", ".cu", ".cuh", ".h"):
             assert not pat.search(p.read_text()), p
+
+
+def test_ptr_kind_of_pageable_host_memory_without_a_device():
+    # cudaPointerGetAttributes answers for plain host memory even when the
+    # runtime finds no device; a caller on a CPU-only host gets PTR_HOST, -1
+    import numpy as np
+    a = np.empty(16, np.float32)
+    assert oq.ptr_kind(a.ctypes.data) == (oq.PTR_HOST, -1)
