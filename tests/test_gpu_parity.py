@@ -289,6 +289,19 @@ def test_host_mirrors_matvec_matmul(ctx, oracle):
     w.free()
 
 
+def test_empty_batch_is_a_no_op(ctx, oracle):
+    # matmul_q with k = 0 columns returns an empty vector (ops.rs:219-230)
+    import torch
+    packed, ws, _ = tern_case(oracle, 64, 256, 1, seed=2)
+    w = ctx.upload(oq.TERNARY2, packed, 64, 256, w_scale=ws)
+    assert ctx.matmul_q(w, np.empty((0, 256), np.float32)).shape == (0, 64)
+    assert ctx.gemm_f32act(w, torch.empty((0, 256), device="cuda")).shape == (0, 64)
+    q = torch.empty((0, 256), dtype=torch.int8, device="cuda")
+    assert ctx.gemm(w, q, torch.empty(0, device="cuda")).shape == (0, 64)
+    w.free()
+    ctx.check_device()
+
+
 # ---------------------------------------------------------------- C5 sizes
 @pytest.mark.parametrize("M,K", [(28672, 8192), (8192, 28672)])
 def test_c5_shapes_batch1_exact(ctx, oracle, M, K):
