@@ -261,6 +261,23 @@ def test_fused_hadamard_sign_gemv(ctx, oracle, M, K, B, block):
     w.free()
 
 
+@pytest.mark.parametrize("M,K,B", [(8192, 28672, 1), (1024, 28672, 2), (2048, 8192, 2)])
+def test_fused_wide_rows_exact(ctx, oracle, M, K, B):
+    # one fused launch quantising rows too wide for one round of loads per
+    # warp (28672 values = 224 units of 128): the later rounds must give the
+    # same codes, scales and sums as the oracle's quantiser
+    packed, ws, x = tern_case(oracle, M, K, B, seed=M + K + B)
+    qr, sr = oracle.quantize_act(x)
+    _, yr = oracle.gemm_tern2(packed, M, K, ws, qr, sr)
+    w = ctx.upload(oq.TERNARY2, packed, M, K, w_scale=ws)
+    xd = dev(x)
+    n0 = ctx.launch_count()
+    y = ctx.gemm_f32act(w, xd)
+    assert ctx.launch_count() - n0 == 1  # the fused path, not quantise + gemm
+    assert np.array_equal(host(y), yr)
+    w.free()
+
+
 def test_fused_group_rejects_oversized_activations(ctx, oracle):
     import torch
     packed, wsc, _ = tern_case(oracle, 64, 28672, 1, seed=3)
