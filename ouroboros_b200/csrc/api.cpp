@@ -87,6 +87,7 @@ struct ouroq_weight {
 
 namespace {
 
+__attribute__((format(printf, 3, 4)))
 ouroq_status fail(ouroq_ctx* ctx, ouroq_status st, const char* fmt, ...) {
   if (ctx) {
     char buf[512];
@@ -854,7 +855,8 @@ ouroq_status ouroq_gemm_group(ouroq_ctx* ctx, int n, const ouroq_weight* const* 
       return fail(ctx, OUROQ_ERR_UNSUPPORTED, "grouped calls take TERNARY2 / SIGN1G128 weights");
     if (w[i]->fmt != w[0]->fmt) return fail(ctx, OUROQ_ERR_UNSUPPORTED, "mixed formats in a group");
     if ((size_t)B * w[i]->K > kGemvMaxXBytes)
-      return fail(ctx, OUROQ_ERR_UNSUPPORTED, "B*K=%d exceeds the grouped GEMV limit", B * w[i]->K);
+      return fail(ctx, OUROQ_ERR_UNSUPPORTED, "B*K=%zu exceeds the grouped GEMV limit",
+                  (size_t)B * w[i]->K);
     if (!aligned16(q[i])) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "q[%d] not 16-byte aligned", i);
     L.jobs[i] = make_job(w[i], q[i], s_x[i], y[i], nullptr);
   }
