@@ -53,10 +53,11 @@ def test_fast_path_near_ties():
     n = rng.integers(-127, 127, 200000).astype(np.float32)
     base = ((n + np.float32(0.5)) * s).astype(np.float32)
     ulps = rng.integers(-8, 9, base.size).astype(np.int32)
-    v = np.nextafter(base, np.float32(np.inf) * np.sign(ulps)).astype(np.float32)
+    toward = np.where(ulps >= 0, np.float32(np.inf), np.float32(-np.inf))
+    v = np.nextafter(base, toward).astype(np.float32)
     v = np.where(ulps == 0, base, v)
     for k in range(2, 9):
-        v2 = np.where(np.abs(ulps) >= k, np.nextafter(v, np.float32(np.inf) * np.sign(ulps)), v)
+        v2 = np.where(np.abs(ulps) >= k, np.nextafter(v, toward), v)
         v = v2.astype(np.float32)
     got, nslow = fast_codes(v, s)
     assert np.array_equal(got, exact_codes(v, s))
