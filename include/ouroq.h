@@ -321,7 +321,8 @@ ouroq_status ouroq_bmts_span(const ouroq_bmts *f, const char *name, uint64_t off
                              uint64_t length, const void **out, char *err, size_t err_len);
 /* Stage::from_shard for one tensor (infer/mod.rs:110-123) plus the device
  * upload: dtype 143 (Tl1) -> OUROQ_FMT_PTQ1_0, 34 (TQ1_0) -> OUROQ_FMT_TQ1_0,
- * GGUF shape [in, out] -> K = shape[0], M = shape[1]. */
+ * 1 (F16) -> OUROQ_FMT_F16, 30 (BF16) -> OUROQ_FMT_BF16; GGUF shape [in, out]
+ * -> K = shape[0], M = shape[1]. Other dtypes: OUROQ_ERR_UNSUPPORTED. */
 ouroq_status ouroq_bmts_upload(ouroq_ctx *ctx, const ouroq_bmts *f, const char *name,
                                ouroq_weight **out, char *err, size_t err_len);
 
