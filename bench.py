@@ -259,12 +259,15 @@ def cpu_oracle_gbs(wl, host_mats, host_signs, B: int, seconds: float, threads: i
     while True:
         if fmt in REF_FMTS:
             # the reference's own algorithm for these formats, restated (threaded like it)
+            # (a workload that rotates: rotate_fwd of a copy before each matmul,
+            # as Qwen35Stage::wh does)
             for (_, M, K, xi), (packed, _) in zip(mats, host_mats):
                 for b in range(B):
+                    x = O.rotate_fwd(xs[xi][b], host_signs[xi], block) if block else xs[xi][b]
                     if fmt == TL1:
-                        O.matvec_tl1_sse(packed, M, K, xs[xi][b], threads)
+                        O.matvec_tl1_sse(packed, M, K, x, threads)
                     else:
-                        O.matvec_tq1(packed, M, K, xs[xi][b], threads)
+                        O.matvec_tq1(packed, M, K, x, threads)
             steps += 1
             dt = time.perf_counter() - t0
             if dt >= seconds:
@@ -343,31 +346,42 @@ def run_reference(args, rank):
     wl = WORKLOADS[args.workload]
     B = args.batch
     threads = O.hw_threads()
-    host_mats, host_signs = host_copy(wl, 11)
+    # The reference's own algorithm: its shard formats as they are; the
+    # TERNARY2 / SIGN1G128 shapes re-encoded as PTQ1_0 groups through
+    # matvec_tl1 (ops.rs:294-363, the SSE accumulation order), the path the
+    # reference runs for ternary and sign shards.
+    ref_wl = wl if wl[1] in REF_FMTS else (wl[0], TL1, wl[2], wl[3], wl[4])
+    host_mats, host_signs = host_copy(ref_wl, 11)
     for _ in range(max(min(args.warmup, 3), 1)):
-        cpu_oracle_gbs(wl, host_mats, host_signs, B, 0.0, threads)
+        cpu_oracle_gbs(ref_wl, host_mats, host_signs, B, 0.0, threads)
     total_t, total_steps = 0.0, 0
     budget = 60.0  # the whole run stays within minutes
     for _ in range(max(1, args.steps)):
-        _, st, dt = cpu_oracle_gbs(wl, host_mats, host_signs, B, 0.0, threads)
+        _, st, dt = cpu_oracle_gbs(ref_wl, host_mats, host_signs, B, 0.0, threads)
         total_t += dt
         total_steps += st
         if total_t >= budget:
             break
+    # the same step as the GPU arm's (same shapes and batch), so GB/s counts
+    # that arm's algorithmic bytes and the two values compare as step times
     gbs = step_bytes(wl, B)["step"] * total_steps / total_t / 1e9
     cfg = workload_config(args, wl, 1)
     cfg["host_cpu"] = True
+    cfg["reference_format"] = FMT_NAME[ref_wl[1]]
     line = {
         "impl": "reference", "metric": "packed-weight GEMV HBM GB/s",
         "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": total_steps,
         "warmup": args.warmup, "ms_per_step": round(1e3 * total_t / total_steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32" if wl[1] in REF_FMTS else "int8",
+        "dtype": "f32",
         "data": "synthetic", "config": cfg,
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": f"{total_steps} steps at batch {B} (" + (
                              "the reference's own fp32 algorithm for this format, restated"
-                             if wl[1] in REF_FMTS else "oracle int8 quantise + GEMV") +
+                             if wl[1] in REF_FMTS else
+                             "the reference's matvec_tl1 in fp32 on the same shapes re-encoded "
+                             "as PTQ1_0" + (", rotate_fwd first" if wl[4] else "") +
+                             ", one matvec per token; GB/s on the GPU arm's step bytes") +
                                    f", {threads} threads, rows chunked as ops.rs:104-105; "
                                    f"capped at {budget:.0f} s)"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
