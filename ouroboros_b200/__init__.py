@@ -153,8 +153,42 @@ def _ptr(t) -> int | None:
     if t is None:
         return None
     if isinstance(t, np.ndarray):
+        if not t.flags.c_contiguous:
+            raise OuroqError(7, "array must be C-contiguous")
         return t.ctypes.data
+    if not t.is_contiguous():
+        raise OuroqError(7, "tensor must be contiguous")
     return t.data_ptr()
+
+
+def _dev(t, dtype: str, numel: int | None, what: str, optional: bool = False) -> int | None:
+    """Address of a contiguous CUDA tensor of `dtype` ("float32", "int8", ...)
+    holding exactly `numel` elements (None: at least one). The C ABI takes bare
+    device pointers with no lengths, so a wrong dtype, size or layout is
+    caught here and raised like the reference's width check (Stage::wm,
+    infer/mod.rs:139-145) instead of becoming an out-of-bounds access."""
+    if t is None:
+        if optional:
+            return None
+        raise OuroqError(7, f"{what}: missing")
+    if isinstance(t, np.ndarray) or not getattr(t, "is_cuda", False):
+        raise OuroqError(7, f"{what}: expected a CUDA tensor")
+    if str(t.dtype) != "torch." + dtype:
+        raise OuroqError(7, f"{what}: dtype {t.dtype}, expected {dtype}")
+    if not t.is_contiguous():
+        raise OuroqError(7, f"{what}: not contiguous")
+    n = t.numel()
+    if (numel is None and n < 1) or (numel is not None and n != numel):
+        raise OuroqError(1, f"{what}: {n} elements, expected {numel if numel is not None else '>= 1'}")
+    return t.data_ptr()
+
+
+def _rows(x, width: int, what: str) -> int:
+    """Rows of an activation tensor [B][width] (a 1-D x of `width` is one row)."""
+    n = x.numel() if hasattr(x, "numel") else 0
+    if width <= 0 or n % width:
+        raise OuroqError(1, f"{what}: {n} elements is not a whole number of rows of {width}")
+    return n // width
 
 
 def _stream_ptr(stream) -> int | None:
@@ -192,6 +226,9 @@ class Weight:
     def __init__(self, ctx: "Context", handle: int, fmt: int, M: int, K: int):
         self.ctx, self.handle, self.fmt, self.M, self.K = ctx, handle, fmt, M, K
         self.w_scale = 0.0
+        # rows held on this device: M, or this rank's share of a row-sharded
+        # matrix (what the unsharded products write; gemm_sharded writes M)
+        self.rows = M
 
     @property
     def out_len(self) -> int:
@@ -277,74 +314,102 @@ class Context:
     # -- device API (torch CUDA tensors) --
     def quantize_act(self, x, signs=None, hadamard_block: int = 0, q=None, s_x=None, stream=None):
         import torch
+        if x.dim() != 2:
+            raise OuroqError(1, "x must be [B][K]")
         B, K = x.shape
         if q is None:
             q = torch.empty((B, K), dtype=torch.int8, device=x.device)
         if s_x is None:
             s_x = torch.empty((B,), dtype=torch.float32, device=x.device)
-        self._check(self.lib.ouroq_quantize_act(self.ctx, _ptr(x), B, K, _ptr(signs), hadamard_block,
-                                                _ptr(q), _ptr(s_x), _stream_ptr(stream)))
+        self._check(self.lib.ouroq_quantize_act(
+            self.ctx, _dev(x, "float32", B * K, "x"), B, K,
+            _dev(signs, "float32", K, "signs", True), hadamard_block,
+            _dev(q, "int8", B * K, "q"), _dev(s_x, "float32", B, "s_x"), _stream_ptr(stream)))
         return q, s_x
 
     def quantize_group(self, xs, qs, sxs, signs=None, blocks=None, stream=None):
         """One launch quantising several activation sets (same batch B)."""
         n = len(xs)
-        B = xs[0].shape[0]
+        if any(x.dim() != 2 for x in xs):
+            raise OuroqError(1, "every x must be [B][K]")
+        B = xs[0].shape[0] if n else 0
+        if any(x.shape[0] != B for x in xs):
+            raise OuroqError(1, "every x must have the same B")
+        K = [x.shape[1] for x in xs]
         arr = lambda vals: (_p * max(n, 1))(*vals)  # noqa: E731
-        Ks = (_i * max(n, 1))(*[x.shape[1] for x in xs])
-        sg = arr([_ptr(s) for s in signs]) if signs is not None else None
+        Ks = (_i * max(n, 1))(*K)
+        sg = (arr([_dev(sv, "float32", K[i], f"signs[{i}]", True) for i, sv in enumerate(signs)])
+              if signs is not None else None)
         bl = (_i * max(n, 1))(*blocks) if blocks is not None else None
         self._check(self.lib.ouroq_quantize_group(
-            self.ctx, n, arr([_ptr(x) for x in xs]), Ks, sg, bl, B, arr([_ptr(q) for q in qs]),
-            arr([_ptr(s) for s in sxs]), _stream_ptr(stream)))
+            self.ctx, n, arr([_dev(x, "float32", B * K[i], f"x[{i}]") for i, x in enumerate(xs)]),
+            Ks, sg, bl, B, arr([_dev(q, "int8", B * K[i], f"q[{i}]") for i, q in enumerate(qs)]),
+            arr([_dev(sv, "float32", B, f"s_x[{i}]") for i, sv in enumerate(sxs)]),
+            _stream_ptr(stream)))
         return qs, sxs
 
     def rotate(self, x, signs=None, block: int = 128, inverse: bool = False, out=None, stream=None):
         import torch
+        if x.dim() != 2:
+            raise OuroqError(1, "x must be [B][K]")
         B, K = x.shape
         if out is None:
             out = torch.empty_like(x)
-        self._check(self.lib.ouroq_rotate(self.ctx, _ptr(x), _ptr(out), B, K, _ptr(signs), block,
-                                          1 if inverse else 0, _stream_ptr(stream)))
+        self._check(self.lib.ouroq_rotate(
+            self.ctx, _dev(x, "float32", B * K, "x"), _dev(out, "float32", B * K, "out"), B, K,
+            _dev(signs, "float32", K, "signs", True), block, 1 if inverse else 0,
+            _stream_ptr(stream)))
         return out
 
     def gemm(self, w: Weight, q, s_x, y=None, acc=None, stream=None):
         import torch
-        B = q.shape[0]
+        B = _rows(q, w.K, "q")
         if y is None:
-            y = torch.empty((B, w.M), dtype=torch.float32, device=q.device)
-        self._check(self.lib.ouroq_gemm(self.ctx, w.handle, _ptr(q), _ptr(s_x), B, _ptr(y),
-                                        _ptr(acc), _stream_ptr(stream)))
+            y = torch.empty((B, w.rows), dtype=torch.float32, device=q.device)
+        nacc = B * w.rows * (w.K // 128 if w.fmt == SIGN1G128 else 1)
+        self._check(self.lib.ouroq_gemm(
+            self.ctx, w.handle, _dev(q, "int8", B * w.K, "q"), _dev(s_x, "float32", B, "s_x"), B,
+            _dev(y, "float32", B * w.rows, "y"), _dev(acc, "int32", nacc, "acc", True),
+            _stream_ptr(stream)))
         return y
 
     def gemm_group(self, ws, qs, sxs, ys, stream=None):
         n = len(ws)
-        B = qs[0].shape[0]
+        B = _rows(qs[0], ws[0].K, "q[0]") if n else 0
         arr = lambda vals: (_p * max(n, 1))(*vals)  # noqa: E731
         self._check(self.lib.ouroq_gemm_group(
-            self.ctx, n, arr([w.handle for w in ws]), arr([_ptr(q) for q in qs]),
-            arr([_ptr(s) for s in sxs]), B, arr([_ptr(y) for y in ys]), _stream_ptr(stream)))
+            self.ctx, n, arr([w.handle for w in ws]),
+            arr([_dev(q, "int8", B * w.K, f"q[{i}]") for i, (w, q) in enumerate(zip(ws, qs))]),
+            arr([_dev(sv, "float32", B, f"s_x[{i}]") for i, sv in enumerate(sxs)]), B,
+            arr([_dev(y, "float32", B * w.rows, f"y[{i}]") for i, (w, y) in enumerate(zip(ws, ys))]),
+            _stream_ptr(stream)))
         return ys
 
     def gemm_group_f32act(self, ws, xs, ys, signs=None, blocks=None, stream=None):
         """One launch: fused quantisation (+ optional rotation) and GEMV for each (W, x)."""
         n = len(ws)
-        B = xs[0].shape[0]
+        B = _rows(xs[0], ws[0].K, "x[0]") if n else 0
         arr = lambda vals: (_p * max(n, 1))(*vals)  # noqa: E731
-        sg = arr([_ptr(s) for s in signs]) if signs is not None else None
+        sg = (arr([_dev(sv, "float32", w.K, f"signs[{i}]", True)
+                   for i, (w, sv) in enumerate(zip(ws, signs))]) if signs is not None else None)
         bl = (_i * max(n, 1))(*blocks) if blocks is not None else None
         self._check(self.lib.ouroq_gemm_group_f32act(
-            self.ctx, n, arr([w.handle for w in ws]), arr([_ptr(x) for x in xs]), B, sg, bl,
-            arr([_ptr(y) for y in ys]), _stream_ptr(stream)))
+            self.ctx, n, arr([w.handle for w in ws]),
+            arr([_dev(x, "float32", B * w.K, f"x[{i}]") for i, (w, x) in enumerate(zip(ws, xs))]),
+            B, sg, bl,
+            arr([_dev(y, "float32", B * w.rows, f"y[{i}]") for i, (w, y) in enumerate(zip(ws, ys))]),
+            _stream_ptr(stream)))
         return ys
 
     def gemm_f32act(self, w: Weight, x, signs=None, hadamard_block: int = 0, y=None, stream=None):
         import torch
-        B = x.shape[0]
+        B = _rows(x, w.K, "x")
         if y is None:
-            y = torch.empty((B, w.M), dtype=torch.float32, device=x.device)
-        self._check(self.lib.ouroq_gemm_f32act(self.ctx, w.handle, _ptr(x), B, _ptr(signs),
-                                               hadamard_block, _ptr(y), _stream_ptr(stream)))
+            y = torch.empty((B, w.rows), dtype=torch.float32, device=x.device)
+        self._check(self.lib.ouroq_gemm_f32act(
+            self.ctx, w.handle, _dev(x, "float32", B * w.K, "x"), B,
+            _dev(signs, "float32", w.K, "signs", True), hadamard_block,
+            _dev(y, "float32", B * w.rows, "y"), _stream_ptr(stream)))
         return y
 
     def gemm_f32act_noalloc(self, w: Weight, x, y, signs=None, hadamard_block: int = 0, stream=None):
@@ -355,9 +420,11 @@ class Context:
         all calls on one device share one scratch area, so two calls in flight at
         once race. The first call on a device does set-up: make it before any
         stream capture."""
-        B = x.shape[0]
-        self._check(self.lib.ouroq_gemm_f32act_noalloc(self.ctx, w.handle, _ptr(x), B, _ptr(signs),
-                                                       hadamard_block, _ptr(y), _stream_ptr(stream)))
+        B = _rows(x, w.K, "x")
+        self._check(self.lib.ouroq_gemm_f32act_noalloc(
+            self.ctx, w.handle, _dev(x, "float32", B * w.K, "x"), B,
+            _dev(signs, "float32", w.K, "signs", True), hadamard_block,
+            _dev(y, "float32", B * w.rows, "y"), _stream_ptr(stream)))
         return y
 
     # -- row-sharded matmul (one process per GPU, NCCL all-gather) --
@@ -385,16 +452,21 @@ class Context:
                                                        ctypes.byref(h)))
         w = Weight(self, h.value, fmt, M, K)
         w.w_scale = float(w_scale)
+        rows = _i()
+        self._check(self.lib.ouroq_weight_info(w.handle, None, ctypes.byref(rows), None, None))
+        w.rows = rows.value
         return w
 
     def gemm_sharded(self, w: Weight, x, y=None, signs=None, hadamard_block: int = 0, stream=None):
         """y [B][M] (full M, every rank) from this rank's rows + an all-gather."""
         import torch
-        B = x.shape[0]
+        B = _rows(x, w.K, "x")
         if y is None:
             y = torch.empty((B, w.M), dtype=torch.float32, device=x.device)
-        self._check(self.lib.ouroq_gemm_sharded(self.ctx, w.handle, _ptr(x), B, _ptr(signs),
-                                                hadamard_block, _ptr(y), _stream_ptr(stream)))
+        self._check(self.lib.ouroq_gemm_sharded(
+            self.ctx, w.handle, _dev(x, "float32", B * w.K, "x"), B,
+            _dev(signs, "float32", w.K, "signs", True), hadamard_block,
+            _dev(y, "float32", B * w.M, "y"), _stream_ptr(stream)))
         return y
 
     def shard_sync(self, stream=None, timeout_ms: int = 10000) -> None:
@@ -404,39 +476,49 @@ class Context:
     def rmsnorm(self, x, w, y=None, residual=None, h=None, eps: float = 1e-5, stream=None):
         """y = rmsnorm(x + residual) * w; h (optional) receives x + residual."""
         import torch
-        B, n = x.shape
+        n = w.numel()
+        B = _rows(x, n, "x")
         if y is None:
             y = torch.empty_like(x)
-        self._check(self.lib.ouroq_rmsnorm(self.ctx, _ptr(x), _ptr(residual), _ptr(h), _ptr(w), _ptr(y),
-                                           B, n, eps, _stream_ptr(stream)))
+        self._check(self.lib.ouroq_rmsnorm(
+            self.ctx, _dev(x, "float32", B * n, "x"), _dev(residual, "float32", B * n, "residual", True),
+            _dev(h, "float32", B * n, "h", True), _dev(w, "float32", n, "w"),
+            _dev(y, "float32", B * n, "y"), B, n, eps, _stream_ptr(stream)))
         return y
 
     def swiglu_rmsnorm(self, gate, up, w, y=None, eps: float = 1e-5, stream=None):
         import torch
-        B, n = gate.shape
+        n = w.numel()
+        B = _rows(gate, n, "gate")
         if y is None:
             y = torch.empty_like(gate)
-        self._check(self.lib.ouroq_swiglu_rmsnorm(self.ctx, _ptr(gate), _ptr(up), _ptr(w), _ptr(y),
-                                                  B, n, eps, _stream_ptr(stream)))
+        self._check(self.lib.ouroq_swiglu_rmsnorm(
+            self.ctx, _dev(gate, "float32", B * n, "gate"), _dev(up, "float32", B * n, "up"),
+            _dev(w, "float32", n, "w"), _dev(y, "float32", B * n, "y"), B, n, eps,
+            _stream_ptr(stream)))
         return y
 
     def rope_kv_append(self, q, k, v, kcache, vcache, pos, n_head: int, n_kv: int,
                        rope_base: float = 500000.0, stream=None):
-        B = q.shape[0]
-        tmax = kcache.shape[-2]
-        self._check(self.lib.ouroq_rope_kv_append(self.ctx, _ptr(q), _ptr(k), _ptr(v), _ptr(kcache),
-                                                  _ptr(vcache), _ptr(pos), B, n_head, n_kv, tmax,
-                                                  rope_base, _stream_ptr(stream)))
+        B, tmax = _rows(q, n_head * 128, "q"), kcache.shape[-2]
+        kv = B * n_kv * 128
+        self._check(self.lib.ouroq_rope_kv_append(
+            self.ctx, _dev(q, "float32", B * n_head * 128, "q"), _dev(k, "float32", kv, "k"),
+            _dev(v, "float32", kv, "v"), _dev(kcache, "float32", kv * tmax, "kcache"),
+            _dev(vcache, "float32", kv * tmax, "vcache"), _dev(pos, "int64", None, "pos"), B,
+            n_head, n_kv, tmax, rope_base, _stream_ptr(stream)))
 
     def attention_decode(self, q, kcache, vcache, pos, n_head: int, n_kv: int, out=None, stream=None):
         import torch
-        B = q.shape[0]
-        tmax = kcache.shape[-2]
+        B, tmax = _rows(q, n_head * 128, "q"), kcache.shape[-2]
         if out is None:
             out = torch.empty((B, n_head * 128), dtype=torch.float32, device=q.device)
-        self._check(self.lib.ouroq_attention_decode(self.ctx, _ptr(q), _ptr(kcache), _ptr(vcache),
-                                                    _ptr(pos), _ptr(out), B, n_head, n_kv, tmax,
-                                                    _stream_ptr(stream)))
+        cache = B * n_kv * tmax * 128
+        self._check(self.lib.ouroq_attention_decode(
+            self.ctx, _dev(q, "float32", B * n_head * 128, "q"),
+            _dev(kcache, "float32", cache, "kcache"), _dev(vcache, "float32", cache, "vcache"),
+            _dev(pos, "int64", None, "pos"), _dev(out, "float32", B * n_head * 128, "out"), B,
+            n_head, n_kv, tmax, _stream_ptr(stream)))
         return out
 
     def gemm_norm_f32act(self, ws, x, norm_w, ys, residual=None, swiglu=False, h=None,
@@ -444,35 +526,46 @@ class Context:
         """ys[i] = W_i (rmsnorm(x + residual) * norm_w), or with swiglu=True
         W_i (rmsnorm(silu(x) * residual) * norm_w); h receives x + residual."""
         n = len(ws)
-        B = x.shape[0]
+        if n == 0:
+            raise OuroqError(1, "no matrices")
+        K = ws[0].K
+        B = _rows(x, K, "x")
         arr = lambda vals: (_p * n)(*vals)  # noqa: E731
         self._check(self.lib.ouroq_gemm_norm_f32act(
-            self.ctx, n, arr([w.handle for w in ws]), _ptr(x), _ptr(residual), 1 if swiglu else 0,
-            _ptr(norm_w), eps, _ptr(h), B, arr([_ptr(y) for y in ys]), _stream_ptr(stream)))
+            self.ctx, n, arr([w.handle for w in ws]), _dev(x, "float32", B * K, "x"),
+            _dev(residual, "float32", B * K, "residual", not swiglu), 1 if swiglu else 0,
+            _dev(norm_w, "float32", K, "norm_w"), eps, _dev(h, "float32", B * K, "h", True), B,
+            arr([_dev(y, "float32", B * w.rows, f"y[{i}]") for i, (w, y) in enumerate(zip(ws, ys))]),
+            _stream_ptr(stream)))
         return ys
 
     def argmax_token(self, w: Weight, x, tokens=None, logits=None, stream=None):
         """Greedy next token of each row of x [B][K] through the F16 / BF16 head w
         (the reference's argmax_token); logits [B][M] are written if given."""
         import torch
-        B = x.shape[0]
+        B = _rows(x, w.K, "x")
         if tokens is None:
             tokens = torch.empty((B,), dtype=torch.long, device=x.device)
-        self._check(self.lib.ouroq_argmax_token(self.ctx, w.handle, _ptr(x), B, _ptr(logits),
-                                                _ptr(tokens), _stream_ptr(stream)))
+        self._check(self.lib.ouroq_argmax_token(
+            self.ctx, w.handle, _dev(x, "float32", B * w.K, "x"), B,
+            _dev(logits, "float32", B * w.rows, "logits", True), _dev(tokens, "int64", B, "tokens"),
+            _stream_ptr(stream)))
         return tokens
 
     def rope_attention_decode(self, q, k, v, kcache, vcache, pos, n_head: int, n_kv: int,
                               rope_base: float = 500000.0, out=None, stream=None):
         """rope_kv_append + attention_decode in one launch; q is not modified."""
         import torch
-        B = q.shape[0]
-        tmax = kcache.shape[-2]
+        B, tmax = _rows(q, n_head * 128, "q"), kcache.shape[-2]
         if out is None:
             out = torch.empty((B, n_head * 128), dtype=torch.float32, device=q.device)
+        kv = B * n_kv * 128
         self._check(self.lib.ouroq_rope_attention_decode(
-            self.ctx, _ptr(q), _ptr(k), _ptr(v), _ptr(kcache), _ptr(vcache), _ptr(pos), _ptr(out),
-            B, n_head, n_kv, tmax, rope_base, _stream_ptr(stream)))
+            self.ctx, _dev(q, "float32", B * n_head * 128, "q"), _dev(k, "float32", kv, "k"),
+            _dev(v, "float32", kv, "v"), _dev(kcache, "float32", kv * tmax, "kcache"),
+            _dev(vcache, "float32", kv * tmax, "vcache"), _dev(pos, "int64", None, "pos"),
+            _dev(out, "float32", B * n_head * 128, "out"), B, n_head, n_kv, tmax, rope_base,
+            _stream_ptr(stream)))
         return out
 
     # -- host-buffer mirrors of the reference operators (numpy in, numpy out) --
@@ -481,7 +574,7 @@ class Context:
         x = np.ascontiguousarray(x, dtype=np.float32)
         if x.shape != (w.K,):
             raise OuroqError(1, f"in_len {w.K} != x len {x.size}")
-        y = np.empty(w.M, dtype=np.float32)
+        y = np.empty(w.rows, dtype=np.float32)
         self._check(self.lib.ouroq_matvec_q(self.ctx, w.handle, _ptr(x), _ptr(y)))
         return y
 
@@ -491,7 +584,7 @@ class Context:
         if x.ndim != 2 or x.shape[1] != w.K:
             raise OuroqError(1, f"in_len {w.K} != x width {x.shape[-1]}")
         k = x.shape[0]
-        y = np.empty((k, w.M), dtype=np.float32)
+        y = np.empty((k, w.rows), dtype=np.float32)
         self._check(self.lib.ouroq_matmul_q(self.ctx, w.handle, _ptr(x), k, _ptr(y)))
         return y
 
