@@ -35,3 +35,19 @@ def test_reference_arm_line(workload):
     assert cb["value"] == d["value"] and cb["cores"] >= 1 and cb["kind"] in ("port", "reference")
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_under_torchrun_prints_once():
+    # the driver launches both arms with torch.distributed.run for N > 1: rank 0
+    # alone runs the host-CPU reference and prints; the other ranks exit 0
+    out = subprocess.run(
+        [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+         "--master-addr", "127.0.0.1", "--master-port", "29617", str(ROOT / "bench.py"),
+         "--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "1",
+         "--workload", "c1"],
+        cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, out.stdout[-2000:]
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
