@@ -20,8 +20,10 @@ Walsh-Hadamard block 128 on the activations).
 
 Arms:
   (default)          the CUDA library (ouroboros_b200 / libouroq.so)
-  --impl reference   the reference arithmetic on the host CPU: the oracle's
-                     threaded restatement, same config / metric / unit
+  --impl reference   the reference's own CPU algorithm on the host cores, as
+                     the oracle restates it (matvec_tl1 / matmul_tl1 on the
+                     workload's shapes in PTQ1_0, matvec_qblock for TQ1_0),
+                     same config / metric / unit
 Launch: python bench.py [--gpus N --steps K --warmup W]; N > 1 under
 torch.distributed.run (one rank per GPU, NCCL), every rank a replica with
 its own weights (no data-path collective: weak scaling).
@@ -260,14 +262,21 @@ def cpu_oracle_gbs(wl, host_mats, host_signs, B: int, seconds: float, threads: i
         if fmt in REF_FMTS:
             # the reference's own algorithm for these formats, restated (threaded like it)
             # (a workload that rotates: rotate_fwd of a copy before each matmul,
-            # as Qwen35Stage::wh does)
+            # as Qwen35Stage::wh does). Several tokens of a Tl1 matrix go through
+            # matmul_tl1's K-column path (Stage::wmat_batched -> matmul_q,
+            # ops.rs:219-230); other formats run one matvec per token there too.
             for (_, M, K, xi), (packed, _) in zip(mats, host_mats):
+                xb = xs[xi]
+                if block:
+                    xb = np.stack([O.rotate_fwd(xb[b], host_signs[xi], block) for b in range(B)])
+                if fmt == TL1 and B > 1:
+                    O.matmul_tl1_sse(packed, M, K, xb, B, threads)
+                    continue
                 for b in range(B):
-                    x = O.rotate_fwd(xs[xi][b], host_signs[xi], block) if block else xs[xi][b]
                     if fmt == TL1:
-                        O.matvec_tl1_sse(packed, M, K, x, threads)
+                        O.matvec_tl1_sse(packed, M, K, xb[b], threads)
                     else:
-                        O.matvec_tq1(packed, M, K, x, threads)
+                        O.matvec_tq1(packed, M, K, xb[b], threads)
             steps += 1
             dt = time.perf_counter() - t0
             if dt >= seconds:
@@ -381,7 +390,8 @@ def run_reference(args, rank):
                              if wl[1] in REF_FMTS else
                              "the reference's matvec_tl1 in fp32 on the same shapes re-encoded "
                              "as PTQ1_0" + (", rotate_fwd first" if wl[4] else "") +
-                             ", one matvec per token; GB/s on the GPU arm's step bytes") +
+                             (", matmul_tl1's K-column path for the batch" if B > 1 else "") +
+                             "; GB/s on the GPU arm's step bytes") +
                                    f", {threads} threads, rows chunked as ops.rs:104-105; "
                                    f"capped at {budget:.0f} s)"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,

@@ -312,7 +312,7 @@ int orc_gemm_sign1(const uint8_t *packed, const uint16_t *scales, int M, int K, 
 /* ---- threaded variants: rows chunked as ceil(out/nt) like ops.rs:104-105 ---- */
 
 typedef struct {
-    int kind; /* 0 tern, 1 sign, 2 tl1 sse, 3 tq1 */
+    int kind; /* 0 tern, 1 sign, 2 tl1 sse, 3 tq1, 4 f16, 5 bf16, 6 tl1 sse K columns (B = k) */
     const uint8_t *packed;
     const uint16_t *scales;
     int r0, r1, M, K, B;
@@ -327,6 +327,8 @@ static void tl1_rows_sse(const uint8_t *payload, int r0, int r1, int in_len, con
                          float *y);
 static void tq1_rows(const uint8_t *payload, int r0, int r1, int in_len, const float *x,
                      float *y);
+static void tl1_rows_sse_k(const uint8_t *payload, int r0, int r1, int in_len, int out_len,
+                           const float *x, int k, float *y);
 static void half_rows(const uint8_t *payload, int r0, int r1, int in_len, const float *x,
                       float *y, int bf16);
 
@@ -350,6 +352,9 @@ static void *mt_worker(void *p) {
         case 4:
         case 5:
             half_rows(j->packed, j->r0, j->r1, j->K, j->xf, j->y, j->kind == 5);
+            break;
+        case 6:
+            tl1_rows_sse_k(j->packed, j->r0, j->r1, j->K, j->M, j->xf, j->B, j->y);
             break;
     }
     return NULL;
@@ -590,6 +595,123 @@ int orc_matmul_tl1_scalar(const uint8_t *payload, int out_len, int in_len, const
     }
     free(sums);
     return 0;
+}
+
+/*
+ * ops.rs:162-215 with tl1_rows_avx2_k (ops.rs:381-481), the x86 K-column path
+ * of matmul_tl1: each stage n of a group is decoded once (qs[0..8], qs[8..16],
+ * qs[16..24] -> 4-lane halves lo/hi) and fed to every column. Per column two
+ * 4-lane accumulators run over the whole row and take (t*d)*x in the order
+ * lo0, hi0, lo1, hi1, lo2, hi2; the qh tail goes to a scalar per-column sum
+ * that starts at zero (the scratch row); at the end of the row
+ * y = tail + (hsum(lo) + hsum(hi)). Output [k][out_len] (y[c*out_len + r]).
+ * This order differs from matvec_tl1's (one accumulator per group), so the two
+ * agree only within the reference's own test tolerance (ops.rs:721-750).
+ */
+#if defined(__x86_64__)
+__attribute__((target("sse4.1"))) static inline void decode8_halves(const uint8_t *p, int pn,
+                                                                    __m128 *lo, __m128 *hi) {
+    __m128i b = _mm_loadl_epi64((const __m128i *)p);
+    __m128i w = _mm_unpacklo_epi8(b, _mm_setzero_si128());
+    __m128i q = _mm_mullo_epi16(w, _mm_set1_epi16((short)pn));
+    q = _mm_and_si128(q, _mm_set1_epi16(0xFF));
+    q = _mm_mullo_epi16(q, _mm_set1_epi16(3));
+    q = _mm_srli_epi16(q, 8);
+    q = _mm_sub_epi16(q, _mm_set1_epi16(1));
+    *lo = _mm_cvtepi32_ps(_mm_cvtepi16_epi32(q));
+    *hi = _mm_cvtepi32_ps(_mm_cvtepi16_epi32(_mm_unpackhi_epi64(q, q)));
+}
+
+__attribute__((target("sse4.1"))) static inline __m128 mac4(__m128 t, __m128 d, const float *xp,
+                                                            __m128 acc) {
+    return _mm_add_ps(_mm_mul_ps(_mm_mul_ps(t, d), _mm_loadu_ps(xp)), acc);
+}
+
+__attribute__((target("sse4.1"))) static void tl1_rows_sse_k(const uint8_t *payload, int r0,
+                                                             int r1, int in_len, int out_len,
+                                                             const float *x, int k, float *y) {
+    if (k <= 0) return;
+    int gpr = in_len / 128;
+    __m128 *acc = (__m128 *)aligned_alloc(16, sizeof(__m128) * 2 * (size_t)k);
+    float *tail = (float *)malloc(sizeof(float) * (size_t)k);
+    for (int row = r0; row < r1; row++) {
+        size_t row_base = (size_t)row * gpr * 28;
+        for (int c = 0; c < 2 * k; c++) acc[c] = _mm_setzero_ps();
+        for (int c = 0; c < k; c++) tail[c] = 0.0f;
+        for (int g = 0; g < gpr; g++) {
+            const uint8_t *qs = payload + row_base + (size_t)g * 28;
+            float d = orc_f16_to_f32((uint16_t)(qs[26] | (qs[27] << 8)));
+            __m128 dv = _mm_set1_ps(d);
+            size_t xg = (size_t)g * 128;
+            for (int n = 0; n < 5; n++) {
+                __m128 lo0, hi0, lo1, hi1, lo2, hi2;
+                decode8_halves(qs, POW3[n], &lo0, &hi0);
+                decode8_halves(qs + 8, POW3[n], &lo1, &hi1);
+                decode8_halves(qs + 16, POW3[n], &lo2, &hi2);
+                for (int c = 0; c < k; c++) {
+                    const float *xp = x + (size_t)c * in_len + xg;
+                    __m128 a = acc[2 * c], b = acc[2 * c + 1];
+                    a = mac4(lo0, dv, xp + n * 16, a);
+                    b = mac4(hi0, dv, xp + n * 16 + 4, b);
+                    a = mac4(lo1, dv, xp + n * 16 + 8, a);
+                    b = mac4(hi1, dv, xp + n * 16 + 12, b);
+                    a = mac4(lo2, dv, xp + 80 + n * 8, a);
+                    b = mac4(hi2, dv, xp + 80 + n * 8 + 4, b);
+                    acc[2 * c] = a;
+                    acc[2 * c + 1] = b;
+                }
+            }
+            const uint8_t *qh = qs + 24;
+            for (int n = 0; n < 4; n++)
+                for (int m = 0; m < 2; m++) {
+                    float t = (float)(digit(qh[m], n) - 1) * d;
+                    for (int c = 0; c < k; c++)
+                        tail[c] = tail[c] + t * x[(size_t)c * in_len + xg + 120 + n * 2 + m];
+                }
+        }
+        for (int c = 0; c < k; c++)
+            y[(size_t)c * out_len + row] = tail[c] + (hsum4(acc[2 * c]) + hsum4(acc[2 * c + 1]));
+    }
+    free(acc);
+    free(tail);
+}
+#else
+/* elsewhere the reference runs tl1_rows_scalar_k (ops.rs:244-286) */
+static void tl1_rows_sse_k(const uint8_t *payload, int r0, int r1, int in_len, int out_len,
+                           const float *x, int k, float *y) {
+    int gpr = in_len / 128;
+    for (int row = r0; row < r1; row++) {
+        size_t row_base = (size_t)row * gpr * 28;
+        for (int c = 0; c < k; c++) {
+            const float *xc = x + (size_t)c * in_len;
+            float acc = 0.0f;
+            for (int g = 0; g < gpr; g++) {
+                const uint8_t *gb = payload + row_base + (size_t)g * 28;
+                float d = orc_f16_to_f32((uint16_t)(gb[26] | (gb[27] << 8)));
+                const float *xg = xc + (size_t)g * 128;
+                for (int n = 0; n < 5; n++) {
+                    for (int m = 0; m < 16; m++)
+                        acc = acc + (float)(digit(gb[m], n) - 1) * d * xg[n * 16 + m];
+                    for (int m = 0; m < 8; m++)
+                        acc = acc + (float)(digit(gb[16 + m], n) - 1) * d * xg[80 + n * 8 + m];
+                }
+                for (int n = 0; n < 4; n++)
+                    for (int m = 0; m < 2; m++)
+                        acc = acc + (float)(digit(gb[24 + m], n) - 1) * d * xg[120 + n * 2 + m];
+            }
+            y[(size_t)c * out_len + row] = acc;
+        }
+    }
+}
+#endif
+
+int orc_matmul_tl1_sse(const uint8_t *payload, int out_len, int in_len, const float *x, int k,
+                       float *y, int threads) {
+    if (in_len % 128 || k < 0 || out_len < 0) return -1;
+    if (k == 0 || out_len == 0) return 0;
+    mt_job j = {0};
+    j.kind = 6, j.packed = payload, j.M = out_len, j.K = in_len, j.B = k, j.xf = x, j.y = y;
+    return run_mt(j, out_len, threads);
 }
 
 /* ops.rs:101-128 with dequant_tq1_row (dequant.rs:96-105) then dot (ops.rs:53-60) */

@@ -18,6 +18,7 @@
  *       - matvec_tl1 (scalar)     cluster/src/infer/ops.rs:294-363
  *       - matvec_tl1 (SSE4.1)     cluster/src/infer/ops.rs:499-584
  *       - matmul_tl1 (scalar K)   cluster/src/infer/ops.rs:162-286
+ *       - matmul_tl1 (SSE4.1 K)   cluster/src/infer/ops.rs:162-215,381-481
  *       - matvec_qblock (TQ1_0)   cluster/src/infer/ops.rs:53-60,101-128
  *       - mt_threads chunking     cluster/src/infer/ops.rs:63-73,104-105
  *
@@ -97,6 +98,9 @@ int orc_matvec_tl1_sse(const uint8_t *payload, int out_len, int in_len, const fl
                        float *y, int threads);
 int orc_matmul_tl1_scalar(const uint8_t *payload, int out_len, int in_len, const float *x,
                           int k, float *y /* [k][out_len] */);
+/* matmul_tl1's x86 K-column path (tl1_rows_avx2_k), rows threaded as ops.rs:166-167 */
+int orc_matmul_tl1_sse(const uint8_t *payload, int out_len, int in_len, const float *x, int k,
+                       float *y /* [k][out_len] */, int threads);
 int orc_matvec_tq1(const uint8_t *payload, int out_len, int in_len, const float *x, float *y,
                    int threads);
 /* 16-bit weights (QuantKind::F16 / Bf16) and the greedy pick */

@@ -68,6 +68,7 @@ def lib() -> ctypes.CDLL:
             "orc_matvec_tl1_scalar": (_i, [_u8p, _i, _i, _f32p, _f32p]),
             "orc_matvec_tl1_sse": (_i, [_u8p, _i, _i, _f32p, _f32p, _i]),
             "orc_matmul_tl1_scalar": (_i, [_u8p, _i, _i, _f32p, _i, _f32p]),
+            "orc_matmul_tl1_sse": (_i, [_u8p, _i, _i, _f32p, _i, _f32p, _i]),
             "orc_matvec_tq1": (_i, [_u8p, _i, _i, _f32p, _f32p, _i]),
             "orc_bf16_to_f32": (ctypes.c_float, [ctypes.c_uint16]),
             "orc_matvec_half": (_i, [_u8p, _i, _i, _f32p, _f32p, _i, _i]),
@@ -274,6 +275,16 @@ def matmul_tl1_scalar(payload, out_len, in_len, x, k):
     y = np.empty(k * out_len, np.float32)
     _chk(lib().orc_matmul_tl1_scalar(_p(payload, _u8p), out_len, in_len, _p(x, _f32p), k,
                                      _p(y, _f32p)), "matmul_tl1_scalar")
+    return y
+
+
+def matmul_tl1_sse(payload, out_len, in_len, x, k, threads=0):
+    """matmul_tl1's x86 K-column path: x [k][in_len] -> y [k * out_len] (y[c*out_len + r])."""
+    payload = np.ascontiguousarray(payload, np.uint8)
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty(k * out_len, np.float32)
+    _chk(lib().orc_matmul_tl1_sse(_p(payload, _u8p), out_len, in_len, _p(x, _f32p), k,
+                                  _p(y, _f32p), threads), "matmul_tl1_sse")
     return y
 
 

@@ -11,7 +11,7 @@ inputs and tolerance, and runs it against oracle/oracle.c:
   dequant.rs:693-702   f16 known values (incl. subnormal)
   ops.rs:782-798       F16 matmul_q == K x matvec_f16 (its payload restated)
   dequant.rs:705-726   TQ1_0 zero block and value set
-  ops.rs:721-750       matmul_tl1 K=4 == K x matvec_tl1
+  ops.rs:721-750       matmul_tl1 K=4 == K x matvec_tl1 (scalar and x86 K-column paths)
   ops.rs:801-838       fused matvec_tl1 == decode-then-dot
 
 The int8-activation arithmetic has no reference test (it lives in the absent
@@ -331,11 +331,58 @@ def test_matmul_tl1_k_columns_matches_matvec(oracle):
     out_len, in_len, k = 97, 384, 4
     payload = _tl1_payload(out_len, in_len, 5)
     x = np.array([((i % 11) - 5.0) * 0.25 for i in range(k * in_len)], np.float32)
-    batched = oracle.matmul_tl1_scalar(payload, out_len, in_len, x, k)
-    for c in range(k):
-        want = oracle.matvec_tl1_sse(payload, out_len, in_len, x[c * in_len:(c + 1) * in_len])
-        got = batched[c * out_len:(c + 1) * out_len]
-        assert np.all(np.abs(got - want) <= 1e-3 * np.maximum(np.abs(want), 1.0))
+    scalar_k = oracle.matmul_tl1_scalar(payload, out_len, in_len, x, k)
+    sse_k = oracle.matmul_tl1_sse(payload, out_len, in_len, x, k)
+    for batched in (scalar_k, sse_k):
+        for c in range(k):
+            want = oracle.matvec_tl1_sse(payload, out_len, in_len, x[c * in_len:(c + 1) * in_len])
+            got = batched[c * out_len:(c + 1) * out_len]
+            assert np.all(np.abs(got - want) <= 1e-3 * np.maximum(np.abs(want), 1.0))
+    # every partial sum of this fixture is a multiple of 129/1024 below 2^18
+    # of them, exact in fp32: all accumulation orders agree bit for bit, which
+    # pins the K-column path's decode and indexing
+    assert np.array_equal(sse_k, scalar_k)
+
+
+def _tl1_k_lanes(oracle, payload, out_len, in_len, x, k):
+    """numpy statement of tl1_rows_avx2_k's order (ops.rs:381-481): two 4-lane
+    accumulators per column over the whole row, a scalar tail sum, and
+    y = tail + (hsum(lo) + hsum(hi)) with hsum(v) = (v0 + v2) + (v1 + v3)."""
+    f32 = np.float32
+    gpr = in_len // 128
+    x = x.reshape(k, in_len)
+    y = np.empty(k * out_len, f32)
+    hs = lambda v: f32(f32(v[0] + v[2]) + f32(v[1] + v[3]))  # noqa: E731
+    for r in range(out_len):
+        lo = np.zeros((k, 4), f32)
+        hi = np.zeros((k, 4), f32)
+        tail = np.zeros(k, f32)
+        for g in range(gpr):
+            w = oracle.tl1_group(payload[(r * gpr + g) * 28:(r * gpr + g + 1) * 28])
+            xg = x[:, g * 128:(g + 1) * 128]
+            for n in range(5):
+                for base, acc in ((n * 16, lo), (n * 16 + 4, hi), (n * 16 + 8, lo),
+                                  (n * 16 + 12, hi), (80 + n * 8, lo), (80 + n * 8 + 4, hi)):
+                    acc[:] = (w[base:base + 4] * xg[:, base:base + 4]) + acc
+            for n in range(4):
+                for m in range(2):
+                    i = 120 + n * 2 + m
+                    tail[:] = tail + w[i] * xg[:, i]
+        for c in range(k):
+            y[c * out_len + r] = f32(tail[c] + f32(hs(lo[c]) + hs(hi[c])))
+    return y
+
+
+def test_matmul_tl1_sse_k_order(oracle):
+    # random scales and activations: the K-column order differs from the
+    # per-group matvec order, and the restatement must follow it exactly
+    out_len, in_len, k = 23, 512, 3
+    payload = oracle.lcg_bytes(123, out_len * (in_len // 128) * 28)
+    g = payload.reshape(-1, 28)
+    g[:, 27] &= 0x3B  # finite f16 scales below 1
+    x = oracle.normals(124, k * in_len)
+    got = oracle.matmul_tl1_sse(payload, out_len, in_len, x, k, threads=3)
+    assert np.array_equal(got, _tl1_k_lanes(oracle, payload, out_len, in_len, x, k))
 
 
 def test_matvec_tq1_matches_decode_then_dot(oracle):
