@@ -12,7 +12,8 @@ nor the oracle to know the expected bytes:
   sign1.npz      SIGN1G128 x int8 products after a block-128 rotation:
                  per-group int32 accumulators and fp32 outputs
   refformat.npz  the reference's own formats: matvec_tl1 (PTQ1_0, scalar and
-                 SSE4.1 accumulation orders), matmul_tl1 (K = 3 columns) and
+                 SSE4.1 accumulation orders), matmul_tl1 (K = 3 columns, scalar and
+                 x86 K-column orders) and
                  matvec_qblock (TQ1_0) on payloads built with the generators of
                  the reference's tests (ops.rs:721-750, 801-838)
 
@@ -104,6 +105,7 @@ def refformat_cases():
     xk = O.normals(700, 3 * in_len)
     d["tl1_xk"] = xk
     d["tl1_matmul_k3"] = O.matmul_tl1_scalar(pay, out_len, in_len, xk, 3)
+    d["tl1_matmul_sse_k3"] = O.matmul_tl1_sse(pay, out_len, in_len, xk, 3, 1)
     # TQ1_0 payload generator of ops.rs:801-838: byte i = (i * (0x9B ^ (i >> 7))) mod 256
     out_len, in_len = 16, 512
     n = out_len * (in_len // 256) * 54

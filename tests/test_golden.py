@@ -60,6 +60,8 @@ def test_oracle_reproduces_reference_formats(oracle):
                           g["tl1_sse"])
     assert np.array_equal(oracle.matmul_tl1_scalar(g["tl1_payload"], o, i, g["tl1_xk"], 3),
                           g["tl1_matmul_k3"])
+    assert np.array_equal(oracle.matmul_tl1_sse(g["tl1_payload"], o, i, g["tl1_xk"], 3, 1),
+                          g["tl1_matmul_sse_k3"])
     # the reference's own tolerance between the two accumulation orders (ops.rs:829)
     np.testing.assert_allclose(g["tl1_sse"], g["tl1_scalar"], rtol=1e-5, atol=1e-5)
     o, i = (int(v) for v in g["tq1_shape"])
