@@ -310,8 +310,11 @@ ouroq_status upload_ref(ouroq_ctx* ctx, ouroq_format fmt, const void* packed, in
 }
 
 // fp32 x [B][K] -> y [B][M] for the reference formats (no quantisation).
+// columns: PTQ1_0 in matmul_tl1's K-column order (the reference's matmul_q)
+// instead of matvec_tl1's order per token (its matvec_q); the other formats
+// have one order for both.
 ouroq_status ref_matvec(ouroq_ctx* ctx, const ouroq_weight* w, const float* x, int B, float* y,
-                        cudaStream_t s) {
+                        cudaStream_t s, bool columns) {
   if (is_half_format(w->fmt)) {
     if ((size_t)B > 65535 * 8) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d too large", B);
     HeadLaunch L{};
@@ -338,6 +341,11 @@ ouroq_status ref_matvec(ouroq_ctx* ctx, const ouroq_weight* w, const float* x, i
   P.K = w->K;
   P.B = B;
   P.ldy = w->M;
+  if (P.fmt == kPtq1 && columns) {
+    CU(ctx, launch_tl1_columns(P, s), "PTQ1_0 K-column launch");
+    ctx->launches++;
+    return OUROQ_OK;
+  }
   const size_t smem = P.fmt == kPtq1 ? tl1_smem_bytes(w->K, tl1_rows_per_cta(w->K, w->M, ctx->num_sms))
                                      : tq1_smem_bytes(w->K);
   if (smem > (size_t)ctx->smem_optin)
@@ -953,8 +961,14 @@ ouroq_status ouroq_gemm_group_f32act(ouroq_ctx* ctx, int n, const ouroq_weight* 
   return run_gemv(ctx, L, s);
 }
 
-ouroq_status ouroq_gemm_f32act(ouroq_ctx* ctx, const ouroq_weight* w, const float* x, int B,
-                               const float* signs, int hadamard_block, float* y, void* stream) {
+// PTQ1_0 order of an fp32-activation product: kAuto = matvec_tl1's for one
+// token, matmul_tl1's K-column order for several (what matvec_q / matmul_q
+// give); the host mirrors pin it to the operator they mirror.
+enum class Tl1Order { kAuto, kMatvec, kColumns };
+
+static ouroq_status f32act_impl(ouroq_ctx* ctx, const ouroq_weight* w, const float* x, int B,
+                                const float* signs, int hadamard_block, float* y, void* stream,
+                                Tl1Order order) {
   if (!ctx || !w) return fail(ctx, OUROQ_ERR_BAD_ARG, "null handle");
   if (B < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d", B);
   if (B == 0) return OUROQ_OK;
@@ -980,7 +994,8 @@ ouroq_status ouroq_gemm_f32act(ouroq_ctx* ctx, const ouroq_weight* w, const floa
       ctx->launches++;
       xin = ctx->rot_scratch;
     }
-    return ref_matvec(ctx, w, xin, B, y, s);
+    const bool columns = order == Tl1Order::kColumns || (order == Tl1Order::kAuto && B > 1);
+    return ref_matvec(ctx, w, xin, B, y, s, columns);
   }
   const int dfmt = w->fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
   if (B <= kFusedMaxB && (hadamard_block == 0 || (hadamard_block >= 32 && hadamard_block <= 128))) {
@@ -1004,6 +1019,11 @@ ouroq_status ouroq_gemm_f32act(ouroq_ctx* ctx, const ouroq_weight* w, const floa
   st = quantize_impl(ctx, x, B, w->K, signs, hadamard_block, ctx->q_scratch, ctx->s_scratch, s);
   if (st != OUROQ_OK) return st;
   return gemm_impl(ctx, w, ctx->q_scratch, ctx->s_scratch, B, y, nullptr, s);
+}
+
+ouroq_status ouroq_gemm_f32act(ouroq_ctx* ctx, const ouroq_weight* w, const float* x, int B,
+                               const float* signs, int hadamard_block, float* y, void* stream) {
+  return f32act_impl(ctx, w, x, B, signs, hadamard_block, y, stream, Tl1Order::kAuto);
 }
 
 // Address of the fixed scratch on each device, looked up the first time a call
@@ -1037,7 +1057,7 @@ ouroq_status ouroq_gemm_f32act_noalloc(ouroq_ctx* ctx, const ouroq_weight* w, co
   if (!x || !y) return fail(ctx, OUROQ_ERR_BAD_ARG, "null buffer");
   if (is_half_format(w->fmt) && hadamard_block == 0) {
     DeviceGuard g(ctx->device);  // no quantisation, no scratch
-    return ref_matvec(ctx, w, x, B, y, static_cast<cudaStream_t>(stream));
+    return ref_matvec(ctx, w, x, B, y, static_cast<cudaStream_t>(stream), false);
   }
   ouroq_status st = check_quant_args(ctx, B, w->K, hadamard_block);
   if (st != OUROQ_OK) return st;
@@ -1053,7 +1073,7 @@ ouroq_status ouroq_gemm_f32act_noalloc(ouroq_ctx* ctx, const ouroq_weight* w, co
     if (hadamard_block)
       return fail(ctx, OUROQ_ERR_UNSUPPORTED,
                   "PTQ1_0 / TQ1_0 with a rotation needs scratch: rotate first, or use ouroq_gemm_f32act");
-    return ref_matvec(ctx, w, x, B, y, static_cast<cudaStream_t>(stream));
+    return ref_matvec(ctx, w, x, B, y, static_cast<cudaStream_t>(stream), B > 1);
   }
   uint8_t* scratch = nullptr;
   st = noalloc_scratch(ctx, &scratch);
@@ -1080,8 +1100,9 @@ ouroq_status ouroq_gemm_f32act_noalloc(ouroq_ctx* ctx, const ouroq_weight* w, co
   return gemm_impl(ctx, w, q, s_x, B, y, nullptr, s);
 }
 
-ouroq_status ouroq_matmul_q(ouroq_ctx* ctx, const ouroq_weight* w, const float* x_host, int k,
-                            float* y_host) {
+// The host-buffer mirrors: x staged in, the product, y copied back, synchronous.
+static ouroq_status host_product(ouroq_ctx* ctx, const ouroq_weight* w, const float* x_host, int k,
+                                 float* y_host, Tl1Order order) {
   if (!ctx || !w) return fail(ctx, OUROQ_ERR_BAD_ARG, "null handle");
   if (k < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "k=%d", k);
   if (k == 0) return OUROQ_OK;
@@ -1094,7 +1115,7 @@ ouroq_status ouroq_matmul_q(ouroq_ctx* ctx, const ouroq_weight* w, const float* 
   cudaStream_t s = ctx->host_stream;
   CU(ctx, cudaMemcpyAsync(ctx->x_stage, x_host, (size_t)k * w->K * 4, cudaMemcpyHostToDevice, s),
      "x upload");
-  st = ouroq_gemm_f32act(ctx, w, ctx->x_stage, k, nullptr, 0, ctx->y_stage, s);
+  st = f32act_impl(ctx, w, ctx->x_stage, k, nullptr, 0, ctx->y_stage, s, order);
   if (st != OUROQ_OK) return st;
   CU(ctx, cudaMemcpyAsync(y_host, ctx->y_stage, (size_t)k * w->M * 4, cudaMemcpyDeviceToHost, s),
      "y download");
@@ -1102,9 +1123,16 @@ ouroq_status ouroq_matmul_q(ouroq_ctx* ctx, const ouroq_weight* w, const float* 
   return OUROQ_OK;
 }
 
+// ops::matmul_q: PTQ1_0 in matmul_tl1's K-column order for every k, k = 1 included
+ouroq_status ouroq_matmul_q(ouroq_ctx* ctx, const ouroq_weight* w, const float* x_host, int k,
+                            float* y_host) {
+  return host_product(ctx, w, x_host, k, y_host, Tl1Order::kColumns);
+}
+
+// ops::matvec_q: PTQ1_0 in matvec_tl1's order
 ouroq_status ouroq_matvec_q(ouroq_ctx* ctx, const ouroq_weight* w, const float* x_host,
                             float* y_host) {
-  return ouroq_matmul_q(ctx, w, x_host, 1, y_host);
+  return host_product(ctx, w, x_host, 1, y_host, Tl1Order::kMatvec);
 }
 
 static ouroq_status rotate_host(ouroq_ctx* ctx, float* x_host, const float* signs_host, size_t n,

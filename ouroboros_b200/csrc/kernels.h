@@ -166,6 +166,9 @@ size_t tl1_smem_bytes(int K, int R);
 int tl1_rows_per_cta(int K, int M, int num_sms);
 size_t tq1_smem_bytes(int K);
 cudaError_t launch_refmt_matvec(const RefLaunch& P, int num_sms, cudaStream_t s);
+// PTQ1_0 x K columns (x [B][K] -> y [B][ldy], B = columns) in matmul_tl1's
+// K-column order rather than the per-column matvec order.
+cudaError_t launch_tl1_columns(const RefLaunch& P, cudaStream_t s);
 
 // 16-bit weights (F16 / BF16 shards, the tied lm_head): fp32 x [B][K] ->
 // y [B][ldy] in the reference's per-row order; with tokens set, also the

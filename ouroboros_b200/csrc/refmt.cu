@@ -120,6 +120,66 @@ __global__ void __launch_bounds__(kTl1Threads, 2) tl1_matvec_kernel(const __grid
   }
 }
 
+// PTQ1_0 times K columns in matmul_tl1's x86 order (tl1_rows_avx2_k,
+// ops.rs:381-481; matmul_q takes it for every K, ops.rs:219-230): for each
+// (row, column) two 4-lane accumulators a, b run over the whole row -- a lane
+// j takes the terms of bytes j, 8+j, 16+j of each stage n (x at n*16+j,
+// n*16+8+j, 80+n*8+j), b lane j those of bytes 4+j, 12+j, 20+j (x at
+// n*16+4+j, n*16+12+j, 80+n*8+4+j) -- and one scalar tail sum takes the eight
+// qh terms, group after group; y = tail + (hsum(a) + hsum(b)) with
+// hsum(v) = (v0 + v2) + (v1 + v3). One thread per (row, column), 32 rows a
+// CTA; the columns of a row read its weights through the read-only cache.
+constexpr int kTl1ColThreads = 256;
+constexpr int kTl1ColRows = 32;
+
+__global__ void __launch_bounds__(kTl1ColThreads) tl1_columns_kernel(const __grid_constant__ RefLaunch P) {
+  const int G = P.K / 128;
+  const int k = P.B;
+  const int row0 = blockIdx.x * kTl1ColRows;
+  for (int p = threadIdx.x; p < kTl1ColRows * k; p += blockDim.x) {
+    const int r = p / k, c = p - (p / k) * k;
+    const int row = row0 + r;
+    if (row >= P.M) continue;
+    const float* x = P.x + (size_t)c * P.K;
+    float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float bv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float tail = 0.0f;
+#pragma unroll 1
+    for (int g = 0; g < G; ++g) {
+      const uint32_t* gw = reinterpret_cast<const uint32_t*>(P.w + ((size_t)row * G + g) * 28);
+      uint32_t wd[7];
+#pragma unroll
+      for (int i = 0; i < 7; ++i) wd[i] = __ldg(gw + i);
+      const float d = __half2float(__ushort_as_half((unsigned short)(wd[6] >> 16)));
+      const float* xg = x + (size_t)g * 128;
+      uint32_t q[24];  // byte * 3^n mod 256 of qs[0..24], advanced one digit per n
+#pragma unroll
+      for (int i = 0; i < 24; ++i) q[i] = (wd[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+#pragma unroll 1
+      for (int n = 0; n < 5; ++n) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          a[j] = __fadd_rn(term(next_digit(&q[j]), d, __ldg(xg + n * 16 + j)), a[j]);
+          bv[j] = __fadd_rn(term(next_digit(&q[4 + j]), d, __ldg(xg + n * 16 + 4 + j)), bv[j]);
+          a[j] = __fadd_rn(term(next_digit(&q[8 + j]), d, __ldg(xg + n * 16 + 8 + j)), a[j]);
+          bv[j] = __fadd_rn(term(next_digit(&q[12 + j]), d, __ldg(xg + n * 16 + 12 + j)), bv[j]);
+          a[j] = __fadd_rn(term(next_digit(&q[16 + j]), d, __ldg(xg + 80 + n * 8 + j)), a[j]);
+          bv[j] = __fadd_rn(term(next_digit(&q[20 + j]), d, __ldg(xg + 80 + n * 8 + 4 + j)), bv[j]);
+        }
+      }
+      uint32_t qh[2] = {wd[6] & 0xFFu, (wd[6] >> 8) & 0xFFu};
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int m = 0; m < 2; ++m)
+          tail = __fadd_rn(tail, term(next_digit(&qh[m]), d, __ldg(xg + 120 + n * 2 + m)));
+    }
+    const float ha = __fadd_rn(__fadd_rn(a[0], a[2]), __fadd_rn(a[1], a[3]));
+    const float hb = __fadd_rn(__fadd_rn(bv[0], bv[2]), __fadd_rn(bv[1], bv[3]));
+    P.y[(size_t)c * P.ldy + row] = __fadd_rn(tail, __fadd_rn(ha, hb));
+  }
+}
+
 // TQ1_0: 32 rows per CTA, four warps. Warps 1-3 decode the weights of a
 // 256-element block times x into a double-buffered product tile [32 rows][256];
 // warp 0 (lane = row) adds each row's products in element order -- the one
@@ -258,6 +318,14 @@ cudaError_t launch_refmt_matvec(const RefLaunch& P, int num_sms, cudaStream_t s)
     return cudaGetLastError();
   }
   return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_tl1_columns(const RefLaunch& P, cudaStream_t s) {
+  if (P.M <= 0 || P.B <= 0) return cudaSuccess;
+  if (P.fmt != kPtq1) return cudaErrorInvalidValue;
+  const dim3 grid((unsigned)((P.M + kTl1ColRows - 1) / kTl1ColRows), 1, 1);
+  tl1_columns_kernel<<<grid, kTl1ColThreads, 0, s>>>(P);
+  return cudaGetLastError();
 }
 
 }  // namespace ouroq

@@ -3,11 +3,13 @@
 PTQ1_0 ("Tl1") and TQ1_0 weights are uploaded byte for byte and multiplied by
 fp32 activations. The kernels repeat the reference's floating-point order, so
 every comparison with the oracle restatement of that order is exact:
-  PTQ1_0: matvec_tl1's x86 order (cluster/src/infer/ops.rs:499-584), per token
-  TQ1_0:  matvec_qblock = dequantise then dot (ops.rs:101-128, 53-60)
-The K-column product (matmul_q, ops.rs:219-230) runs each column in the
-matvec order; the reference's own K-column kernel differs from that order
-only within the tolerance its test states (ops.rs:721-750), checked here too.
+  PTQ1_0: matvec_tl1's x86 order (cluster/src/infer/ops.rs:499-584) for one
+          token (matvec_q); matmul_tl1's x86 K-column order (ops.rs:381-481)
+          for a batch and for every host matmul_q call (ops.rs:219-230)
+  TQ1_0:  matvec_qblock = dequantise then dot (ops.rs:101-128, 53-60), per
+          token in both cases (matmul_q runs K matvecs for it)
+The two PTQ1_0 orders differ within the tolerance the reference's own test
+states (ops.rs:721-750), checked here too.
 """
 import numpy as np
 import pytest
@@ -51,9 +53,11 @@ def test_tl1_matches_reference_order(ctx, oracle, M, K, B):
     x = oracle.normals(K + 5, B * K).reshape(B, K)
     w = ctx.upload(oq.PTQ1_0, payload, M, K)
     y = _host(ctx.gemm_f32act(w, _dev(x)))
-    for b in range(B):
-        want = oracle.matvec_tl1_sse(payload, M, K, x[b])
-        assert np.array_equal(y[b], want), int(np.sum(y[b] != want))
+    if B == 1:
+        want = oracle.matvec_tl1_sse(payload, M, K, x[0]).reshape(1, M)
+    else:
+        want = oracle.matmul_tl1_sse(payload, M, K, x, B).reshape(B, M)
+    assert np.array_equal(y, want), int(np.sum(y != want))
     w.free()
 
 
@@ -93,25 +97,28 @@ def test_tl1_k_columns(ctx, oracle):
     x = oracle.normals(42, k * in_len).reshape(k, in_len)
     w = ctx.upload(oq.PTQ1_0, payload, out_len, in_len)
     y = ctx.matmul_q(w, x)
-    kcol = oracle.matmul_tl1_scalar(payload, out_len, in_len, x.reshape(-1), k).reshape(k, out_len)
+    kcol = oracle.matmul_tl1_sse(payload, out_len, in_len, x, k).reshape(k, out_len)
+    assert np.array_equal(y, kcol)
     for c in range(k):
         want = oracle.matvec_tl1_sse(payload, out_len, in_len, x[c])
-        assert np.array_equal(y[c], want)
-        assert np.all(np.abs(y[c] - kcol[c]) <= 1e-3 * np.maximum(np.abs(kcol[c]), 1.0))
+        assert np.all(np.abs(y[c] - want) <= 1e-3 * np.maximum(np.abs(want), 1.0))
+    # one column through matmul_q keeps the K-column order; matvec_q the matvec order
+    y1 = ctx.matmul_q(w, x[:1])
+    assert np.array_equal(y1[0], oracle.matmul_tl1_sse(payload, out_len, in_len, x[0], 1))
+    assert np.array_equal(ctx.matvec_q(w, x[0]), oracle.matvec_tl1_sse(payload, out_len, in_len, x[0]))
     w.free()
 
 
 def test_tl1_with_rotation(ctx, oracle):
-    # Qwen35Stage::wh: rotate_fwd(x, signs, block) then matvec_q
+    # Qwen35Stage::wh: rotate_fwd(x, signs, block) then the product (two tokens: matmul_q)
     M, K, B, block = 256, 4096, 2, 128
     payload = tl1_payload(oracle, M, K, seed=77)
     x = oracle.outliers(78, oracle.normals(79, B * K), 0.01, 20.0).reshape(B, K)
     sg = oracle.signs(80, K).astype(np.float32)
     w = ctx.upload(oq.PTQ1_0, payload, M, K)
     y = _host(ctx.gemm_f32act(w, _dev(x), signs=_dev(sg), hadamard_block=block))
-    for b in range(B):
-        xr = oracle.rotate_fwd(x[b], sg, block)
-        assert np.array_equal(y[b], oracle.matvec_tl1_sse(payload, M, K, xr))
+    xr = np.stack([oracle.rotate_fwd(x[b], sg, block) for b in range(B)])
+    assert np.array_equal(y, oracle.matmul_tl1_sse(payload, M, K, xr, B).reshape(B, M))
     w.free()
 
 
@@ -122,6 +129,8 @@ def test_reference_formats_golden(ctx):
     o, i = (int(v) for v in g["tl1_shape"])
     w = ctx.upload(oq.PTQ1_0, g["tl1_payload"], o, i)
     assert np.array_equal(ctx.matvec_q(w, g["tl1_x"]), g["tl1_sse"])
+    assert np.array_equal(ctx.matmul_q(w, g["tl1_xk"].reshape(3, i)).reshape(-1),
+                          g["tl1_matmul_sse_k3"])
     w.free()
     o, i = (int(v) for v in g["tq1_shape"])
     w = ctx.upload(oq.TQ1_0, g["tq1_payload"], o, i)
