@@ -60,7 +60,9 @@ typedef enum {
    * (ouroq_gemm_f32act, ouroq_matvec_q, ouroq_matmul_q, ouroq_gemm_sharded):
    *   PTQ1_0 ("Tl1", QuantKind::Tl1, dequant.rs:123-171): per 128 weights
    *     28 bytes qs[24] | qh[2] | f16 d; K multiple of 128. Results are
-   *     bit-identical to matvec_tl1's x86 order (ops.rs:499-584), per token.
+   *     bit-identical to matvec_tl1's x86 order (ops.rs:499-584) for one
+   *     token (ouroq_matvec_q, B = 1), and to matmul_tl1's x86 K-column order
+   *     (ops.rs:381-481) for B > 1 and for every ouroq_matmul_q call.
    *   TQ1_0 (QuantKind::Tq1_0, dequant.rs:50-105): per 256 weights 54 bytes
    *     qs[48] | qh[4] | f16 d; K multiple of 256. Results are bit-identical
    *     to matvec_qblock (dequantise, then dot in element order, ops.rs:53-60). */
@@ -332,7 +334,8 @@ ouroq_status ouroq_bmts_upload(ouroq_ctx *ctx, const ouroq_bmts *f, const char *
 ouroq_status ouroq_matvec_q(ouroq_ctx *ctx, const ouroq_weight *w, const float *x_host,
                             float *y_host);
 /* ops::matmul_q (ops.rs:219-230): x_host [k][K] -> y_host [k][M]
- * (= the reference's y[c*out_len + r]). */
+ * (= the reference's y[c*out_len + r]); PTQ1_0 in matmul_tl1's K-column
+ * order for every k, as matmul_q gives. */
 ouroq_status ouroq_matmul_q(ouroq_ctx *ctx, const ouroq_weight *w, const float *x_host, int k,
                             float *y_host);
 /* hadamard::rotate_fwd (hadamard.rs:41-53) in place on a host buffer of n floats. */
