@@ -1,7 +1,7 @@
 // common.cuh -- device-side primitives shared by the ouroq kernels (sm_100a).
 //
 // Hand-written inline PTX for the Blackwell async machinery the kernels use:
-// mbarrier phase tracking, 1-D bulk copies (cp.async.bulk, no multicast),
+// mbarrier phase tracking, 1-D bulk copies (cp.async.bulk, one CTA each),
 // programmatic dependent launch (griddepcontrol), and the mixed-sign dp4a.
 // Every spin-wait is bounded: on expiry it records an error code in the
 // context's device status word and returns false instead of hanging the GPU.
@@ -99,7 +99,7 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return p;
 }
 
-// 2-D TMA tile load (no multicast) completing on an mbarrier; x is the
+// 2-D TMA tile load into this CTA only, completing on an mbarrier; x is the
 // innermost coordinate (its byte offset must be a multiple of 16)
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
                                             uint64_t* bar) {
