@@ -183,9 +183,16 @@ def _dev(t, dtype: str, numel: int | None, what: str, optional: bool = False) ->
     return t.data_ptr()
 
 
+def _ndim(t) -> int:
+    """Dimensions of a tensor (-1 for anything else)."""
+    return t.dim() if hasattr(t, "dim") else -1
+
+
 def _rows(x, width: int, what: str) -> int:
     """Rows of an activation tensor [B][width] (a 1-D x of `width` is one row)."""
-    n = x.numel() if hasattr(x, "numel") else 0
+    if not hasattr(x, "numel"):
+        raise OuroqError(7, f"{what}: expected a CUDA tensor")
+    n = x.numel()
     if width <= 0 or n % width:
         raise OuroqError(1, f"{what}: {n} elements is not a whole number of rows of {width}")
     return n // width
@@ -314,8 +321,8 @@ class Context:
     # -- device API (torch CUDA tensors) --
     def quantize_act(self, x, signs=None, hadamard_block: int = 0, q=None, s_x=None, stream=None):
         import torch
-        if x.dim() != 2:
-            raise OuroqError(1, "x must be [B][K]")
+        if _ndim(x) != 2:
+            raise OuroqError(1, "x must be a [B][K] CUDA tensor")
         B, K = x.shape
         if q is None:
             q = torch.empty((B, K), dtype=torch.int8, device=x.device)
@@ -330,8 +337,8 @@ class Context:
     def quantize_group(self, xs, qs, sxs, signs=None, blocks=None, stream=None):
         """One launch quantising several activation sets (same batch B)."""
         n = len(xs)
-        if any(x.dim() != 2 for x in xs):
-            raise OuroqError(1, "every x must be [B][K]")
+        if any(_ndim(x) != 2 for x in xs):
+            raise OuroqError(1, "every x must be a [B][K] CUDA tensor")
         B = xs[0].shape[0] if n else 0
         if any(x.shape[0] != B for x in xs):
             raise OuroqError(1, "every x must have the same B")
@@ -350,8 +357,8 @@ class Context:
 
     def rotate(self, x, signs=None, block: int = 128, inverse: bool = False, out=None, stream=None):
         import torch
-        if x.dim() != 2:
-            raise OuroqError(1, "x must be [B][K]")
+        if _ndim(x) != 2:
+            raise OuroqError(1, "x must be a [B][K] CUDA tensor")
         B, K = x.shape
         if out is None:
             out = torch.empty_like(x)

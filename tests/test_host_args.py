@@ -82,3 +82,19 @@ def test_context_methods_check_before_calling_the_library():
     assert _status(lambda: ctx.gemm_f32act(w, x, y=y_short)) == 1
     assert _status(lambda: ctx.gemm_f32act_noalloc(w, x, FakeCuda(torch.float16, 128))) == 7
     assert _status(lambda: ctx.argmax_token(w, x, tokens=FakeCuda(torch.int32, 2))) == 7
+
+
+def test_numpy_input_to_a_device_method_is_an_ouroq_error():
+    class NoLib:
+        def __getattr__(self, name):
+            return lambda *a: pytest.fail(f"{name} was called")
+
+    ctx = oq.Context.__new__(oq.Context)
+    ctx.lib, ctx.ctx = NoLib(), None
+    x = np.zeros((2, 256), np.float32)
+    assert _status(lambda: ctx.quantize_act(x)) == 1
+    assert _status(lambda: ctx.rotate(x)) == 1
+    assert _status(lambda: ctx.quantize_group([x], [None], [None])) == 1
+    w = oq.Weight(ctx, 0, oq.TERNARY2, 64, 256)
+    assert _status(lambda: ctx.gemm_f32act(w, x)) == 7
+    assert _status(lambda: ctx.argmax_token(w, x)) == 7
