@@ -783,3 +783,80 @@ int orc_finite_argmax(const float *l, int n) {
     }
     return best;
 }
+
+/* ---- the decode step's host ops (ops.rs:11-60, infer/mod.rs:338-365), fp32 ---- */
+
+/* rmsnorm (ops.rs:12-17): ms = (sum of v*v in element order) / n,
+ * inv = 1 / sqrt(ms + eps), y = (x * inv) * w */
+void orc_rmsnorm(const float *x, const float *w, int n, float eps, float *y) {
+    float ss = 0.0f;
+    for (int i = 0; i < n; i++) ss = ss + x[i] * x[i];
+    float ms = ss / (float)n;
+    float inv = 1.0f / sqrtf(ms + eps);
+    for (int i = 0; i < n; i++) y[i] = x[i] * inv * w[i];
+}
+
+/* rope_neox (ops.rs:21-33), in place over the first `rot` values of one head:
+ * theta_i = 1 / base^(2i / rot), angle = t * theta_i, pairs (i, i + rot/2) */
+void orc_rope_neox(float *v, long long t, int rot, float base) {
+    int half = rot / 2;
+    for (int i = 0; i < half; i++) {
+        float theta = 1.0f / powf(base, (float)(2 * i) / (float)rot);
+        float ang = (float)t * theta;
+        float c = cosf(ang), s = sinf(ang);
+        float x0 = v[i], x1 = v[i + half];
+        v[i] = x0 * c - x1 * s;
+        v[i + half] = x1 * c + x0 * s;
+    }
+}
+
+/* silu (ops.rs:34-36): x / (1 + exp(-x)) */
+float orc_silu(float x) { return x / (1.0f + expf(-x)); }
+
+/* softmax (ops.rs:39-50), in place: m = max (NaN ignored, as f32::max),
+ * e = exp(x - m) summed in order, then each times 1 / sum */
+void orc_softmax(float *v, int n) {
+    float m = -INFINITY;
+    for (int i = 0; i < n; i++) m = fmaxf(m, v[i]);
+    float s = 0.0f;
+    for (int i = 0; i < n; i++) {
+        v[i] = expf(v[i] - m);
+        s = s + v[i];
+    }
+    float inv = 1.0f / s;
+    for (int i = 0; i < n; i++) v[i] = v[i] * inv;
+}
+
+/* dot (ops.rs:53-60): one running sum in element order */
+float orc_dot(const float *a, const float *b, int n) {
+    float s = 0.0f;
+    for (int i = 0; i < n; i++) s = s + a[i] * b[i];
+    return s;
+}
+
+/* attend (infer/mod.rs:338-365): causal GQA over positions 0..seq-1 of one
+ * sequence. k, v: [seq][n_kv * hd]; q, out: [n_head * hd]. Per head: scores =
+ * dot(q, k_t) * (1 / sqrt(hd)), softmax, out += w_t * v_t for t ascending. */
+int orc_attend(const float *q, const float *k, const float *v, int seq, int n_head, int n_kv,
+               int hd, float *out) {
+    if (seq < 1 || n_kv < 1 || n_head % n_kv || hd < 1) return -1;
+    int groups = n_head / n_kv, kv_dim = n_kv * hd;
+    float scale = 1.0f / sqrtf((float)hd);
+    float *sc = (float *)malloc(sizeof(float) * (size_t)seq);
+    if (!sc) return -1;
+    for (int i = 0; i < n_head * hd; i++) out[i] = 0.0f;
+    for (int h = 0; h < n_head; h++) {
+        const float *qh = q + (size_t)h * hd;
+        int kvh = h / groups;
+        for (int t = 0; t < seq; t++)
+            sc[t] = orc_dot(qh, k + (size_t)t * kv_dim + (size_t)kvh * hd, hd) * scale;
+        orc_softmax(sc, seq);
+        float *o = out + (size_t)h * hd;
+        for (int t = 0; t < seq; t++) {
+            const float *vt = v + (size_t)t * kv_dim + (size_t)kvh * hd;
+            for (int i = 0; i < hd; i++) o[i] = o[i] + sc[t] * vt[i];
+        }
+    }
+    free(sc);
+    return 0;
+}

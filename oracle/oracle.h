@@ -21,6 +21,8 @@
  *       - matmul_tl1 (SSE4.1 K)   cluster/src/infer/ops.rs:162-215,381-481
  *       - matvec_qblock (TQ1_0)   cluster/src/infer/ops.rs:53-60,101-128
  *       - mt_threads chunking     cluster/src/infer/ops.rs:63-73,104-105
+ *       - rmsnorm, rope_neox, silu, softmax, dot   ops.rs:11-60
+ *       - attend (causal GQA)     cluster/src/infer/mod.rs:338-365
  *
  *  2. The int8-activation arithmetic of BitNet b1.58 that this library
  *     targets but the reference does not contain (it lives in the un-vendored bitnet-cpp submodule,
@@ -108,6 +110,15 @@ float orc_bf16_to_f32(uint16_t bits);
 int orc_matvec_half(const uint8_t *payload, int out_len, int in_len, const float *x, float *y,
                     int bf16, int threads);
 int orc_finite_argmax(const float *l, int n);
+
+/* ---- the decode step's host ops (ops.rs:11-60, infer/mod.rs:338-365), fp32 ---- */
+void orc_rmsnorm(const float *x, const float *w, int n, float eps, float *y);
+void orc_rope_neox(float *v, long long t, int rot, float base); /* in place, one head */
+float orc_silu(float x);
+void orc_softmax(float *v, int n);                                /* in place */
+float orc_dot(const float *a, const float *b, int n);
+int orc_attend(const float *q, const float *k, const float *v, int seq, int n_head, int n_kv,
+               int hd, float *out); /* k, v [seq][n_kv*hd]; q, out [n_head*hd] */
 int orc_hw_threads(void);
 
 #ifdef __cplusplus

@@ -73,6 +73,12 @@ def lib() -> ctypes.CDLL:
             "orc_bf16_to_f32": (ctypes.c_float, [ctypes.c_uint16]),
             "orc_matvec_half": (_i, [_u8p, _i, _i, _f32p, _f32p, _i, _i]),
             "orc_finite_argmax": (_i, [_f32p, _i]),
+            "orc_rmsnorm": (None, [_f32p, _f32p, _i, ctypes.c_float, _f32p]),
+            "orc_rope_neox": (None, [_f32p, ctypes.c_longlong, _i, ctypes.c_float]),
+            "orc_silu": (ctypes.c_float, [ctypes.c_float]),
+            "orc_softmax": (None, [_f32p, _i]),
+            "orc_dot": (ctypes.c_float, [_f32p, _f32p, _i]),
+            "orc_attend": (_i, [_f32p, _f32p, _f32p, _i, _i, _i, _i, _f32p]),
             "orc_hw_threads": (_i, []),
         }
         for name, (res, args) in sig.items():
@@ -316,6 +322,51 @@ def finite_argmax(logits) -> int:
     """infer/mod.rs:70-83."""
     l = np.ascontiguousarray(logits, dtype=np.float32)
     return int(lib().orc_finite_argmax(_p(l, _f32p), l.size))
+
+
+# ---- the decode step's host ops (ops.rs:11-60, infer/mod.rs:338-365) ----
+def rmsnorm(x, w, eps: float) -> np.ndarray:
+    """ops.rs:12-17 on one row."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    y = np.empty_like(x)
+    lib().orc_rmsnorm(_p(x, _f32p), _p(w, _f32p), x.size, eps, _p(y, _f32p))
+    return y
+
+
+def rope_neox(v, t: int, rot: int, base: float) -> np.ndarray:
+    """ops.rs:21-33 on one head vector (returns a rotated copy)."""
+    v = np.ascontiguousarray(v, np.float32).copy()
+    lib().orc_rope_neox(_p(v, _f32p), int(t), rot, base)
+    return v
+
+
+def silu(x: float) -> float:
+    return float(lib().orc_silu(x))
+
+
+def softmax(v) -> np.ndarray:
+    v = np.ascontiguousarray(v, np.float32).copy()
+    lib().orc_softmax(_p(v, _f32p), v.size)
+    return v
+
+
+def dot(a, b) -> float:
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    return float(lib().orc_dot(_p(a, _f32p), _p(b, _f32p), a.size))
+
+
+def attend(q, k, v, n_head: int, n_kv: int, hd: int = 128) -> np.ndarray:
+    """infer/mod.rs:338-365 for one sequence: q [n_head*hd], k/v [seq][n_kv*hd]."""
+    q = np.ascontiguousarray(q, np.float32)
+    k = np.ascontiguousarray(k, np.float32)
+    v = np.ascontiguousarray(v, np.float32)
+    seq = k.size // (n_kv * hd)
+    out = np.empty(n_head * hd, np.float32)
+    _chk(lib().orc_attend(_p(q, _f32p), _p(k, _f32p), _p(v, _f32p), seq, n_head, n_kv, hd,
+                          _p(out, _f32p)), "attend")
+    return out
 
 
 def hw_threads() -> int:
