@@ -345,9 +345,12 @@ def run_reference(args, rank):
                            "batch": args.batch, "host_cpu": True},
                 "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": threads,
                                  "kind": "port",
-                                 "sample": f"{n} single-layer passes (the reference's TQ1_0 "
-                                           f"matvec_qblock) scaled to 30 layers, plus the lm_head "
-                                           f"in the reference's matvec_f16 order, {threads} threads"},
+                                 "sample": f"{n} single-layer passes of run_layer in the "
+                                           f"reference's fp32 order (TQ1_0 matvec_qblock "
+                                           f"projections, rmsnorm, RoPE, attend over 1025 "
+                                           f"positions, silu) scaled to 30 layers, plus the "
+                                           f"lm_head in the reference's matvec_f16 order, "
+                                           f"{threads} threads for the matvecs"},
                 "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
@@ -620,12 +623,15 @@ def run_ouroq(args, rank, world, local_rank):
 
 
 def cpu_decode_tokens_per_s(B: int, seconds: float, threads: int):
-    """The same decode step on the host cores as the reference computes it,
-    bounded: one layer's seven projections as TQ1_0 shards through the
-    oracle's restatement of matvec_qblock (dequantise, then an fp32 dot in
-    element order, threaded over rows), its norms and attention over the
-    1024-token context in numpy, scaled to 30 layers, plus the tied lm_head in
-    the reference's f16 order (an eighth of the vocabulary, scaled)."""
+    """The same decode step on the host cores as the reference computes it
+    (run_layer, infer/mod.rs:298-336), bounded: one layer -- rmsnorm, the
+    seven projections as TQ1_0 shards through matvec_qblock (dequantise, then
+    an fp32 dot in element order, threaded over rows like mt_threads), NeoX
+    RoPE of q and k, the KV append, attend over the 1025 cached positions,
+    the sub-norm, the residual adds, silu(gate) * up -- every op in the
+    reference's fp32 order as the oracle restates it, scaled to 30 layers;
+    plus the tied lm_head in the reference's f16 order (an eighth of the
+    vocabulary, scaled)."""
     from oracle import pyoracle as O
     rng = np.random.default_rng(5)
     shapes = [(2560, 2560), (640, 2560), (640, 2560), (2560, 2560), (6912, 2560), (6912, 2560),
@@ -637,32 +643,40 @@ def cpu_decode_tokens_per_s(B: int, seconds: float, threads: int):
         pay[:, 52] = sc & 0xFF
         pay[:, 53] = sc >> 8
         mats.append((pay.reshape(-1), M, K))
-    kc = rng.standard_normal((B, 5, 1024, 128), dtype=np.float32)
-    vc = rng.standard_normal((B, 5, 1024, 128), dtype=np.float32)
-    emb = (0.02 * rng.standard_normal((128256, 2560))).astype(np.float16)
+    norms = {n: (1 + 0.02 * rng.standard_normal(k)).astype(np.float32)
+             for n, k in (("attn", 2560), ("attn_sub", 2560), ("ffn", 2560), ("ffn_sub", 6912))}
+    # per sequence the cache as the reference keeps it: [position][kv_dim], the
+    # 1024-token context plus the token being decoded (position 1024)
+    kc = rng.standard_normal((B, 1025, 640), dtype=np.float32)
+    vc = rng.standard_normal((B, 1025, 640), dtype=np.float32)
+    # the rows of the tied head that the timed sample reads (an eighth, scaled below)
+    emb = (0.02 * rng.standard_normal((16384, 2560), dtype=np.float32)).astype(np.float16)
     x = rng.standard_normal((B, 2560), dtype=np.float32)
+    pos, rope_base = 1024, 500000.0
 
-    kv_head = np.arange(20) // 4  # GQA: query head h reads KV head h // 4
-
-    def rms(v):
-        return (v / np.sqrt((v * v).mean(-1, keepdims=True) + 1e-5)).astype(np.float32)
+    def rms(v, w):
+        return np.stack([O.rmsnorm(v[b], w, 1e-5) for b in range(B)])
 
     def proj(i, v):
         pay, M, K = mats[i]
         return np.stack([O.matvec_tq1(pay, M, K, v[b], threads) for b in range(B)])
 
     def layer():
-        a = rms(x)
-        q, _, _ = (proj(i, a) for i in range(3))
-        qh = q.reshape(B, 20, 128)
-        att = np.einsum("bhd,bhtd->bht", qh, kc[:, kv_head]) / np.sqrt(128.0)
-        pr = np.exp(att - att.max(-1, keepdims=True))
-        pr /= pr.sum(-1, keepdims=True)
-        o = np.einsum("bht,bhtd->bhd", pr, vc[:, kv_head]).reshape(B, 2560)
-        h1 = x + proj(3, rms(o))
-        f = rms(h1)
-        g_, u_ = proj(4, f), proj(5, f)
-        proj(6, rms(g_ / (1 + np.exp(-g_)) * u_))
+        a = rms(x, norms["attn"])
+        q, k, v = (proj(i, a) for i in range(3))
+        attn = np.empty((B, 2560), np.float32)
+        for b in range(B):
+            qr = np.concatenate([O.rope_neox(q[b, h * 128:(h + 1) * 128], pos, 128, rope_base)
+                                 for h in range(20)])
+            kc[b, pos] = np.concatenate([O.rope_neox(k[b, h * 128:(h + 1) * 128], pos, 128,
+                                                     rope_base) for h in range(5)])
+            vc[b, pos] = v[b]
+            attn[b] = O.attend(qr, kc[b], vc[b], 20, 5)
+        h1 = x + proj(3, rms(attn, norms["attn_sub"]))
+        f = rms(h1, norms["ffn"])
+        u_, g_ = proj(4, f), proj(5, f)
+        act = np.stack([O.swiglu(g_[b], u_[b]) for b in range(B)])
+        return h1 + proj(6, rms(act, norms["ffn_sub"]))
 
     t0 = time.perf_counter()
     n = 0
@@ -674,7 +688,7 @@ def cpu_decode_tokens_per_s(B: int, seconds: float, threads: int):
     t_layer = (time.perf_counter() - t0) / n
     # the tied lm_head as the reference computes it (matvec_f16: one fp32 chain
     # per row, threaded over rows), on an eighth of the vocabulary, scaled
-    head = np.ascontiguousarray(emb[:16384]).view(np.uint16)
+    head = np.ascontiguousarray(emb).view(np.uint16)
     t1 = time.perf_counter()
     for b in range(B):
         O.matvec_half(head, 16384, 2560, x[b], threads=threads)

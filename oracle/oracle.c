@@ -813,6 +813,11 @@ void orc_rope_neox(float *v, long long t, int rot, float base) {
 /* silu (ops.rs:34-36): x / (1 + exp(-x)) */
 float orc_silu(float x) { return x / (1.0f + expf(-x)); }
 
+/* the FFN activation of run_layer (infer/mod.rs:330): silu(gate) * up */
+void orc_swiglu(const float *gate, const float *up, int n, float *out) {
+    for (int i = 0; i < n; i++) out[i] = orc_silu(gate[i]) * up[i];
+}
+
 /* softmax (ops.rs:39-50), in place: m = max (NaN ignored, as f32::max),
  * e = exp(x - m) summed in order, then each times 1 / sum */
 void orc_softmax(float *v, int n) {

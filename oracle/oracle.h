@@ -115,6 +115,7 @@ int orc_finite_argmax(const float *l, int n);
 void orc_rmsnorm(const float *x, const float *w, int n, float eps, float *y);
 void orc_rope_neox(float *v, long long t, int rot, float base); /* in place, one head */
 float orc_silu(float x);
+void orc_swiglu(const float *gate, const float *up, int n, float *out); /* silu(g) * u */
 void orc_softmax(float *v, int n);                                /* in place */
 float orc_dot(const float *a, const float *b, int n);
 int orc_attend(const float *q, const float *k, const float *v, int seq, int n_head, int n_kv,

@@ -76,6 +76,7 @@ def lib() -> ctypes.CDLL:
             "orc_rmsnorm": (None, [_f32p, _f32p, _i, ctypes.c_float, _f32p]),
             "orc_rope_neox": (None, [_f32p, ctypes.c_longlong, _i, ctypes.c_float]),
             "orc_silu": (ctypes.c_float, [ctypes.c_float]),
+            "orc_swiglu": (None, [_f32p, _f32p, _i, _f32p]),
             "orc_softmax": (None, [_f32p, _i]),
             "orc_dot": (ctypes.c_float, [_f32p, _f32p, _i]),
             "orc_attend": (_i, [_f32p, _f32p, _f32p, _i, _i, _i, _i, _f32p]),
@@ -343,6 +344,15 @@ def rope_neox(v, t: int, rot: int, base: float) -> np.ndarray:
 
 def silu(x: float) -> float:
     return float(lib().orc_silu(x))
+
+
+def swiglu(gate, up) -> np.ndarray:
+    """silu(gate) * up element by element (infer/mod.rs:330)."""
+    gate = np.ascontiguousarray(gate, np.float32)
+    up = np.ascontiguousarray(up, np.float32)
+    out = np.empty_like(gate)
+    lib().orc_swiglu(_p(gate, _f32p), _p(up, _f32p), gate.size, _p(out, _f32p))
+    return out
 
 
 def softmax(v) -> np.ndarray:
