@@ -40,7 +40,9 @@ def build() -> Path:
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
-        if not LIB_PATH.exists():
+        srcs = [HERE / "oracle.c", HERE / "oracle.h"]
+        if not LIB_PATH.exists() or any(
+                f.exists() and f.stat().st_mtime > LIB_PATH.stat().st_mtime for f in srcs):
             build()
         L = ctypes.CDLL(str(LIB_PATH))
         sig = {
