@@ -249,15 +249,28 @@ def make_copy(torch, ctx, oq, wl, gen, device):
     return out
 
 
+def cpu_model() -> str:
+    """The host CPU's model string (for the CPU lines)."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_oracle_gbs(wl, host_mats, host_signs, B: int, seconds: float, threads: int):
     """Oracle (threaded int8 restatement) on one copy at batch B, looping until
-    `seconds` have passed (at least one pass). Returns GB/s, passes, seconds."""
+    `seconds` have passed (at least one pass). Returns GB/s at the median step
+    time, passes, seconds, median seconds per step."""
     from oracle import pyoracle as O
     _, fmt, mats, widths, block = wl
     rng = np.random.default_rng(7)
     xs = [rng.standard_normal((B, k), dtype=np.float32) for k in widths]
     nb = step_bytes(wl, B)["step"]
     steps, t0 = 0, time.perf_counter()
+    durs, ts = [], t0
     while True:
         if fmt in REF_FMTS:
             # the reference's own algorithm for these formats, restated (threaded like it)
@@ -278,7 +291,10 @@ def cpu_oracle_gbs(wl, host_mats, host_signs, B: int, seconds: float, threads: i
                     else:
                         O.matvec_tq1(packed, M, K, xb[b], threads)
             steps += 1
-            dt = time.perf_counter() - t0
+            now = time.perf_counter()
+            durs.append(now - ts)
+            ts = now
+            dt = now - t0
             if dt >= seconds:
                 break
             continue
@@ -290,10 +306,14 @@ def cpu_oracle_gbs(wl, host_mats, host_signs, B: int, seconds: float, threads: i
             else:
                 O.gemm_sign1_mt(packed, aux, M, K, q, s, threads)
         steps += 1
-        dt = time.perf_counter() - t0
+        now = time.perf_counter()
+        durs.append(now - ts)
+        ts = now
+        dt = now - t0
         if dt >= seconds:
             break
-    return nb * steps / dt / 1e9, steps, dt
+    med = statistics.median(durs)
+    return nb / med / 1e9, steps, dt, med
 
 
 def host_copy(wl, seed: int):
@@ -344,7 +364,7 @@ def run_reference(args, rank):
                 "config": {"workload": f"bitnet2b-decode-b{args.batch}-ctx1024-gen256",
                            "batch": args.batch, "host_cpu": True},
                 "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": threads,
-                                 "kind": "port",
+                                 "kind": "port", "cpu_model": cpu_model(),
                                  "sample": f"{n} single-layer passes of run_layer in the "
                                            f"reference's fp32 order (TQ1_0 matvec_qblock "
                                            f"projections, rmsnorm, RoPE, attend over 1025 "
@@ -366,29 +386,33 @@ def run_reference(args, rank):
     host_mats, host_signs = host_copy(ref_wl, 11)
     for _ in range(max(min(args.warmup, 3), 1)):
         cpu_oracle_gbs(ref_wl, host_mats, host_signs, B, 0.0, threads)
-    total_t, total_steps = 0.0, 0
+    total_t, total_steps, durs = 0.0, 0, []
     budget = 60.0  # the whole run stays within minutes
     for _ in range(max(1, args.steps)):
-        _, st, dt = cpu_oracle_gbs(ref_wl, host_mats, host_signs, B, 0.0, threads)
+        _, st, dt, _ = cpu_oracle_gbs(ref_wl, host_mats, host_signs, B, 0.0, threads)
         total_t += dt
         total_steps += st
+        durs.append(dt / st)
         if total_t >= budget:
             break
     # the same step as the GPU arm's (same shapes and batch), so GB/s counts
-    # that arm's algorithmic bytes and the two values compare as step times
-    gbs = step_bytes(wl, B)["step"] * total_steps / total_t / 1e9
+    # that arm's algorithmic bytes and the two values compare as step times;
+    # the median step after the warm-up
+    med = statistics.median(durs)
+    gbs = step_bytes(wl, B)["step"] / med / 1e9
     cfg = workload_config(args, wl, 1)
     cfg["host_cpu"] = True
     cfg["reference_format"] = FMT_NAME[ref_wl[1]]
     line = {
         "impl": "reference", "metric": "packed-weight GEMV HBM GB/s",
         "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": total_steps,
-        "warmup": args.warmup, "ms_per_step": round(1e3 * total_t / total_steps, 4),
+        "warmup": args.warmup, "ms_per_step": round(1e3 * med, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic", "config": cfg,
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{total_steps} steps at batch {B} (" + (
+                         "cpu_model": cpu_model(),
+                         "sample": f"median of {total_steps} steps at batch {B} (" + (
                              "the reference's own fp32 algorithm for this format, restated"
                              if wl[1] in REF_FMTS else
                              "the reference's matvec_tl1 in fp32 on the same shapes re-encoded "
@@ -588,9 +612,11 @@ def run_ouroq(args, rank, world, local_rank):
             host_mats.append((p.cpu().numpy(), aux))
         host_signs = [s.cpu().numpy() for s in signs] if block else None
         threads = O.hw_threads()
-        gbs, st, dt = cpu_oracle_gbs(wl, host_mats, host_signs, B, args.cpu_seconds, threads)
+        cpu_oracle_gbs(wl, host_mats, host_signs, B, 0.0, threads)  # warm-up
+        gbs, st, dt, _ = cpu_oracle_gbs(wl, host_mats, host_signs, B, args.cpu_seconds, threads)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{st} steps ({dt:.1f} s) at batch {B}: " + (
+               "cpu_model": cpu_model(),
+               "sample": f"median of {st} steps ({dt:.1f} s) at batch {B}: " + (
                    "the reference's own fp32 algorithm for this format (matvec_tl1 x86 order / "
                    "matvec_qblock), restated" if fmt in REF_FMTS else
                    "oracle int8 quantise + GEMV") + f", {threads} threads"}
@@ -780,10 +806,12 @@ def run_decode(args, rank, world, local_rank):
         threads = O.hw_threads()
         v, n, dt = cpu_decode_tokens_per_s(B, args.cpu_seconds, threads)
         cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"{n} single-layer passes at batch {B} (the reference's TQ1_0 "
-                         f"matvec_qblock for the projections, numpy norms and attention over "
-                         f"1024 tokens) scaled to 30 layers, plus the lm_head in the reference's "
-                         f"matvec_f16 order (1/8 of the vocabulary, scaled); {threads} threads"}
+               "cpu_model": cpu_model(),
+               "sample": f"{n} single-layer passes at batch {B} of run_layer in the "
+                         f"reference's fp32 order (TQ1_0 matvec_qblock projections, rmsnorm, "
+                         f"RoPE, attend over 1025 positions, silu) scaled to 30 layers, plus the "
+                         f"lm_head in the reference's matvec_f16 order (1/8 of the vocabulary, "
+                         f"scaled); {threads} threads for the matvecs"}
     if rank == 0:
         line = {
             "metric": "decode tokens/s", "value": round(tok_s, 2), "unit": "tokens/s",
