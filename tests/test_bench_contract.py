@@ -51,3 +51,20 @@ def test_reference_arm_under_torchrun_prints_once():
     assert len(lines) == 1, out.stdout[-2000:]
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
+
+
+def test_algorithmic_bytes_match_the_configs():
+    # the per-call byte counts of the benchmark configurations: packed weights
+    # (+ fp16 scales), int8 activations + one fp32 scale per token, fp32 outputs
+    sys.path.insert(0, str(ROOT))
+    import bench
+    assert bench.step_bytes(bench.WORKLOADS["c1"], 1)["gemm"] == 4_453_892
+    assert bench.step_bytes(bench.WORKLOADS["layer"], 1)["weights"] == 17_367_040
+    assert bench.step_bytes(bench.WORKLOADS["c3-4096"], 1)["weights"] == 2_359_296
+    assert bench.step_bytes(bench.WORKLOADS["c3-11008"], 1)["weights"] == 6_340_608
+    assert bench.step_bytes(bench.WORKLOADS["c5-up"], 1)["weights"] == 58_720_256
+    assert bench.step_bytes(bench.WORKLOADS["c5-down"], 1)["weights"] == 58_720_256
+    # every step streams from HBM: the rotated copies exceed twice the L2
+    for name, wl in bench.WORKLOADS.items():
+        if wl[2]:
+            assert bench.n_copies(wl) * bench.step_bytes(wl, 1)["weights"] >= 2 * bench.L2_BYTES
