@@ -1,7 +1,9 @@
 // refmt.cu -- GPU decode of the reference's own ternary shard formats behind
 // matvec_q / matmul_q: fp32 activations in, fp32 outputs out, no activation
-// quantisation. Both kernels reproduce the reference's floating-point
-// operation order exactly, so their outputs are bit-identical to it.
+// quantisation. Every kernel reproduces the reference's floating-point
+// operation order exactly, so its outputs are bit-identical to it: PTQ1_0 in
+// matvec_tl1's order for one token and in matmul_tl1's K-column order for a
+// batch (tl1_columns_kernel, below), TQ1_0 in matvec_qblock's order.
 //
 // PTQ1_0 ("Tl1", cluster/src/infer/dequant.rs:123-171): groups of 128 weights
 //   in 28 bytes: qs[24] | qh[2] | f16 d. Element order: n*16+m for qs[0..16],
