@@ -59,7 +59,7 @@ class BmtsShard:
         h = ctypes.c_void_p()
         st = self.lib.ouroq_bmts_open(path.encode(), ctypes.byref(h), err, len(err))
         if st != 0:
-            raise OuroqError(st, err.value.decode())
+            raise OuroqError(st, err.value.decode(errors="replace"))
         self.handle = h.value
         node, n = ctypes.c_int(), ctypes.c_int()
         start, dlen = ctypes.c_uint64(), ctypes.c_uint64()
@@ -95,7 +95,7 @@ class BmtsShard:
         st = self.lib.ouroq_bmts_span(self.handle, name.encode(), offset, length, ctypes.byref(p),
                                       err, len(err))
         if st != 0:
-            raise OuroqError(st, err.value.decode())
+            raise OuroqError(st, err.value.decode(errors="replace"))
         if length == 0:
             return np.zeros(0, np.uint8)
         return np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_uint8)),
@@ -114,7 +114,7 @@ class BmtsShard:
         st = self.lib.ouroq_bmts_upload(ctx.ctx, self.handle, name.encode(), ctypes.byref(h), err,
                                         len(err))
         if st != 0:
-            raise OuroqError(st, err.value.decode())
+            raise OuroqError(st, err.value.decode(errors="replace"))
         t = next(t for t in self.tensors if t.name == name)
         fmt = {DTYPE_TL1: PTQ1_0, DTYPE_TQ1_0: TQ1_0, DTYPE_F16: F16, DTYPE_BF16: BF16}[t.dtype]
         return Weight(ctx, h.value, fmt, int(t.shape[1]), int(t.shape[0]))

@@ -56,9 +56,56 @@ void set_err(char* err, size_t len, const char* fmt, ...) {
   va_end(ap);
 }
 
+// Whole-table UTF-8 check: the reference parses the table with serde_json from
+// bytes, which refuses invalid UTF-8 (overlong forms, surrogates, code points
+// past U+10FFFF, truncated sequences).
+bool valid_utf8(const uint8_t* p, const uint8_t* e) {
+  while (p < e) {
+    const uint8_t c = *p++;
+    if (c < 0x80) continue;
+    int n;
+    uint32_t v;
+    if (c >= 0xC2 && c <= 0xDF) n = 1, v = c & 0x1F;
+    else if (c >= 0xE0 && c <= 0xEF) n = 2, v = c & 0x0F;
+    else if (c >= 0xF0 && c <= 0xF4) n = 3, v = c & 0x07;
+    else return false;
+    if (e - p < n) return false;
+    for (int i = 0; i < n; ++i) {
+      if ((p[i] & 0xC0) != 0x80) return false;
+      v = (v << 6) | (p[i] & 0x3F);
+    }
+    p += n;
+    if ((n == 2 && v < 0x800) || (n == 3 && v < 0x10000) || v > 0x10FFFF ||
+        (v >= 0xD800 && v <= 0xDFFF))
+      return false;
+  }
+  return true;
+}
+
+void put_utf8(std::string& s, uint32_t v) {
+  if (v < 0x80) {
+    s += (char)v;
+  } else if (v < 0x800) {
+    s += (char)(0xC0 | (v >> 6));
+    s += (char)(0x80 | (v & 0x3F));
+  } else if (v < 0x10000) {
+    s += (char)(0xE0 | (v >> 12));
+    s += (char)(0x80 | ((v >> 6) & 0x3F));
+    s += (char)(0x80 | (v & 0x3F));
+  } else {
+    s += (char)(0xF0 | (v >> 18));
+    s += (char)(0x80 | ((v >> 12) & 0x3F));
+    s += (char)(0x80 | ((v >> 6) & 0x3F));
+    s += (char)(0x80 | (v & 0x3F));
+  }
+}
+
 // Minimal JSON reader for the tensor table: an array of objects whose values
 // are strings, unsigned integers or arrays of unsigned integers. Unknown keys
-// are skipped (any JSON value).
+// are skipped (any JSON value, nested at most kMaxDepth deep). Strings follow
+// the JSON grammar: no raw control characters, the eight escapes, \u with
+// surrogate pairs.
+constexpr int kMaxDepth = 128;
 struct Json {
   const char* p;
   const char* e;
@@ -80,48 +127,58 @@ struct Json {
     ws();
     return p < e && *p == c;
   }
+  bool hex4(uint32_t* v) {
+    if (e - p < 4) return (err = "bad \\u escape"), false;
+    *v = 0;
+    for (int i = 0; i < 4; ++i) {
+      const char h = *p++;
+      *v <<= 4;
+      if (h >= '0' && h <= '9') *v |= (uint32_t)(h - '0');
+      else if (h >= 'a' && h <= 'f') *v |= (uint32_t)(h - 'a' + 10);
+      else if (h >= 'A' && h <= 'F') *v |= (uint32_t)(h - 'A' + 10);
+      else return (err = "bad \\u escape"), false;
+    }
+    return true;
+  }
   bool string(std::string* out) {
     if (!expect('"')) return false;
     std::string s;
     while (p < e && *p != '"') {
-      char c = *p++;
-      if (c == '\\') {
-        if (p >= e) break;
-        char x = *p++;
-        switch (x) {
-          case 'n': s += '\n'; break;
-          case 't': s += '\t'; break;
-          case 'r': s += '\r'; break;
-          case 'b': s += '\b'; break;
-          case 'f': s += '\f'; break;
-          case 'u': {
-            if (e - p < 4) return (err = "bad \\u escape"), false;
-            unsigned v = 0;
-            for (int i = 0; i < 4; ++i) {
-              char h = *p++;
-              v <<= 4;
-              if (h >= '0' && h <= '9') v |= (unsigned)(h - '0');
-              else if (h >= 'a' && h <= 'f') v |= (unsigned)(h - 'a' + 10);
-              else if (h >= 'A' && h <= 'F') v |= (unsigned)(h - 'A' + 10);
-              else return (err = "bad \\u escape"), false;
-            }
-            // tensor names are ASCII; other code points are kept as UTF-8
-            if (v < 0x80) {
-              s += (char)v;
-            } else if (v < 0x800) {
-              s += (char)(0xC0 | (v >> 6));
-              s += (char)(0x80 | (v & 0x3F));
-            } else {
-              s += (char)(0xE0 | (v >> 12));
-              s += (char)(0x80 | ((v >> 6) & 0x3F));
-              s += (char)(0x80 | (v & 0x3F));
-            }
-            break;
-          }
-          default: s += x;
-        }
-      } else {
+      const char c = *p++;
+      if ((unsigned char)c < 0x20) return (err = "control character in a string"), false;
+      if (c != '\\') {
         s += c;
+        continue;
+      }
+      if (p >= e) break;
+      const char x = *p++;
+      switch (x) {
+        case '"': s += '"'; break;
+        case '\\': s += '\\'; break;
+        case '/': s += '/'; break;
+        case 'n': s += '\n'; break;
+        case 't': s += '\t'; break;
+        case 'r': s += '\r'; break;
+        case 'b': s += '\b'; break;
+        case 'f': s += '\f'; break;
+        case 'u': {
+          uint32_t v;
+          if (!hex4(&v)) return false;
+          if (v >= 0xDC00 && v <= 0xDFFF) return (err = "lone surrogate in \\u escape"), false;
+          if (v >= 0xD800 && v <= 0xDBFF) {
+            uint32_t lo;
+            if (e - p < 2 || p[0] != '\\' || p[1] != 'u')
+              return (err = "lone surrogate in \\u escape"), false;
+            p += 2;
+            if (!hex4(&lo)) return false;
+            if (lo < 0xDC00 || lo > 0xDFFF) return (err = "lone surrogate in \\u escape"), false;
+            v = 0x10000 + ((v - 0xD800) << 10) + (lo - 0xDC00);
+          }
+          put_utf8(s, v);
+          break;
+        }
+        default:
+          return (err = "invalid escape in a string"), false;
       }
     }
     if (!expect('"')) return false;
@@ -141,9 +198,40 @@ struct Json {
     *out = v;
     return true;
   }
-  bool skip_value() {
+  bool literal(const char* word) {
+    const size_t n = std::strlen(word);
+    if ((size_t)(e - p) < n || std::memcmp(p, word, n) != 0) return (err = "bad value"), false;
+    p += n;
+    return true;
+  }
+  // JSON number: -?(0|[1-9][0-9]*)(.[0-9]+)?([eE][+-]?[0-9]+)?
+  bool number() {
+    auto digits = [&]() {
+      const char* s = p;
+      while (p < e && *p >= '0' && *p <= '9') ++p;
+      return p > s;
+    };
+    if (p < e && *p == '-') ++p;
+    if (p < e && *p == '0') {
+      ++p;
+    } else if (!digits()) {
+      return (err = "bad value"), false;
+    }
+    if (p < e && *p == '.') {
+      ++p;
+      if (!digits()) return (err = "bad number"), false;
+    }
+    if (p < e && (*p == 'e' || *p == 'E')) {
+      ++p;
+      if (p < e && (*p == '+' || *p == '-')) ++p;
+      if (!digits()) return (err = "bad number"), false;
+    }
+    return true;
+  }
+  bool skip_value(int depth = 0) {
     ws();
     if (p >= e) return (err = "truncated"), false;
+    if (depth > kMaxDepth) return (err = "values nested too deep"), false;
     if (*p == '"') return string(nullptr);
     if (*p == '{' || *p == '[') {
       const char open = *p, close = open == '{' ? '}' : ']';
@@ -153,7 +241,7 @@ struct Json {
         if (open == '{') {
           if (!string(nullptr) || !expect(':')) return false;
         }
-        if (!skip_value()) return false;
+        if (!skip_value(depth + 1)) return false;
         if (peek(',')) {
           ++p;
           continue;
@@ -161,11 +249,10 @@ struct Json {
         return expect(close);
       }
     }
-    // number, true, false, null
-    const char* s = p;
-    while (p < e && *p != ',' && *p != '}' && *p != ']' && *p != ' ' && *p != '\n') ++p;
-    if (p == s) return (err = "bad value"), false;
-    return true;
+    if (*p == 't') return literal("true");
+    if (*p == 'f') return literal("false");
+    if (*p == 'n') return literal("null");
+    return number();
   }
   bool uint_array(std::vector<uint64_t>* out) {
     if (!expect('[')) return false;
@@ -195,6 +282,8 @@ struct Json {
           uint64_t v = 0;
           if (key == "name") {
             if (!string(&t.name)) return false;
+            if (t.name.find('\0') != std::string::npos)
+              return (err = "tensor name holds a NUL character"), false;
             have[0] = true;
           } else if (key == "shape") {
             if (!uint_array(&t.shape)) return false;
@@ -299,6 +388,10 @@ ouroq_status ouroq_bmts_open(const char* path, ouroq_bmts** out, char* err, size
     set_err(err, err_len,
             "unsupported BMTS version %u in %s (only v1, JSON meta, is read here)", version, path);
     return bail(OUROQ_ERR_UNSUPPORTED);
+  }
+  if (!valid_utf8(b + kBmtsHeaderLen, b + kBmtsHeaderLen + meta_len)) {
+    set_err(err, err_len, "BMTS meta is not valid UTF-8: %s", path);
+    return bail(OUROQ_ERR_BAD_SHAPE);
   }
   ouroq_bmts* f = new (std::nothrow) ouroq_bmts;
   if (!f) return bail(OUROQ_ERR_OOM);

@@ -90,6 +90,48 @@ def test_bmts_json_extras_and_escapes(tmp_path):
     assert bytes(shard.read_tensor('blk.0.attn"q')) == bytes(range(16))
 
 
+def _one_entry(extra: bytes, name: bytes = b'"w"') -> bytes:
+    return (b'[{"name":' + name + b',"shape":[8,8],"dtype":34,"offset":0,"length":16'
+            + extra + b'}]')
+
+
+def test_bmts_string_escapes_follow_json(tmp_path):
+    # a surrogate pair becomes one code point (U+1F600), as serde_json decodes it
+    path = tmp_path / "pair.bmts"
+    meta = _one_entry(b"", b'"w\\ud83d\\ude00\\/x"')
+    path.write_bytes(_header(meta_len=len(meta)) + meta + bytes(16))
+    assert BmtsShard(str(path)).tensors[0].name == "w\U0001F600/x"
+
+
+@pytest.mark.parametrize("case,meta", [
+    ("lone_high_surrogate", _one_entry(b"", b'"w\\ud83d"')),
+    ("lone_low_surrogate", _one_entry(b"", b'"w\\ude00"')),
+    ("unknown_escape", _one_entry(b"", b'"w\\q"')),
+    ("raw_control_char", _one_entry(b"", b'"w\tx"')),
+    ("nul_in_name", _one_entry(b"", b'"w\\u0000x"')),
+    ("invalid_utf8", _one_entry(b"", b'"w\xc3\x28"')),
+    ("overlong_utf8", _one_entry(b"", b'"w\xc0\xaf"')),
+    ("bad_literal", _one_entry(b',"x":tru')),
+    ("bad_number", _one_entry(b',"x":1.e5')),
+    ("deep_nesting", _one_entry(b',"x":' + b"[" * 100000 + b"]" * 100000)),
+])
+def test_bmts_refuses_malformed_json(tmp_path, case, meta):
+    # serde_json refuses all of these; so does the reader, without reading past
+    # the table or recursing without bound
+    path = tmp_path / f"{case}.bmts"
+    path.write_bytes(_header(meta_len=len(meta)) + meta + bytes(16))
+    with pytest.raises(oq.OuroqError):
+        BmtsShard(str(path))
+
+
+def test_bmts_unknown_values_of_every_json_kind(tmp_path):
+    path = tmp_path / "kinds.bmts"
+    meta = _one_entry(b',"a":-1.5e3,"b":0,"c":false,"d":null,"e":"s","f":[],"g":{},'
+                      b'"h":' + b"[" * 100 + b"]" * 100)
+    path.write_bytes(_header(meta_len=len(meta)) + meta + bytes(16))
+    assert BmtsShard(str(path)).tensors[0].name == "w"
+
+
 @pytest.mark.gpu
 def test_bmts_upload_and_matvec(ctx, oracle, tmp_path):
     # a small stage shard: one Tl1 and one TQ1_0 projection, GGUF shape [in, out]
