@@ -468,8 +468,10 @@ ouroq_status ouroq_bmts_span(const ouroq_bmts* f, const char* name, uint64_t off
             (unsigned long long)t->length);
     return OUROQ_ERR_BAD_SHAPE;
   }
-  const uint64_t start = f->data_start + t->offset + offset;
-  if (t->offset > f->size || start > f->size || length > f->size - start) {
+  uint64_t start = 0;
+  if (__builtin_add_overflow(f->data_start, t->offset, &start) ||
+      __builtin_add_overflow(start, offset, &start) || start > f->size ||
+      length > f->size - start) {
     set_err(err, err_len, "tensor %s range exceeds file %s", name, f->path.c_str());
     return OUROQ_ERR_BAD_SHAPE;
   }

@@ -154,3 +154,27 @@ def test_bmts_upload_and_matvec(ctx, oracle, tmp_path):
     w1.free()
     w2.free()
     shard.close()
+
+
+def test_bmts_span_arithmetic_does_not_wrap(tmp_path):
+    # offsets and lengths near 2^64: a span whose end wraps around must be
+    # refused, not mapped onto the start of the file
+    path = tmp_path / "wrap.bmts"
+    big = 2**64 - 1
+    meta = (b'[{"name":"w","shape":[8,8],"dtype":34,"offset":%d,"length":%d}]'
+            % (2**64 - 8, big))
+    path.write_bytes(_header(meta_len=len(meta)) + meta + bytes(64))
+    shard = BmtsShard(str(path))
+    for off, ln in ((0, 8), (2**64 - 100, 50), (big, 0), (16, 8)):
+        with pytest.raises(oq.OuroqError):
+            shard.read_span("w", off, ln)
+    shard.close()
+    # data offset 0, a huge declared length: a span offset chosen so that
+    # data_start + offset wraps to byte 4 of the file (inside its header)
+    meta = b'[{"name":"w","shape":[8,8],"dtype":34,"offset":0,"length":%d}]' % big
+    path.write_bytes(_header(meta_len=len(meta)) + meta + bytes(64))
+    shard = BmtsShard(str(path))
+    assert bytes(shard.read_span("w", 0, 16)) == bytes(16)
+    with pytest.raises(oq.OuroqError):
+        shard.read_span("w", 2**64 - shard.data_start + 4, 8)
+    shard.close()
