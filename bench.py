@@ -194,6 +194,11 @@ class ClockSampler:
     def __enter__(self):
         self._t = threading.Thread(target=self._run, daemon=True)
         self._t.start()
+        # the first nvidia-smi call forks a process: let it finish before the
+        # caller opens its timed region, so the fork is not inside it
+        t0 = time.perf_counter()
+        while not self.rows and self._t.is_alive() and time.perf_counter() - t0 < 2.0:
+            time.sleep(0.01)
         return self
 
     def __exit__(self, *a):
@@ -211,6 +216,27 @@ class ClockSampler:
                           if len(r) > 5 + i and r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(self.rows)}
+
+
+def gate(torch, replays: int):
+    """Hold the current stream on the device for a moment (a spin kernel of
+    torch's) before the timed region opens, so that the CPU has submitted the
+    whole region (`replays` graph launches) before the GPU reaches its first
+    event: the CPU's submit latency then stays out of the measurement."""
+    seconds = 2e-3 + 1e-4 * replays
+    torch.cuda._sleep(int(seconds * 2.0e9))  # cycles at ~2 GHz
+
+
+def graph_plan(steps: int, ncop: int, max_passes: int = 64):
+    """Cover exactly `steps` steps with CUDA graphs: a graph of G steps (G a
+    multiple of the copy count, so replays keep the rotation) replayed
+    `reps` times, then one graph of the remaining `rest` steps (copies
+    0..rest-1, which follow a full pass). Returns (G, reps, rest)."""
+    passes = max(1, min(steps // ncop, max_passes))
+    G = passes * ncop
+    if steps < G:
+        return 0, 0, steps
+    return G, steps // G, steps % G
 
 
 # ---------------------------------------------------------------- data
@@ -486,27 +512,45 @@ def run_ouroq(args, rank, world, local_rank):
         for j, (_, _, _, xi) in enumerate(mats):
             ctx.gemm(wts[i % ncop][j], qs[0][xi], sxs[0][xi], y=ys[i % 2][j], stream=stream)
 
-    def capture(fn):
-        with torch.cuda.stream(stream):
-            for i in range(max(args.warmup, 3)):
-                fn(i)
-        stream.synchronize()
+    def capture(fn, n):
+        """One CUDA graph of steps 0..n-1 (launch-bound loop -> graph replay)."""
         n0 = ctx.launch_count()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
-            for i in range(ncop):
+            for i in range(n):
                 fn(i)
-        return g, (ctx.launch_count() - n0) / ncop
+        return g, (ctx.launch_count() - n0) / max(n, 1)
 
-    def timed(fn, n):
+    def graphs_for(fn, nsteps):
+        """Graphs that run exactly nsteps steps: [(graph, replays)]."""
+        G, reps, rest = graph_plan(nsteps, ncop)
+        out, per = [], 0.0
+        if reps:
+            g, per = capture(fn, G)
+            out.append((g, reps))
+        if rest:
+            g, per = capture(fn, rest)
+            out.append((g, 1))
+        return out, per
+
+    def run_graphs(gs):
+        for g, reps in gs:
+            for _ in range(reps):
+                g.replay()
+
+    def timed(gs):
+        """Device time of the graphs gs (exactly their steps), max over ranks.
+        A spin kernel queued first keeps the CPU's submission out of the window."""
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(device)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        fn(n)
-        e1.record(stream)
+        with torch.cuda.stream(stream):
+            gate(torch, sum(r for _, r in gs))
+            e0.record(stream)
+            run_graphs(gs)
+            e1.record(stream)
         e1.synchronize()
         torch.cuda.synchronize(device)
         ms = e0.elapsed_time(e1)
@@ -516,21 +560,20 @@ def run_ouroq(args, rank, world, local_rank):
             ms = float(t.item())
         return ms
 
-    # CUDA graph of one pass over the copies (launch-bound loop -> graph replay)
-    graph, launches_per_step = capture(step)
-    def replay(n_passes, g=graph):
-        for _ in range(n_passes):
-            g.replay()
-
+    # eager warm-up (allocations, kernel loading), then the graphs of exactly
+    # args.steps steps, replayed once untimed with the warm-up
     with torch.cuda.stream(stream):
-        replay(max(1, args.warmup // ncop) + 1)
+        for i in range(max(args.warmup, 3)):
+            step(i)
     stream.synchronize()
-    passes = max(1, args.steps // ncop)
-    steps = passes * ncop
+    steps = max(1, args.steps)
+    graphs, launches_per_step = graphs_for(step, steps)
+    with torch.cuda.stream(stream):
+        run_graphs(graphs)
+    stream.synchronize()
 
     with ClockSampler(local_rank) as clk:
-        with torch.cuda.stream(stream):
-            ms = timed(replay, passes)
+        ms = timed(graphs)
     clocks = clk.summary()
 
     nb = step_bytes(wl, B)
@@ -547,10 +590,10 @@ def run_ouroq(args, rank, world, local_rank):
                   f"gemv_kernel<{'kTern2' if fmt == TERN else 'kSign1'},B={B}> (fused quantisation)")
     else:
         # matmul launches alone, on pre-quantised activations, timed the same way
-        g2, _ = capture(gemm_only)
+        g2, _ = graphs_for(gemm_only, steps)
         with torch.cuda.stream(stream):
-            replay(1, g2)
-            kms = timed(lambda n: replay(n, g2), passes)
+            run_graphs(g2)
+        kms = timed(g2)
         kern_s = kms / 1e3 / steps
         kern_bytes = nb["gemm"]
         kernel = ("gemm_tc_kernel (tcgen05 kind::i8)" if fmt == TERN and B >= 16
@@ -623,7 +666,9 @@ def run_ouroq(args, rank, world, local_rank):
 
     if rank == 0:
         cfg = workload_config(args, wl, world)
-        cfg.update({"pdl": not args.no_pdl, "launch": f"CUDA graph of {ncop} steps"})
+        cfg.update({"pdl": not args.no_pdl,
+                    "launch": "CUDA graphs of exactly the timed steps, queued behind a spin "
+                              "kernel before the first event"})
         line = {
             "metric": "packed-weight GEMV HBM GB/s",
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": steps,
@@ -644,7 +689,7 @@ def run_ouroq(args, rank, world, local_rank):
         if args.workload == "layer":
             line["decode_tokens_per_s_ternary_only"] = round(B * world / (ms / 1e3 / steps * 30), 1)
         print(json.dumps(line), flush=True)
-    del graph
+    del graphs
     ctx.close()
 
 
@@ -753,6 +798,7 @@ def run_decode(args, rank, world, local_rank):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(dec.stream):
+            gate(torch, n)
             e0.record(dec.stream)
             for _ in range(n):
                 g.replay()
@@ -891,26 +937,38 @@ def run_sharded(args, rank, world, local_rank):
     def local(i):
         ctx.gemm_f32act(copies[i % ncop], xs[i % ncop], y=ylocal, stream=stream)
 
-    def capture(fn):
+    def capture(fn, n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(n):
+                fn(i)
+        return g
+
+    def graphs_for(fn, nsteps):
+        """Graphs that run exactly nsteps steps, after an eager warm-up."""
         with torch.cuda.stream(stream):
             for i in range(max(args.warmup, 3)):
                 fn(i)
         ctx.shard_sync(stream, timeout_ms=60000)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            for i in range(ncop):
-                fn(i)
-        return g
+        G, reps, rest = graph_plan(nsteps, ncop)
+        out = []
+        if reps:
+            out.append((capture(fn, G), reps))
+        if rest:
+            out.append((capture(fn, rest), 1))
+        return out
 
-    def timed(g, n):
+    def timed(gs):
         dist.barrier() if world > 1 else None
         torch.cuda.synchronize(device)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
+            gate(torch, sum(r for _, r in gs))
             e0.record(stream)
-            for _ in range(n):
-                g.replay()
+            for g, reps in gs:
+                for _ in range(reps):
+                    g.replay()
             e1.record(stream)
         ctx.shard_sync(stream, timeout_ms=120000)
         torch.cuda.synchronize(device)
@@ -921,16 +979,15 @@ def run_sharded(args, rank, world, local_rank):
             ms = float(t.item())
         return ms
 
-    g_step = capture(step)
-    g_local = capture(local)
-    passes = max(1, args.steps // ncop)
-    steps = passes * ncop
-    timed(g_step, 1)
+    steps = max(1, args.steps)
+    g_step = graphs_for(step, steps)
+    g_local = graphs_for(local, steps)
+    timed(g_step)
     with ClockSampler(local_rank) as clk:
-        ms = timed(g_step, passes)
+        ms = timed(g_step)
     clocks = clk.summary()
-    timed(g_local, 1)
-    lms = timed(g_local, passes)
+    timed(g_local)
+    lms = timed(g_local)
 
     nb = step_bytes(wl, B)
     value = nb["step"] * steps / (ms / 1e3) / 1e9  # the full matrix once per step, all ranks
@@ -949,7 +1006,7 @@ def run_sharded(args, rank, world, local_rank):
                        "parallelism": f"row-sharded x{world}, " + (
                            "peer stores over NVLink" if args.transport == "peer"
                            else "in-place NCCL all-gather"),
-                       "launch": f"CUDA graph of {ncop} steps"},
+                       "launch": "CUDA graphs of exactly the timed steps"},
             "local_product_us": round(1e3 * lms / steps, 3),
             "gather_and_sync_us": round(1e3 * (ms - lms) / steps, 3),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,

@@ -68,3 +68,16 @@ def test_algorithmic_bytes_match_the_configs():
     for name, wl in bench.WORKLOADS.items():
         if wl[2]:
             assert bench.n_copies(wl) * bench.step_bytes(wl, 1)["weights"] >= 2 * bench.L2_BYTES
+
+
+@pytest.mark.parametrize("steps", [1, 5, 16, 20, 37, 1000, 30000])
+def test_graph_plan_runs_exactly_the_requested_steps(steps):
+    # the timed region replays graphs whose steps add up to --steps exactly
+    # (the driver checks the printed step count against the one it asked for),
+    # and the full-pass graph keeps the weight-copy rotation across replays
+    sys.path.insert(0, str(ROOT))
+    import bench
+    ncop = bench.n_copies(bench.WORKLOADS["layer"])
+    G, reps, rest = bench.graph_plan(steps, ncop)
+    assert G * reps + rest == steps
+    assert G % ncop == 0 and G <= 64 * ncop and rest < max(G, steps + 1)
