@@ -616,33 +616,55 @@ def run_ouroq(args, rank, world, local_rank):
     roof["traffic"] = profiled_traffic(f"{args.workload}_b{B}")
     roof["kernel"] = kernel
 
-    # ---- e2e through the public API with host buffers (pinned), eager calls.
-    # A step's activations sit back to back in one pinned buffer and cross in
-    # one copy; its outputs come back in one copy (every segment starts on a
-    # 512-byte boundary: widths are multiples of 128, output rows of 4).
+    # ---- e2e: the same steps through the reference-facing host-buffer call
+    # (ouroq_matmul_q_group: the step's projections in one synchronous round
+    # trip, host fp32 x in, host fp32 y out), page-locked host buffers, timed
+    # on the host clock around whole calls (each returns after its copy back).
+    # A step's activations sit back to back in one buffer and cross in one
+    # copy; its outputs come back in one copy (widths are multiples of 128).
     xoff = np.cumsum([0] + [B * k for k in widths]).tolist()
     yoff = np.cumsum([0] + [B * M for _, M, _, _ in mats]).tolist()
     xh = [torch.cat([x.reshape(-1) for x in xl]).cpu().pin_memory() for xl in xs[:2]]
     yh = torch.empty(yoff[-1], dtype=torch.float32).pin_memory()
-    xcat = torch.empty(xoff[-1], device=device)
-    ycat = torch.empty(yoff[-1], device=device)
-    xd = [xcat[xoff[j]:xoff[j + 1]].view(B, k) for j, k in enumerate(widths)]
-    yd = [ycat[yoff[j]:yoff[j + 1]].view(B, M) for j, (_, M, _, _) in enumerate(mats)]
-    e2e_steps = min(steps, 600)
+    xhv = [[xc[xoff[j]:xoff[j + 1]] for j in range(len(widths))] for xc in xh]
+    yhv = [yh[yoff[j]:yoff[j + 1]] for j in range(len(mats))]
     h2d = B * sum(widths) * 4
     d2h = B * sum(M for _, M, _, _ in mats) * 4
 
-    def e2e(n):
-        for i in range(n):
-            xcat.copy_(xh[i % 2], non_blocking=True)
-            run_step(wts[i % ncop], xd, yd, qs[0], sxs[0])
-            yh.copy_(ycat, non_blocking=True)
+    if not block:  # the host mirrors take no rotation (rotate_fwd is its own call)
+        def e2e(n):
+            for i in range(n):
+                ctx.matmul_q_group(wts[i % ncop], [xhv[i % 2][xi] for _, _, _, xi in mats], yhv)
+        how = ("ouroq_matmul_q_group (the C-ABI host-buffer operator: one synchronous call a "
+               "step, page-locked host x in, host y out), host clock around the calls")
+    else:
+        xcat = torch.empty(xoff[-1], device=device)
+        ycat = torch.empty(yoff[-1], device=device)
+        xd = [xcat[xoff[j]:xoff[j + 1]].view(B, k) for j, k in enumerate(widths)]
+        yd = [ycat[yoff[j]:yoff[j + 1]].view(B, M) for j, (_, M, _, _) in enumerate(mats)]
 
-    with torch.cuda.stream(stream):
-        e2e(5)
-        stream.synchronize()
-        e2e_ms = timed(e2e, e2e_steps)
-    e2e_value = nb["step"] * e2e_steps * world / (e2e_ms / 1e3) / 1e9
+        def e2e(n):
+            with torch.cuda.stream(stream):
+                for i in range(n):
+                    xcat.copy_(xh[i % 2], non_blocking=True)
+                    run_step(wts[i % ncop], xd, yd, qs[0], sxs[0])
+                    yh.copy_(ycat, non_blocking=True)
+                stream.synchronize()
+        how = ("device API with the rotation fused (the host mirrors take none), page-locked "
+               "host buffers: one copy in and one copy out a step, host clock")
+    e2e(5)
+    torch.cuda.synchronize(device)
+    e2e_steps = max(1, min(steps, 2000))
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    e2e(e2e_steps)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = nb["step"] * e2e_steps * world / e2e_s / 1e9
 
     # ---- CPU baseline (rank 0, N = 1 only), bounded sample of the same workload
     cpu = None
@@ -680,9 +702,8 @@ def run_ouroq(args, rank, world, local_rank):
             "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h,
-                    "how": ("eager Python calls of the public API, pinned host buffers: "
-                            "one copy in and one copy out a step")},
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "ms_per_step": round(1e3 * e2e_s / e2e_steps, 5), "how": how},
             "gpu_launches": int(round(launches_per_step * steps)),
             "clocks": clocks,
         }

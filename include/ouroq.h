@@ -338,6 +338,18 @@ ouroq_status ouroq_matvec_q(ouroq_ctx *ctx, const ouroq_weight *w, const float *
  * order for every k, as matmul_q gives. */
 ouroq_status ouroq_matmul_q(ouroq_ctx *ctx, const ouroq_weight *w, const float *x_host, int k,
                             float *y_host);
+/* The projections of one stage call in one round trip: Stage::wm /
+ * wmat_batched (infer/mod.rs:138-167) run once per named tensor of a layer
+ * (q, k, v, o, gate, up, down: run_layer, infer/mod.rs:305-335), each a
+ * matvec_q / matmul_q. Here n (<= 8) such products go in one call:
+ * y_host[i] [k][M_i] = W_i . x_host[i] [k][K_i], entries may share an input.
+ * Results are those of ouroq_matmul_q on each entry (ouroq_matvec_q's for
+ * k = 1). Synchronous. Page-locked host buffers (cudaHostAlloc /
+ * cudaHostRegister) are copied by DMA directly, and buffers that sit back to
+ * back in memory cross in one copy; pageable ones go through the context's
+ * page-locked staging buffer. */
+ouroq_status ouroq_matmul_q_group(ouroq_ctx *ctx, int n, const ouroq_weight *const *w,
+                                  const float *const *x_host, int k, float *const *y_host);
 /* hadamard::rotate_fwd (hadamard.rs:41-53) in place on a host buffer of n floats. */
 ouroq_status ouroq_rotate_fwd(ouroq_ctx *ctx, float *x_host, const float *signs_host, size_t n,
                               size_t block);

@@ -103,6 +103,7 @@ ABI_FUNCTIONS = {
     "ouroq_bmts_upload": (_i, [_p, _p, ctypes.c_char_p, ctypes.POINTER(_p), ctypes.c_char_p, _sz]),
     "ouroq_matvec_q": (_i, [_p, _p, _p, _p]),
     "ouroq_matmul_q": (_i, [_p, _p, _p, _i, _p]),
+    "ouroq_matmul_q_group": (_i, [_p, _i, _p, _p, _i, _p]),
     "ouroq_rotate_fwd": (_i, [_p, _p, _p, _sz, _sz]),
     "ouroq_rotate_inv": (_i, [_p, _p, _p, _sz, _sz]),
 }
@@ -594,6 +595,40 @@ class Context:
         y = np.empty((k, w.rows), dtype=np.float32)
         self._check(self.lib.ouroq_matmul_q(self.ctx, w.handle, _ptr(x), k, _ptr(y)))
         return y
+
+    def matmul_q_group(self, ws, xs, ys=None):
+        """Several matmul_q products in one synchronous round trip: ys[i] [k][M_i]
+        = W_i . xs[i] [k][K_i] (host buffers: numpy arrays or CPU tensors; page-locked
+        ones are copied by DMA directly). Entries may share an input. Returns ys."""
+        n = len(ws)
+        if len(xs) != n or (ys is not None and len(ys) != n):
+            raise OuroqError(1, "one input and one output per weight")
+
+        def size_of(a):
+            return a.size if isinstance(a, np.ndarray) else a.numel()
+
+        def f32(a):
+            return str(getattr(a, "dtype", "")) in ("float32", "torch.float32")
+        k = None
+        for w, x in zip(ws, xs):
+            if getattr(x, "is_cuda", False):
+                raise OuroqError(7, "matmul_q_group takes host buffers")
+            if w.K <= 0 or size_of(x) % w.K or not f32(x):
+                raise OuroqError(1, f"in_len {w.K}: input of {size_of(x)} values is not [k][{w.K}] float32")
+            rows = size_of(x) // w.K
+            if k is not None and rows != k:
+                raise OuroqError(1, "every input has the same number of columns k")
+            k = rows
+        if ys is None:
+            ys = [np.empty((k, w.rows), dtype=np.float32) for w in ws]
+        for w, y in zip(ws, ys):
+            if getattr(y, "is_cuda", False) or size_of(y) != k * w.rows or not f32(y):
+                raise OuroqError(1, f"output of {size_of(y)} values, expected host [{k}][{w.rows}] float32")
+        W = (_p * n)(*[w.handle for w in ws])
+        X = (_p * n)(*[_ptr(x) for x in xs])
+        Y = (_p * n)(*[_ptr(y) for y in ys])
+        self._check(self.lib.ouroq_matmul_q_group(self.ctx, n, W, X, k or 0, Y))
+        return ys
 
     def rotate_fwd(self, x: np.ndarray, signs: np.ndarray | None, block: int) -> np.ndarray:
         """hadamard::rotate_fwd in place on a host fp32 buffer (returns it)."""

@@ -48,6 +48,11 @@ struct ouroq_ctx {
   size_t y_cap = 0;
   float* sign_stage = nullptr;
   size_t sign_cap = 0;
+  // page-locked host staging of the host-buffer calls (pageable inputs/outputs)
+  float* hx_stage = nullptr;
+  size_t hx_cap = 0;
+  float* hy_stage = nullptr;
+  size_t hy_cap = 0;
   // rotated fp32 activations for the reference formats (hadamard_block != 0)
   float* rot_scratch = nullptr;
   float* norm_scratch = nullptr;  // normalised activations when the norm is not fused
@@ -682,6 +687,8 @@ ouroq_status ouroq_ctx_destroy(ouroq_ctx* ctx) {
   cudaFree(ctx->x_stage);
   cudaFree(ctx->y_stage);
   cudaFree(ctx->sign_stage);
+  cudaFreeHost(ctx->hx_stage);
+  cudaFreeHost(ctx->hy_stage);
   cudaFree(ctx->rot_scratch);
   cudaFree(ctx->attn_part);
   cudaFree(ctx->attn_ctr);
@@ -1133,6 +1140,138 @@ ouroq_status ouroq_matmul_q(ouroq_ctx* ctx, const ouroq_weight* w, const float* 
 ouroq_status ouroq_matvec_q(ouroq_ctx* ctx, const ouroq_weight* w, const float* x_host,
                             float* y_host) {
   return host_product(ctx, w, x_host, 1, y_host, Tl1Order::kMatvec);
+}
+
+// Page-locked host memory (cudaHostAlloc / cudaHostRegister): DMA-able as it is.
+static bool host_pinned(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();  // clear the error an unknown pointer leaves
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
+static ouroq_status grow_pinned(ouroq_ctx* ctx, float*& buf, size_t& cap, size_t n,
+                                const char* what) {
+  if (n <= cap) return OUROQ_OK;
+  if (buf) cudaFreeHost(buf);
+  buf = nullptr;
+  cap = 0;
+  const size_t want = n < 4096 ? 4096 : n;
+  cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&buf), want * sizeof(float),
+                                cudaHostAllocDefault);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+  cap = want;
+  return OUROQ_OK;
+}
+
+// One host<->device transfer of a host-buffer call: `host` is the caller's
+// buffer, `dev_off` the float offset of its slot in the device stage.
+struct HostSeg {
+  float* host;
+  size_t dev_off, n;
+  bool pinned;
+};
+
+// Issue the copies of `segs` (in stage order) on s: pinned buffers directly,
+// pageable ones through the page-locked stage `hstage` (same offsets), and
+// runs that sit back to back on both sides as one copy.
+static ouroq_status copy_segs(ouroq_ctx* ctx, std::vector<HostSeg>& segs, float* dstage,
+                              float* hstage, bool to_device, cudaStream_t s) {
+  size_t i = 0;
+  while (i < segs.size()) {
+    float* h0 = segs[i].pinned ? segs[i].host : hstage + segs[i].dev_off;
+    const size_t off0 = segs[i].dev_off;
+    size_t n = segs[i].n, j = i + 1;
+    while (j < segs.size()) {
+      float* hj = segs[j].pinned ? segs[j].host : hstage + segs[j].dev_off;
+      if (hj != h0 + n || segs[j].dev_off != off0 + n) break;
+      n += segs[j].n;
+      ++j;
+    }
+    if (to_device)
+      CU(ctx, cudaMemcpyAsync(dstage + off0, h0, n * 4, cudaMemcpyHostToDevice, s), "x upload");
+    else
+      CU(ctx, cudaMemcpyAsync(h0, dstage + off0, n * 4, cudaMemcpyDeviceToHost, s), "y download");
+    i = j;
+  }
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_matmul_q_group(ouroq_ctx* ctx, int n, const ouroq_weight* const* w,
+                                  const float* const* x_host, int k, float* const* y_host) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  if (n < 0 || n > kMaxGemvJobs)
+    return fail(ctx, OUROQ_ERR_BAD_SHAPE, "group size %d (max %d)", n, kMaxGemvJobs);
+  if (k < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "k=%d", k);
+  if (n == 0 || k == 0) return OUROQ_OK;
+  if (!w || !x_host || !y_host) return fail(ctx, OUROQ_ERR_BAD_ARG, "null array");
+  for (int i = 0; i < n; ++i)
+    if (!w[i] || !x_host[i] || !y_host[i]) return fail(ctx, OUROQ_ERR_BAD_ARG, "null entry %d", i);
+  DeviceGuard g(ctx->device);
+  // distinct inputs (same pointer and width) share one slot of the device stage
+  std::vector<HostSeg> xs, ys;
+  int slot[kMaxGemvJobs];
+  size_t xtot = 0, ytot = 0;
+  for (int i = 0; i < n; ++i) {
+    int j = 0;
+    while (j < i && !(x_host[j] == x_host[i] && w[j]->K == w[i]->K)) ++j;
+    if (j < i) {
+      slot[i] = slot[j];
+    } else {
+      slot[i] = (int)xs.size();
+      xs.push_back({const_cast<float*>(x_host[i]), xtot, (size_t)k * w[i]->K, false});
+      xtot += ((size_t)k * w[i]->K + 3) / 4 * 4;  // slots start 16-byte aligned
+    }
+    ys.push_back({y_host[i], ytot, (size_t)k * w[i]->M, false});
+    ytot += ((size_t)k * w[i]->M + 3) / 4 * 4;
+  }
+  ouroq_status st = grow(ctx, ctx->x_stage, ctx->x_cap, xtot, "x stage");
+  if (st != OUROQ_OK) return st;
+  st = grow(ctx, ctx->y_stage, ctx->y_cap, ytot, "y stage");
+  if (st != OUROQ_OK) return st;
+  bool x_staged = false, y_staged = false;
+  for (HostSeg& sg : xs) x_staged |= !(sg.pinned = host_pinned(sg.host));
+  for (HostSeg& sg : ys) y_staged |= !(sg.pinned = host_pinned(sg.host));
+  if (x_staged) {
+    st = grow_pinned(ctx, ctx->hx_stage, ctx->hx_cap, xtot, "pinned x stage");
+    if (st != OUROQ_OK) return st;
+    for (const HostSeg& sg : xs)
+      if (!sg.pinned) std::memcpy(ctx->hx_stage + sg.dev_off, sg.host, sg.n * 4);
+  }
+  if (y_staged) {
+    st = grow_pinned(ctx, ctx->hy_stage, ctx->hy_cap, ytot, "pinned y stage");
+    if (st != OUROQ_OK) return st;
+  }
+  cudaStream_t s = ctx->host_stream;
+  st = copy_segs(ctx, xs, ctx->x_stage, ctx->hx_stage, true, s);
+  if (st != OUROQ_OK) return st;
+  const float* xd[kMaxGemvJobs];
+  float* yd[kMaxGemvJobs];
+  bool same_fmt = true;
+  for (int i = 0; i < n; ++i) {
+    xd[i] = ctx->x_stage + xs[slot[i]].dev_off;
+    yd[i] = ctx->y_stage + ys[i].dev_off;
+    same_fmt &= w[i]->fmt == w[0]->fmt;
+  }
+  // the quantised formats at small k: one grouped launch (as ouroq_gemm_group_f32act)
+  bool done = false;
+  if (same_fmt && !is_ref_format(w[0]->fmt) && !is_half_format(w[0]->fmt) && k <= kGemvMaxB) {
+    st = ouroq_gemm_group_f32act(ctx, n, w, xd, k, nullptr, nullptr, yd, s);
+    if (st == OUROQ_OK) done = true;
+    else if (st != OUROQ_ERR_UNSUPPORTED) return st;
+  }
+  for (int i = 0; i < n && !done; ++i) {
+    st = f32act_impl(ctx, w[i], xd[i], k, nullptr, 0, yd[i], s, Tl1Order::kAuto);
+    if (st != OUROQ_OK) return st;
+  }
+  st = copy_segs(ctx, ys, ctx->y_stage, ctx->hy_stage, false, s);
+  if (st != OUROQ_OK) return st;
+  CU(ctx, cudaStreamSynchronize(s), "stream sync");
+  for (const HostSeg& sg : ys)
+    if (!sg.pinned) std::memcpy(sg.host, ctx->hy_stage + sg.dev_off, sg.n * 4);
+  return OUROQ_OK;
 }
 
 static ouroq_status rotate_host(ouroq_ctx* ctx, float* x_host, const float* signs_host, size_t n,

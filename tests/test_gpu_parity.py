@@ -306,6 +306,41 @@ def test_host_mirrors_matvec_matmul(ctx, oracle):
     w.free()
 
 
+@pytest.mark.parametrize("k", [1, 2, 5, 20])
+def test_host_group_call_matches_oracle(ctx, oracle, k):
+    # ouroq_matmul_q_group: the projections of one layer call (shapes of the
+    # BitNet-2B layer scaled down in rows, gate and up sharing their input) in
+    # one synchronous host-buffer call; every entry equals the oracle's
+    # product, with pageable numpy buffers and with page-locked buffers that
+    # sit back to back (the bench's e2e path)
+    import torch
+    shapes = [(384, 2560, 0), (256, 2560, 1), (700, 2560, 2), (700, 2560, 2), (256, 6912, 3)]
+    xs = [oracle.normals(90 + i, k * K).reshape(k, K) for i, K in enumerate([2560, 2560, 2560, 6912])]
+    ws, want = [], []
+    for i, (M, K, xi) in enumerate(shapes):
+        wt = oracle.ternary(70 + i, M * K).reshape(M, K)
+        wsc = oracle.absmean_scale(wt, 0.02)
+        ws.append(ctx.upload(oq.TERNARY2, oracle.pack_tern2(wt), M, K, w_scale=wsc))
+        qr, sr = oracle.quantize_act(xs[xi])
+        want.append(oracle.gemm_tern2(oracle.pack_tern2(wt), M, K, wsc, qr, sr)[1])
+    got = ctx.matmul_q_group(ws, [xs[xi] for _, _, xi in shapes])
+    for g, r in zip(got, want):
+        assert np.array_equal(g, r)
+    xcat = torch.from_numpy(np.concatenate([x.reshape(-1) for x in xs])).pin_memory()
+    off = np.cumsum([0] + [x.size for x in xs])
+    ycat = torch.empty(sum(k * M for M, _, _ in shapes), dtype=torch.float32).pin_memory()
+    yoff = np.cumsum([0] + [k * M for M, _, _ in shapes])
+    ys = [ycat[yoff[i]:yoff[i + 1]] for i in range(len(shapes))]
+    ctx.matmul_q_group(ws, [xcat[off[xi]:off[xi + 1]] for _, _, xi in shapes], ys)
+    for y, r in zip(ys, want):
+        assert np.array_equal(y.numpy().reshape(r.shape), r)
+    with pytest.raises(oq.OuroqError):
+        ctx.matmul_q_group(ws[:1], [xs[0][:, :100]])
+    for w in ws:
+        w.free()
+    ctx.check_device()
+
+
 def test_empty_batch_is_a_no_op(ctx, oracle):
     # matmul_q with k = 0 columns returns an empty vector (ops.rs:219-230)
     import torch
