@@ -32,6 +32,7 @@ struct ouroq_ctx {
   int smem_optin = 0;  // opt-in shared memory per block (bytes)
   bool pdl = true;
   bool use_tc = true;  // tensor-core path for batches >= 16
+  bool stream_gemv = true;  // fused one/two-token ternary launches on gemv_stream_kernel
   std::string err;
   unsigned* d_status = nullptr;
   uint64_t launches = 0;
@@ -194,6 +195,16 @@ GemvJob make_job(const ouroq_weight* w, const int8_t* q, const float* s_x, float
 ouroq_status run_gemv(ouroq_ctx* ctx, GemvLaunch& L, cudaStream_t s) {
   L.status = ctx->d_status;
   if (L.njobs == 0 || L.B == 0) return OUROQ_OK;
+  if (ctx->stream_gemv) {
+    GemvLaunch S = L;
+    int grid = 0;
+    size_t smem = 0;
+    if (gemv_stream_prepare(S, ctx->num_sms, &grid, &smem)) {
+      CU(ctx, launch_gemv_stream(S, grid, smem, s, ctx->pdl), "gemv launch");
+      if (S.ntiles > 0) ctx->launches++;
+      return OUROQ_OK;
+    }
+  }
   if (!gemv_fits(ctx, L))
     return fail(ctx, OUROQ_ERR_UNSUPPORTED,
                 "B=%d: the activations of one CTA's matrices do not fit in shared memory", L.B);

@@ -139,6 +139,10 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 __device__ __forceinline__ void named_bar_sync(unsigned id, unsigned nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// Arrive at a named barrier without waiting (the other side bar.syncs).
+__device__ __forceinline__ void named_bar_arrive(unsigned id, unsigned nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 
 // acc + sum_{i<4} u8(a.byte[i]) * s8(b.byte[i])
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int acc) {

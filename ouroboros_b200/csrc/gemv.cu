@@ -891,6 +891,61 @@ cudaError_t launch_fmt(const GemvLaunch& L, int grid, size_t smem, cudaStream_t 
 
 }  // namespace
 
+void balance_tiles(GemvLaunch& L, int grid, int per_chunk) {
+  // Tiles of job j weigh K_j / per_chunk (proportional to their bytes). The
+  // contiguous split that minimises the heaviest CTA: the smallest bound cap
+  // for which filling CTAs greedily (a CTA takes the next tile while its load
+  // stays within cap) needs at most `grid` CTAs, found by bisection. A launch
+  // ends with its heaviest CTA, so this bound is what the split costs.
+  const int tiles = L.ntiles;
+  auto weight = [&](int t, int& j) {
+    while (j + 1 < L.njobs && t >= L.jobs[j + 1].tile_begin) ++j;
+    return (long long)(L.jobs[j].K / per_chunk);
+  };
+  long long total = 0, heaviest = 0;
+  {
+    int j = 0;
+    for (int t = 0; t < tiles; ++t) {
+      const long long w = weight(t, j);
+      total += w;
+      heaviest = w > heaviest ? w : heaviest;
+    }
+  }
+  auto ctas_needed = [&](long long cap) {
+    int n = 1, j = 0;
+    long long load = 0;
+    for (int t = 0; t < tiles; ++t) {
+      const long long w = weight(t, j);
+      if (load + w > cap) {
+        ++n;
+        load = 0;
+      }
+      load += w;
+    }
+    return n;
+  };
+  long long lo = (total + grid - 1) / grid;
+  if (lo < heaviest) lo = heaviest;
+  long long hi = lo + heaviest;  // greedy under this cap never needs more than grid CTAs
+  while (lo < hi) {
+    const long long mid = (lo + hi) / 2;
+    if (ctas_needed(mid) <= grid) hi = mid;
+    else lo = mid + 1;
+  }
+  int c = 0, j = 0;
+  long long load = 0;
+  L.cta_tile[0] = 0;
+  for (int t = 0; t < tiles; ++t) {
+    const long long w = weight(t, j);
+    if (load + w > lo) {
+      L.cta_tile[++c] = (uint16_t)t;
+      load = 0;
+    }
+    load += w;
+  }
+  while (c < grid) L.cta_tile[++c] = (uint16_t)tiles;
+}
+
 bool gemv_prepare(GemvLaunch& L, int num_sms, int smem_optin, int* grid_out, size_t* smem_out) {
   const int wpc = L.fmt == kTern2 ? 64 : 128;
   int tiles = 0;
@@ -908,21 +963,8 @@ bool gemv_prepare(GemvLaunch& L, int num_sms, int smem_optin, int* grid_out, siz
   if (tiles > 65535 || L.B < 1 || L.B > kGemvMaxB) return false;
   int grid = tiles < num_sms ? tiles : num_sms;
   if (grid > kMaxGemvCtas) grid = kMaxGemvCtas;
-  // CTA c starts at the first tile whose cumulative weight reaches c * total / grid
-  {
-    int j = 0, t = 0;
-    long long w = 0;  // weight of tiles [0, t)
-    for (int c = 0; c <= grid; ++c) {
-      const long long target = total * c / grid;
-      while (t < tiles && w < target) {
-        while (j + 1 < L.njobs && t >= L.jobs[j + 1].tile_begin) ++j;
-        w += L.jobs[j].K / wpc;
-        ++t;
-      }
-      L.cta_tile[c] = (uint16_t)t;
-    }
-    L.cta_tile[grid] = (uint16_t)tiles;
-  }
+  (void)total;
+  balance_tiles(L, grid, wpc);
   // activations one CTA keeps resident: the jobs its tile range touches (one
   // row for all of them under a fused norm)
   int xcap = 0, gcap = 0;

@@ -1,0 +1,541 @@
+// gemv_stream.cu -- the decode GEMV for one or two tokens (K2 at B <= 2):
+// packed ternary weights x fp32 activations, the per-token absmax int8
+// quantisation fused in, grouped over up to eight matrices per launch.
+//
+// Reference operator: ops::matvec_q (cluster/src/infer/ops.rs:76-84), called
+// once per named tensor by Stage::wm (cluster/src/infer/mod.rs:138-147), seven
+// times per layer in run_layer (infer/mod.rs:305-335). Arithmetic: this
+// library's BitNet b1.58 form with the conventions fixed by the CPU oracle
+// (oracle/oracle.h): s_x = absmax / 127, q = clamp(rint(x / s_x)), int32
+// accumulation, y = ((float)acc * w_scale) * s_x -- bit-identical to it.
+//
+// Why a second GEMV kernel. At one token a layer's five projections move
+// 17.4 MB, 117 KB per SM: a few microseconds of HBM time, so what bounds a
+// launch is its critical path, not bandwidth. This kernel shortens it:
+//  * The weight stream starts at CTA entry: the producer warp initialises
+//    the ring's mbarriers itself and issues its copies straight from the
+//    launch parameters, before anything else runs. Weights never depend on
+//    the previous kernel; only the activations do, and only the consumers
+//    wait for it (griddepcontrol.wait), so the copies overlap the previous
+//    launch's tail and this launch's prologue. Built for one CTA per SM
+//    (kStreamCps = 1) a CTA's whole share (up to 13 x 16 KB) is in flight at
+//    once; built for two (<= 112 registers, <= 113 KB of shared memory each)
+//    the next launch's CTA can sit beside this one and stream while it
+//    computes.
+//  * Chunk-major stages. A stage is a K-slice of up to four 32-row tiles of
+//    one matrix (one bulk copy per tile: in the tiled layout a K-slice of a
+//    tile is contiguous). A consumer warp takes one 16-byte chunk position
+//    of the stage, loads the int8 activations of that chunk into registers
+//    once and applies them to the same chunk of every tile of the stage: one
+//    shared-memory load and 16 mask + 16 dp4a per tile and lane, with 4 x T
+//    independent accumulator chains per lane.
+//  * A short prologue: the activations of the CTA's matrices are loaded with
+//    every load issued before any use, each distinct input row once (gate
+//    and up share theirs), reduced and quantised in registers, with the
+//    rounding done in the full-rate pipes.
+//
+// Layout (kernels.h): tile t, chunk c, row r at (t * C + c) * 512 + r * 16.
+// In a stage, tile i's chunks [c0, c1) sit at i * (c1 - c0) * 512, so lane r
+// reading chunk k of tile i touches 512 contiguous bytes (no bank conflicts).
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "hadamard.cuh"
+#include "kernels.h"
+
+namespace ouroq {
+namespace {
+
+constexpr int kRows = kTileRows;
+constexpr int kCW = 8;                      // consumer warps
+constexpr int kSThreads = (kCW + 1) * 32;   // + one producer warp
+constexpr int kMaxT = 4;                    // tiles per stage
+constexpr uint32_t kStage = 16u * 1024u;    // bytes per ring slot
+constexpr int kMaxNS = 13;                  // ring depth limit
+constexpr int kMaxIn = kMaxGemvJobs;        // distinct inputs of one CTA
+constexpr int kRegUnits = 10;               // 128-value units a warp keeps in registers
+#ifndef OUROQ_STREAM_CPS
+#define OUROQ_STREAM_CPS 1
+#endif
+constexpr int kStreamCps = OUROQ_STREAM_CPS;  // CTAs per SM the kernel is built for
+
+__host__ __device__ constexpr uint32_t al128(uint32_t v) { return (v + 127u) & ~127u; }
+
+// Shared-memory plan (dynamic part), every region 128-byte aligned.
+struct SPlan {
+  uint32_t bars, red, xq, ring, total;
+};
+__host__ __device__ inline SPlan splan(int B, int ns, int xcap) {
+  SPlan p;
+  p.bars = al128(sizeof(GemvLaunch));
+  p.red = p.bars + 256;  // full[13] + empty[13] mbarriers
+  p.xq = p.red + al128((uint32_t)kCW * kMaxT * B * 32 * 4);
+  p.ring = p.xq + al128((uint32_t)xcap);
+  p.total = p.ring + (uint32_t)ns * kStage;
+  return p;
+}
+
+// Per-CTA tables, filled by consumer thread 0 before the dependency wait.
+struct STab {
+  const float* x[kMaxIn];   // distinct fp32 inputs
+  int K[kMaxIn];
+  int xoff[kMaxIn];         // byte offset of input i's codes [B][K] in xq
+  int ufirst[kMaxIn + 1];   // first 128-value unit of input i (all B rows)
+  int in_of[kMaxGemvJobs];  // job (relative to the CTA's first job) -> input
+  int nin;
+  float sx[kMaxIn][2];      // per-token scales
+  int qtot[kMaxIn][2];      // per-token code sums
+  int amax[kMaxIn][2];      // absmax bits
+};
+
+__device__ __forceinline__ int job_of(const GemvLaunch& L, int t) {
+  int j = 0;
+  while (j + 1 < L.njobs && t >= L.jobs[j + 1].tile_begin) ++j;
+  return j;
+}
+
+// Stage geometry of a tile group of T tiles of a K-chunk row: slices of at
+// most `sc` chunks (kStage / 512 / T, rounded down to a multiple of kCW), cut
+// evenly into multiples of kCW where possible.
+struct Geo {
+  int C, ns, per;
+};
+__device__ __forceinline__ Geo geo(int K, int T) {
+  Geo g;
+  g.C = K / 64;
+  int sc = (int)(kStage / 512u) / T;
+  if (sc >= kCW) sc -= sc % kCW;
+  g.ns = (g.C + sc - 1) / sc;
+  int per = (g.C + g.ns - 1) / g.ns;
+  if (per % kCW) {
+    const int up = per + kCW - per % kCW;
+    if (up <= sc) per = up;
+  }
+  g.per = per;
+  g.ns = (g.C + per - 1) / per;
+  return g;
+}
+
+// quant_code (hadamard.cuh) with the rounding done by the 1.5 * 2^23 addend
+// instead of rint + float-to-int conversion (both on the quarter-rate
+// conversion pipe): for |t| < 2^22, t + 1.5 * 2^23 rounds t to the nearest
+// integer, ties to even, exactly as rint does, and that integer sits in the
+// low mantissa bits. The tie guard and the division fallback are unchanged,
+// so the code is still rint(__fdiv_rn(v, s)) clamped to +-127, bit for bit.
+__device__ __forceinline__ int quant_code_fast(float v, float s, float rs) {
+  if (s == 0.0f) return 0;
+  const float t = __fmul_rn(v, rs);
+  const float m = __fadd_rn(t, 0x1.8p23f);
+  const float r = __fsub_rn(m, 0x1.8p23f);
+  int q;
+  if (fabsf(__fsub_rn(t, r)) < 0.5f - 0x1p-14f) {
+    q = __float_as_int(m) - 0x4B400000;
+  } else {
+    q = (int)fminf(fmaxf(rintf(__fdiv_rn(v, s)), -127.0f), 127.0f);
+  }
+  return q < -127 ? -127 : (q > 127 ? 127 : q);
+}
+
+// Four int8 codes of a, b, c, d packed into a word; their sum added to *sum.
+__device__ __forceinline__ uint32_t quant4s(float a, float b, float c, float d, float s, float rs,
+                                            int* sum) {
+  const int c0 = quant_code_fast(a, s, rs), c1 = quant_code_fast(b, s, rs),
+            c2 = quant_code_fast(c, s, rs), c3 = quant_code_fast(d, s, rs);
+  *sum += c0 + c1 + c2 + c3;
+  return (uint32_t)(c0 & 0xFF) | ((uint32_t)(c1 & 0xFF) << 8) | ((uint32_t)(c2 & 0xFF) << 16) |
+         ((uint32_t)c3 << 24);
+}
+
+// Unit u (128 consecutive values of one token row) -> (input, token, offset
+// of the unit in the input's [B][K] block). B <= 2: no division.
+__device__ __forceinline__ void unit_at(const STab& S, int B, int u, int& in, int& b, int& off) {
+  in = 0;
+  while (in + 1 < S.nin && u >= S.ufirst[in + 1]) ++in;
+  const int r = u - S.ufirst[in];
+  b = (B > 1 && r >= S.K[in] / 128) ? 1 : 0;
+  off = r * 128;  // = b * K + (unit within the row) * 128
+}
+
+// Consumer prologue: quantise every distinct input row of the CTA into xq.
+template <int B>
+__device__ void stream_prologue(STab& S, int8_t* xq, int warp, int lane) {
+  const int nunits = S.ufirst[S.nin];
+  float v[kRegUnits][4];
+  // pass 1: load (all loads first), per-unit absmax -> per-row max
+#pragma unroll
+  for (int k = 0; k < kRegUnits; ++k) {
+    const int u = warp + k * kCW;
+    if (u < nunits) {
+      int in, b, off;
+      unit_at(S, B, u, in, b, off);
+      const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
+      v[k][0] = t.x;
+      v[k][1] = t.y;
+      v[k][2] = t.z;
+      v[k][3] = t.w;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kRegUnits; ++k) {
+    const int u = warp + k * kCW;
+    if (u < nunits) {  // warp-uniform
+      int in, b, off;
+      unit_at(S, B, u, in, b, off);
+      float m = fmaxf(fmaxf(fabsf(v[k][0]), fabsf(v[k][1])), fmaxf(fabsf(v[k][2]), fabsf(v[k][3])));
+      m = warp_max(m);
+      if (lane == 0) atomicMax(&S.amax[in][b], __float_as_int(m));
+    }
+  }
+  for (int u0 = warp + kRegUnits * kCW; u0 < nunits; u0 += kCW) {  // units beyond the registers
+    int in, b, off;
+    unit_at(S, B, u0, in, b, off);
+    const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
+    float m = fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w)));
+    m = warp_max(m);
+    if (lane == 0) atomicMax(&S.amax[in][b], __float_as_int(m));
+  }
+  named_bar_sync(1, kCW * 32);
+  if (threadIdx.x < S.nin * B) {
+    const int in = threadIdx.x / B, b = threadIdx.x - in * B;
+    S.sx[in][b] = __fdiv_rn(__int_as_float(S.amax[in][b]), 127.0f);
+  }
+  named_bar_sync(1, kCW * 32);
+  // pass 2: codes into xq, code sums per row
+  auto quant_unit = [&](const float* w, int u) {
+    int in, b, off;
+    unit_at(S, B, u, in, b, off);
+    const float sc = S.sx[in][b];
+    const float rsc = __frcp_rn(sc);
+    int sum = 0;
+    *reinterpret_cast<uint32_t*>(xq + S.xoff[in] + off + lane * 4) =
+        quant4s(w[0], w[1], w[2], w[3], sc, rsc, &sum);
+    sum = warp_sum(sum);
+    if (lane == 0) atomicAdd(&S.qtot[in][b], sum);
+  };
+#pragma unroll
+  for (int k = 0; k < kRegUnits; ++k) {
+    const int u = warp + k * kCW;
+    if (u < nunits) quant_unit(v[k], u);
+  }
+  for (int u0 = warp + kRegUnits * kCW; u0 < nunits; u0 += kCW) {
+    int in, b, off;
+    unit_at(S, B, u0, in, b, off);
+    const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
+    const float w[4] = {t.x, t.y, t.z, t.w};
+    quant_unit(w, u0);
+  }
+  named_bar_sync(1, kCW * 32);
+}
+
+template <int B>
+__global__ void __launch_bounds__(kSThreads, kStreamCps)
+    gemv_stream_kernel(const __grid_constant__ GemvLaunch Lp) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ STab S;
+  const int NS = Lp.stages;
+  const SPlan P = splan(B, NS, Lp.xcap);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.bars);
+  uint64_t* empty = full + kMaxNS;
+  uint8_t* ring = smem + P.ring;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t_begin = Lp.cta_tile[blockIdx.x], t_end = Lp.cta_tile[blockIdx.x + 1];
+  if (t_begin >= t_end) return;  // (the host launches no empty CTA)
+
+  if (warp == kCW) {
+    // ---------------- producer: weights only, never waits for the previous
+    // grid; it reads the job table from the launch parameters so that its
+    // first copy goes out before the rest of the CTA has set up
+    if (lane == 0) {
+      for (int i = 0; i < NS; ++i) {
+        mbar_init(&full[i], 1);
+        mbar_init(&empty[i], kCW);
+      }
+      fence_mbar_init();
+      __threadfence_block();
+    }
+    __syncwarp();
+    named_bar_arrive(2, kSThreads);  // the consumers' first wait comes after this
+    pdl_launch_dependents();
+    const uint64_t pol = policy_evict_first();
+    int st = 0;
+    bool ok = true;
+    for (int t0 = t_begin; t0 < t_end && ok;) {
+      const int j = job_of(Lp, t0);
+      const GemvJob& J = Lp.jobs[j];
+      const int seg_end =
+          (j + 1 < Lp.njobs && Lp.jobs[j + 1].tile_begin < t_end) ? Lp.jobs[j + 1].tile_begin : t_end;
+      const int nt = seg_end - t0;
+      const int ng = (nt + kMaxT - 1) / kMaxT;
+      const int T0 = (nt + ng - 1) / ng;
+      const uint8_t* wbase = J.w;
+      const int tb = J.tile_begin;
+      const Geo G0 = geo(J.K, T0);
+      for (int tg = t0; tg < seg_end && ok; tg += T0) {
+        const int T = seg_end - tg < T0 ? seg_end - tg : T0;
+        const Geo G = T == T0 ? G0 : geo(J.K, T);
+        for (int s = 0; s < G.ns; ++s, ++st) {
+          const int slot = st % NS;
+          if (st >= NS && !mbar_wait(&empty[slot], ((st / NS) - 1) & 1, Lp.status)) {
+            ok = false;
+            break;
+          }
+          const int c0 = s * G.per;
+          const int c1 = c0 + G.per < G.C ? c0 + G.per : G.C;
+          const uint32_t nb = (uint32_t)(c1 - c0) * 512u;
+          if (lane == 0) {
+            uint8_t* dst = ring + (size_t)slot * kStage;
+            mbar_arrive_expect_tx(&full[slot], nb * (uint32_t)T);
+            const size_t tile0 = (size_t)(tg - tb);
+            for (int i = 0; i < T; ++i)
+              bulk_g2s_stream(dst + (size_t)i * nb, wbase + ((tile0 + i) * G.C + c0) * 512, nb,
+                              &full[slot], pol);
+          }
+          __syncwarp();
+        }
+      }
+      t0 = seg_end;
+    }
+    // every copy into this CTA's shared memory lands before the CTA exits
+    for (int i = (st > NS ? st - NS : 0); i < st; ++i) mbar_wait(&full[i % NS], (i / NS) & 1, Lp.status);
+    return;
+  }
+
+  // ---------------- consumers: job table into shared memory, distinct inputs
+  {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(&Lp);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(smem);
+    for (int i = threadIdx.x; i < (int)(sizeof(GemvLaunch) / 4); i += kCW * 32) dst[i] = src[i];
+  }
+  named_bar_sync(1, kCW * 32);
+  const GemvLaunch& L = *reinterpret_cast<const GemvLaunch*>(smem);
+  const int j_lo = job_of(L, t_begin);
+  if (threadIdx.x == 0) {
+    const int j_hi = job_of(L, t_end - 1);
+    int nin = 0, xo = 0, uo = 0;
+    for (int j = j_lo; j <= j_hi; ++j) {
+      const GemvJob& J = L.jobs[j];
+      int i = 0;
+      while (i < nin && !(S.x[i] == J.xf && S.K[i] == J.K)) ++i;
+      if (i == nin) {
+        S.x[i] = J.xf;
+        S.K[i] = J.K;
+        S.xoff[i] = xo;
+        S.ufirst[i] = uo;
+        for (int b = 0; b < 2; ++b) {
+          S.amax[i][b] = 0;
+          S.qtot[i][b] = 0;
+        }
+        xo += B * J.K;
+        uo += B * (J.K / 128);
+        ++nin;
+      }
+      S.in_of[j - j_lo] = i;
+    }
+    S.ufirst[nin] = uo;
+    S.nin = nin;
+  }
+  named_bar_sync(1, kCW * 32);
+  pdl_launch_dependents();
+
+  int8_t* xq = reinterpret_cast<int8_t*>(smem + P.xq);
+  int* red = reinterpret_cast<int*>(smem + P.red);
+  pdl_wait();
+  stream_prologue<B>(S, xq, warp, lane);
+  named_bar_sync(2, kSThreads);  // the producer has initialised the ring's barriers
+
+  int st = 0;
+  bool ok = true;
+  for (int t0 = t_begin; t0 < t_end;) {
+    const int j = job_of(L, t0);
+    const GemvJob& J = L.jobs[j];
+    const int in = S.in_of[j - j_lo];
+    const int8_t* xrow = xq + S.xoff[in];
+    const int K = J.K;
+    const int seg_end = (j + 1 < L.njobs && L.jobs[j + 1].tile_begin < t_end) ? L.jobs[j + 1].tile_begin : t_end;
+    const int nt = seg_end - t0;
+    const int ng = (nt + kMaxT - 1) / kMaxT;
+    const int T0 = (nt + ng - 1) / ng;
+    for (int tg = t0; tg < seg_end; tg += T0) {
+      const int T = seg_end - tg < T0 ? seg_end - tg : T0;
+      const Geo G = geo(K, T);
+      int A[kMaxT][B][4];
+#pragma unroll
+      for (int i = 0; i < kMaxT; ++i)
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+#pragma unroll
+          for (int m = 0; m < 4; ++m) A[i][b][m] = 0;
+      for (int s = 0; s < G.ns; ++s, ++st) {
+        const int slot = st % NS;
+        if (ok) ok = mbar_wait(&full[slot], (st / NS) & 1, L.status);
+        const int c0 = s * G.per;
+        const int nck = (c0 + G.per < G.C ? c0 + G.per : G.C) - c0;
+        const uint8_t* sb = ring + (size_t)slot * kStage + lane * 16;
+        // chunk k of stage st belongs to warp (k + st) % kCW: leftover chunks of
+        // short stages fall on different warps from stage to stage
+        for (int k = ((warp - st) % kCW + kCW) % kCW; k < nck; k += kCW) {
+          uint4 xv[B][4];
+#pragma unroll
+          for (int b = 0; b < B; ++b) {
+            const uint4* xp = reinterpret_cast<const uint4*>(xrow + (size_t)b * K + (size_t)(c0 + k) * 64);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) xv[b][q] = xp[q];
+          }
+          uint4 wv[kMaxT];
+#pragma unroll
+          for (int i = 0; i < kMaxT; ++i)
+            if (i < T) wv[i] = *reinterpret_cast<const uint4*>(sb + ((size_t)i * nck + k) * 512);
+#pragma unroll
+          for (int i = 0; i < kMaxT; ++i) {
+            if (i >= T) break;
+            const uint32_t wl[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+              const uint32_t xw[4][4] = {{xv[b][0].x, xv[b][0].y, xv[b][0].z, xv[b][0].w},
+                                         {xv[b][1].x, xv[b][1].y, xv[b][1].z, xv[b][1].w},
+                                         {xv[b][2].x, xv[b][2].y, xv[b][2].z, xv[b][2].w},
+                                         {xv[b][3].x, xv[b][3].y, xv[b][3].z, xv[b][3].w}};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                A[i][b][0] = dp4a_us(wl[q] & 0x03030303u, xw[q][0], A[i][b][0]);
+                A[i][b][1] = dp4a_us(wl[q] & 0x0C0C0C0Cu, xw[q][1], A[i][b][1]);
+                A[i][b][2] = dp4a_us(wl[q] & 0x30303030u, xw[q][2], A[i][b][2]);
+                A[i][b][3] = dp4a_us(wl[q] & 0xC0C0C0C0u, xw[q][3], A[i][b][3]);
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+      }
+      // cross-warp reduction of the tile group: exact per-warp partials
+#pragma unroll
+      for (int i = 0; i < kMaxT; ++i)
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+          if (i < T)
+            red[((warp * kMaxT + i) * B + b) * 32 + lane] =
+                A[i][b][0] + (A[i][b][1] >> 2) + (A[i][b][2] >> 4) + (A[i][b][3] >> 6);
+      named_bar_sync(1, kCW * 32);
+      for (int p = warp; p < T * B; p += kCW) {
+        const int i = p / B, b = p - (p / B) * B;
+        int acc = -S.qtot[in][b];
+#pragma unroll
+        for (int w = 0; w < kCW; ++w) acc += red[((w * kMaxT + i) * B + b) * 32 + lane];
+        const int row = (tg + i - J.tile_begin) * kRows + lane;
+        if (row < J.M) {
+          J.y[(size_t)b * J.ldy + row] = __fmul_rn(__fmul_rn(__int2float_rn(acc), J.w_scale), S.sx[in][b]);
+          if (J.acc) J.acc[(size_t)b * J.M + row] = acc;
+        }
+      }
+      named_bar_sync(1, kCW * 32);
+    }
+    t0 = seg_end;
+  }
+}
+
+// Shared memory one CTA may use so that kStreamCps of them fit on an SM.
+int stream_smem_budget() {
+  static int budget[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (dev < 64 && budget[dev]) return budget[dev];
+  int per_sm = 0, reserved = 0, optin = 0;
+  if (cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+    return 0;
+  cudaFuncAttributes fa, fb;
+  if (cudaFuncGetAttributes(&fa, gemv_stream_kernel<1>) != cudaSuccess ||
+      cudaFuncGetAttributes(&fb, gemv_stream_kernel<2>) != cudaSuccess)
+    return 0;
+  const int st = (int)(fa.sharedSizeBytes > fb.sharedSizeBytes ? fa.sharedSizeBytes : fb.sharedSizeBytes);
+  int b = per_sm / kStreamCps - reserved - st;
+  if (b > optin - st) b = optin - st;
+  if (dev < 64) budget[dev] = b;
+  return b;
+}
+
+template <int B>
+cudaError_t launch_stream_t(const GemvLaunch& L, int grid, size_t smem, cudaStream_t s, bool pdl) {
+  static int done[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 64 || !done[dev]) {
+    e = cudaFuncSetAttribute(gemv_stream_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             stream_smem_budget());
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(gemv_stream_kernel<B>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             100);
+    if (e != cudaSuccess) return e;
+    if (dev < 64) done[dev] = 1;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kSThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<B>, L);
+}
+
+}  // namespace
+
+bool gemv_stream_prepare(GemvLaunch& L, int num_sms, int* grid_out, size_t* smem_out) {
+  *grid_out = 0;
+  *smem_out = 0;
+  if (L.fmt != kTern2 || !L.fused || L.norm.w || L.B < 1 || L.B > 2) return false;
+  int tiles = 0;
+  for (int j = 0; j < L.njobs; ++j) {
+    const GemvJob& J = L.jobs[j];
+    if (J.had_block || J.K % 128 || J.K <= 0) return false;
+    L.jobs[j].tile_begin = tiles;
+    tiles += (J.M + kRows - 1) / kRows;
+  }
+  L.ntiles = tiles;
+  if (tiles <= 0) return true;
+  if (tiles > 65535) return false;
+  int grid = tiles < num_sms ? tiles : num_sms;
+  if (grid > kMaxGemvCtas) grid = kMaxGemvCtas;
+  balance_tiles(L, grid, 64);
+  // no empty CTA: the split fills CTAs from the first one on
+  while (grid > 1 && L.cta_tile[grid - 1] >= L.cta_tile[grid]) --grid;
+  // int8 codes one CTA keeps: the distinct inputs of the jobs its tiles touch
+  int xcap = 0;
+  for (int c = 0; c < grid; ++c) {
+    int jlo = 0, jhi = 0;
+    while (jlo + 1 < L.njobs && L.cta_tile[c] >= L.jobs[jlo + 1].tile_begin) ++jlo;
+    while (jhi + 1 < L.njobs && L.cta_tile[c + 1] - 1 >= L.jobs[jhi + 1].tile_begin) ++jhi;
+    int x = 0;
+    for (int j = jlo; j <= jhi; ++j) {
+      bool seen = false;
+      for (int i = jlo; i < j; ++i) seen |= L.jobs[i].xf == L.jobs[j].xf && L.jobs[i].K == L.jobs[j].K;
+      if (!seen) x += L.B * L.jobs[j].K;
+    }
+    xcap = x > xcap ? x : xcap;
+  }
+  L.xcap = xcap;
+  const int budget = stream_smem_budget();
+  if (budget <= 0) return false;
+  int ns = kMaxNS;
+  while (ns > 2 && (int)splan(L.B, ns, xcap).total > budget) --ns;
+  if ((int)splan(L.B, ns, xcap).total > budget) return false;
+  L.stages = ns;
+  *grid_out = grid;
+  *smem_out = splan(L.B, ns, xcap).total;
+  return true;
+}
+
+cudaError_t launch_gemv_stream(GemvLaunch& L, int grid, size_t smem, cudaStream_t s, bool pdl) {
+  if (grid == 0) return cudaSuccess;
+  if (L.B == 1) return launch_stream_t<1>(L, grid, smem, s, pdl);
+  if (L.B == 2) return launch_stream_t<2>(L, grid, smem, s, pdl);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace ouroq

@@ -124,6 +124,14 @@ cudaError_t launch_rotate(const float* x, float* out, const float* signs, int B,
 // false when the activations of one CTA's jobs cannot be kept in shared memory.
 bool gemv_prepare(GemvLaunch& L, int num_sms, int smem_optin, int* grid, size_t* smem);
 cudaError_t launch_gemv(GemvLaunch& L, int num_sms, int smem_optin, cudaStream_t s, bool pdl);
+// Contiguous tile ranges per CTA (L.cta_tile[0..grid]) that minimise the
+// heaviest CTA's weight bytes; needs L.ntiles and the jobs' tile_begin.
+void balance_tiles(GemvLaunch& L, int grid, int per_chunk);
+// The streaming decode GEMV (gemv_stream.cu): fused ternary launches of one or
+// two tokens without rotation or norm. prepare returns false when the launch
+// is not of that kind (the caller then uses launch_gemv).
+bool gemv_stream_prepare(GemvLaunch& L, int num_sms, int* grid, size_t* smem);
+cudaError_t launch_gemv_stream(GemvLaunch& L, int grid, size_t smem, cudaStream_t s, bool pdl);
 size_t tiled_weight_bytes(int fmt, int M, int K);
 size_t tiled_scale_bytes(int M, int K);
 cudaError_t launch_repack(int fmt, const uint8_t* canon, uint8_t* dev, int M, int K, cudaStream_t s);
