@@ -181,7 +181,7 @@ ouroq_status ouroq_gemm_f32act(ouroq_ctx *ctx, const ouroq_weight *w, const floa
 /* ouroq_gemm_f32act for callers that must not allocate device memory while
  * they run. This entry point has no counterpart in the reference.
  *
- * Who needs it: ouroq_gemm_f32act quantises batches it cannot fuse (B > 8)
+ * Who needs it: ouroq_gemm_f32act quantises batches it cannot fuse (B > 2)
  * into a context-owned buffer, and grows that buffer with cudaMalloc, freeing
  * the old one, the first time a larger batch arrives. A serving loop that
  * reserved the GPU's memory up front for weights and caches cannot take that
@@ -189,8 +189,12 @@ ouroq_status ouroq_gemm_f32act(ouroq_ctx *ctx, const ouroq_weight *w, const floa
  * waits for the whole device). This variant allocates nothing: it uses a
  * fixed scratch area compiled into the library, one per device.
  *
- * Limits: B <= 4096 and B * K <= 4 MiB (4194304); larger batches return
- * OUROQ_ERR_BAD_SHAPE with nothing launched; split them into calls that fit.
+ * Limits (TERNARY2 / SIGN1G128): B <= 4096 and B * K <= 4 MiB (4194304);
+ * larger batches return OUROQ_ERR_BAD_SHAPE with nothing launched; split them
+ * into calls that fit. The reference formats (PTQ1_0, TQ1_0, F16, BF16) are
+ * not quantised and take any batch, but PTQ1_0 / TQ1_0 with a rotation
+ * (hadamard_block != 0) return OUROQ_ERR_UNSUPPORTED: rotate the activations
+ * first (ouroq_rotate), then call this.
  * The first call on a device does one-time set-up (loads this library's
  * kernels on that device and looks up the scratch address); make it before
  * any stream capture. All calls on one device share the one scratch area,

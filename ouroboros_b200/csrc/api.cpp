@@ -1080,25 +1080,27 @@ ouroq_status ouroq_gemm_f32act_noalloc(ouroq_ctx* ctx, const ouroq_weight* w, co
   ouroq_status st = check_quant_args(ctx, B, w->K, hadamard_block);
   if (st != OUROQ_OK) return st;
   if (!aligned16(x)) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "x not 16-byte aligned");
-  if (B > kNoAllocMaxTokens || (size_t)B * w->K > kNoAllocQBytes)
-    return fail(ctx, OUROQ_ERR_BAD_SHAPE,
-                "B=%d, K=%d: the fixed scratch holds at most %d tokens and B*K <= %zu "
-                "(split the batch, or use ouroq_gemm_f32act)",
-                B, w->K, kNoAllocMaxTokens, kNoAllocQBytes);
   DeviceGuard g(ctx->device);
   if (is_ref_format(w->fmt)) {
-    // no quantisation, so no scratch; the rotation would need a buffer
+    // no quantisation, so no scratch and no batch limit; the rotation would
+    // need a buffer
     if (hadamard_block)
       return fail(ctx, OUROQ_ERR_UNSUPPORTED,
                   "PTQ1_0 / TQ1_0 with a rotation needs scratch: rotate first, or use ouroq_gemm_f32act");
     return ref_matvec(ctx, w, x, B, y, static_cast<cudaStream_t>(stream), B > 1);
   }
+  if (B > kNoAllocMaxTokens || (size_t)B * w->K > kNoAllocQBytes)
+    return fail(ctx, OUROQ_ERR_BAD_SHAPE,
+                "B=%d, K=%d: the fixed scratch holds at most %d tokens and B*K <= %zu "
+                "(split the batch, or use ouroq_gemm_f32act)",
+                B, w->K, kNoAllocMaxTokens, kNoAllocQBytes);
   uint8_t* scratch = nullptr;
   st = noalloc_scratch(ctx, &scratch);
   if (st != OUROQ_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (B <= kGemvMaxB && (hadamard_block == 0 || (hadamard_block >= 32 && hadamard_block <= 128))) {
-    // one launch, no scratch: rotate + quantise in the GEMV prologue
+  if (B <= kFusedMaxB && (hadamard_block == 0 || (hadamard_block >= 32 && hadamard_block <= 128))) {
+    // one launch, no scratch: rotate + quantise in the GEMV prologue (the
+    // batches ouroq_gemm_f32act fuses; larger ones quantise once, below)
     GemvLaunch L{};
     L.njobs = 1;
     L.B = B;
