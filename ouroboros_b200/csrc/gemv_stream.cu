@@ -18,8 +18,8 @@
 //    the previous kernel; only the activations do, and only the consumers
 //    wait for it (griddepcontrol.wait), so the copies overlap the previous
 //    launch's tail and this launch's prologue. Built for one CTA per SM
-//    (kStreamCps = 1) a CTA's whole share (up to 13 x 16 KB) is in flight at
-//    once; built for two (<= 112 registers, <= 113 KB of shared memory each)
+//    (kStreamCps = 1) a CTA's whole share (up to 6 x 32 KB) is in flight at
+//    once; built for two (<= 56 registers, <= 113 KB of shared memory each)
 //    the next launch's CTA can sit beside this one and stream while it
 //    computes.
 //  * Chunk-major stages. A stage is a K-slice of up to four 32-row tiles of
@@ -28,7 +28,9 @@
 //    of the stage, loads the int8 activations of that chunk into registers
 //    once and applies them to the same chunk of every tile of the stage: one
 //    shared-memory load and 16 mask + 16 dp4a per tile and lane, with 4 x T
-//    independent accumulator chains per lane.
+//    independent accumulator chains per lane (measured on resident weights:
+//    about 45 packed bytes per clock per SM; mma.sync m16n8k32 u8 x s8 with
+//    the same masking reached 31).
 //  * A short prologue: the activations of the CTA's matrices are loaded with
 //    every load issued before any use, each distinct input row once (gate
 //    and up share theirs), reduced and quantised in registers, with the
@@ -46,18 +48,21 @@
 namespace ouroq {
 namespace {
 
-constexpr int kRows = kTileRows;
-constexpr int kCW = 8;                      // consumer warps
-constexpr int kSThreads = (kCW + 1) * 32;   // + one producer warp
-constexpr int kMaxT = 4;                    // tiles per stage
-constexpr uint32_t kStage = 16u * 1024u;    // bytes per ring slot
-constexpr int kMaxNS = 13;                  // ring depth limit
-constexpr int kMaxIn = kMaxGemvJobs;        // distinct inputs of one CTA
-constexpr int kRegUnits = 10;               // 128-value units a warp keeps in registers
 #ifndef OUROQ_STREAM_CPS
 #define OUROQ_STREAM_CPS 1
 #endif
 constexpr int kStreamCps = OUROQ_STREAM_CPS;  // CTAs per SM the kernel is built for
+constexpr int kRows = kTileRows;
+// consumer warps: 15 (16 with the producer, 128 registers) for one CTA per
+// SM; 8 (112 registers) when two must fit
+constexpr int kCW = kStreamCps == 1 ? 15 : 8;
+constexpr int kSThreads = (kCW + 1) * 32;   // + one producer warp
+constexpr int kMaxT = 4;                    // tiles per stage
+constexpr uint32_t kStage = (kStreamCps == 1 ? 32u : 16u) * 1024u;  // bytes per ring slot
+constexpr int kMaxNS = 6;                   // ring depth limit
+constexpr int kMaxIn = kMaxGemvJobs;        // distinct inputs of one CTA
+constexpr int kRegUnits = kStreamCps == 1 ? 5 : 10;  // 128-value units a warp keeps in registers
+constexpr int kMaxGroups = 16;              // tile groups of one CTA whose partials can wait
 
 __host__ __device__ constexpr uint32_t al128(uint32_t v) { return (v + 127u) & ~127u; }
 
@@ -65,11 +70,13 @@ __host__ __device__ constexpr uint32_t al128(uint32_t v) { return (v + 127u) & ~
 struct SPlan {
   uint32_t bars, red, xq, ring, total;
 };
-__host__ __device__ inline SPlan splan(int B, int ns, int xcap) {
+// `groups`: tile groups whose partial sums are kept until the CTA's end (0:
+// one buffer, reduced after every group).
+__host__ __device__ inline SPlan splan(int B, int ns, int xcap, int groups) {
   SPlan p;
   p.bars = al128(sizeof(GemvLaunch));
-  p.red = p.bars + 256;  // full[13] + empty[13] mbarriers
-  p.xq = p.red + al128((uint32_t)kCW * kMaxT * B * 32 * 4);
+  p.red = p.bars + 128;  // full[6] + empty[6] mbarriers
+  p.xq = p.red + al128((uint32_t)(groups > 0 ? groups : 1) * kCW * kMaxT * B * 32 * 4);
   p.ring = p.xq + al128((uint32_t)xcap);
   p.total = p.ring + (uint32_t)ns * kStage;
   return p;
@@ -157,17 +164,24 @@ __device__ __forceinline__ void unit_at(const STab& S, int B, int u, int& in, in
 }
 
 // Consumer prologue: quantise every distinct input row of the CTA into xq.
+// A warp takes units u = warp, warp + kCW, ...; consecutive units of a warp
+// almost always belong to one row, so a lane keeps a running max (then sum)
+// per row and the warp reduces once per row it leaves, not once per unit.
 template <int B>
 __device__ void stream_prologue(STab& S, int8_t* xq, int warp, int lane) {
   const int nunits = S.ufirst[S.nin];
   float v[kRegUnits][4];
-  // pass 1: load (all loads first), per-unit absmax -> per-row max
+  int seg[kRegUnits], uoff[kRegUnits];  // row (input * 2 + token) and offset of each unit
+  // pass 1: every load issued before any use
 #pragma unroll
   for (int k = 0; k < kRegUnits; ++k) {
     const int u = warp + k * kCW;
+    seg[k] = -1;
     if (u < nunits) {
       int in, b, off;
       unit_at(S, B, u, in, b, off);
+      seg[k] = in * 2 + b;
+      uoff[k] = off;
       const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
       v[k][0] = t.x;
       v[k][1] = t.y;
@@ -175,56 +189,151 @@ __device__ void stream_prologue(STab& S, int8_t* xq, int warp, int lane) {
       v[k][3] = t.w;
     }
   }
+  int cur = -1;
+  float m = 0.0f;
+  auto flush_max = [&]() {
+    if (cur >= 0) {
+      const float t = warp_max(m);
+      if (lane == 0) atomicMax(&S.amax[cur >> 1][cur & 1], __float_as_int(t));
+    }
+    m = 0.0f;
+  };
+  auto absmax4 = [](float a, float b, float c, float d) {
+    return fmaxf(fmaxf(fabsf(a), fabsf(b)), fmaxf(fabsf(c), fabsf(d)));
+  };
 #pragma unroll
   for (int k = 0; k < kRegUnits; ++k) {
-    const int u = warp + k * kCW;
-    if (u < nunits) {  // warp-uniform
-      int in, b, off;
-      unit_at(S, B, u, in, b, off);
-      float m = fmaxf(fmaxf(fabsf(v[k][0]), fabsf(v[k][1])), fmaxf(fabsf(v[k][2]), fabsf(v[k][3])));
-      m = warp_max(m);
-      if (lane == 0) atomicMax(&S.amax[in][b], __float_as_int(m));
+    if (seg[k] < 0) continue;  // warp-uniform
+    if (seg[k] != cur) {
+      flush_max();
+      cur = seg[k];
     }
+    m = fmaxf(m, absmax4(v[k][0], v[k][1], v[k][2], v[k][3]));
   }
   for (int u0 = warp + kRegUnits * kCW; u0 < nunits; u0 += kCW) {  // units beyond the registers
     int in, b, off;
     unit_at(S, B, u0, in, b, off);
     const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
-    float m = fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w)));
-    m = warp_max(m);
-    if (lane == 0) atomicMax(&S.amax[in][b], __float_as_int(m));
+    if (in * 2 + b != cur) {
+      flush_max();
+      cur = in * 2 + b;
+    }
+    m = fmaxf(m, absmax4(t.x, t.y, t.z, t.w));
   }
+  flush_max();
   named_bar_sync(1, kCW * 32);
+  // every thread derives the scales it needs from the maxima; threads 0..
+  // also publish them for the epilogue
   if (threadIdx.x < S.nin * B) {
     const int in = threadIdx.x / B, b = threadIdx.x - in * B;
     S.sx[in][b] = __fdiv_rn(__int_as_float(S.amax[in][b]), 127.0f);
   }
-  named_bar_sync(1, kCW * 32);
-  // pass 2: codes into xq, code sums per row
-  auto quant_unit = [&](const float* w, int u) {
-    int in, b, off;
-    unit_at(S, B, u, in, b, off);
-    const float sc = S.sx[in][b];
-    const float rsc = __frcp_rn(sc);
-    int sum = 0;
-    *reinterpret_cast<uint32_t*>(xq + S.xoff[in] + off + lane * 4) =
+  // pass 2: codes into xq, code sums per row (integer: the order is free)
+  cur = -1;
+  int sum = 0;
+  float sc = 0.0f, rsc = 0.0f;
+  auto flush_sum = [&]() {
+    if (cur >= 0) {
+      const int t = warp_sum(sum);
+      if (lane == 0) atomicAdd(&S.qtot[cur >> 1][cur & 1], t);
+    }
+    sum = 0;
+  };
+  auto quant_unit = [&](const float* w, int sg, int off) {
+    if (sg != cur) {
+      flush_sum();
+      cur = sg;
+      sc = __fdiv_rn(__int_as_float(S.amax[sg >> 1][sg & 1]), 127.0f);
+      rsc = __frcp_rn(sc);
+    }
+    *reinterpret_cast<uint32_t*>(xq + S.xoff[sg >> 1] + off + lane * 4) =
         quant4s(w[0], w[1], w[2], w[3], sc, rsc, &sum);
-    sum = warp_sum(sum);
-    if (lane == 0) atomicAdd(&S.qtot[in][b], sum);
   };
 #pragma unroll
-  for (int k = 0; k < kRegUnits; ++k) {
-    const int u = warp + k * kCW;
-    if (u < nunits) quant_unit(v[k], u);
-  }
+  for (int k = 0; k < kRegUnits; ++k)
+    if (seg[k] >= 0) quant_unit(v[k], seg[k], uoff[k]);
   for (int u0 = warp + kRegUnits * kCW; u0 < nunits; u0 += kCW) {
     int in, b, off;
     unit_at(S, B, u0, in, b, off);
     const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
     const float w[4] = {t.x, t.y, t.z, t.w};
-    quant_unit(w, u0);
+    quant_unit(w, in * 2 + b, off);
   }
+  flush_sum();
   named_bar_sync(1, kCW * 32);
+}
+
+// The consumer side of one tile group: T tiles (TC = T known at compile
+// time, or 0: T <= kMaxT at run time) of one matrix through its G.ns stages;
+// each warp's exact partial sums end in red[warp][tile][token][lane].
+template <int B, int TC>
+__device__ __forceinline__ void consume_group(int T_rt, const Geo& G, const int8_t* xrow, int K,
+                                              const uint8_t* ring, uint64_t* full, uint64_t* empty,
+                                              int NS, int& st, int& cslot, int& cphase, bool& ok,
+                                              unsigned* status, int* red, int warp, int lane) {
+  const int T = TC ? TC : T_rt;
+  int A[kMaxT][B][4];
+#pragma unroll
+  for (int i = 0; i < kMaxT; ++i)
+#pragma unroll
+    for (int b = 0; b < B; ++b)
+#pragma unroll
+      for (int m = 0; m < 4; ++m) A[i][b][m] = 0;
+  for (int s = 0; s < G.ns; ++s, ++st) {
+    const int slot = cslot;
+    if (ok) ok = mbar_wait(&full[slot], cphase, status);
+    if (++cslot == NS) {
+      cslot = 0;
+      cphase ^= 1;
+    }
+    const int c0 = s * G.per;
+    const int nck = (c0 + G.per < G.C ? c0 + G.per : G.C) - c0;
+    const uint8_t* sb = ring + (size_t)slot * kStage + lane * 16;
+    // chunk k of stage st belongs to warp (k + st) % kCW: leftover chunks of
+    // short stages fall on different warps from stage to stage
+    for (int k = ((warp - st) % kCW + kCW) % kCW; k < nck; k += kCW) {
+      uint4 xv[B][4];
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const uint4* xp = reinterpret_cast<const uint4*>(xrow + (size_t)b * K + (size_t)(c0 + k) * 64);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) xv[b][q] = xp[q];
+      }
+      uint4 wv[kMaxT];
+#pragma unroll
+      for (int i = 0; i < kMaxT; ++i)
+        if (i < T) wv[i] = *reinterpret_cast<const uint4*>(sb + ((size_t)i * nck + k) * 512);
+#pragma unroll
+      for (int i = 0; i < kMaxT; ++i) {
+        if (i >= T) break;
+        const uint32_t wl[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          const uint32_t xw[4][4] = {{xv[b][0].x, xv[b][0].y, xv[b][0].z, xv[b][0].w},
+                                     {xv[b][1].x, xv[b][1].y, xv[b][1].z, xv[b][1].w},
+                                     {xv[b][2].x, xv[b][2].y, xv[b][2].z, xv[b][2].w},
+                                     {xv[b][3].x, xv[b][3].y, xv[b][3].z, xv[b][3].w}};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            A[i][b][0] = dp4a_us(wl[q] & 0x03030303u, xw[q][0], A[i][b][0]);
+            A[i][b][1] = dp4a_us(wl[q] & 0x0C0C0C0Cu, xw[q][1], A[i][b][1]);
+            A[i][b][2] = dp4a_us(wl[q] & 0x30303030u, xw[q][2], A[i][b][2]);
+            A[i][b][3] = dp4a_us(wl[q] & 0xC0C0C0C0u, xw[q][3], A[i][b][3]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+  // exact shift-back of the four masked accumulators
+#pragma unroll
+  for (int i = 0; i < kMaxT; ++i)
+#pragma unroll
+    for (int b = 0; b < B; ++b)
+      if (i < T)
+        red[((warp * kMaxT + i) * B + b) * 32 + lane] =
+            A[i][b][0] + (A[i][b][1] >> 2) + (A[i][b][2] >> 4) + (A[i][b][3] >> 6);
 }
 
 template <int B>
@@ -232,38 +341,53 @@ __global__ void __launch_bounds__(kSThreads, kStreamCps)
     gemv_stream_kernel(const __grid_constant__ GemvLaunch Lp) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ STab S;
+  __shared__ int grp_job[kMaxGroups], grp_t0[kMaxGroups], grp_T[kMaxGroups];
   const int NS = Lp.stages;
-  const SPlan P = splan(B, NS, Lp.xcap);
+  const SPlan P = splan(B, NS, Lp.xcap, Lp.defer);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.bars);
   uint64_t* empty = full + kMaxNS;
   uint8_t* ring = smem + P.ring;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t_begin = Lp.cta_tile[blockIdx.x], t_end = Lp.cta_tile[blockIdx.x + 1];
-  if (t_begin >= t_end) return;  // (the host launches no empty CTA)
+  const GemvLaunch& L = *reinterpret_cast<const GemvLaunch*>(smem);
 
   if (warp == kCW) {
     // ---------------- producer: weights only, never waits for the previous
-    // grid; it reads the job table from the launch parameters so that its
-    // first copy goes out before the rest of the CTA has set up
+    // grid. Its 32 lanes copy the launch parameters into shared memory with
+    // independent loads (one round trip, instead of the dependent chain of
+    // parameter reads a walk over the job table would be), then it issues
+    // the copies of every stage the ring can hold.
+    {
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(&Lp);
+      uint32_t* dst = reinterpret_cast<uint32_t*>(smem);
+      constexpr int kWords = (int)(sizeof(GemvLaunch) / 4);
+      uint32_t v[(kWords + 31) / 32];
+#pragma unroll
+      for (int r = 0; r < (kWords + 31) / 32; ++r)
+        if (r * 32 + lane < kWords) v[r] = src[r * 32 + lane];
+#pragma unroll
+      for (int r = 0; r < (kWords + 31) / 32; ++r)
+        if (r * 32 + lane < kWords) dst[r * 32 + lane] = v[r];
+    }
     if (lane == 0) {
       for (int i = 0; i < NS; ++i) {
         mbar_init(&full[i], 1);
         mbar_init(&empty[i], kCW);
       }
       fence_mbar_init();
-      __threadfence_block();
     }
+    __threadfence_block();
     __syncwarp();
-    named_bar_arrive(2, kSThreads);  // the consumers' first wait comes after this
+    named_bar_arrive(2, kSThreads);  // job table and ring barriers ready for the consumers
     pdl_launch_dependents();
+    const int t_begin = L.cta_tile[blockIdx.x], t_end = L.cta_tile[blockIdx.x + 1];
     const uint64_t pol = policy_evict_first();
-    int st = 0;
+    int st = 0, pslot = 0, pphase = 0;  // stage count, ring slot, slot wrap parity
     bool ok = true;
     for (int t0 = t_begin; t0 < t_end && ok;) {
-      const int j = job_of(Lp, t0);
-      const GemvJob& J = Lp.jobs[j];
+      const int j = job_of(L, t0);
+      const GemvJob& J = L.jobs[j];
       const int seg_end =
-          (j + 1 < Lp.njobs && Lp.jobs[j + 1].tile_begin < t_end) ? Lp.jobs[j + 1].tile_begin : t_end;
+          (j + 1 < L.njobs && L.jobs[j + 1].tile_begin < t_end) ? L.jobs[j + 1].tile_begin : t_end;
       const int nt = seg_end - t0;
       const int ng = (nt + kMaxT - 1) / kMaxT;
       const int T0 = (nt + ng - 1) / ng;
@@ -274,10 +398,14 @@ __global__ void __launch_bounds__(kSThreads, kStreamCps)
         const int T = seg_end - tg < T0 ? seg_end - tg : T0;
         const Geo G = T == T0 ? G0 : geo(J.K, T);
         for (int s = 0; s < G.ns; ++s, ++st) {
-          const int slot = st % NS;
-          if (st >= NS && !mbar_wait(&empty[slot], ((st / NS) - 1) & 1, Lp.status)) {
+          const int slot = pslot;
+          if (st >= NS && !mbar_wait(&empty[slot], pphase ^ 1, L.status)) {
             ok = false;
             break;
+          }
+          if (++pslot == NS) {
+            pslot = 0;
+            pphase ^= 1;
           }
           const int c0 = s * G.per;
           const int c1 = c0 + G.per < G.C ? c0 + G.per : G.C;
@@ -296,18 +424,13 @@ __global__ void __launch_bounds__(kSThreads, kStreamCps)
       t0 = seg_end;
     }
     // every copy into this CTA's shared memory lands before the CTA exits
-    for (int i = (st > NS ? st - NS : 0); i < st; ++i) mbar_wait(&full[i % NS], (i / NS) & 1, Lp.status);
+    for (int i = (st > NS ? st - NS : 0); i < st; ++i) mbar_wait(&full[i % NS], (i / NS) & 1, L.status);
     return;
   }
 
-  // ---------------- consumers: job table into shared memory, distinct inputs
-  {
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(&Lp);
-    uint32_t* dst = reinterpret_cast<uint32_t*>(smem);
-    for (int i = threadIdx.x; i < (int)(sizeof(GemvLaunch) / 4); i += kCW * 32) dst[i] = src[i];
-  }
-  named_bar_sync(1, kCW * 32);
-  const GemvLaunch& L = *reinterpret_cast<const GemvLaunch*>(smem);
+  // ---------------- consumers: distinct inputs and tile groups of the CTA
+  named_bar_sync(2, kSThreads);  // the producer has copied the job table and set up the ring
+  const int t_begin = L.cta_tile[blockIdx.x], t_end = L.cta_tile[blockIdx.x + 1];
   const int j_lo = job_of(L, t_begin);
   if (threadIdx.x == 0) {
     const int j_hi = job_of(L, t_end - 1);
@@ -341,10 +464,31 @@ __global__ void __launch_bounds__(kSThreads, kStreamCps)
   int* red = reinterpret_cast<int*>(smem + P.red);
   pdl_wait();
   stream_prologue<B>(S, xq, warp, lane);
-  named_bar_sync(2, kSThreads);  // the producer has initialised the ring's barriers
 
-  int st = 0;
+  // tile groups; with L.defer the partial sums of all of them stay in shared
+  // memory and are reduced after the last one (one CTA barrier), otherwise
+  // each group is reduced (two barriers) before the next reuses the buffer
+  const bool defer = L.defer != 0;
+  const int gstride = kCW * kMaxT * B * 32;  // ints of one group's partials
+  auto reduce_group = [&](int g, const int* rg) {
+    const int j = grp_job[g], tg = grp_t0[g], T = grp_T[g];
+    const GemvJob& J = L.jobs[j];
+    const int in = S.in_of[j - j_lo];
+    for (int p = warp; p < T * B; p += kCW) {
+      const int i = p / B, b = p - (p / B) * B;
+      int acc = -S.qtot[in][b];
+#pragma unroll
+      for (int w = 0; w < kCW; ++w) acc += rg[((w * kMaxT + i) * B + b) * 32 + lane];
+      const int row = (tg + i - J.tile_begin) * kRows + lane;
+      if (row < J.M) {
+        J.y[(size_t)b * J.ldy + row] = __fmul_rn(__fmul_rn(__int2float_rn(acc), J.w_scale), S.sx[in][b]);
+        if (J.acc) J.acc[(size_t)b * J.M + row] = acc;
+      }
+    }
+  };
+  int st = 0, cslot = 0, cphase = 0;  // stage count, ring slot, slot wrap parity
   bool ok = true;
+  int ngrp = 0;
   for (int t0 = t_begin; t0 < t_end;) {
     const int j = job_of(L, t0);
     const GemvJob& J = L.jobs[j];
@@ -355,82 +499,33 @@ __global__ void __launch_bounds__(kSThreads, kStreamCps)
     const int nt = seg_end - t0;
     const int ng = (nt + kMaxT - 1) / kMaxT;
     const int T0 = (nt + ng - 1) / ng;
-    for (int tg = t0; tg < seg_end; tg += T0) {
+    for (int tg = t0; tg < seg_end; tg += T0, ++ngrp) {
       const int T = seg_end - tg < T0 ? seg_end - tg : T0;
       const Geo G = geo(K, T);
-      int A[kMaxT][B][4];
-#pragma unroll
-      for (int i = 0; i < kMaxT; ++i)
-#pragma unroll
-        for (int b = 0; b < B; ++b)
-#pragma unroll
-          for (int m = 0; m < 4; ++m) A[i][b][m] = 0;
-      for (int s = 0; s < G.ns; ++s, ++st) {
-        const int slot = st % NS;
-        if (ok) ok = mbar_wait(&full[slot], (st / NS) & 1, L.status);
-        const int c0 = s * G.per;
-        const int nck = (c0 + G.per < G.C ? c0 + G.per : G.C) - c0;
-        const uint8_t* sb = ring + (size_t)slot * kStage + lane * 16;
-        // chunk k of stage st belongs to warp (k + st) % kCW: leftover chunks of
-        // short stages fall on different warps from stage to stage
-        for (int k = ((warp - st) % kCW + kCW) % kCW; k < nck; k += kCW) {
-          uint4 xv[B][4];
-#pragma unroll
-          for (int b = 0; b < B; ++b) {
-            const uint4* xp = reinterpret_cast<const uint4*>(xrow + (size_t)b * K + (size_t)(c0 + k) * 64);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) xv[b][q] = xp[q];
-          }
-          uint4 wv[kMaxT];
-#pragma unroll
-          for (int i = 0; i < kMaxT; ++i)
-            if (i < T) wv[i] = *reinterpret_cast<const uint4*>(sb + ((size_t)i * nck + k) * 512);
-#pragma unroll
-          for (int i = 0; i < kMaxT; ++i) {
-            if (i >= T) break;
-            const uint32_t wl[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
-#pragma unroll
-            for (int b = 0; b < B; ++b) {
-              const uint32_t xw[4][4] = {{xv[b][0].x, xv[b][0].y, xv[b][0].z, xv[b][0].w},
-                                         {xv[b][1].x, xv[b][1].y, xv[b][1].z, xv[b][1].w},
-                                         {xv[b][2].x, xv[b][2].y, xv[b][2].z, xv[b][2].w},
-                                         {xv[b][3].x, xv[b][3].y, xv[b][3].z, xv[b][3].w}};
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                A[i][b][0] = dp4a_us(wl[q] & 0x03030303u, xw[q][0], A[i][b][0]);
-                A[i][b][1] = dp4a_us(wl[q] & 0x0C0C0C0Cu, xw[q][1], A[i][b][1]);
-                A[i][b][2] = dp4a_us(wl[q] & 0x30303030u, xw[q][2], A[i][b][2]);
-                A[i][b][3] = dp4a_us(wl[q] & 0xC0C0C0C0u, xw[q][3], A[i][b][3]);
-              }
-            }
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
+      const int g = defer ? ngrp : 0;
+      int* rg = red + (size_t)g * gstride;
+      if (threadIdx.x == 0) {
+        grp_job[g] = j;
+        grp_t0[g] = tg;
+        grp_T[g] = T;
       }
-      // cross-warp reduction of the tile group: exact per-warp partials
-#pragma unroll
-      for (int i = 0; i < kMaxT; ++i)
-#pragma unroll
-        for (int b = 0; b < B; ++b)
-          if (i < T)
-            red[((warp * kMaxT + i) * B + b) * 32 + lane] =
-                A[i][b][0] + (A[i][b][1] >> 2) + (A[i][b][2] >> 4) + (A[i][b][3] >> 6);
-      named_bar_sync(1, kCW * 32);
-      for (int p = warp; p < T * B; p += kCW) {
-        const int i = p / B, b = p - (p / B) * B;
-        int acc = -S.qtot[in][b];
-#pragma unroll
-        for (int w = 0; w < kCW; ++w) acc += red[((w * kMaxT + i) * B + b) * 32 + lane];
-        const int row = (tg + i - J.tile_begin) * kRows + lane;
-        if (row < J.M) {
-          J.y[(size_t)b * J.ldy + row] = __fmul_rn(__fmul_rn(__int2float_rn(acc), J.w_scale), S.sx[in][b]);
-          if (J.acc) J.acc[(size_t)b * J.M + row] = acc;
-        }
+      if (T == kMaxT)
+        consume_group<B, kMaxT>(T, G, xrow, K, ring, full, empty, NS, st, cslot, cphase, ok, L.status,
+                                rg, warp, lane);
+      else
+        consume_group<B, 0>(T, G, xrow, K, ring, full, empty, NS, st, cslot, cphase, ok, L.status, rg,
+                            warp, lane);
+      if (!defer) {
+        named_bar_sync(1, kCW * 32);
+        reduce_group(0, red);
+        named_bar_sync(1, kCW * 32);
       }
-      named_bar_sync(1, kCW * 32);
     }
     t0 = seg_end;
+  }
+  if (defer) {
+    named_bar_sync(1, kCW * 32);
+    for (int g = 0; g < ngrp; ++g) reduce_group(g, red + (size_t)g * gstride);
   }
 }
 
@@ -520,14 +615,30 @@ bool gemv_stream_prepare(GemvLaunch& L, int num_sms, int* grid_out, size_t* smem
     xcap = x > xcap ? x : xcap;
   }
   L.xcap = xcap;
+  // tile groups of each CTA (runs of up to kMaxT tiles of one matrix)
+  int maxg = 0;
+  for (int c = 0; c < grid; ++c) {
+    int n = 0;
+    for (int t0 = L.cta_tile[c]; t0 < L.cta_tile[c + 1];) {
+      int j = 0;
+      while (j + 1 < L.njobs && t0 >= L.jobs[j + 1].tile_begin) ++j;
+      const int seg_end = (j + 1 < L.njobs && L.jobs[j + 1].tile_begin < L.cta_tile[c + 1])
+                              ? L.jobs[j + 1].tile_begin : L.cta_tile[c + 1];
+      n += (seg_end - t0 + kMaxT - 1) / kMaxT;
+      t0 = seg_end;
+    }
+    maxg = n > maxg ? n : maxg;
+  }
   const int budget = stream_smem_budget();
   if (budget <= 0) return false;
+  // keep every group's partials when that still leaves a ring of four stages
+  L.defer = maxg <= kMaxGroups && (int)splan(L.B, 4, xcap, maxg).total <= budget ? maxg : 0;
   int ns = kMaxNS;
-  while (ns > 2 && (int)splan(L.B, ns, xcap).total > budget) --ns;
-  if ((int)splan(L.B, ns, xcap).total > budget) return false;
+  while (ns > 2 && (int)splan(L.B, ns, xcap, L.defer).total > budget) --ns;
+  if ((int)splan(L.B, ns, xcap, L.defer).total > budget) return false;
   L.stages = ns;
   *grid_out = grid;
-  *smem_out = splan(L.B, ns, xcap).total;
+  *smem_out = splan(L.B, ns, xcap, L.defer).total;
   return true;
 }
 

@@ -369,18 +369,54 @@ def test_c5_shapes_batch1_exact(ctx, oracle, M, K):
     w.free()
 
 
-def test_c5_batch16_accumulators_vs_float64(ctx, oracle):
-    # size-independent property at full size: acc == exact integer product
+def _epilogue(acc, w_scale, s_x):
+    """The oracle's fp32 epilogue y = ((float)acc * w_scale) * s_x, each product
+    rounded to fp32 on its own (oracle/oracle.h)."""
+    a = acc.astype(np.float32)
+    return ((a * np.float32(w_scale)).astype(np.float32) * s_x[:, None].astype(np.float32)).astype(np.float32)
+
+
+@pytest.mark.parametrize("M,K,B", [(8192, 28672, 16), (28672, 8192, 16), (8192, 28672, 256),
+                                   (28672, 8192, 256)])
+def test_c5_batched_exact(ctx, oracle, M, K, B):
+    # configuration 5 at its full size through the batched paths (B = 16 and
+    # 256: the tensor-core GEMM). acc must equal the exact integer product
+    # (float64 on the GPU: every partial sum is an integer below 2^53) and y
+    # the oracle's epilogue applied to it, bit for bit.
     import torch
-    M, K, B = 8192, 28672, 16
-    wt = oracle.ternary(555, M * K).reshape(M, K)
-    x = oracle.normals(556, B * K).reshape(B, K)
+    wt = oracle.ternary(555 + B, M * K).reshape(M, K)
+    ws = float(oracle.absmean_scale(wt, 0.02))
+    x = oracle.normals(556 + B, B * K).reshape(B, K)
     qr, sr = oracle.quantize_act(x)
-    w = ctx.upload(oq.TERNARY2, oracle.pack_tern2(wt), M, K, w_scale=0.02)
+    w = ctx.upload(oq.TERNARY2, oracle.pack_tern2(wt), M, K, w_scale=ws)
     acc = torch.empty((B, M), dtype=torch.int32, device="cuda")
-    ctx.gemm(w, dev(qr), dev(sr), acc=acc)
-    exact = dev(qr).double() @ dev(wt).double().T
+    y = ctx.gemm(w, dev(qr), dev(sr), acc=acc)
+    wd = dev(wt).double()
+    exact = dev(qr).double() @ wd.T
+    del wd
     assert torch.equal(acc.double(), exact)
+    assert np.array_equal(host(y), _epilogue(host(acc), ws, sr))
+    w.free()
+    ctx.check_device()
+
+
+@pytest.mark.parametrize("M,K", [(3840, 2560), (2560, 2560), (6912, 2560), (2560, 6912)])
+def test_c2_layer_shapes_batch512(ctx, oracle, M, K):
+    # configuration 2 at its largest batch, every projection shape of the layer
+    # (gate and up share 6912 x 2560), against the oracle (threaded GEMM for y,
+    # exact integer product for acc)
+    import torch
+    B = 512
+    packed, ws, x = tern_case(oracle, M, K, B, seed=M + K + 512)
+    qr, sr = oracle.quantize_act(x)
+    yr = oracle.gemm_tern2_mt(packed, M, K, ws, qr, sr)
+    wt = oracle.ternary(M + K + 512, M * K).reshape(M, K)
+    w = ctx.upload(oq.TERNARY2, packed, M, K, w_scale=ws)
+    acc = torch.empty((B, M), dtype=torch.int32, device="cuda")
+    y = ctx.gemm(w, dev(qr), dev(sr), acc=acc)
+    assert torch.equal(acc.double(), dev(qr).double() @ dev(wt).double().T)
+    assert np.array_equal(host(y), yr)
+    assert np.array_equal(host(ctx.gemm_f32act(w, dev(x))), yr)
     w.free()
 
 
