@@ -263,15 +263,16 @@ __device__ void stream_prologue(STab& S, int8_t* xq, int warp, int lane) {
   named_bar_sync(1, kCW * 32);
 }
 
-// The consumer side of one tile group: T tiles (TC = T known at compile
-// time, or 0: T <= kMaxT at run time) of one matrix through its G.ns stages;
-// each warp's exact partial sums end in red[warp][tile][token][lane].
+// The consumer side of one tile group: TC tiles (1..kMaxT, a compile-time
+// constant) of one matrix through its G.ns stages; each warp's exact partial
+// sums end in red[warp][tile][token][lane].
 template <int B, int TC>
 __device__ __forceinline__ void consume_group(int T_rt, const Geo& G, const int8_t* xrow, int K,
                                               const uint8_t* ring, uint64_t* full, uint64_t* empty,
                                               int NS, int& st, int& cslot, int& cphase, bool& ok,
                                               unsigned* status, int* red, int warp, int lane) {
-  const int T = TC ? TC : T_rt;
+  constexpr int T = TC;
+  (void)T_rt;
   int A[kMaxT][B][4];
 #pragma unroll
   for (int i = 0; i < kMaxT; ++i)
@@ -388,15 +389,12 @@ __global__ void __launch_bounds__(kSThreads, kStreamCps)
       const GemvJob& J = L.jobs[j];
       const int seg_end =
           (j + 1 < L.njobs && L.jobs[j + 1].tile_begin < t_end) ? L.jobs[j + 1].tile_begin : t_end;
-      const int nt = seg_end - t0;
-      const int ng = (nt + kMaxT - 1) / kMaxT;
-      const int T0 = (nt + ng - 1) / ng;
       const uint8_t* wbase = J.w;
       const int tb = J.tile_begin;
-      const Geo G0 = geo(J.K, T0);
-      for (int tg = t0; tg < seg_end && ok; tg += T0) {
-        const int T = seg_end - tg < T0 ? seg_end - tg : T0;
-        const Geo G = T == T0 ? G0 : geo(J.K, T);
+      const Geo G0 = geo(J.K, kMaxT);
+      for (int tg = t0; tg < seg_end && ok; tg += kMaxT) {
+        const int T = seg_end - tg < kMaxT ? seg_end - tg : kMaxT;
+        const Geo G = T == kMaxT ? G0 : geo(J.K, T);
         for (int s = 0; s < G.ns; ++s, ++st) {
           const int slot = pslot;
           if (st >= NS && !mbar_wait(&empty[slot], pphase ^ 1, L.status)) {
@@ -496,11 +494,9 @@ __global__ void __launch_bounds__(kSThreads, kStreamCps)
     const int8_t* xrow = xq + S.xoff[in];
     const int K = J.K;
     const int seg_end = (j + 1 < L.njobs && L.jobs[j + 1].tile_begin < t_end) ? L.jobs[j + 1].tile_begin : t_end;
-    const int nt = seg_end - t0;
-    const int ng = (nt + kMaxT - 1) / kMaxT;
-    const int T0 = (nt + ng - 1) / ng;
-    for (int tg = t0; tg < seg_end; tg += T0, ++ngrp) {
-      const int T = seg_end - tg < T0 ? seg_end - tg : T0;
+    // groups of kMaxT tiles, the remainder last
+    for (int tg = t0; tg < seg_end; tg += kMaxT, ++ngrp) {
+      const int T = seg_end - tg < kMaxT ? seg_end - tg : kMaxT;
       const Geo G = geo(K, T);
       const int g = defer ? ngrp : 0;
       int* rg = red + (size_t)g * gstride;
@@ -509,12 +505,25 @@ __global__ void __launch_bounds__(kSThreads, kStreamCps)
         grp_t0[g] = tg;
         grp_T[g] = T;
       }
-      if (T == kMaxT)
-        consume_group<B, kMaxT>(T, G, xrow, K, ring, full, empty, NS, st, cslot, cphase, ok, L.status,
-                                rg, warp, lane);
-      else
-        consume_group<B, 0>(T, G, xrow, K, ring, full, empty, NS, st, cslot, cphase, ok, L.status, rg,
-                            warp, lane);
+      // the tile count as a compile-time constant: straight-line loop bodies
+      switch (T) {
+        case 4:
+          consume_group<B, 4>(T, G, xrow, K, ring, full, empty, NS, st, cslot, cphase, ok, L.status,
+                              rg, warp, lane);
+          break;
+        case 3:
+          consume_group<B, 3>(T, G, xrow, K, ring, full, empty, NS, st, cslot, cphase, ok, L.status,
+                              rg, warp, lane);
+          break;
+        case 2:
+          consume_group<B, 2>(T, G, xrow, K, ring, full, empty, NS, st, cslot, cphase, ok, L.status,
+                              rg, warp, lane);
+          break;
+        default:
+          consume_group<B, 1>(T, G, xrow, K, ring, full, empty, NS, st, cslot, cphase, ok, L.status,
+                              rg, warp, lane);
+          break;
+      }
       if (!defer) {
         named_bar_sync(1, kCW * 32);
         reduce_group(0, red);
@@ -624,7 +633,7 @@ bool gemv_stream_prepare(GemvLaunch& L, int num_sms, int* grid_out, size_t* smem
       while (j + 1 < L.njobs && t0 >= L.jobs[j + 1].tile_begin) ++j;
       const int seg_end = (j + 1 < L.njobs && L.jobs[j + 1].tile_begin < L.cta_tile[c + 1])
                               ? L.jobs[j + 1].tile_begin : L.cta_tile[c + 1];
-      n += (seg_end - t0 + kMaxT - 1) / kMaxT;
+      n += (seg_end - t0 + kMaxT - 1) / kMaxT;  // full groups of kMaxT, the remainder last
       t0 = seg_end;
     }
     maxg = n > maxg ? n : maxg;
