@@ -92,6 +92,9 @@ def parse():
     ap.add_argument("--workload", default="layer", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ouroq", choices=["ouroq", "reference"])
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--prefetch", default="on", choices=["on", "off"],
+                    help="each step's GEMV launch prefetches the next step's weights into L2 "
+                         "(ouroq_set_prefetch), as a decode loop does for its next projection group")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="bound of the CPU-baseline sample (0 = skip)")
     ap.add_argument("--shard", action="store_true",
@@ -505,7 +508,11 @@ def run_ouroq(args, rank, world, local_rank):
             for j, (_, _, _, xi) in enumerate(mats):
                 ctx.gemm(wl_[j], qbuf[xi], sbuf[xi], y=yout[j], stream=stream)
 
+    prefetch = args.prefetch == "on" and fused and fmt not in REF_FMTS
+
     def step(i):
+        if prefetch:
+            ctx.set_prefetch(wts[(i + 1) % ncop])
         run_step(wts[i % ncop], xs[i % ncop], ys[i % 2], qs[i % 2], sxs[i % 2])
 
     def gemm_only(i):
@@ -688,7 +695,7 @@ def run_ouroq(args, rank, world, local_rank):
 
     if rank == 0:
         cfg = workload_config(args, wl, world)
-        cfg.update({"pdl": not args.no_pdl,
+        cfg.update({"pdl": not args.no_pdl, "l2_prefetch_of_next_step": prefetch,
                     "launch": "CUDA graphs of exactly the timed steps, queued behind a spin "
                               "kernel before the first event"})
         line = {

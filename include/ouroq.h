@@ -108,6 +108,15 @@ ouroq_status ouroq_ptr_kind(const void *p, int *kind, int *device);
 uint64_t ouroq_launch_count(const ouroq_ctx *ctx);
 /* 1 = launch GEMV kernels with programmatic dependent launch (default), 0 = off. */
 ouroq_status ouroq_set_pdl(ouroq_ctx *ctx, int enable);
+/* New (the reference's matvec_q streams each payload when it is called):
+ * the weights the call after the next GEMV launch will read. That launch
+ * prefetches them into L2 once its own weight copies are issued, so the
+ * next call streams from L2 instead of waiting on HBM at its start. A
+ * caller that knows its next projection (the next group of a layer, the
+ * next layer) sets it before each call; the list is consumed by the next
+ * GEMV launch (at most 8 ranges, weights and scales); n = 0 clears it. A
+ * hint: results never depend on it. */
+ouroq_status ouroq_set_prefetch(ouroq_ctx *ctx, int n, const ouroq_weight *const *w);
 
 /* ---- weights ----
  * Upload a packed matrix (HOST pointers, canonical layout above) to device

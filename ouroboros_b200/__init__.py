@@ -62,6 +62,7 @@ ABI_FUNCTIONS = {
     "ouroq_ptr_kind": (_i, [_p, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     "ouroq_launch_count": (ctypes.c_uint64, [_p]),
     "ouroq_set_pdl": (_i, [_p, _i]),
+    "ouroq_set_prefetch": (_i, [_p, _i, _p]),
     "ouroq_weight_upload": (_i, [_p, _i, _p, _i, _i, _p, _f, ctypes.POINTER(_p)]),
     "ouroq_weight_upload_device": (_i, [_p, _i, _p, _i, _i, _p, _f, ctypes.POINTER(_p)]),
     "ouroq_weight_free": (_i, [_p, _p]),
@@ -290,6 +291,13 @@ class Context:
 
     def set_pdl(self, enable: bool) -> None:
         self._check(self.lib.ouroq_set_pdl(self.ctx, 1 if enable else 0))
+
+    def set_prefetch(self, ws) -> None:
+        """The weights the call after the next GEMV launch reads: that launch
+        prefetches them into L2 (a hint; results never depend on it)."""
+        n = len(ws)
+        arr = (_p * max(n, 1))(*[w.handle for w in ws])
+        self._check(self.lib.ouroq_set_prefetch(self.ctx, n, arr))
 
     def check_device(self) -> None:
         self._check(self.lib.ouroq_check_device(self.ctx))

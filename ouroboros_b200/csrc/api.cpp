@@ -33,6 +33,8 @@ struct ouroq_ctx {
   bool pdl = true;
   bool use_tc = true;  // tensor-core path for batches >= 16
   bool stream_gemv = true;  // fused one/two-token ternary launches on gemv_stream_kernel
+  // weights the next GEMV launch prefetches into L2 (ouroq_set_prefetch)
+  std::vector<std::pair<const uint8_t*, uint32_t>> prefetch;
   std::string err;
   unsigned* d_status = nullptr;
   uint64_t launches = 0;
@@ -194,6 +196,13 @@ GemvJob make_job(const ouroq_weight* w, const int8_t* q, const float* s_x, float
 
 ouroq_status run_gemv(ouroq_ctx* ctx, GemvLaunch& L, cudaStream_t s) {
   L.status = ctx->d_status;
+  L.npf = 0;
+  for (const auto& r : ctx->prefetch) {
+    if (L.npf == kMaxGemvJobs) break;
+    L.pf_ptr[L.npf] = r.first;
+    L.pf_bytes[L.npf++] = r.second;
+  }
+  ctx->prefetch.clear();
   if (L.njobs == 0 || L.B == 0) return OUROQ_OK;
   if (ctx->stream_gemv) {
     GemvLaunch S = L;
@@ -717,6 +726,34 @@ uint64_t ouroq_launch_count(const ouroq_ctx* ctx) { return ctx ? ctx->launches :
 ouroq_status ouroq_set_pdl(ouroq_ctx* ctx, int enable) {
   if (!ctx) return OUROQ_ERR_BAD_ARG;
   ctx->pdl = enable != 0;
+  return OUROQ_OK;
+}
+
+ouroq_status ouroq_set_prefetch(ouroq_ctx* ctx, int n, const ouroq_weight* const* w) {
+  if (!ctx) return OUROQ_ERR_BAD_ARG;
+  if (n < 0 || (n > 0 && !w)) return fail(ctx, OUROQ_ERR_BAD_ARG, "bad prefetch list");
+  ctx->prefetch.clear();
+  // whole 16-byte units only (a hint: a ragged tail is left out, never overrun)
+  auto add = [&](const void* p, size_t bytes) {
+    const uint8_t* b = static_cast<const uint8_t*>(p);
+    bytes &= ~size_t{15};
+    while (bytes > 0) {
+      const size_t n1 = bytes < 0x40000000u ? bytes : 0x40000000u;
+      ctx->prefetch.emplace_back(b, (uint32_t)n1);
+      b += n1;
+      bytes -= n1;
+    }
+  };
+  for (int i = 0; i < n; ++i) {
+    if (!w[i]) return fail(ctx, OUROQ_ERR_BAD_ARG, "null weight %d in the prefetch list", i);
+    size_t wb = w[i]->bytes;
+    if (w[i]->scales) {
+      const size_t sb = tiled_scale_bytes(w[i]->M, w[i]->K);
+      wb -= sb;
+      add(w[i]->scales, sb);
+    }
+    add(w[i]->w, wb);
+  }
   return OUROQ_OK;
 }
 

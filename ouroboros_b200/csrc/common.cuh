@@ -83,6 +83,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Bring [src, src + bytes) of global memory into L2 (16-byte aligned, a
+// multiple of 16 bytes); no completion mechanism, nothing waits for it.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Same, with an L2 evict-first hint: streamed weights are read exactly once.
 __device__ __forceinline__ void bulk_g2s_stream(void* dst, const void* src, uint32_t bytes,
                                                 uint64_t* bar, uint64_t policy) {

@@ -12,16 +12,17 @@
 // Why a second GEMV kernel. At one token a layer's five projections move
 // 17.4 MB, 117 KB per SM: a few microseconds of HBM time, so what bounds a
 // launch is its critical path, not bandwidth. This kernel shortens it:
-//  * The weight stream starts at CTA entry: the producer warp initialises
-//    the ring's mbarriers itself and issues its copies straight from the
-//    launch parameters, before anything else runs. Weights never depend on
-//    the previous kernel; only the activations do, and only the consumers
-//    wait for it (griddepcontrol.wait), so the copies overlap the previous
-//    launch's tail and this launch's prologue. Built for one CTA per SM
-//    (kStreamCps = 1) a CTA's whole share (up to 6 x 32 KB) is in flight at
-//    once; built for two (<= 56 registers, <= 113 KB of shared memory each)
-//    the next launch's CTA can sit beside this one and stream while it
-//    computes.
+//  * The weight stream starts at CTA entry: the producer warp copies the
+//    launch parameters with one round of independent loads, initialises the
+//    ring's mbarriers and issues its copies before anything else runs. With
+//    one CTA per SM a CTA's whole share (up to 6 x 32 KB) is in flight at
+//    once. Weights never depend on the previous kernel; only the activations
+//    do, and only the consumers wait for it (griddepcontrol.wait), so the
+//    copies overlap the previous launch's tail and this launch's prologue.
+//    (Two CTAs per SM, so that the next launch streams beside this one,
+//    measured slower: 8 consumer warps compute too slowly.)
+//  * An optional L2 prefetch of the next call's weights (ouroq_set_prefetch),
+//    issued once the CTA's own copies are out.
 //  * Chunk-major stages. A stage is a K-slice of up to four 32-row tiles of
 //    one matrix (one bulk copy per tile: in the tiled layout a K-slice of a
 //    tile is contiguous). A consumer warp takes one 16-byte chunk position
@@ -48,20 +49,14 @@
 namespace ouroq {
 namespace {
 
-#ifndef OUROQ_STREAM_CPS
-#define OUROQ_STREAM_CPS 1
-#endif
-constexpr int kStreamCps = OUROQ_STREAM_CPS;  // CTAs per SM the kernel is built for
 constexpr int kRows = kTileRows;
-// consumer warps: 15 (16 with the producer, 128 registers) for one CTA per
-// SM; 8 (112 registers) when two must fit
-constexpr int kCW = kStreamCps == 1 ? 15 : 8;
+constexpr int kCW = 15;                     // consumer warps (16 with the producer: 128 registers)
 constexpr int kSThreads = (kCW + 1) * 32;   // + one producer warp
 constexpr int kMaxT = 4;                    // tiles per stage
-constexpr uint32_t kStage = (kStreamCps == 1 ? 32u : 16u) * 1024u;  // bytes per ring slot
+constexpr uint32_t kStage = 32u * 1024u;    // bytes per ring slot
 constexpr int kMaxNS = 6;                   // ring depth limit
 constexpr int kMaxIn = kMaxGemvJobs;        // distinct inputs of one CTA
-constexpr int kRegUnits = kStreamCps == 1 ? 5 : 10;  // 128-value units a warp keeps in registers
+constexpr int kRegUnits = 5;                // 128-value units a warp keeps in registers
 constexpr int kMaxGroups = 16;              // tile groups of one CTA whose partials can wait
 
 __host__ __device__ constexpr uint32_t al128(uint32_t v) { return (v + 127u) & ~127u; }
@@ -153,6 +148,30 @@ __device__ __forceinline__ uint32_t quant4s(float a, float b, float c, float d, 
          ((uint32_t)c3 << 24);
 }
 
+// The same four codes without a branch: the rounding of quant_code_fast for
+// each value, and `exact` cleared when any of them lies within 2^-14 of a
+// tie (or rs overflowed). The caller redoes a unit with quant4s -- the
+// division fallback -- when any lane of the warp reports that, so the codes
+// are always rint(__fdiv_rn(v, s)) clamped, bit for bit.
+__device__ __forceinline__ uint32_t quant4_nobranch(const float* v, float rs, int* sum, bool* exact) {
+  uint32_t w = 0;
+  int su = 0;
+  bool ok = true;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float t = __fmul_rn(v[i], rs);
+    const float m = __fadd_rn(t, 0x1.8p23f);
+    ok &= fabsf(__fsub_rn(t, __fsub_rn(m, 0x1.8p23f))) < 0.5f - 0x1p-14f;
+    int q = __float_as_int(m) - 0x4B400000;
+    q = q < -127 ? -127 : (q > 127 ? 127 : q);
+    su += q;
+    w |= (uint32_t)(q & 0xFF) << (8 * i);
+  }
+  *sum += su;
+  *exact = ok;
+  return w;
+}
+
 // Unit u (128 consecutive values of one token row) -> (input, token, offset
 // of the unit in the input's [B][K] block). B <= 2: no division.
 __device__ __forceinline__ void unit_at(const STab& S, int B, int u, int& in, int& b, int& off) {
@@ -161,6 +180,15 @@ __device__ __forceinline__ void unit_at(const STab& S, int B, int u, int& in, in
   const int r = u - S.ufirst[in];
   b = (B > 1 && r >= S.K[in] / 128) ? 1 : 0;
   off = r * 128;  // = b * K + (unit within the row) * 128
+}
+
+// The exact path for one unit (some value of the warp's unit lies next to a
+// rounding tie, or the scale is 0): codes through quant4s, out of line so
+// that the common path stays short. Returns (codes, their sum).
+__device__ __noinline__ uint2 quant4_exact(float a, float b, float c, float d, float s, float rs) {
+  int sum = 0;
+  const uint32_t w = quant4s(a, b, c, d, s, rs, &sum);
+  return make_uint2(w, (uint32_t)sum);
 }
 
 // Consumer prologue: quantise every distinct input row of the CTA into xq.
@@ -228,10 +256,41 @@ __device__ void stream_prologue(STab& S, int8_t* xq, int warp, int lane) {
     const int in = threadIdx.x / B, b = threadIdx.x - in * B;
     S.sx[in][b] = __fdiv_rn(__int_as_float(S.amax[in][b]), 127.0f);
   }
-  // pass 2: codes into xq, code sums per row (integer: the order is free)
+  // pass 2: codes into xq, code sums per row (integer: the order is free).
+  // Scales first (a warp's units span one or two rows), then the codes of all
+  // register-held units in straight-line code; one warp vote sends the rare
+  // unit with a value next to a rounding tie through the exact division.
+  float scu[kRegUnits], rsu[kRegUnits];
+  {
+    int c = -1;
+    float sc = 0.0f, rs = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kRegUnits; ++k) {
+      if (seg[k] >= 0 && seg[k] != c) {
+        c = seg[k];
+        sc = __fdiv_rn(__int_as_float(S.amax[c >> 1][c & 1]), 127.0f);
+        rs = __frcp_rn(sc);
+      }
+      scu[k] = sc;
+      rsu[k] = rs;
+    }
+  }
+  uint32_t code[kRegUnits];
+  int usum[kRegUnits];
+#pragma unroll
+  for (int k = 0; k < kRegUnits; ++k) {
+    bool ok = true;
+    usum[k] = 0;
+    code[k] = quant4_nobranch(v[k], rsu[k], &usum[k], &ok);
+    ok = (seg[k] < 0) || (ok && scu[k] != 0.0f);
+    if (__any_sync(0xffffffffu, !ok)) {
+      const uint2 e = quant4_exact(v[k][0], v[k][1], v[k][2], v[k][3], scu[k], rsu[k]);
+      code[k] = e.x;
+      usum[k] = (int)e.y;
+    }
+  }
   cur = -1;
   int sum = 0;
-  float sc = 0.0f, rsc = 0.0f;
   auto flush_sum = [&]() {
     if (cur >= 0) {
       const int t = warp_sum(sum);
@@ -239,25 +298,27 @@ __device__ void stream_prologue(STab& S, int8_t* xq, int warp, int lane) {
     }
     sum = 0;
   };
-  auto quant_unit = [&](const float* w, int sg, int off) {
-    if (sg != cur) {
-      flush_sum();
-      cur = sg;
-      sc = __fdiv_rn(__int_as_float(S.amax[sg >> 1][sg & 1]), 127.0f);
-      rsc = __frcp_rn(sc);
-    }
-    *reinterpret_cast<uint32_t*>(xq + S.xoff[sg >> 1] + off + lane * 4) =
-        quant4s(w[0], w[1], w[2], w[3], sc, rsc, &sum);
-  };
 #pragma unroll
-  for (int k = 0; k < kRegUnits; ++k)
-    if (seg[k] >= 0) quant_unit(v[k], seg[k], uoff[k]);
-  for (int u0 = warp + kRegUnits * kCW; u0 < nunits; u0 += kCW) {
+  for (int k = 0; k < kRegUnits; ++k) {
+    if (seg[k] < 0) continue;  // warp-uniform
+    if (seg[k] != cur) {
+      flush_sum();
+      cur = seg[k];
+    }
+    sum += usum[k];
+    *reinterpret_cast<uint32_t*>(xq + S.xoff[seg[k] >> 1] + uoff[k] + lane * 4) = code[k];
+  }
+  for (int u0 = warp + kRegUnits * kCW; u0 < nunits; u0 += kCW) {  // units beyond the registers
     int in, b, off;
     unit_at(S, B, u0, in, b, off);
     const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
-    const float w[4] = {t.x, t.y, t.z, t.w};
-    quant_unit(w, in * 2 + b, off);
+    if (in * 2 + b != cur) {
+      flush_sum();
+      cur = in * 2 + b;
+    }
+    const float sc = __fdiv_rn(__int_as_float(S.amax[in][b]), 127.0f);
+    *reinterpret_cast<uint32_t*>(xq + S.xoff[in] + off + lane * 4) =
+        quant4s(t.x, t.y, t.z, t.w, sc, __frcp_rn(sc), &sum);
   }
   flush_sum();
   named_bar_sync(1, kCW * 32);
@@ -337,8 +398,30 @@ __device__ __forceinline__ void consume_group(int T_rt, const Geo& G, const int8
             A[i][b][0] + (A[i][b][1] >> 2) + (A[i][b][2] >> 4) + (A[i][b][3] >> 6);
 }
 
+// This CTA's even share of the next launch's weight ranges, into L2 (the
+// next launch then streams them from L2: measured 1.4 us instead of 3.3 us
+// for a cold 117 KB per SM).
+__device__ __noinline__ void prefetch_next(const GemvLaunch& L) {
+  if (L.npf <= 0) return;
+  uint64_t total = 0;
+  for (int e = 0; e < L.npf; ++e) total += L.pf_bytes[e];
+  const uint64_t share = ((total + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
+  const uint64_t lo = (uint64_t)blockIdx.x * share;
+  const uint64_t hi = lo + share < total ? lo + share : total;
+  uint64_t base = 0;
+  for (int e = 0; e < L.npf && lo < hi; ++e) {
+    const uint64_t end = base + L.pf_bytes[e];
+    const uint64_t b0 = lo > base ? lo : base, b1 = hi < end ? hi : end;
+    for (uint64_t a = b0; a < b1; a += 32768) {
+      const uint64_t n = b1 - a < 32768 ? b1 - a : 32768;
+      prefetch_l2(L.pf_ptr[e] + (a - base), (uint32_t)n);
+    }
+    base = end;
+  }
+}
+
 template <int B>
-__global__ void __launch_bounds__(kSThreads, kStreamCps)
+__global__ void __launch_bounds__(kSThreads, 1)
     gemv_stream_kernel(const __grid_constant__ GemvLaunch Lp) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ STab S;
@@ -421,6 +504,7 @@ __global__ void __launch_bounds__(kSThreads, kStreamCps)
       }
       t0 = seg_end;
     }
+    if (lane == 0) prefetch_next(L);
     // every copy into this CTA's shared memory lands before the CTA exits
     for (int i = (st > NS ? st - NS : 0); i < st; ++i) mbar_wait(&full[i % NS], (i / NS) & 1, L.status);
     return;
@@ -538,7 +622,7 @@ __global__ void __launch_bounds__(kSThreads, kStreamCps)
   }
 }
 
-// Shared memory one CTA may use so that kStreamCps of them fit on an SM.
+// Shared memory one CTA may use (one CTA per SM).
 int stream_smem_budget() {
   static int budget[64] = {0};
   int dev = 0;
@@ -554,7 +638,7 @@ int stream_smem_budget() {
       cudaFuncGetAttributes(&fb, gemv_stream_kernel<2>) != cudaSuccess)
     return 0;
   const int st = (int)(fa.sharedSizeBytes > fb.sharedSizeBytes ? fa.sharedSizeBytes : fb.sharedSizeBytes);
-  int b = per_sm / kStreamCps - reserved - st;
+  int b = per_sm - reserved - st;
   if (b > optin - st) b = optin - st;
   if (dev < 64) budget[dev] = b;
   return b;

@@ -91,6 +91,12 @@ struct GemvLaunch {
   int gcap;                 // per-group activation sums one CTA keeps resident (ints)
   int defer;                // ternary: > 0 = tile slots for the end-of-CTA reduction
   unsigned* status;         // device status word
+  // L2 prefetch of the weights the next launch reads (gemv_stream_kernel):
+  // npf ranges, 16-byte aligned, multiples of 16 bytes, split evenly over the
+  // CTAs and issued after each CTA's own copies; nothing waits for them.
+  const uint8_t* pf_ptr[kMaxGemvJobs];
+  uint32_t pf_bytes[kMaxGemvJobs];
+  int npf;
   // CTA c owns tiles [cta_tile[c], cta_tile[c+1]): ranges balanced by weight
   // bytes on the host, so the kernel does no 64-bit division at start-up.
   uint16_t cta_tile[kMaxGemvCtas + 1];
