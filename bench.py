@@ -103,6 +103,10 @@ def parse():
                     help="how --shard moves rows between ranks")
     ap.add_argument("--tokens", type=int, default=256,
                     help="decode workload: tokens generated per sequence in the timed region")
+    ap.add_argument("--shard-record", default="on", choices=["on", "off"],
+                    help="layer workload: add the row-sharded 8192x28672 sub-record over the ranks")
+    ap.add_argument("--decode-tokens", type=int, default=64,
+                    help="layer workload: tokens of the configuration-4 decode sub-record (0 = skip)")
     ap.add_argument("--layers", type=int, default=30,
                     help="decode workload: layers (30 = BitNet-2B; fewer only to profile a small case)")
     return ap.parse_args()
@@ -594,7 +598,8 @@ def run_ouroq(args, rank, world, local_rank):
         kern_bytes = nb["step"]
         kernel = (f"{'tl1' if fmt == TL1 else 'tq1'}_matvec_kernel (reference order)"
                   if fmt in REF_FMTS else
-                  f"gemv_kernel<{'kTern2' if fmt == TERN else 'kSign1'},B={B}> (fused quantisation)")
+                  (f"gemv_stream_kernel<B={B}> (fused quantisation)" if fmt == TERN and B <= 2 and not block
+                   else f"gemv_kernel<{'kTern2' if fmt == TERN else 'kSign1'},B={B}> (fused quantisation)"))
     else:
         # matmul launches alone, on pre-quantised activations, timed the same way
         g2, _ = graphs_for(gemm_only, steps)
@@ -716,9 +721,193 @@ def run_ouroq(args, rank, world, local_rank):
         }
         if args.workload == "layer":
             line["decode_tokens_per_s_ternary_only"] = round(B * world / (ms / 1e3 / steps * 30), 1)
-        print(json.dumps(line), flush=True)
     del graphs
+    if args.workload == "layer" and B == 1 and args.shard_record == "on":
+        try:
+            rec = sharded_record(ctx, device, world, rank)
+        except Exception as e:  # reported, never fatal to the headline line
+            rec = {"error": f"{type(e).__name__}: {e}"[:300]}
+        if rank == 0:
+            line["sharded"] = rec
+    if args.workload == "layer" and B <= 2 and args.decode_tokens > 0:
+        rec = decode_record(ctx, device, B, args.decode_tokens, world, rank,
+                            min(args.cpu_seconds, 3.0))
+        if rank == 0:
+            line["decode"] = rec
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     ctx.close()
+
+
+def decode_record(ctx, device, B: int, tokens: int, world: int, rank: int, cpu_seconds: float):
+    """Configuration 4 as a sub-record of the default line: BitNet-2B-class
+    decode (30 layers, KV context 1024, tied F16 lm_head with the greedy
+    pick), one CUDA graph per token, `tokens` tokens timed on the device (max
+    over ranks); the ternary-matmul share is the same projections replayed
+    alone over the step's time. Rank 0 at N = 1 adds the reference's fp32
+    run_layer on the host cores (bounded sample) as in run_decode."""
+    import torch
+    import torch.distributed as dist
+    from ouroboros_b200.decode import Decoder
+    dec = Decoder(ctx, layers=30, batch=B, context=1024, generate=tokens + 8, device=device,
+                  seed=29 + rank)
+    n0 = ctx.launch_count()
+    g_full = dec.capture(dec.step)
+    launches = (ctx.launch_count() - n0) / 3
+    g_tern = dec.capture(dec.ternary_only_step)
+
+    def timed(g, n):
+        if world > 1:
+            dist.barrier()
+        dec.pos.fill_(1024)
+        torch.cuda.synchronize(device)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(dec.stream):
+            gate(torch, n)
+            e0.record(dec.stream)
+            for _ in range(n):
+                g.replay()
+            e1.record(dec.stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    timed(g_full, 3)
+    ms_full = timed(g_full, tokens)
+    ms_tern = timed(g_tern, tokens)
+    rec = {"workload": f"bitnet2b-decode-b{B}-ctx1024-30layers", "tokens_timed": tokens,
+           "tokens_per_s": round(B * world * tokens / (ms_full / 1e3), 2),
+           "us_per_token": round(1e3 * ms_full / tokens, 2),
+           "ternary_matmul_share": round(ms_tern / ms_full, 4),
+           "gpu_launches_per_token": round(launches, 1),
+           "how": "one CUDA graph per decode step (RMSNorm fused into the projection launches, "
+                  "RoPE + KV append + GQA attention in one launch, F16 lm_head with the argmax), "
+                  "device events, max over ranks"}
+    del g_full, g_tern
+    dec.free()
+    del dec
+    torch.cuda.empty_cache()
+    if rank == 0 and world == 1 and cpu_seconds > 0:
+        from oracle import pyoracle as O
+        threads = O.hw_threads()
+        v, n, _ = cpu_decode_tokens_per_s(B, cpu_seconds, threads)
+        rec["cpu_reference_tokens_per_s"] = round(v, 3)
+        rec["cpu_reference_sample"] = (f"{n} single-layer passes of run_layer in the reference's fp32 "
+                                       f"order (TQ1_0 projections), scaled to 30 layers + the f16 "
+                                       f"lm_head; {threads} host threads")
+    return rec
+
+
+def random_tern2_packed(rng, M: int, K: int) -> np.ndarray:
+    """Packed ternary codes [M][K/4] with p(-1, 0, +1) = .25, .5, .25: random
+    2-bit fields with the code 3 folded onto 1 (vectorised over bytes)."""
+    b = rng.integers(0, 256, size=M * K // 4, dtype=np.uint8)
+    for j in range(4):
+        three = ((b >> (2 * j)) & 3) == 3
+        b[three] ^= np.uint8(2 << (2 * j))
+    return b.reshape(M, K // 4)
+
+
+def sharded_record(ctx, device, world: int, rank: int, steps: int = 200):
+    """Configuration 5 row-sharded over the job's ranks (every rank holds M/N
+    rows of 8192 x 28672, the down projection of a 70B-class FFN): per
+    transport (NCCL in-place all-gather; this library's peer stores over
+    NVLink) and batch (1, 16), the local product alone, one isolated call
+    (product + gather + sync, end to end on the device) and `steps` calls back
+    to back in a CUDA graph (gather i overlapping product i + 1 where the
+    stream allows). Device events, max over ranks. At N = 1 the same calls on
+    one GPU are the baseline."""
+    import torch
+    import torch.distributed as dist
+    import ouroboros_b200 as oq
+    from ouroboros_b200 import shard
+    M, K = 8192, 28672
+    if world > 1:
+        shard.join(ctx)
+    else:
+        ctx.shard_init(oq.shard_unique_id(), 1, 0)
+    # enough copies that this rank's rows exceed twice the L2 (every step streams
+    # from HBM); each rank draws only the rows it holds (the rest of the full
+    # host matrix is never read)
+    row0, rows = oq.shard_rows(M, world, rank)
+    ncop = min(40, max(2, -(-2 * L2_BYTES // (rows * K // 4))))
+    ws = []
+    for c in range(ncop):
+        full = np.zeros((M, K // 4), np.uint8)
+        full[row0:row0 + rows] = random_tern2_packed(np.random.default_rng(4321 + 1000 * c + rank), rows, K)
+        ws.append(ctx.upload_shard(oq.TERNARY2, full, M, K, None, 0.01))
+        del full
+    stream = torch.cuda.Stream(device=device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(99)
+    rec = {"shape": [M, K], "ranks": world, "rows_per_rank": M // world, "weight_copies": ncop,
+           "steps": steps, "bytes_per_step": M * K // 4,
+           "how": "device events around CUDA graphs, max over ranks; local = the rank's rows only; "
+                  "single = one call (product + gather) then stream sync; pipelined = calls back to back"}
+
+    def timed(g, reps=1):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            gate(torch, reps)
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+        ctx.shard_sync(stream, timeout_ms=60000)
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    def graph(fn, n):
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                fn(i)
+        ctx.shard_sync(stream, timeout_ms=60000)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(n):
+                fn(i)
+        return g
+
+    for B in (1, 16):
+        xs = [torch.randn((B, K), generator=gen, device=device) for _ in range(ncop)]
+        ys = [torch.empty((B, M), device=device) for _ in range(2)]
+        ylocal = torch.empty((B, M // world), device=device)
+        g_local = graph(lambda i: ctx.gemm_f32act(ws[i % ncop], xs[i % ncop], y=ylocal, stream=stream), steps)
+        timed(g_local)
+        local_us = 1e3 * timed(g_local) / steps
+        del g_local
+        for tr in ("nccl", "peer"):
+            ctx.shard_set_transport(tr)
+            step = lambda i: ctx.gemm_sharded(ws[i % ncop], xs[i % ncop], y=ys[i % 2], stream=stream)  # noqa: E731
+            g_one = graph(step, 1)
+            g_pipe = graph(step, steps)
+            timed(g_pipe)
+            single = [timed(g_one) for _ in range(5)]
+            pipe_us = 1e3 * timed(g_pipe) / steps
+            rec[f"b{B}_{tr}"] = {"local_product_us": round(local_us, 3),
+                                 "single_call_us": round(1e3 * statistics.median(single), 3),
+                                 "pipelined_us_per_step": round(pipe_us, 3),
+                                 "pipelined_GBs": round(M * K / 4 / (pipe_us / 1e6) / 1e9, 1)}
+            del g_one, g_pipe
+        del xs, ys, ylocal
+    for w in ws:
+        w.free()
+    ctx.shard_finalize()
+    return rec
 
 
 def cpu_decode_tokens_per_s(B: int, seconds: float, threads: int):
