@@ -145,6 +145,33 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 __device__ __forceinline__ void named_bar_sync(unsigned id, unsigned nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// Thread-block clusters: this CTA's rank and the cluster's CTA count.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory location in CTA `cta` of the cluster.
+__device__ __forceinline__ uint32_t peer_smem(const void* local, uint32_t cta) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(cta));
+  return r;
+}
+// Store to (possibly another CTA's) shared memory in the cluster.
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+// Every thread of every CTA of the cluster: stores before it (shared memory
+// of any CTA of the cluster included) are visible to all after it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // Arrive at a named barrier without waiting (the other side bar.syncs).
 __device__ __forceinline__ void named_bar_arrive(unsigned id, unsigned nthreads) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

@@ -58,6 +58,13 @@ constexpr int kMaxNS = 6;                   // ring depth limit
 constexpr int kMaxIn = kMaxGemvJobs;        // distinct inputs of one CTA
 constexpr int kRegUnits = 5;                // 128-value units a warp keeps in registers
 constexpr int kMaxGroups = 16;              // tile groups of one CTA whose partials can wait
+constexpr int kClusterCtas = 4;             // CTAs of a cluster that share the quantisation
+#ifndef OUROQ_STREAM_CLUSTER_MIN_UNITS
+// A CTA whose inputs hold more 128-value units than this quantises them
+// together with the other CTAs of a cluster (below it the quantisation is one
+// round of loads, shorter than the two cluster barriers sharing costs).
+#define OUROQ_STREAM_CLUSTER_MIN_UNITS 80
+#endif
 
 __host__ __device__ constexpr uint32_t al128(uint32_t v) { return (v + 127u) & ~127u; }
 
@@ -170,6 +177,24 @@ __device__ __forceinline__ uint32_t quant4_nobranch(const float* v, float rs, in
   *sum += su;
   *exact = ok;
   return w;
+}
+
+// Relaxed reductions into (possibly another CTA's) shared memory of the
+// cluster, and the two halves of the cluster barrier.
+__device__ __forceinline__ void red_max_cluster(uint32_t addr, int v) {
+  asm volatile("red.relaxed.cluster.shared::cluster.max.s32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_add_cluster(uint32_t addr, int v) {
+  asm volatile("red.relaxed.cluster.shared::cluster.add.s32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+// (.aligned: the whole warp executes them together, hence the __syncwarp)
+__device__ __forceinline__ void cluster_arrive() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  __syncwarp();
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 // Unit u (128 consecutive values of one token row) -> (input, token, offset
@@ -324,6 +349,146 @@ __device__ void stream_prologue(STab& S, int8_t* xq, int warp, int lane) {
   named_bar_sync(1, kCW * 32);
 }
 
+// The same quantisation shared by the `cs` CTAs of a cluster, which hold the
+// same inputs (the union of the cluster's jobs, at the same offsets in every
+// CTA's xq). CTA `rank` takes units u = rank + cs * (warp + kCW * k): its
+// row maxima go to every CTA's S.amax by remote max-reductions, its codes to
+// every CTA's xq by remote stores and its code sums to every S.qtot by remote
+// adds. Three cluster barrier phases order it: phase 0 (arrived at by the
+// caller once the tables are built, waited for here after the loads are
+// issued) -- every CTA's S.amax / S.qtot are zeroed; phase 1 -- every maximum
+// is in; phase 2 -- every code and sum is in. Nothing is read from another
+// CTA, and nothing is written to one after phase 2, so no CTA can leave while
+// a peer still addresses its memory. Results are those of stream_prologue:
+// max and integer sums do not depend on the order.
+template <int B>
+__device__ void stream_prologue_cluster(STab& S, int8_t* xq, int warp, int lane, int cs, int rank) {
+  const int nunits = S.ufirst[S.nin];
+  const int u0 = rank + cs * warp, ustep = cs * kCW;
+  float v[kRegUnits][4];
+  int seg[kRegUnits], uoff[kRegUnits];
+#pragma unroll
+  for (int k = 0; k < kRegUnits; ++k) {
+    const int u = u0 + k * ustep;
+    seg[k] = -1;
+    if (u < nunits) {
+      int in, b, off;
+      unit_at(S, B, u, in, b, off);
+      seg[k] = in * 2 + b;
+      uoff[k] = off;
+      const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
+      v[k][0] = t.x;
+      v[k][1] = t.y;
+      v[k][2] = t.z;
+      v[k][3] = t.w;
+    }
+  }
+  cluster_wait();  // phase 0: the peers' tables are ready for remote updates
+  int cur = -1;
+  float m = 0.0f;
+  auto flush_max = [&]() {
+    if (cur >= 0) {
+      const float t = warp_max(m);
+      if (lane < cs) red_max_cluster(peer_smem(&S.amax[cur >> 1][cur & 1], lane), __float_as_int(t));
+    }
+    m = 0.0f;
+  };
+  auto absmax4 = [](float a, float b, float c, float d) {
+    return fmaxf(fmaxf(fabsf(a), fabsf(b)), fmaxf(fabsf(c), fabsf(d)));
+  };
+#pragma unroll
+  for (int k = 0; k < kRegUnits; ++k) {
+    if (seg[k] < 0) continue;  // warp-uniform
+    if (seg[k] != cur) {
+      flush_max();
+      cur = seg[k];
+    }
+    m = fmaxf(m, absmax4(v[k][0], v[k][1], v[k][2], v[k][3]));
+  }
+  for (int u = u0 + kRegUnits * ustep; u < nunits; u += ustep) {  // units beyond the registers
+    int in, b, off;
+    unit_at(S, B, u, in, b, off);
+    const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
+    if (in * 2 + b != cur) {
+      flush_max();
+      cur = in * 2 + b;
+    }
+    m = fmaxf(m, absmax4(t.x, t.y, t.z, t.w));
+  }
+  flush_max();
+  cluster_arrive();
+  cluster_wait();  // phase 1: every CTA's S.amax holds the full row maxima
+  if (threadIdx.x < S.nin * B) {
+    const int in = threadIdx.x / B, b = threadIdx.x - in * B;
+    S.sx[in][b] = __fdiv_rn(__int_as_float(S.amax[in][b]), 127.0f);
+  }
+  float scu[kRegUnits], rsu[kRegUnits];
+  {
+    int c = -1;
+    float sc = 0.0f, rs = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kRegUnits; ++k) {
+      if (seg[k] >= 0 && seg[k] != c) {
+        c = seg[k];
+        sc = __fdiv_rn(__int_as_float(S.amax[c >> 1][c & 1]), 127.0f);
+        rs = __frcp_rn(sc);
+      }
+      scu[k] = sc;
+      rsu[k] = rs;
+    }
+  }
+  uint32_t code[kRegUnits];
+  int usum[kRegUnits];
+#pragma unroll
+  for (int k = 0; k < kRegUnits; ++k) {
+    bool ok = true;
+    usum[k] = 0;
+    code[k] = quant4_nobranch(v[k], rsu[k], &usum[k], &ok);
+    ok = (seg[k] < 0) || (ok && scu[k] != 0.0f);
+    if (__any_sync(0xffffffffu, !ok)) {
+      const uint2 e = quant4_exact(v[k][0], v[k][1], v[k][2], v[k][3], scu[k], rsu[k]);
+      code[k] = e.x;
+      usum[k] = (int)e.y;
+    }
+  }
+  cur = -1;
+  int sum = 0;
+  auto flush_sum = [&]() {
+    if (cur >= 0) {
+      const int t = warp_sum(sum);
+      if (lane < cs) red_add_cluster(peer_smem(&S.qtot[cur >> 1][cur & 1], lane), t);
+    }
+    sum = 0;
+  };
+  auto put = [&](const int8_t* dst, uint32_t w) {
+    for (int q = 0; q < cs; ++q) st_cluster_u32(peer_smem(dst, q), w);
+  };
+#pragma unroll
+  for (int k = 0; k < kRegUnits; ++k) {
+    if (seg[k] < 0) continue;  // warp-uniform
+    if (seg[k] != cur) {
+      flush_sum();
+      cur = seg[k];
+    }
+    sum += usum[k];
+    put(xq + S.xoff[seg[k] >> 1] + uoff[k] + lane * 4, code[k]);
+  }
+  for (int u = u0 + kRegUnits * ustep; u < nunits; u += ustep) {  // units beyond the registers
+    int in, b, off;
+    unit_at(S, B, u, in, b, off);
+    const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
+    if (in * 2 + b != cur) {
+      flush_sum();
+      cur = in * 2 + b;
+    }
+    const float sc = __fdiv_rn(__int_as_float(S.amax[in][b]), 127.0f);
+    put(xq + S.xoff[in] + off + lane * 4, quant4s(t.x, t.y, t.z, t.w, sc, __frcp_rn(sc), &sum));
+  }
+  flush_sum();
+  cluster_arrive();
+  cluster_wait();  // phase 2: codes and code sums complete in every CTA
+}
+
 // The consumer side of one tile group: TC tiles (1..kMaxT, a compile-time
 // constant) of one matrix through its G.ns stages; each warp's exact partial
 // sums end in red[warp][tile][token][lane].
@@ -467,6 +632,21 @@ __global__ void __launch_bounds__(kSThreads, 1)
     const uint64_t pol = policy_evict_first();
     int st = 0, pslot = 0, pphase = 0;  // stage count, ring slot, slot wrap parity
     bool ok = true;
+    // In a cluster every thread takes part in the prologue's three barrier
+    // phases. The producer passes them once the ring is full (before its first
+    // wait for a free slot: the consumers free slots only after phase 2), or
+    // after its last copy when the ring never fills.
+    const bool clustered = Lp.cluster > 1;
+    bool joined = !clustered;
+    auto join_cluster = [&]() {
+      cluster_wait();
+      cluster_arrive();
+      cluster_wait();
+      cluster_arrive();
+      cluster_wait();
+      joined = true;
+    };
+    if (clustered) cluster_arrive();  // phase 0
     for (int t0 = t_begin; t0 < t_end && ok;) {
       const int j = job_of(L, t0);
       const GemvJob& J = L.jobs[j];
@@ -480,6 +660,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
         const Geo G = T == kMaxT ? G0 : geo(J.K, T);
         for (int s = 0; s < G.ns; ++s, ++st) {
           const int slot = pslot;
+          if (st >= NS && !joined) join_cluster();
           if (st >= NS && !mbar_wait(&empty[slot], pphase ^ 1, L.status)) {
             ok = false;
             break;
@@ -504,6 +685,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
       }
       t0 = seg_end;
     }
+    if (!joined) join_cluster();
     if (lane == 0) prefetch_next(L);
     // every copy into this CTA's shared memory lands before the CTA exits
     for (int i = (st > NS ? st - NS : 0); i < st; ++i) mbar_wait(&full[i % NS], (i / NS) & 1, L.status);
@@ -513,9 +695,15 @@ __global__ void __launch_bounds__(kSThreads, 1)
   // ---------------- consumers: distinct inputs and tile groups of the CTA
   named_bar_sync(2, kSThreads);  // the producer has copied the job table and set up the ring
   const int t_begin = L.cta_tile[blockIdx.x], t_end = L.cta_tile[blockIdx.x + 1];
-  const int j_lo = job_of(L, t_begin);
+  // the inputs quantised here: those of this CTA's tiles, or in a cluster
+  // those of all its CTAs' tiles (the same table in every CTA of it)
+  const int cs = L.cluster > 1 ? L.cluster : 1;
+  const int rank = cs > 1 ? (int)cluster_rank() : 0;
+  const int c0 = (int)blockIdx.x - rank;
+  const int u_begin = L.cta_tile[c0], u_end = L.cta_tile[c0 + cs];
+  const int j_lo = job_of(L, u_begin);
   if (threadIdx.x == 0) {
-    const int j_hi = job_of(L, t_end - 1);
+    const int j_hi = job_of(L, u_end - 1);
     int nin = 0, xo = 0, uo = 0;
     for (int j = j_lo; j <= j_hi; ++j) {
       const GemvJob& J = L.jobs[j];
@@ -540,12 +728,16 @@ __global__ void __launch_bounds__(kSThreads, 1)
     S.nin = nin;
   }
   named_bar_sync(1, kCW * 32);
+  if (cs > 1) cluster_arrive();  // phase 0: this CTA's table is ready
   pdl_launch_dependents();
 
   int8_t* xq = reinterpret_cast<int8_t*>(smem + P.xq);
   int* red = reinterpret_cast<int*>(smem + P.red);
   pdl_wait();
-  stream_prologue<B>(S, xq, warp, lane);
+  if (cs > 1)
+    stream_prologue_cluster<B>(S, xq, warp, lane, cs, rank);
+  else
+    stream_prologue<B>(S, xq, warp, lane);
 
   // tile groups; with L.defer the partial sums of all of them stay in shared
   // memory and are reduced after the last one (one CTA barrier), otherwise
@@ -664,12 +856,58 @@ cudaError_t launch_stream_t(const GemvLaunch& L, int grid, size_t smem, cudaStre
   cfg.blockDim = dim3(kSThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (L.cluster > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = (unsigned)L.cluster;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<B>, L);
+}
+
+// CTAs of gemv_stream_kernel<B> that run at once in clusters of kClusterCtas
+// (one CTA per SM; clusters do not span GPCs, so this can be below the SM
+// count). 0 when clusters cannot be launched.
+template <int B>
+int cluster_ctas_t() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (dev < 64 && cache[dev]) return cache[dev] > 0 ? cache[dev] : 0;
+  int n = -1;
+  const int budget = stream_smem_budget();
+  if (budget > 0 &&
+      cudaFuncSetAttribute(gemv_stream_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, budget) ==
+          cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kClusterCtas, 1, 1);
+    cfg.blockDim = dim3(kSThreads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)budget;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kClusterCtas;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemv_stream_kernel<B>, &cfg) == cudaSuccess &&
+        clusters > 0)
+      n = clusters * kClusterCtas;
+  }
+  cudaGetLastError();  // a refused query leaves no error behind
+  if (dev < 64) cache[dev] = n;
+  return n > 0 ? n : 0;
 }
 
 }  // namespace
@@ -688,25 +926,54 @@ bool gemv_stream_prepare(GemvLaunch& L, int num_sms, int* grid_out, size_t* smem
   L.ntiles = tiles;
   if (tiles <= 0) return true;
   if (tiles > 65535) return false;
-  int grid = tiles < num_sms ? tiles : num_sms;
-  if (grid > kMaxGemvCtas) grid = kMaxGemvCtas;
-  balance_tiles(L, grid, 64);
-  // no empty CTA: the split fills CTAs from the first one on
-  while (grid > 1 && L.cta_tile[grid - 1] >= L.cta_tile[grid]) --grid;
-  // int8 codes one CTA keeps: the distinct inputs of the jobs its tiles touch
-  int xcap = 0;
-  for (int c = 0; c < grid; ++c) {
+  // int8 codes of the distinct inputs of the jobs that tiles [t0, t1) touch
+  auto codes_of = [&](int t0, int t1) {
     int jlo = 0, jhi = 0;
-    while (jlo + 1 < L.njobs && L.cta_tile[c] >= L.jobs[jlo + 1].tile_begin) ++jlo;
-    while (jhi + 1 < L.njobs && L.cta_tile[c + 1] - 1 >= L.jobs[jhi + 1].tile_begin) ++jhi;
+    while (jlo + 1 < L.njobs && t0 >= L.jobs[jlo + 1].tile_begin) ++jlo;
+    while (jhi + 1 < L.njobs && t1 - 1 >= L.jobs[jhi + 1].tile_begin) ++jhi;
     int x = 0;
     for (int j = jlo; j <= jhi; ++j) {
       bool seen = false;
       for (int i = jlo; i < j; ++i) seen |= L.jobs[i].xf == L.jobs[j].xf && L.jobs[i].K == L.jobs[j].K;
       if (!seen) x += L.B * L.jobs[j].K;
     }
+    return x;
+  };
+  // the split over single CTAs; the largest share of codes a CTA quantises
+  auto split = [&](int grid_max, int cs) {
+    int grid = tiles < grid_max ? tiles : grid_max;
+    balance_tiles(L, grid, 64);
+    // no empty CTA beyond the last cluster: the split fills CTAs from the first one on
+    while (grid > 1 && L.cta_tile[grid - 1] >= L.cta_tile[grid]) --grid;
+    const int used = grid;
+    grid = (grid + cs - 1) / cs * cs;  // <= grid_max, a multiple of cs
+    for (int c = used + 1; c <= grid; ++c) L.cta_tile[c] = L.cta_tile[used];  // empty CTAs
+    return grid;
+  };
+  int cs = 1;
+  int grid = split(num_sms < kMaxGemvCtas ? num_sms : kMaxGemvCtas, 1);
+  int xcap = 0;
+  for (int c = 0; c < grid; ++c) {
+    const int x = codes_of(L.cta_tile[c], L.cta_tile[c + 1]);
     xcap = x > xcap ? x : xcap;
   }
+  if (xcap / 128 > OUROQ_STREAM_CLUSTER_MIN_UNITS && grid >= kClusterCtas) {
+    // large inputs: quantise each once per cluster instead of once per CTA
+    int gmax = L.B == 1 ? cluster_ctas_t<1>() : cluster_ctas_t<2>();
+    if (gmax > num_sms) gmax = num_sms;
+    if (gmax > kMaxGemvCtas) gmax = kMaxGemvCtas;
+    gmax -= gmax % kClusterCtas;
+    if (gmax >= kClusterCtas) {
+      cs = kClusterCtas;
+      grid = split(gmax, cs);
+      xcap = 0;
+      for (int c = 0; c < grid; c += cs) {
+        const int x = codes_of(L.cta_tile[c], L.cta_tile[c + cs]);
+        xcap = x > xcap ? x : xcap;
+      }
+    }
+  }
+  L.cluster = cs;
   L.xcap = xcap;
   // tile groups of each CTA (runs of up to kMaxT tiles of one matrix)
   int maxg = 0;

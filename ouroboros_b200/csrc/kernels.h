@@ -97,6 +97,7 @@ struct GemvLaunch {
   const uint8_t* pf_ptr[kMaxGemvJobs];
   uint32_t pf_bytes[kMaxGemvJobs];
   int npf;
+  int cluster;              // gemv_stream_kernel: CTAs per cluster sharing the quantisation
   // CTA c owns tiles [cta_tile[c], cta_tile[c+1]): ranges balanced by weight
   // bytes on the host, so the kernel does no 64-bit division at start-up.
   uint16_t cta_tile[kMaxGemvCtas + 1];

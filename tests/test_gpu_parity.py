@@ -278,6 +278,38 @@ def test_fused_wide_rows_exact(ctx, oracle, M, K, B):
     w.free()
 
 
+@pytest.mark.parametrize("B", [1, 2])
+def test_fused_group_cluster_shared_quantisation(ctx, oracle, B):
+    # rows of 28672 and 12800 values: the one-token GEMV quantises them once per
+    # cluster of CTAs (each CTA a quarter of the units, codes, maxima and sums
+    # exchanged through distributed shared memory). Clusters here mix inputs
+    # (x0 and x1, x0 and x2) and the last one holds an empty CTA (11 tiles);
+    # token 1 of x1 is all zeros (scale 0) and x0 carries outliers
+    import torch
+    shapes = [(100, 28672, 0), (70, 12800, 1), (40, 28672, 0), (33, 384, 2)]
+    xs = [oracle.outliers(600, oracle.normals(601, B * 28672), 0.01, 20.0).reshape(B, 28672),
+          oracle.normals(602, B * 12800).reshape(B, 12800),
+          oracle.normals(603, B * 384).reshape(B, 384)]
+    if B == 2:
+        xs[1][1] = 0.0
+    xd = [dev(x) for x in xs]
+    ws_, ys, want = [], [], []
+    for i, (M, K, xi) in enumerate(shapes):
+        packed, wsc, _ = tern_case(oracle, M, K, 1, seed=610 + i)
+        qr, sr = oracle.quantize_act(xs[xi])
+        want.append(oracle.gemm_tern2(packed, M, K, wsc, qr, sr)[1])
+        ws_.append(ctx.upload(oq.TERNARY2, packed, M, K, w_scale=wsc))
+        ys.append(torch.empty((B, M), dtype=torch.float32, device="cuda"))
+    n0 = ctx.launch_count()
+    ctx.gemm_group_f32act(ws_, [xd[xi] for _, _, xi in shapes], ys)
+    assert ctx.launch_count() - n0 == 1
+    for y, yr in zip(ys, want):
+        assert np.array_equal(host(y), yr)
+    for w in ws_:
+        w.free()
+    ctx.check_device()
+
+
 def test_fused_group_rejects_oversized_activations(ctx, oracle):
     import torch
     packed, wsc, _ = tern_case(oracle, 64, 28672, 1, seed=3)
