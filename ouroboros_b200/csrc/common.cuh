@@ -145,6 +145,19 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 __device__ __forceinline__ void named_bar_sync(unsigned id, unsigned nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// from this CTA's shared memory to `dst` in another CTA of the cluster,
+// counted in bytes on the mbarrier `bar` of that CTA (both are
+// shared::cluster addresses, from peer_smem).
+__device__ __forceinline__ void bulk_s2s_cluster(uint32_t dst, const void* src, uint32_t bytes,
+                                                 uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "r"(smem_u32(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 // Thread-block clusters: this CTA's rank and the cluster's CTA count.
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -169,6 +182,7 @@ __device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
 // Every thread of every CTA of the cluster: stores before it (shared memory
 // of any CTA of the cluster included) are visible to all after it.
 __device__ __forceinline__ void cluster_sync_all() {
+  __syncwarp();  // .aligned: the whole warp executes it together
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 

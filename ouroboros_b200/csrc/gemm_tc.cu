@@ -28,6 +28,17 @@
 // cost a 4x write plus a 4x MMA read per packed byte, more shared-memory
 // bandwidth than the HBM stream feeds.
 // The accumulator is D[row][token] = sum_k c * q; acc = D - sum_k q.
+//
+// Split K. A CTA's rate is set by the MMAs it issues: on B200 one
+// tcgen05.mma of kind::i8 (M = 128, K = 32) takes 110-160 clocks alone at any
+// N from 16 to 256 (one or several accumulators), about 210 (N = 16) to 390
+// (N = 256) clocks inside this kernel. When the (row tile x token tile) grid
+// leaves SMs idle, the launcher splits
+// K over a cluster of 2 or 4 CTAs (grid z): each accumulates its K range,
+// then CTAs z > 0 stage their int32 partials D and token sums in their own
+// shared memory and send them to CTA 0's with one bulk shared-to-shared copy
+// each (completion counted on an mbarrier of CTA 0), and CTA 0 adds them and
+// writes the outputs. Integer sums: exact in any order.
 // Every wait is bounded and reports through the status word.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -148,7 +159,7 @@ struct TcPlan {
 __host__ __device__ inline TcPlan tc_plan(int N, int stages) {
   TcPlan p;
   p.ks = N <= 64 ? 512 : (N <= 128 ? 256 : 128);
-  p.bars = 0;    // full[6], sfree[6], afull[8], afree[8], accfull
+  p.bars = 0;    // full[6], sfree[6], afull[8], afree[8], accfull, xfull
   p.tmem = 256;  // allocated tensor-memory address
   p.qsum = 512;  // int [256]
   p.stage0 = 2048;
@@ -172,6 +183,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* afull = sfree + kMaxTcStages;
   uint64_t* afree = afull + kTmemABufs;
   uint64_t* accfull = afree + kTmemABufs;
+  uint64_t* xfull = accfull + 1;  // split K, CTA 0: the other CTAs' partials landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + pl.tmem);
   int* qsum = reinterpret_cast<int*>(smem + pl.qsum);
   uint8_t* stages = smem + pl.stage0;
@@ -181,7 +193,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // token tile of this CTA: [tok_base, tok_base + nv), at most P.N tokens
   const int tok_base = P.tok0 + blockIdx.y * P.N;
   const int nv = P.nvalid - blockIdx.y * P.N < P.N ? P.nvalid - blockIdx.y * P.N : P.N;
-  const int nstages = (P.K + KS - 1) / KS;  // the last stage may be shorter
+  // this CTA's K range [kb, ke) (split K: CTA z of the cluster takes the
+  // z-th of Z even parts, in whole 128-k sub-blocks, never empty), walked in
+  // stages of KS (the last one may be shorter)
+  const int Z = P.ksplit > 1 ? P.ksplit : 1;
+  const int z = Z > 1 ? (int)blockIdx.z : 0;
+  const int nsb = P.K / kSliceK;
+  const int kb = (int)((long long)nsb * z / Z) * kSliceK;
+  const int ke = (int)((long long)nsb * (z + 1) / Z) * kSliceK;
+  const int nstages = (ke - kb + KS - 1) / KS;
   const int C = P.K / 64;  // 16-byte chunks per packed row
 
   if (threadIdx.x == 0) {
@@ -194,6 +214,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&afree[i], 1);
     }
     mbar_init(accfull, 1);
+    mbar_init(xfull, 1);
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
@@ -212,17 +233,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int ntiles = (P.M + kTileRows - 1) / kTileRows - row0 / kTileRows;
       const int vt = ntiles < 4 ? ntiles : 4;
       bool waited = false;
-      for (int s = 0; s < nstages; ++s) {
-        const int slot = s % S;
-        if (s >= S && !mbar_wait(&sfree[slot], ((s / S) - 1) & 1, P.status)) break;
-        const int ks = P.K - s * KS < KS ? P.K - s * KS : KS;
+      for (int i = 0; i < nstages; ++i) {
+        const int k0 = kb + i * KS;
+        const int slot = i % S;
+        if (i >= S && !mbar_wait(&sfree[slot], ((i / S) - 1) & 1, P.status)) break;
+        const int ks = ke - k0 < KS ? ke - k0 : KS;
         const int SUB = ks / kSliceK;
         const uint32_t wbytes = (uint32_t)ks * 8u;  // per 32-row tile
         uint8_t* st = stages + (size_t)slot * pl.stage_bytes;
         mbar_arrive_expect_tx(&full[slot], wbytes * (uint32_t)vt + (uint32_t)(P.N * ks));
         for (int t = 0; t < vt; ++t) {
           const size_t tile = (size_t)(row0 / kTileRows + t);
-          bulk_g2s_stream(st + t * (KS * 8), P.w + (tile * C + (size_t)s * (KS / 64)) * 512, wbytes,
+          bulk_g2s_stream(st + t * (KS * 8), P.w + (tile * C + (size_t)(k0 / 64)) * 512, wbytes,
                           &full[slot], pol);
         }
         if (!waited) {
@@ -231,7 +253,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         for (int u = 0; u < SUB; ++u)
           tma_load_2d(st + pl.act_off + (uint32_t)u * (uint32_t)P.N * 128u, &act_map,
-                      s * KS + u * kSliceK, tok_base, &full[slot]);
+                      k0 + u * kSliceK, tok_base, &full[slot]);
       }
     }
     __syncwarp();
@@ -243,11 +265,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                              ((uint32_t)(kTcRows >> 4) << 24);
       bool ok = true;
       int g = 0;
-      for (int s = 0; s < nstages && ok; ++s) {
-        const int slot = s % S;
-        ok = mbar_wait(&full[slot], (s / S) & 1, P.status);
+      for (int i = 0; i < nstages && ok; ++i) {
+        const int k0 = kb + i * KS;
+        const int slot = i % S;
+        ok = mbar_wait(&full[slot], (i / S) & 1, P.status);
         uint8_t* st = stages + (size_t)slot * pl.stage_bytes;
-        const int SUB = (P.K - s * KS < KS ? P.K - s * KS : KS) / kSliceK;
+        const int SUB = (ke - k0 < KS ? ke - k0 : KS) / kSliceK;
         for (int u = 0; u < SUB && ok; ++u, ++g) {
           const int b = g % kTmemABufs;
           ok = mbar_wait(&afull[b], (g / kTmemABufs) & 1, P.status);
@@ -260,7 +283,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             //    1024 B apart (SBO); K block mb starts 32 B into the row
             const uint64_t bd = smem_desc(act + mb * 32, 16, 1024, 2);
             mma_i8_ts(tmem, tmem + kTmemA0 + (uint32_t)b * 32u + (uint32_t)mb * 8u, bd, idesc,
-                      (s > 0 || u > 0 || mb > 0) ? 1u : 0u);
+                      (i > 0 || u > 0 || mb > 0) ? 1u : 0u);
           }
           mma_commit(&afree[b]);  // the A buffer may be refilled once these MMAs finished
         }
@@ -283,15 +306,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int e = ((warp - 2) & 3) * 32 + lane;
     bool ok = true;
     int g = 0;
-    for (int s = 0; s < nstages; ++s) {
-      const int slot = s % S;
-      const int SUB = (P.K - s * KS < KS ? P.K - s * KS : KS) / kSliceK;
+    for (int i = 0; i < nstages; ++i) {
+      const int k0 = kb + i * KS;
+      const int slot = i % S;
+      const int SUB = (ke - k0 < KS ? ke - k0 : KS) / kSliceK;
       // a stage holds a sub-block of this half unless it has one sub-block of the other
       if (SUB == 1 && ((g & 1) != h)) {
         ++g;
         continue;
       }
-      if (ok) ok = mbar_wait(&full[slot], (s / S) & 1, P.status);
+      if (ok) ok = mbar_wait(&full[slot], (i / S) & 1, P.status);
       const uint8_t* st = stages + (size_t)slot * pl.stage_bytes;
       const uint8_t* src = st + (r >> 5) * (KS * 8) + (r & 31) * 16;
       for (int u = 0; u < SUB; ++u, ++g) {
@@ -340,13 +364,70 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (e < P.N) atomicAdd(&qsum[e], qs0);
     if (e + 128 < P.N) atomicAdd(&qsum[e + 128], qs1);
     named_bar_sync(1, kXWarps * 32);
-    // ---- epilogue: D[row][token] from tensor memory, 32-column chunks split by half
     if (ok) ok = mbar_wait(accfull, 0, P.status);
     tc_fence_after();
+  }
+  // ---- split K: the partials of CTA z > 0 go to slot z - 1 of CTA 0's stage
+  // area. A slot: D as [row][NP] int32 (NP = N + 4: rows 16-byte aligned,
+  // spread over the banks), then the token sums [N].
+  const int NP = P.N + 4;
+  const uint32_t slot_bytes = (uint32_t)(kTcRows * NP + P.N) * 4u;
+  if (Z > 1) {
+    if (z == 0 && threadIdx.x == 0) mbar_arrive_expect_tx(xfull, (uint32_t)(Z - 1) * slot_bytes);
+    cluster_sync_all();  // every CTA's MMAs are done: the stage areas are free
+    if (z > 0 && warp >= 2) {
+      const int q = warp & 3, h = (warp - 2) >> 2, r = q * 32 + lane;
+      const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+      int* stg = reinterpret_cast<int*>(stages);
+      for (int j0 = h * 32; j0 < P.N; j0 += 64) {
+        uint32_t d[32];
+        tmem_ld32(tmem + lane_base + (uint32_t)j0, d);
+        uint4* dst = reinterpret_cast<uint4*>(stg + r * NP + j0);
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+          if (j0 + 4 * v < P.N) dst[v] = make_uint4(d[4 * v], d[4 * v + 1], d[4 * v + 2], d[4 * v + 3]);
+      }
+      const int e = ((warp - 2) & 3) * 32 + lane;
+      if (h == 0)
+        for (int t = e; t < P.N; t += 128) stg[kTcRows * NP + t] = qsum[t];
+      fence_proxy_async_smem();  // visible to the bulk copy
+      named_bar_sync(1, kXWarps * 32);
+      if (warp == 2 && lane == 0)
+        bulk_s2s_cluster(peer_smem(stages + (size_t)(z - 1) * slot_bytes, 0), stages, slot_bytes,
+                         peer_smem(xfull, 0));
+    }
+  }
+  if (z == 0 && warp >= 2) {
+    // ---- epilogue: D[row][token] from tensor memory (plus the other CTAs'
+    // partials), 32-column chunks split by half
+    const int q = warp & 3, h = (warp - 2) >> 2, r = q * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const int* part = reinterpret_cast<const int*>(stages);
+    if (Z > 1) {
+      mbar_wait(xfull, 0, P.status);
+      const int e = ((warp - 2) & 3) * 32 + lane;
+      if (h == 0)
+        for (int t = e; t < P.N; t += 128)
+          for (int zz = 1; zz < Z; ++zz) qsum[t] += part[(size_t)(zz - 1) * (slot_bytes / 4) + kTcRows * NP + t];
+      named_bar_sync(1, kXWarps * 32);
+    }
     const int row = row0 + r;
     for (int j0 = h * 32; j0 < P.N; j0 += 64) {
       uint32_t d[32];
       tmem_ld32(tmem + lane_base + (uint32_t)j0, d);
+      for (int zz = 1; zz < Z; ++zz) {
+        const uint4* src =
+            reinterpret_cast<const uint4*>(part + (size_t)(zz - 1) * (slot_bytes / 4) + r * NP + j0);
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+          if (j0 + 4 * v < P.N) {
+            const uint4 pv = src[v];
+            d[4 * v] += pv.x;
+            d[4 * v + 1] += pv.y;
+            d[4 * v + 2] += pv.z;
+            d[4 * v + 3] += pv.w;
+          }
+      }
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const int n = j0 + j;
@@ -360,6 +441,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   }
+  // CTA 0 has read every partial (its copies completed): the other CTAs'
+  // shared memory may go
+  if (Z > 1) cluster_sync_all();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -376,16 +460,33 @@ bool gemm_tc_supported(int fmt, int M, int K, int B) {
   return fmt == kTern2 && M > 0 && K % kSliceK == 0 && B >= 1;
 }
 
-int gemm_tc_tile_n(int M, int B, int num_sms) {
-  // Largest token tile (multiple of 16, <= 256) that still gives the grid
-  // about one CTA per SM; each halving doubles the expansion work per MMA, so
-  // stop at 32.
-  const int mt = (M + kTcRows - 1) / kTcRows;
-  int N = (B < 256 ? B : 256);
-  N = (N + 15) / 16 * 16;
-  while (N > 32 && (long)mt * ((B + N - 1) / N) < (long)num_sms * 4 / 5) N = ((N / 2) + 15) / 16 * 16;
-  return N < 16 ? 16 : N;
+namespace {
+// Clusters of `cs` CTAs of gemm_tc_kernel (one per SM) that fit at once; 0
+// when clusters cannot be launched.
+int tc_cluster_capacity(int cs, size_t smem) {
+  static int cache[64][3] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const int k = cs == 2 ? 0 : (cs == 4 ? 1 : 2);
+  if (dev < 64 && cache[dev][k]) return cache[dev][k] > 0 ? cache[dev][k] : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, (unsigned)cs);
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)cs;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel, &cfg) != cudaSuccess) n = 0;
+  cudaGetLastError();
+  if (dev < 64) cache[dev][k] = n > 0 ? n : -1;
+  return n;
 }
+}  // namespace
 
 cudaError_t launch_gemm_tc(const TcLaunch& L0, const int8_t* q, int Btot, int smem_optin,
                            int num_sms, cudaStream_t s) {
@@ -395,11 +496,67 @@ cudaError_t launch_gemm_tc(const TcLaunch& L0, const int8_t* q, int Btot, int sm
   if (e != cudaSuccess) return e;
   if (L0.nvalid <= 0) return cudaSuccess;
   TcLaunch L = L0;
-  L.N = gemm_tc_tile_n(L.M, L.nvalid, num_sms);
-  int stages = kMaxTcStages;
-  while (stages > 2 && tc_plan(L.N, stages).total > (uint32_t)smem_optin - 2048u) --stages;
+  int dev = 0, per_sm = 0;
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  if (e != cudaSuccess) return e;
+  // One CTA per SM, always: every CTA allocates all 512 tensor-memory
+  // columns, so a second CTA on the SM would wait in tcgen05.alloc until the
+  // first one ends -- forever, if both belong to one cluster and the first
+  // waits for it at a cluster barrier. More than half of the SM's shared
+  // memory per CTA rules that out.
+  const size_t smem_floor = (size_t)per_sm / 2 + 1024;
+  if (smem_floor > (size_t)smem_optin) return cudaErrorInvalidValue;
+  auto stages_for = [&](int N) {
+    int st = kMaxTcStages;
+    while (st > 2 && tc_plan(N, st).total > (uint32_t)smem_optin - 2048u) --st;
+    return st;
+  };
+  // Token tile N (even tiles: N = ceil(B / nt) rounded up to 16) and K split
+  // Z: the pair with the smallest modelled time. Model (clocks, from traces of
+  // this kernel on B200): waves x (K / 32 / Z MMAs x (200 + 0.75 N) + the
+  // split's exchange, 1000 + 30 N (Z - 1)). A split needs a sub-block per
+  // part, room in CTA 0's stage area for the partials, and its clusters
+  // resident at once.
+  const int mt = (L.M + kTcRows - 1) / kTcRows;
+  const int nsb = L.K / kSliceK;
+  double best = -1.0;
+  int bestN = 16, bestZ = 1;
+  for (int nt = 1; nt <= (L.nvalid + 15) / 16; ++nt) {
+    int N = (L.nvalid + nt - 1) / nt;
+    N = (N + 15) / 16 * 16;
+    if (N > 256) continue;
+    if ((L.nvalid + N - 1) / N != nt) continue;  // the same tiling as a smaller nt
+    const int st = stages_for(N);
+    const TcPlan pl = tc_plan(N, st);
+    for (int Z = 1; Z <= 4; Z *= 2) {
+      if (Z > 1) {
+        if (nsb < Z) break;
+        if ((size_t)(Z - 1) * (kTcRows * (N + 4) + N) * 4 > (size_t)st * pl.stage_bytes) break;
+        const long cap = tc_cluster_capacity(Z, smem_floor);
+        if (cap <= 0) break;
+      }
+      const long ctas = (long)mt * nt * Z;
+      const long slots = Z > 1 ? (long)tc_cluster_capacity(Z, smem_floor) * Z : num_sms;
+      const long waves = (ctas + slots - 1) / slots;
+      const double t = (double)waves * ((double)L.K / 32.0 / Z * (200.0 + 0.75 * N) +
+                                        (Z > 1 ? 1000.0 + 30.0 * N * (Z - 1) : 0.0));
+      if (best < 0.0 || t < best) {
+        best = t;
+        bestN = N;
+        bestZ = Z;
+      }
+    }
+  }
+  L.N = bestN;
+  L.ksplit = bestZ;
+  const int stages = stages_for(L.N);
   L.stages = stages;
-  const size_t smem = tc_plan(L.N, stages).total;
+  size_t smem = tc_plan(L.N, stages).total;
+  if (smem < smem_floor) smem = smem_floor;
+  if (smem > (size_t)smem_optin) return cudaErrorInvalidValue;
+  const int nt = (L.nvalid + L.N - 1) / L.N;
   // activations [Btot][K] int8, box 128 B x N rows, 128-byte swizzle, zero fill
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)L.K, (cuuint64_t)Btot};
@@ -410,13 +567,20 @@ cudaError_t launch_gemm_tc(const TcLaunch& L0, const int8_t* q, int Btot, int sm
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
-  // one CTA per (128-row tile, token tile)
-  const dim3 grid((L.M + kTcRows - 1) / kTcRows, (L.nvalid + L.N - 1) / L.N, 1);
+  // one CTA per (128-row tile, token tile, part of K)
+  const dim3 grid(mt, nt, L.ksplit);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kTcThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)L.ksplit;
+  cfg.attrs = attr;
+  cfg.numAttrs = L.ksplit > 1 ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, map, L);
 }
 

@@ -157,14 +157,15 @@ struct TcLaunch {
   int N;              // tokens per CTA tile (multiple of 16, 16..256), filled by the launcher
   int nvalid;         // valid tokens from tok0 (all token tiles)
   int stages;         // filled by the launcher
+  int ksplit;         // CTAs of a cluster splitting K (1, 2 or 4), filled by the launcher
   unsigned* status;
 };
 
 bool gemm_tc_supported(int fmt, int M, int K, int B);
 size_t gemm_tc_smem_bytes(int N, int stages);
 // q: int8 activations [Btot][K] (16-byte aligned rows). One launch; the grid
-// covers (128-row tiles) x (token tiles of gemm_tc_tile_n tokens).
-int gemm_tc_tile_n(int M, int B, int num_sms);
+// covers (128-row tiles) x (token tiles) x (parts of K), sizes chosen by the
+// launcher.
 cudaError_t launch_gemm_tc(const TcLaunch& L, const int8_t* q, int Btot, int smem_optin,
                            int num_sms, cudaStream_t s);
 
