@@ -24,7 +24,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
               "-Xptxas", "-warn-spills", "--threads", "0", "-I", str(ROOT / "include"),
               "-I", str(CSRC)]
-CU_SOURCES = ["quant.cu", "gemv.cu", "gemv_stream.cu", "repack.cu", "gemm_tc.cu", "noalloc.cu", "shard.cu", "refmt.cu", "decode.cu",
+CU_SOURCES = ["quant.cu", "gemv.cu", "gemv_stream.cu", "repack.cu", "gemm_tc.cu", "gemm_sign_tc.cu", "noalloc.cu", "shard.cu", "refmt.cu", "decode.cu",
               "head.cu"]
 CPP_SOURCES = ["api.cpp", "bmts.cpp"]
 

@@ -222,12 +222,29 @@ ouroq_status run_gemv(ouroq_ctx* ctx, GemvLaunch& L, cudaStream_t s) {
   return OUROQ_OK;
 }
 
-// Token batches from this size up run on the tensor cores (ternary weights).
+// Token batches from this size up run on the tensor cores (ternary and sign weights).
 constexpr int kTcMinBatch = 16;
 
 ouroq_status gemm_impl(ouroq_ctx* ctx, const ouroq_weight* w, const int8_t* q, const float* s_x,
                        int B, float* y, int32_t* acc, cudaStream_t s) {
   const int dfmt = w->fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
+  if (dfmt == kSign1 && B >= kTcMinBatch && ctx->use_tc && gemm_sign_tc_supported(w->M, w->K, B)) {
+    TcLaunch L{};
+    L.w = w->w;
+    L.scales = w->scales;
+    L.y = y;
+    L.acc = acc;
+    L.s_x = s_x;
+    L.M = w->M;
+    L.K = w->K;
+    L.ldy = w->M;
+    L.tok0 = 0;
+    L.nvalid = B;
+    L.status = ctx->d_status;
+    CU(ctx, launch_gemm_sign_tc(L, q, B, ctx->smem_optin, s), "sign tensor-core gemm launch");
+    ctx->launches++;
+    return OUROQ_OK;
+  }
   if (B >= kTcMinBatch && ctx->use_tc && gemm_tc_supported(dfmt, w->M, w->K, B)) {
     TcLaunch L{};
     L.w = w->w;

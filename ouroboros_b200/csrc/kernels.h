@@ -147,9 +147,10 @@ cudaError_t launch_repack_scales(const uint16_t* canon, uint16_t* dev, int M, in
 
 // One tensor-core GEMM launch (ternary): 128 weight rows per CTA x N tokens.
 struct TcLaunch {
-  const uint8_t* w;   // tiled device layout (kTern2)
+  const uint8_t* w;   // tiled device layout (kTern2 or kSign1)
+  const uint16_t* scales;  // kSign1: tiled fp16 group scales; else null
   float* y;           // [tokens][ldy]
-  int32_t* acc;       // optional debug [tokens][M]
+  int32_t* acc;       // optional debug: kTern2 [tokens][M]; kSign1 [tokens][M][K/128]
   const float* s_x;   // [tokens]
   float w_scale;
   int M, K, ldy;
@@ -168,6 +169,12 @@ size_t gemm_tc_smem_bytes(int N, int stages);
 // launcher.
 cudaError_t launch_gemm_tc(const TcLaunch& L, const int8_t* q, int Btot, int smem_optin,
                            int num_sms, cudaStream_t s);
+// Sign weights (kSign1) on the tensor cores: one group accumulator per 128 k,
+// the fp32 fold in ascending group order. The grid covers (128-row tiles) x
+// (token tiles of 16, 32 or 64).
+bool gemm_sign_tc_supported(int M, int K, int B);
+cudaError_t launch_gemm_sign_tc(const TcLaunch& L, const int8_t* q, int Btot, int smem_optin,
+                                cudaStream_t s);
 
 // The reference's own shard formats (PTQ1_0 "Tl1", TQ1_0), stored on the device
 // exactly as in the shard (row-major, no repack): fp32 x [B][K] -> y [B][ldy].

@@ -202,6 +202,28 @@ def test_gemm_sign1_c3_batch32(ctx, oracle, M):
     w.free()
 
 
+@pytest.mark.parametrize("M,K,B", [(4096, 4096, 32), (11008, 4096, 32), (300, 384, 17), (77, 128, 16),
+                                   (256, 2176, 40), (128, 512, 100)])
+def test_gemm_sign1_tensor_core(ctx, oracle, M, K, B):
+    # batches from 16 tokens run the sign tensor-core kernel (one launch): the
+    # per-group accumulators and the ascending-group fp32 fold must equal the
+    # oracle's bit for bit; row counts off the 128-row tile, K off the 512-k
+    # stage (a last stage of one group), token tiles of 16 and 32 with padding
+    import torch
+    packed, sc, x = sign_case(oracle, M, K, B, seed=3 * M + K + B)
+    qr, sr = oracle.quantize_act(x, None, 0)
+    accr, yr = oracle.gemm_sign1(packed, sc, M, K, qr, sr)
+    w = ctx.upload(oq.SIGN1G128, packed, M, K, scales=sc)
+    acc = torch.empty((B, M, K // 128), dtype=torch.int32, device="cuda")
+    n0 = ctx.launch_count()
+    y = ctx.gemm(w, dev(qr), dev(sr), acc=acc)
+    assert ctx.launch_count() - n0 == 1
+    assert np.array_equal(host(acc), accr)
+    assert np.array_equal(host(y), yr)
+    ctx.check_device()
+    w.free()
+
+
 # ---------------------------------------------------------------- grouped / host mirrors
 def test_gemm_group_c2_layer(ctx, oracle):
     shapes = [(3840, 2560), (2560, 2560), (6912, 2560), (6912, 2560), (2560, 6912)]
