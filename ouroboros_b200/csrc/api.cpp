@@ -26,6 +26,24 @@
 
 using namespace ouroq;
 
+// A planned stream-GEMV launch (tile split, shared-memory plan) for one set
+// of shapes: planning balances hundreds of tiles on the host (tens of
+// microseconds), so each context keeps the plans of the shapes it saw last.
+// The key is everything gemv_stream_prepare reads besides the pointers: the
+// format, batch, per job M, K and rotation, and which jobs share an input.
+struct StreamPlan {
+  bool used = false, ok = false;
+  int fmt = 0, B = 0, njobs = 0, nsms = 0;
+  int M[ouroq::kMaxGemvJobs], K[ouroq::kMaxGemvJobs], had[ouroq::kMaxGemvJobs],
+      cls[ouroq::kMaxGemvJobs];
+  // results
+  int grid = 0, ntiles = 0, xcap = 0, defer = 0, stages = 0, cluster = 1;
+  size_t smem = 0;
+  int tile_begin[ouroq::kMaxGemvJobs];
+  uint16_t cta_tile[ouroq::kMaxGemvCtas + 1];
+};
+constexpr int kStreamPlans = 16;
+
 struct ouroq_ctx {
   int device = 0;
   int num_sms = 0;
@@ -35,6 +53,8 @@ struct ouroq_ctx {
   bool stream_gemv = true;  // fused one/two-token ternary launches on gemv_stream_kernel
   // weights the next GEMV launch prefetches into L2 (ouroq_set_prefetch)
   std::vector<std::pair<const uint8_t*, uint32_t>> prefetch;
+  StreamPlan plans[kStreamPlans];  // recent stream-GEMV plans, replaced round robin
+  int next_plan = 0;
   std::string err;
   unsigned* d_status = nullptr;
   uint64_t launches = 0;
@@ -204,12 +224,63 @@ ouroq_status run_gemv(ouroq_ctx* ctx, GemvLaunch& L, cudaStream_t s) {
   }
   ctx->prefetch.clear();
   if (L.njobs == 0 || L.B == 0) return OUROQ_OK;
-  if (ctx->stream_gemv) {
-    GemvLaunch S = L;
-    int grid = 0;
-    size_t smem = 0;
-    if (gemv_stream_prepare(S, ctx->num_sms, &grid, &smem)) {
-      CU(ctx, launch_gemv_stream(S, grid, smem, s, ctx->pdl), "gemv launch");
+  if (ctx->stream_gemv && L.fmt == kTern2 && L.fused && !L.norm.w && L.B >= 1 && L.B <= 2) {
+    // the plan of these shapes, from the context's recent plans or made now
+    StreamPlan key;
+    key.fmt = L.fmt;
+    key.B = L.B;
+    key.njobs = L.njobs;
+    key.nsms = ctx->num_sms;
+    for (int j = 0; j < L.njobs; ++j) {
+      key.M[j] = L.jobs[j].M;
+      key.K[j] = L.jobs[j].K;
+      key.had[j] = L.jobs[j].had_block;
+      int c = 0;
+      while (c < j && !(L.jobs[c].xf == L.jobs[j].xf && L.jobs[c].K == L.jobs[j].K)) ++c;
+      key.cls[j] = c;
+    }
+    auto same = [&](const StreamPlan& p) {
+      if (!p.used || p.fmt != key.fmt || p.B != key.B || p.njobs != key.njobs || p.nsms != key.nsms)
+        return false;
+      for (int j = 0; j < key.njobs; ++j)
+        if (p.M[j] != key.M[j] || p.K[j] != key.K[j] || p.had[j] != key.had[j] || p.cls[j] != key.cls[j])
+          return false;
+      return true;
+    };
+    StreamPlan* plan = nullptr;
+    for (StreamPlan& p : ctx->plans)
+      if (same(p)) plan = &p;
+    if (!plan) {
+      GemvLaunch S = L;
+      int grid = 0;
+      size_t smem = 0;
+      plan = &ctx->plans[ctx->next_plan];
+      ctx->next_plan = (ctx->next_plan + 1) % kStreamPlans;
+      *plan = key;
+      plan->used = true;
+      plan->ok = gemv_stream_prepare(S, ctx->num_sms, &grid, &smem);
+      if (plan->ok) {
+        plan->grid = grid;
+        plan->smem = smem;
+        plan->ntiles = S.ntiles;
+        plan->xcap = S.xcap;
+        plan->defer = S.defer;
+        plan->stages = S.stages;
+        plan->cluster = S.cluster;
+        for (int j = 0; j < L.njobs; ++j) plan->tile_begin[j] = S.jobs[j].tile_begin;
+        std::memcpy(plan->cta_tile, S.cta_tile, sizeof(plan->cta_tile));
+      }
+    }
+    if (plan->ok) {
+      GemvLaunch S = L;
+      S.ntiles = plan->ntiles;
+      S.xcap = plan->xcap;
+      S.defer = plan->defer;
+      S.stages = plan->stages;
+      S.cluster = plan->cluster;
+      for (int j = 0; j < L.njobs; ++j) S.jobs[j].tile_begin = plan->tile_begin[j];
+      std::memcpy(S.cta_tile, plan->cta_tile, sizeof(S.cta_tile));
+      CU(ctx, launch_gemv_stream(S, plan->grid, plan->smem, s, ctx->pdl), "gemv launch");
       if (S.ntiles > 0) ctx->launches++;
       return OUROQ_OK;
     }

@@ -6,7 +6,7 @@
 // wmat_batched, cluster/src/infer/qwen35.rs:810-812, infer/mod.rs:152-167;
 // ops::matmul_tl1, ops.rs:162-215): K activation columns share each weight
 // row. Arithmetic: this library's sign form, bit-identical to the CPU oracle
-// (oracle/oracle.c, sign_rows): per 128-k group g,
+// (oracle/oracle.h, the sign GEMM): per 128-k group g,
 //   acc_g = sum_{k in g} (bit ? +1 : -1) * q_k           (exact int32)
 //   y = (sum over g ascending of fp32(acc_g) * scale_g) * s_x   (fp32, in order)
 //
