@@ -279,6 +279,93 @@ __global__ void __launch_bounds__(kTq1Threads) tq1_matvec_kernel(const __grid_co
   }
 }
 
+// The same K-column order with each group's trits decoded once per row for
+// all the columns of a block (up to kTl1BlkCols at a time): thread = (row,
+// lane j), lane j carrying a[j] and b[j] of every column of the block (lane 0
+// also the tail), the four lanes of a row combined by shuffles at the end --
+// the same additions in the same order as tl1_columns_kernel, per column.
+// x of the block sits in shared memory column-interleaved, a chunk of groups
+// at a time, so one 16-byte load gives four columns' x of one element.
+constexpr int kTl1BlkCols = 8;
+constexpr int kTl1BlkRows = 64;
+constexpr int kTl1BlkThreads = kTl1BlkRows * 4;
+constexpr int kTl1BlkChunk = 8;  // groups of x staged at a time (32 KB)
+
+__global__ void __launch_bounds__(kTl1BlkThreads) tl1_colblock_kernel(const __grid_constant__ RefLaunch P) {
+  __shared__ __align__(16) float xs[kTl1BlkChunk * 128 * kTl1BlkCols];
+  const int G = P.K / 128;
+  const int c0 = blockIdx.y * kTl1BlkCols;
+  const int nc = P.B - c0 < kTl1BlkCols ? P.B - c0 : kTl1BlkCols;
+  const int r = threadIdx.x >> 2, j = threadIdx.x & 3;
+  const int row = blockIdx.x * kTl1BlkRows + r;
+  const bool live = row < P.M;
+  float a[kTl1BlkCols], bv[kTl1BlkCols], tail[kTl1BlkCols];
+#pragma unroll
+  for (int c = 0; c < kTl1BlkCols; ++c) a[c] = bv[c] = tail[c] = 0.0f;
+  for (int g0 = 0; g0 < G; g0 += kTl1BlkChunk) {
+    const int ng = G - g0 < kTl1BlkChunk ? G - g0 : kTl1BlkChunk;
+    __syncthreads();  // the previous chunk's x is no longer read
+    for (int i = threadIdx.x; i < ng * 128 * kTl1BlkCols; i += kTl1BlkThreads) {
+      const int e = i / kTl1BlkCols, c = i - e * kTl1BlkCols;
+      xs[i] = c < nc ? P.x[(size_t)(c0 + c) * P.K + (size_t)g0 * 128 + e] : 0.0f;
+    }
+    __syncthreads();
+    if (!live) continue;
+    for (int gi = 0; gi < ng; ++gi) {
+      const uint32_t* gw = reinterpret_cast<const uint32_t*>(P.w + ((size_t)row * G + g0 + gi) * 28);
+      uint32_t wd[7];
+#pragma unroll
+      for (int i = 0; i < 7; ++i) wd[i] = __ldg(gw + i);
+      const float d = __half2float(__ushort_as_half((unsigned short)(wd[6] >> 16)));
+      const float* xg = xs + gi * 128 * kTl1BlkCols;
+      // lane j's bytes: qs[j + 4i] = byte j of word i, i = 0..5
+      uint32_t q[6];
+#pragma unroll
+      for (int i = 0; i < 6; ++i) q[i] = (wd[i] >> (8 * j)) & 0xFFu;
+      auto apply = [&](uint32_t digit, int e, float* acc) {
+        const float t = digit == 0u ? -1.0f : (digit == 1u ? 0.0f : 1.0f);
+        const float td = __fmul_rn(t, d);
+        const float4* xp = reinterpret_cast<const float4*>(xg + e * kTl1BlkCols);
+        const float4 x0 = xp[0], x1 = xp[1];
+        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int c = 0; c < kTl1BlkCols; ++c) acc[c] = __fadd_rn(__fmul_rn(td, xv[c]), acc[c]);
+      };
+#pragma unroll 1
+      for (int n = 0; n < 5; ++n) {
+        apply(next_digit(&q[0]), n * 16 + j, a);
+        apply(next_digit(&q[1]), n * 16 + 4 + j, bv);
+        apply(next_digit(&q[2]), n * 16 + 8 + j, a);
+        apply(next_digit(&q[3]), n * 16 + 12 + j, bv);
+        apply(next_digit(&q[4]), 80 + n * 8 + j, a);
+        apply(next_digit(&q[5]), 80 + n * 8 + 4 + j, bv);
+      }
+      if (j == 0) {
+        uint32_t qh[2] = {wd[6] & 0xFFu, (wd[6] >> 8) & 0xFFu};
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+#pragma unroll
+          for (int m = 0; m < 2; ++m) apply(next_digit(&qh[m]), 120 + n * 2 + m, tail);
+      }
+    }
+  }
+  // hsum(a) = (a0 + a2) + (a1 + a3) over the lanes of the row, likewise b
+  const unsigned lanes = 0xffffffffu;
+  const int base = (threadIdx.x & 31) & ~3;
+#pragma unroll
+  for (int c = 0; c < kTl1BlkCols; ++c) {
+    const float a1 = __shfl_sync(lanes, a[c], base + 1), a2 = __shfl_sync(lanes, a[c], base + 2),
+                a3 = __shfl_sync(lanes, a[c], base + 3);
+    const float b1 = __shfl_sync(lanes, bv[c], base + 1), b2 = __shfl_sync(lanes, bv[c], base + 2),
+                b3 = __shfl_sync(lanes, bv[c], base + 3);
+    if (j == 0 && live && c < nc) {
+      const float ha = __fadd_rn(__fadd_rn(a[c], a2), __fadd_rn(a1, a3));
+      const float hb = __fadd_rn(__fadd_rn(bv[c], b2), __fadd_rn(b1, b3));
+      P.y[(size_t)(c0 + c) * P.ldy + row] = __fadd_rn(tail[c], __fadd_rn(ha, hb));
+    }
+  }
+}
+
 }  // namespace
 
 size_t tl1_smem_bytes(int K, int R) {
@@ -325,6 +412,13 @@ cudaError_t launch_refmt_matvec(const RefLaunch& P, int num_sms, cudaStream_t s)
 cudaError_t launch_tl1_columns(const RefLaunch& P, cudaStream_t s) {
   if (P.M <= 0 || P.B <= 0) return cudaSuccess;
   if (P.fmt != kPtq1) return cudaErrorInvalidValue;
+  // from two columns on, decode each group once for a block of up to eight
+  if (P.B >= 2) {
+    const dim3 grid((unsigned)((P.M + kTl1BlkRows - 1) / kTl1BlkRows),
+                    (unsigned)((P.B + kTl1BlkCols - 1) / kTl1BlkCols), 1);
+    tl1_colblock_kernel<<<grid, kTl1BlkThreads, 0, s>>>(P);
+    return cudaGetLastError();
+  }
   const dim3 grid((unsigned)((P.M + kTl1ColRows - 1) / kTl1ColRows), 1, 1);
   tl1_columns_kernel<<<grid, kTl1ColThreads, 0, s>>>(P);
   return cudaGetLastError();

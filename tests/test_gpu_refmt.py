@@ -109,6 +109,20 @@ def test_tl1_k_columns(ctx, oracle):
     w.free()
 
 
+@pytest.mark.parametrize("out_len,in_len,k", [(130, 2560, 9), (64, 1152, 2), (33, 128, 8)])
+def test_tl1_k_columns_blocks(ctx, oracle, out_len, in_len, k):
+    # from two columns on, the K-column kernel decodes each group once for up
+    # to eight columns (a second block of one column at k = 9, x staged in
+    # chunks of eight groups, rows off the 64-row tile): still matmul_tl1's
+    # order bit for bit
+    payload = tl1_payload(oracle, out_len, in_len, seed=out_len + k)
+    x = oracle.normals(in_len + k, k * in_len).reshape(k, in_len)
+    w = ctx.upload(oq.PTQ1_0, payload, out_len, in_len)
+    y = ctx.matmul_q(w, x)
+    assert np.array_equal(y, oracle.matmul_tl1_sse(payload, out_len, in_len, x, k).reshape(k, out_len))
+    w.free()
+
+
 def test_tl1_with_rotation(ctx, oracle):
     # Qwen35Stage::wh: rotate_fwd(x, signs, block) then the product (two tokens: matmul_q)
     M, K, B, block = 256, 4096, 2, 128
