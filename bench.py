@@ -95,6 +95,9 @@ def parse():
     ap.add_argument("--prefetch", default="on", choices=["on", "off"],
                     help="each step's GEMV launch prefetches the next step's weights into L2 "
                          "(ouroq_set_prefetch), as a decode loop does for its next projection group")
+    ap.add_argument("--prefetch-ahead", type=int, default=1,
+                    help="with --prefetch on: the step whose weights each launch prefetches, counted "
+                         "ahead of the current one (1 = the next step)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="bound of the CPU-baseline sample (0 = skip)")
     ap.add_argument("--shard", action="store_true",
@@ -516,7 +519,7 @@ def run_ouroq(args, rank, world, local_rank):
 
     def step(i):
         if prefetch:
-            ctx.set_prefetch(wts[(i + 1) % ncop])
+            ctx.set_prefetch(wts[(i + args.prefetch_ahead) % ncop])
         run_step(wts[i % ncop], xs[i % ncop], ys[i % 2], qs[i % 2], sxs[i % 2])
 
     def gemm_only(i):
@@ -596,9 +599,10 @@ def run_ouroq(args, rank, world, local_rank):
         # reference-format kernel per matrix): bytes of the step / the timed region
         kern_s = ms / 1e3 / steps
         kern_bytes = nb["step"]
-        kernel = (f"{'tl1' if fmt == TL1 else 'tq1'}_matvec_kernel (reference order)"
+        kernel = ("tl1_colblock_kernel (matmul_tl1's K-column order)" if fmt == TL1 and B > 1
+                  else f"{'tl1' if fmt == TL1 else 'tq1'}_matvec_kernel (reference order)"
                   if fmt in REF_FMTS else
-                  (f"gemv_stream_kernel<B={B}> (fused quantisation)" if fmt == TERN and B <= 2 and not block
+                  (f"gemv_stream_kernel<B={B}> (fused quantisation)" if fmt == TERN and B <= 8 and not block
                    else f"gemv_kernel<{'kTern2' if fmt == TERN else 'kSign1'},B={B}> (fused quantisation)"))
     else:
         # matmul launches alone, on pre-quantised activations, timed the same way
@@ -702,6 +706,7 @@ def run_ouroq(args, rank, world, local_rank):
     if rank == 0:
         cfg = workload_config(args, wl, world)
         cfg.update({"pdl": not args.no_pdl, "l2_prefetch_of_next_step": prefetch,
+                    "prefetch_ahead": args.prefetch_ahead if prefetch else 0,
                     "launch": "CUDA graphs of exactly the timed steps, queued behind a spin "
                               "kernel before the first event"})
         line = {

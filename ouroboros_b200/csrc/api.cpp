@@ -214,6 +214,65 @@ GemvJob make_job(const ouroq_weight* w, const int8_t* q, const float* s_x, float
   return j;
 }
 
+// The stream-GEMV plan of these shapes, from the context's recent plans or
+// made now; null when the launch is not one the stream kernel takes
+// (ternary, fused quantisation, no rotation, no fused norm, 1..8 tokens).
+StreamPlan* stream_plan(ouroq_ctx* ctx, const GemvLaunch& L) {
+  if (!ctx->stream_gemv || L.fmt != kTern2 || !L.fused || L.norm.w || L.B < 1 || L.B > kStreamMaxB)
+    return nullptr;
+  StreamPlan key;
+  key.fmt = L.fmt;
+  key.B = L.B;
+  key.njobs = L.njobs;
+  key.nsms = ctx->num_sms;
+  for (int j = 0; j < L.njobs; ++j) {
+    key.M[j] = L.jobs[j].M;
+    key.K[j] = L.jobs[j].K;
+    key.had[j] = L.jobs[j].had_block;
+    int c = 0;
+    while (c < j && !(L.jobs[c].xf == L.jobs[j].xf && L.jobs[c].K == L.jobs[j].K)) ++c;
+    key.cls[j] = c;
+  }
+  auto same = [&](const StreamPlan& p) {
+    if (!p.used || p.fmt != key.fmt || p.B != key.B || p.njobs != key.njobs || p.nsms != key.nsms)
+      return false;
+    for (int j = 0; j < key.njobs; ++j)
+      if (p.M[j] != key.M[j] || p.K[j] != key.K[j] || p.had[j] != key.had[j] || p.cls[j] != key.cls[j])
+        return false;
+    return true;
+  };
+  for (StreamPlan& p : ctx->plans)
+    if (same(p)) return &p;
+  GemvLaunch S = L;
+  int grid = 0;
+  size_t smem = 0;
+  StreamPlan* plan = &ctx->plans[ctx->next_plan];
+  ctx->next_plan = (ctx->next_plan + 1) % kStreamPlans;
+  *plan = key;
+  plan->used = true;
+  plan->ok = gemv_stream_prepare(S, ctx->num_sms, &grid, &smem);
+  if (plan->ok) {
+    plan->grid = grid;
+    plan->smem = smem;
+    plan->ntiles = S.ntiles;
+    plan->xcap = S.xcap;
+    plan->defer = S.defer;
+    plan->stages = S.stages;
+    plan->cluster = S.cluster;
+    for (int j = 0; j < L.njobs; ++j) plan->tile_begin[j] = S.jobs[j].tile_begin;
+    std::memcpy(plan->cta_tile, S.cta_tile, sizeof(plan->cta_tile));
+  }
+  return plan;
+}
+
+// Does a fused launch of more than kFusedMaxB tokens run on the stream
+// kernel (one launch, each distinct input quantised once per CTA or
+// cluster)? Otherwise such batches are quantised in a launch of their own.
+bool stream_takes(ouroq_ctx* ctx, const GemvLaunch& L) {
+  const StreamPlan* p = stream_plan(ctx, L);
+  return p && p->ok;
+}
+
 ouroq_status run_gemv(ouroq_ctx* ctx, GemvLaunch& L, cudaStream_t s) {
   L.status = ctx->d_status;
   L.npf = 0;
@@ -224,53 +283,7 @@ ouroq_status run_gemv(ouroq_ctx* ctx, GemvLaunch& L, cudaStream_t s) {
   }
   ctx->prefetch.clear();
   if (L.njobs == 0 || L.B == 0) return OUROQ_OK;
-  if (ctx->stream_gemv && L.fmt == kTern2 && L.fused && !L.norm.w && L.B >= 1 && L.B <= 2) {
-    // the plan of these shapes, from the context's recent plans or made now
-    StreamPlan key;
-    key.fmt = L.fmt;
-    key.B = L.B;
-    key.njobs = L.njobs;
-    key.nsms = ctx->num_sms;
-    for (int j = 0; j < L.njobs; ++j) {
-      key.M[j] = L.jobs[j].M;
-      key.K[j] = L.jobs[j].K;
-      key.had[j] = L.jobs[j].had_block;
-      int c = 0;
-      while (c < j && !(L.jobs[c].xf == L.jobs[j].xf && L.jobs[c].K == L.jobs[j].K)) ++c;
-      key.cls[j] = c;
-    }
-    auto same = [&](const StreamPlan& p) {
-      if (!p.used || p.fmt != key.fmt || p.B != key.B || p.njobs != key.njobs || p.nsms != key.nsms)
-        return false;
-      for (int j = 0; j < key.njobs; ++j)
-        if (p.M[j] != key.M[j] || p.K[j] != key.K[j] || p.had[j] != key.had[j] || p.cls[j] != key.cls[j])
-          return false;
-      return true;
-    };
-    StreamPlan* plan = nullptr;
-    for (StreamPlan& p : ctx->plans)
-      if (same(p)) plan = &p;
-    if (!plan) {
-      GemvLaunch S = L;
-      int grid = 0;
-      size_t smem = 0;
-      plan = &ctx->plans[ctx->next_plan];
-      ctx->next_plan = (ctx->next_plan + 1) % kStreamPlans;
-      *plan = key;
-      plan->used = true;
-      plan->ok = gemv_stream_prepare(S, ctx->num_sms, &grid, &smem);
-      if (plan->ok) {
-        plan->grid = grid;
-        plan->smem = smem;
-        plan->ntiles = S.ntiles;
-        plan->xcap = S.xcap;
-        plan->defer = S.defer;
-        plan->stages = S.stages;
-        plan->cluster = S.cluster;
-        for (int j = 0; j < L.njobs; ++j) plan->tile_begin[j] = S.jobs[j].tile_begin;
-        std::memcpy(plan->cta_tile, S.cta_tile, sizeof(plan->cta_tile));
-      }
-    }
+  if (StreamPlan* plan = stream_plan(ctx, L)) {
     if (plan->ok) {
       GemvLaunch S = L;
       S.ntiles = plan->ntiles;
@@ -312,7 +325,7 @@ ouroq_status gemm_impl(ouroq_ctx* ctx, const ouroq_weight* w, const int8_t* q, c
     L.tok0 = 0;
     L.nvalid = B;
     L.status = ctx->d_status;
-    CU(ctx, launch_gemm_sign_tc(L, q, B, ctx->smem_optin, s), "sign tensor-core gemm launch");
+    CU(ctx, launch_gemm_sign_tc(L, q, B, ctx->smem_optin, ctx->num_sms, s, ctx->pdl), "sign tensor-core gemm launch");
     ctx->launches++;
     return OUROQ_OK;
   }
@@ -329,7 +342,7 @@ ouroq_status gemm_impl(ouroq_ctx* ctx, const ouroq_weight* w, const int8_t* q, c
     L.tok0 = 0;
     L.nvalid = B;
     L.status = ctx->d_status;
-    CU(ctx, launch_gemm_tc(L, q, B, ctx->smem_optin, ctx->num_sms, s), "tensor-core gemm launch");
+    CU(ctx, launch_gemm_tc(L, q, B, ctx->smem_optin, ctx->num_sms, s, ctx->pdl), "tensor-core gemm launch");
     ctx->launches++;
     return OUROQ_OK;
   }
@@ -1051,16 +1064,18 @@ ouroq_status ouroq_gemm_group_f32act(ouroq_ctx* ctx, int n, const ouroq_weight* 
     maxK = w[i]->K > maxK ? w[i]->K : maxK;
   }
   L.fmt = w[0]->fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // ternary without rotation, up to kStreamMaxB tokens: one stream-GEMV launch
+  if (B <= kGemvMaxB && stream_takes(ctx, L)) return run_gemv(ctx, L, s);
   if (B > kGemvMaxB || !gemv_fits(ctx, L))
     return fail(ctx, OUROQ_ERR_UNSUPPORTED,
                 "B=%d, K=%d: activations do not fit the fused GEMV (use quantize + gemm_group)",
                 B, maxK);
-  DeviceGuard g(ctx->device);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (B <= kFusedMaxB) return run_gemv(ctx, L, s);
-  // Larger batches: every CTA would quantise all tokens of its matrices again,
-  // so quantise each distinct activation set once (one launch) into scratch
-  // and run the grouped GEMV on the int8 codes.
+  // Larger batches off the stream kernel: every CTA would quantise all tokens
+  // of its matrices again, so quantise each distinct activation set once (one
+  // launch) into scratch and run the grouped GEMV on the int8 codes.
   QuantLaunch Q{};
   Q.B = B;
   int set_of[kMaxGemvJobs];
@@ -1141,8 +1156,10 @@ static ouroq_status f32act_impl(ouroq_ctx* ctx, const ouroq_weight* w, const flo
     return ref_matvec(ctx, w, xin, B, y, s, columns);
   }
   const int dfmt = w->fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
-  if (B <= kFusedMaxB && (hadamard_block == 0 || (hadamard_block >= 32 && hadamard_block <= 128))) {
-    // one launch: rotate + quantise in the GEMV prologue
+  if (B <= kGemvMaxB && (hadamard_block == 0 || (hadamard_block >= 32 && hadamard_block <= 128))) {
+    // one launch: rotate + quantise in the GEMV prologue (up to kFusedMaxB
+    // tokens; larger batches only on the stream kernel, which quantises each
+    // input once per CTA or cluster, else they quantise once, below)
     GemvLaunch L{};
     L.njobs = 1;
     L.B = B;
@@ -1153,7 +1170,7 @@ static ouroq_status f32act_impl(ouroq_ctx* ctx, const ouroq_weight* w, const flo
     L.jobs[0].signs = signs;
     L.jobs[0].had_block = hadamard_block;
     L.jobs[0].had_scale = hadamard_block ? 1.0f / std::sqrt((float)hadamard_block) : 1.0f;
-    if (gemv_fits(ctx, L)) return run_gemv(ctx, L, s);
+    if (stream_takes(ctx, L) || (B <= kFusedMaxB && gemv_fits(ctx, L))) return run_gemv(ctx, L, s);
   }
   st = grow(ctx, ctx->q_scratch, ctx->q_cap, (size_t)B * w->K, "q scratch");
   if (st != OUROQ_OK) return st;
@@ -1223,7 +1240,7 @@ ouroq_status ouroq_gemm_f32act_noalloc(ouroq_ctx* ctx, const ouroq_weight* w, co
   st = noalloc_scratch(ctx, &scratch);
   if (st != OUROQ_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (B <= kFusedMaxB && (hadamard_block == 0 || (hadamard_block >= 32 && hadamard_block <= 128))) {
+  if (B <= kGemvMaxB && (hadamard_block == 0 || (hadamard_block >= 32 && hadamard_block <= 128))) {
     // one launch, no scratch: rotate + quantise in the GEMV prologue (the
     // batches ouroq_gemm_f32act fuses; larger ones quantise once, below)
     GemvLaunch L{};
@@ -1236,7 +1253,7 @@ ouroq_status ouroq_gemm_f32act_noalloc(ouroq_ctx* ctx, const ouroq_weight* w, co
     L.jobs[0].signs = signs;
     L.jobs[0].had_block = hadamard_block;
     L.jobs[0].had_scale = hadamard_block ? 1.0f / std::sqrt((float)hadamard_block) : 1.0f;
-    if (gemv_fits(ctx, L)) return run_gemv(ctx, L, s);
+    if (stream_takes(ctx, L) || (B <= kFusedMaxB && gemv_fits(ctx, L))) return run_gemv(ctx, L, s);
   }
   int8_t* q = reinterpret_cast<int8_t*>(scratch);
   float* s_x = reinterpret_cast<float*>(scratch + kNoAllocQBytes);

@@ -404,7 +404,7 @@ int tc_cluster_capacity(int cs, size_t smem) {
 }  // namespace
 
 cudaError_t launch_gemm_tc(const TcLaunch& L0, const int8_t* q, int Btot, int smem_optin,
-                           int num_sms, cudaStream_t s) {
+                           int num_sms, cudaStream_t s, bool pdl) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return cudaErrorNotSupported;
   cudaError_t e = ensure_max_smem<gemm_tc_kernel>();
@@ -489,13 +489,22 @@ cudaError_t launch_gemm_tc(const TcLaunch& L0, const int8_t* q, int Btot, int sm
   cfg.blockDim = dim3(kTcThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = (unsigned)L.ksplit;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (L.ksplit > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = (unsigned)L.ksplit;
+    ++na;
+  }
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = L.ksplit > 1 ? 1 : 0;
+  cfg.numAttrs = (unsigned)na;
   return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, map, L);
 }
 

@@ -1,4 +1,4 @@
-// gemv_stream.cu -- the decode GEMV for one or two tokens (K2 at B <= 2):
+// gemv_stream.cu -- the decode GEMV for one to eight tokens (K2 at B <= 8):
 // packed ternary weights x fp32 activations, the per-token absmax int8
 // quantisation fused in, grouped over up to eight matrices per launch.
 //
@@ -31,7 +31,11 @@
 //    shared-memory load and 16 mask + 16 dp4a per tile and lane, with 4 x T
 //    independent accumulator chains per lane (measured on resident weights:
 //    about 45 packed bytes per clock per SM; mma.sync m16n8k32 u8 x s8 with
-//    the same masking reached 31).
+//    the same masking reached 31). From three tokens on, a stage holds two
+//    tiles (five tokens on: one), the masked weight words of a chunk stay in
+//    registers and the activations are loaded token by token (broadcast
+//    shared-memory loads), so a lane's accumulators still fit its registers;
+//    the batched verify of K = 4-8 columns (qwen35.rs:1378-1409) runs here.
 //  * A short prologue: the activations of the CTA's matrices are loaded with
 //    every load issued before any use, each distinct input row once (gate
 //    and up share theirs), reduced and quantised in registers, with the
@@ -52,7 +56,12 @@ namespace {
 constexpr int kRows = kTileRows;
 constexpr int kCW = 15;                     // consumer warps (16 with the producer: 128 registers)
 constexpr int kSThreads = (kCW + 1) * 32;   // + one producer warp
-constexpr int kMaxT = 4;                    // tiles per stage
+// Tiles per stage (one accumulator set each) at batch B: four up to two
+// tokens, fewer beyond, so that a lane's accumulators stay in registers.
+__host__ __device__ constexpr int tiles_for(int B) { return B <= 2 ? 4 : (B <= 4 ? 2 : 1); }
+// A prologue row (input i, token b) is encoded as i << kSegShift | b.
+constexpr int kSegShift = 3;
+constexpr int kSegMask = (1 << kSegShift) - 1;
 constexpr uint32_t kStage = 32u * 1024u;    // bytes per ring slot
 constexpr int kMaxNS = 6;                   // ring depth limit
 constexpr int kMaxIn = kMaxGemvJobs;        // distinct inputs of one CTA
@@ -78,7 +87,7 @@ __host__ __device__ inline SPlan splan(int B, int ns, int xcap, int groups) {
   SPlan p;
   p.bars = al128(sizeof(GemvLaunch));
   p.red = p.bars + 128;  // full[6] + empty[6] mbarriers
-  p.xq = p.red + al128((uint32_t)(groups > 0 ? groups : 1) * kCW * kMaxT * B * 32 * 4);
+  p.xq = p.red + al128((uint32_t)(groups > 0 ? groups : 1) * kCW * tiles_for(B) * B * 32 * 4);
   p.ring = p.xq + al128((uint32_t)xcap);
   p.total = p.ring + (uint32_t)ns * kStage;
   return p;
@@ -92,9 +101,9 @@ struct STab {
   int ufirst[kMaxIn + 1];   // first 128-value unit of input i (all B rows)
   int in_of[kMaxGemvJobs];  // job (relative to the CTA's first job) -> input
   int nin;
-  float sx[kMaxIn][2];      // per-token scales
-  int qtot[kMaxIn][2];      // per-token code sums
-  int amax[kMaxIn][2];      // absmax bits
+  float sx[kMaxIn][kStreamMaxB];  // per-token scales
+  int qtot[kMaxIn][kStreamMaxB];  // per-token code sums
+  int amax[kMaxIn][kStreamMaxB];  // absmax bits
 };
 
 __device__ __forceinline__ int job_of(const GemvLaunch& L, int t) {
@@ -199,11 +208,15 @@ __device__ __forceinline__ void cluster_wait() {
 
 // Unit u (128 consecutive values of one token row) -> (input, token, offset
 // of the unit in the input's [B][K] block). B <= 2: no division.
-__device__ __forceinline__ void unit_at(const STab& S, int B, int u, int& in, int& b, int& off) {
+template <int B>
+__device__ __forceinline__ void unit_at(const STab& S, int u, int& in, int& b, int& off) {
   in = 0;
   while (in + 1 < S.nin && u >= S.ufirst[in + 1]) ++in;
   const int r = u - S.ufirst[in];
-  b = (B > 1 && r >= S.K[in] / 128) ? 1 : 0;
+  if constexpr (B <= 2)
+    b = (B > 1 && r >= S.K[in] / 128) ? 1 : 0;
+  else
+    b = r / (S.K[in] / 128);
   off = r * 128;  // = b * K + (unit within the row) * 128
 }
 
@@ -232,8 +245,8 @@ __device__ void stream_prologue(STab& S, int8_t* xq, int warp, int lane) {
     seg[k] = -1;
     if (u < nunits) {
       int in, b, off;
-      unit_at(S, B, u, in, b, off);
-      seg[k] = in * 2 + b;
+      unit_at<B>(S, u, in, b, off);
+      seg[k] = (in << kSegShift | b);
       uoff[k] = off;
       const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
       v[k][0] = t.x;
@@ -247,7 +260,7 @@ __device__ void stream_prologue(STab& S, int8_t* xq, int warp, int lane) {
   auto flush_max = [&]() {
     if (cur >= 0) {
       const float t = warp_max(m);
-      if (lane == 0) atomicMax(&S.amax[cur >> 1][cur & 1], __float_as_int(t));
+      if (lane == 0) atomicMax(&S.amax[cur >> kSegShift][cur & kSegMask], __float_as_int(t));
     }
     m = 0.0f;
   };
@@ -265,11 +278,11 @@ __device__ void stream_prologue(STab& S, int8_t* xq, int warp, int lane) {
   }
   for (int u0 = warp + kRegUnits * kCW; u0 < nunits; u0 += kCW) {  // units beyond the registers
     int in, b, off;
-    unit_at(S, B, u0, in, b, off);
+    unit_at<B>(S, u0, in, b, off);
     const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
-    if (in * 2 + b != cur) {
+    if ((in << kSegShift | b) != cur) {
       flush_max();
-      cur = in * 2 + b;
+      cur = (in << kSegShift | b);
     }
     m = fmaxf(m, absmax4(t.x, t.y, t.z, t.w));
   }
@@ -293,7 +306,7 @@ __device__ void stream_prologue(STab& S, int8_t* xq, int warp, int lane) {
     for (int k = 0; k < kRegUnits; ++k) {
       if (seg[k] >= 0 && seg[k] != c) {
         c = seg[k];
-        sc = __fdiv_rn(__int_as_float(S.amax[c >> 1][c & 1]), 127.0f);
+        sc = __fdiv_rn(__int_as_float(S.amax[c >> kSegShift][c & kSegMask]), 127.0f);
         rs = __frcp_rn(sc);
       }
       scu[k] = sc;
@@ -319,7 +332,7 @@ __device__ void stream_prologue(STab& S, int8_t* xq, int warp, int lane) {
   auto flush_sum = [&]() {
     if (cur >= 0) {
       const int t = warp_sum(sum);
-      if (lane == 0) atomicAdd(&S.qtot[cur >> 1][cur & 1], t);
+      if (lane == 0) atomicAdd(&S.qtot[cur >> kSegShift][cur & kSegMask], t);
     }
     sum = 0;
   };
@@ -331,15 +344,15 @@ __device__ void stream_prologue(STab& S, int8_t* xq, int warp, int lane) {
       cur = seg[k];
     }
     sum += usum[k];
-    *reinterpret_cast<uint32_t*>(xq + S.xoff[seg[k] >> 1] + uoff[k] + lane * 4) = code[k];
+    *reinterpret_cast<uint32_t*>(xq + S.xoff[seg[k] >> kSegShift] + uoff[k] + lane * 4) = code[k];
   }
   for (int u0 = warp + kRegUnits * kCW; u0 < nunits; u0 += kCW) {  // units beyond the registers
     int in, b, off;
-    unit_at(S, B, u0, in, b, off);
+    unit_at<B>(S, u0, in, b, off);
     const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
-    if (in * 2 + b != cur) {
+    if ((in << kSegShift | b) != cur) {
       flush_sum();
-      cur = in * 2 + b;
+      cur = (in << kSegShift | b);
     }
     const float sc = __fdiv_rn(__int_as_float(S.amax[in][b]), 127.0f);
     *reinterpret_cast<uint32_t*>(xq + S.xoff[in] + off + lane * 4) =
@@ -373,8 +386,8 @@ __device__ void stream_prologue_cluster(STab& S, int8_t* xq, int warp, int lane,
     seg[k] = -1;
     if (u < nunits) {
       int in, b, off;
-      unit_at(S, B, u, in, b, off);
-      seg[k] = in * 2 + b;
+      unit_at<B>(S, u, in, b, off);
+      seg[k] = (in << kSegShift | b);
       uoff[k] = off;
       const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
       v[k][0] = t.x;
@@ -389,7 +402,7 @@ __device__ void stream_prologue_cluster(STab& S, int8_t* xq, int warp, int lane,
   auto flush_max = [&]() {
     if (cur >= 0) {
       const float t = warp_max(m);
-      if (lane < cs) red_max_cluster(peer_smem(&S.amax[cur >> 1][cur & 1], lane), __float_as_int(t));
+      if (lane < cs) red_max_cluster(peer_smem(&S.amax[cur >> kSegShift][cur & kSegMask], lane), __float_as_int(t));
     }
     m = 0.0f;
   };
@@ -407,11 +420,11 @@ __device__ void stream_prologue_cluster(STab& S, int8_t* xq, int warp, int lane,
   }
   for (int u = u0 + kRegUnits * ustep; u < nunits; u += ustep) {  // units beyond the registers
     int in, b, off;
-    unit_at(S, B, u, in, b, off);
+    unit_at<B>(S, u, in, b, off);
     const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
-    if (in * 2 + b != cur) {
+    if ((in << kSegShift | b) != cur) {
       flush_max();
-      cur = in * 2 + b;
+      cur = (in << kSegShift | b);
     }
     m = fmaxf(m, absmax4(t.x, t.y, t.z, t.w));
   }
@@ -430,7 +443,7 @@ __device__ void stream_prologue_cluster(STab& S, int8_t* xq, int warp, int lane,
     for (int k = 0; k < kRegUnits; ++k) {
       if (seg[k] >= 0 && seg[k] != c) {
         c = seg[k];
-        sc = __fdiv_rn(__int_as_float(S.amax[c >> 1][c & 1]), 127.0f);
+        sc = __fdiv_rn(__int_as_float(S.amax[c >> kSegShift][c & kSegMask]), 127.0f);
         rs = __frcp_rn(sc);
       }
       scu[k] = sc;
@@ -456,7 +469,7 @@ __device__ void stream_prologue_cluster(STab& S, int8_t* xq, int warp, int lane,
   auto flush_sum = [&]() {
     if (cur >= 0) {
       const int t = warp_sum(sum);
-      if (lane < cs) red_add_cluster(peer_smem(&S.qtot[cur >> 1][cur & 1], lane), t);
+      if (lane < cs) red_add_cluster(peer_smem(&S.qtot[cur >> kSegShift][cur & kSegMask], lane), t);
     }
     sum = 0;
   };
@@ -471,15 +484,15 @@ __device__ void stream_prologue_cluster(STab& S, int8_t* xq, int warp, int lane,
       cur = seg[k];
     }
     sum += usum[k];
-    put(xq + S.xoff[seg[k] >> 1] + uoff[k] + lane * 4, code[k]);
+    put(xq + S.xoff[seg[k] >> kSegShift] + uoff[k] + lane * 4, code[k]);
   }
   for (int u = u0 + kRegUnits * ustep; u < nunits; u += ustep) {  // units beyond the registers
     int in, b, off;
-    unit_at(S, B, u, in, b, off);
+    unit_at<B>(S, u, in, b, off);
     const float4 t = *reinterpret_cast<const float4*>(S.x[in] + off + lane * 4);
-    if (in * 2 + b != cur) {
+    if ((in << kSegShift | b) != cur) {
       flush_sum();
-      cur = in * 2 + b;
+      cur = (in << kSegShift | b);
     }
     const float sc = __fdiv_rn(__int_as_float(S.amax[in][b]), 127.0f);
     put(xq + S.xoff[in] + off + lane * 4, quant4s(t.x, t.y, t.z, t.w, sc, __frcp_rn(sc), &sum));
@@ -489,19 +502,20 @@ __device__ void stream_prologue_cluster(STab& S, int8_t* xq, int warp, int lane,
   cluster_wait();  // phase 2: codes and code sums complete in every CTA
 }
 
-// The consumer side of one tile group: TC tiles (1..kMaxT, a compile-time
-// constant) of one matrix through its G.ns stages; each warp's exact partial
-// sums end in red[warp][tile][token][lane].
+// The consumer side of one tile group: TC tiles (1..tiles_for(B), a
+// compile-time constant) of one matrix through its G.ns stages; each warp's
+// exact partial sums end in red[warp][tile][token][lane].
 template <int B, int TC>
-__device__ __forceinline__ void consume_group(int T_rt, const Geo& G, const int8_t* xrow, int K,
+__device__ __forceinline__ void consume_group(const Geo& G, const int8_t* xrow, int K,
                                               const uint8_t* ring, uint64_t* full, uint64_t* empty,
                                               int NS, int& st, int& cslot, int& cphase, bool& ok,
                                               unsigned* status, int* red, int warp, int lane) {
   constexpr int T = TC;
-  (void)T_rt;
-  int A[kMaxT][B][4];
+  constexpr int TM = tiles_for(B);
+  static_assert(T >= 1 && T <= TM, "tile count");
+  int A[T][B][4];
 #pragma unroll
-  for (int i = 0; i < kMaxT; ++i)
+  for (int i = 0; i < T; ++i)
 #pragma unroll
     for (int b = 0; b < B; ++b)
 #pragma unroll
@@ -519,34 +533,66 @@ __device__ __forceinline__ void consume_group(int T_rt, const Geo& G, const int8
     // chunk k of stage st belongs to warp (k + st) % kCW: leftover chunks of
     // short stages fall on different warps from stage to stage
     for (int k = ((warp - st) % kCW + kCW) % kCW; k < nck; k += kCW) {
-      uint4 xv[B][4];
-#pragma unroll
-      for (int b = 0; b < B; ++b) {
-        const uint4* xp = reinterpret_cast<const uint4*>(xrow + (size_t)b * K + (size_t)(c0 + k) * 64);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) xv[b][q] = xp[q];
-      }
-      uint4 wv[kMaxT];
-#pragma unroll
-      for (int i = 0; i < kMaxT; ++i)
-        if (i < T) wv[i] = *reinterpret_cast<const uint4*>(sb + ((size_t)i * nck + k) * 512);
-#pragma unroll
-      for (int i = 0; i < kMaxT; ++i) {
-        if (i >= T) break;
-        const uint32_t wl[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+      if constexpr (B <= 2) {
+        // the activations of the chunk in registers, applied to every tile
+        uint4 xv[B][4];
 #pragma unroll
         for (int b = 0; b < B; ++b) {
-          const uint32_t xw[4][4] = {{xv[b][0].x, xv[b][0].y, xv[b][0].z, xv[b][0].w},
-                                     {xv[b][1].x, xv[b][1].y, xv[b][1].z, xv[b][1].w},
-                                     {xv[b][2].x, xv[b][2].y, xv[b][2].z, xv[b][2].w},
-                                     {xv[b][3].x, xv[b][3].y, xv[b][3].z, xv[b][3].w}};
+          const uint4* xp = reinterpret_cast<const uint4*>(xrow + (size_t)b * K + (size_t)(c0 + k) * 64);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) xv[b][q] = xp[q];
+        }
+        uint4 wv[T];
+#pragma unroll
+        for (int i = 0; i < T; ++i) wv[i] = *reinterpret_cast<const uint4*>(sb + ((size_t)i * nck + k) * 512);
+#pragma unroll
+        for (int i = 0; i < T; ++i) {
+          const uint32_t wl[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+#pragma unroll
+          for (int b = 0; b < B; ++b) {
+            const uint32_t xw[4][4] = {{xv[b][0].x, xv[b][0].y, xv[b][0].z, xv[b][0].w},
+                                       {xv[b][1].x, xv[b][1].y, xv[b][1].z, xv[b][1].w},
+                                       {xv[b][2].x, xv[b][2].y, xv[b][2].z, xv[b][2].w},
+                                       {xv[b][3].x, xv[b][3].y, xv[b][3].z, xv[b][3].w}};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              A[i][b][0] = dp4a_us(wl[q] & 0x03030303u, xw[q][0], A[i][b][0]);
+              A[i][b][1] = dp4a_us(wl[q] & 0x0C0C0C0Cu, xw[q][1], A[i][b][1]);
+              A[i][b][2] = dp4a_us(wl[q] & 0x30303030u, xw[q][2], A[i][b][2]);
+              A[i][b][3] = dp4a_us(wl[q] & 0xC0C0C0C0u, xw[q][3], A[i][b][3]);
+            }
+          }
+        }
+      } else {
+        // more tokens: the masked weight words of the chunk in registers, the
+        // activations loaded token by token (broadcast shared-memory loads)
+        uint32_t wm[T][4][4];
+#pragma unroll
+        for (int i = 0; i < T; ++i) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(sb + ((size_t)i * nck + k) * 512);
+          const uint32_t wl[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            A[i][b][0] = dp4a_us(wl[q] & 0x03030303u, xw[q][0], A[i][b][0]);
-            A[i][b][1] = dp4a_us(wl[q] & 0x0C0C0C0Cu, xw[q][1], A[i][b][1]);
-            A[i][b][2] = dp4a_us(wl[q] & 0x30303030u, xw[q][2], A[i][b][2]);
-            A[i][b][3] = dp4a_us(wl[q] & 0xC0C0C0C0u, xw[q][3], A[i][b][3]);
+            wm[i][q][0] = wl[q] & 0x03030303u;
+            wm[i][q][1] = wl[q] & 0x0C0C0C0Cu;
+            wm[i][q][2] = wl[q] & 0x30303030u;
+            wm[i][q][3] = wl[q] & 0xC0C0C0C0u;
           }
+        }
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          const uint4* xp = reinterpret_cast<const uint4*>(xrow + (size_t)b * K + (size_t)(c0 + k) * 64);
+          const uint4 x0 = xp[0], x1 = xp[1], x2 = xp[2], x3 = xp[3];
+          const uint32_t xw[4][4] = {{x0.x, x0.y, x0.z, x0.w},
+                                     {x1.x, x1.y, x1.z, x1.w},
+                                     {x2.x, x2.y, x2.z, x2.w},
+                                     {x3.x, x3.y, x3.z, x3.w}};
+#pragma unroll
+          for (int i = 0; i < T; ++i)
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+              for (int m = 0; m < 4; ++m) A[i][b][m] = dp4a_us(wm[i][q][m], xw[q][m], A[i][b][m]);
         }
       }
     }
@@ -555,12 +601,11 @@ __device__ __forceinline__ void consume_group(int T_rt, const Geo& G, const int8
   }
   // exact shift-back of the four masked accumulators
 #pragma unroll
-  for (int i = 0; i < kMaxT; ++i)
+  for (int i = 0; i < T; ++i)
 #pragma unroll
     for (int b = 0; b < B; ++b)
-      if (i < T)
-        red[((warp * kMaxT + i) * B + b) * 32 + lane] =
-            A[i][b][0] + (A[i][b][1] >> 2) + (A[i][b][2] >> 4) + (A[i][b][3] >> 6);
+      red[((warp * TM + i) * B + b) * 32 + lane] =
+          A[i][b][0] + (A[i][b][1] >> 2) + (A[i][b][2] >> 4) + (A[i][b][3] >> 6);
 }
 
 // This CTA's even share of the next launch's weight ranges, into L2 (the
@@ -654,10 +699,11 @@ __global__ void __launch_bounds__(kSThreads, 1)
           (j + 1 < L.njobs && L.jobs[j + 1].tile_begin < t_end) ? L.jobs[j + 1].tile_begin : t_end;
       const uint8_t* wbase = J.w;
       const int tb = J.tile_begin;
-      const Geo G0 = geo(J.K, kMaxT);
-      for (int tg = t0; tg < seg_end && ok; tg += kMaxT) {
-        const int T = seg_end - tg < kMaxT ? seg_end - tg : kMaxT;
-        const Geo G = T == kMaxT ? G0 : geo(J.K, T);
+      constexpr int TM = tiles_for(B);
+      const Geo G0 = geo(J.K, TM);
+      for (int tg = t0; tg < seg_end && ok; tg += TM) {
+        const int T = seg_end - tg < TM ? seg_end - tg : TM;
+        const Geo G = T == TM ? G0 : geo(J.K, T);
         for (int s = 0; s < G.ns; ++s, ++st) {
           const int slot = pslot;
           if (st >= NS && !joined) join_cluster();
@@ -714,7 +760,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
         S.K[i] = J.K;
         S.xoff[i] = xo;
         S.ufirst[i] = uo;
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kStreamMaxB; ++b) {
           S.amax[i][b] = 0;
           S.qtot[i][b] = 0;
         }
@@ -743,7 +789,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
   // memory and are reduced after the last one (one CTA barrier), otherwise
   // each group is reduced (two barriers) before the next reuses the buffer
   const bool defer = L.defer != 0;
-  const int gstride = kCW * kMaxT * B * 32;  // ints of one group's partials
+  constexpr int TM = tiles_for(B);
+  const int gstride = kCW * TM * B * 32;  // ints of one group's partials
   auto reduce_group = [&](int g, const int* rg) {
     const int j = grp_job[g], tg = grp_t0[g], T = grp_T[g];
     const GemvJob& J = L.jobs[j];
@@ -752,7 +799,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
       const int i = p / B, b = p - (p / B) * B;
       int acc = -S.qtot[in][b];
 #pragma unroll
-      for (int w = 0; w < kCW; ++w) acc += rg[((w * kMaxT + i) * B + b) * 32 + lane];
+      for (int w = 0; w < kCW; ++w) acc += rg[((w * TM + i) * B + b) * 32 + lane];
       const int row = (tg + i - J.tile_begin) * kRows + lane;
       if (row < J.M) {
         J.y[(size_t)b * J.ldy + row] = __fmul_rn(__fmul_rn(__int2float_rn(acc), J.w_scale), S.sx[in][b]);
@@ -770,9 +817,9 @@ __global__ void __launch_bounds__(kSThreads, 1)
     const int8_t* xrow = xq + S.xoff[in];
     const int K = J.K;
     const int seg_end = (j + 1 < L.njobs && L.jobs[j + 1].tile_begin < t_end) ? L.jobs[j + 1].tile_begin : t_end;
-    // groups of kMaxT tiles, the remainder last
-    for (int tg = t0; tg < seg_end; tg += kMaxT, ++ngrp) {
-      const int T = seg_end - tg < kMaxT ? seg_end - tg : kMaxT;
+    // groups of TM tiles, the remainder last
+    for (int tg = t0; tg < seg_end; tg += TM, ++ngrp) {
+      const int T = seg_end - tg < TM ? seg_end - tg : TM;
       const Geo G = geo(K, T);
       const int g = defer ? ngrp : 0;
       int* rg = red + (size_t)g * gstride;
@@ -782,24 +829,24 @@ __global__ void __launch_bounds__(kSThreads, 1)
         grp_T[g] = T;
       }
       // the tile count as a compile-time constant: straight-line loop bodies
-      switch (T) {
-        case 4:
-          consume_group<B, 4>(T, G, xrow, K, ring, full, empty, NS, st, cslot, cphase, ok, L.status,
-                              rg, warp, lane);
-          break;
-        case 3:
-          consume_group<B, 3>(T, G, xrow, K, ring, full, empty, NS, st, cslot, cphase, ok, L.status,
-                              rg, warp, lane);
-          break;
-        case 2:
-          consume_group<B, 2>(T, G, xrow, K, ring, full, empty, NS, st, cslot, cphase, ok, L.status,
-                              rg, warp, lane);
-          break;
-        default:
-          consume_group<B, 1>(T, G, xrow, K, ring, full, empty, NS, st, cslot, cphase, ok, L.status,
-                              rg, warp, lane);
-          break;
+#define OUROQ_CONSUME(TC) \
+  consume_group<B, TC>(G, xrow, K, ring, full, empty, NS, st, cslot, cphase, ok, L.status, rg, warp, lane)
+      if constexpr (TM == 4) {
+        switch (T) {
+          case 4: OUROQ_CONSUME(4); break;
+          case 3: OUROQ_CONSUME(3); break;
+          case 2: OUROQ_CONSUME(2); break;
+          default: OUROQ_CONSUME(1); break;
+        }
+      } else if constexpr (TM == 2) {
+        if (T == 2)
+          OUROQ_CONSUME(2);
+        else
+          OUROQ_CONSUME(1);
+      } else {
+        OUROQ_CONSUME(1);
       }
+#undef OUROQ_CONSUME
       if (!defer) {
         named_bar_sync(1, kCW * 32);
         reduce_group(0, red);
@@ -825,9 +872,10 @@ int stream_smem_budget() {
       cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
     return 0;
+  // static shared memory: the same tables at every batch size
   cudaFuncAttributes fa, fb;
   if (cudaFuncGetAttributes(&fa, gemv_stream_kernel<1>) != cudaSuccess ||
-      cudaFuncGetAttributes(&fb, gemv_stream_kernel<2>) != cudaSuccess)
+      cudaFuncGetAttributes(&fb, gemv_stream_kernel<kStreamMaxB>) != cudaSuccess)
     return 0;
   const int st = (int)(fa.sharedSizeBytes > fb.sharedSizeBytes ? fa.sharedSizeBytes : fb.sharedSizeBytes);
   int b = per_sm - reserved - st;
@@ -910,12 +958,26 @@ int cluster_ctas_t() {
   return n > 0 ? n : 0;
 }
 
+int cluster_ctas(int B) {
+  switch (B) {
+    case 1: return cluster_ctas_t<1>();
+    case 2: return cluster_ctas_t<2>();
+    case 3: return cluster_ctas_t<3>();
+    case 4: return cluster_ctas_t<4>();
+    case 5: return cluster_ctas_t<5>();
+    case 6: return cluster_ctas_t<6>();
+    case 7: return cluster_ctas_t<7>();
+    case 8: return cluster_ctas_t<8>();
+    default: return 0;
+  }
+}
+
 }  // namespace
 
 bool gemv_stream_prepare(GemvLaunch& L, int num_sms, int* grid_out, size_t* smem_out) {
   *grid_out = 0;
   *smem_out = 0;
-  if (L.fmt != kTern2 || !L.fused || L.norm.w || L.B < 1 || L.B > 2) return false;
+  if (L.fmt != kTern2 || !L.fused || L.norm.w || L.B < 1 || L.B > kStreamMaxB) return false;
   int tiles = 0;
   for (int j = 0; j < L.njobs; ++j) {
     const GemvJob& J = L.jobs[j];
@@ -959,7 +1021,7 @@ bool gemv_stream_prepare(GemvLaunch& L, int num_sms, int* grid_out, size_t* smem
   }
   if (xcap / 128 > OUROQ_STREAM_CLUSTER_MIN_UNITS && grid >= kClusterCtas) {
     // large inputs: quantise each once per cluster instead of once per CTA
-    int gmax = L.B == 1 ? cluster_ctas_t<1>() : cluster_ctas_t<2>();
+    int gmax = cluster_ctas(L.B);
     if (gmax > num_sms) gmax = num_sms;
     if (gmax > kMaxGemvCtas) gmax = kMaxGemvCtas;
     gmax -= gmax % kClusterCtas;
@@ -975,7 +1037,8 @@ bool gemv_stream_prepare(GemvLaunch& L, int num_sms, int* grid_out, size_t* smem
   }
   L.cluster = cs;
   L.xcap = xcap;
-  // tile groups of each CTA (runs of up to kMaxT tiles of one matrix)
+  // tile groups of each CTA (runs of up to tiles_for(B) tiles of one matrix)
+  const int TM = tiles_for(L.B);
   int maxg = 0;
   for (int c = 0; c < grid; ++c) {
     int n = 0;
@@ -984,7 +1047,7 @@ bool gemv_stream_prepare(GemvLaunch& L, int num_sms, int* grid_out, size_t* smem
       while (j + 1 < L.njobs && t0 >= L.jobs[j + 1].tile_begin) ++j;
       const int seg_end = (j + 1 < L.njobs && L.jobs[j + 1].tile_begin < L.cta_tile[c + 1])
                               ? L.jobs[j + 1].tile_begin : L.cta_tile[c + 1];
-      n += (seg_end - t0 + kMaxT - 1) / kMaxT;  // full groups of kMaxT, the remainder last
+      n += (seg_end - t0 + TM - 1) / TM;  // full groups of TM, the remainder last
       t0 = seg_end;
     }
     maxg = n > maxg ? n : maxg;
@@ -1004,9 +1067,17 @@ bool gemv_stream_prepare(GemvLaunch& L, int num_sms, int* grid_out, size_t* smem
 
 cudaError_t launch_gemv_stream(GemvLaunch& L, int grid, size_t smem, cudaStream_t s, bool pdl) {
   if (grid == 0) return cudaSuccess;
-  if (L.B == 1) return launch_stream_t<1>(L, grid, smem, s, pdl);
-  if (L.B == 2) return launch_stream_t<2>(L, grid, smem, s, pdl);
-  return cudaErrorInvalidValue;
+  switch (L.B) {
+    case 1: return launch_stream_t<1>(L, grid, smem, s, pdl);
+    case 2: return launch_stream_t<2>(L, grid, smem, s, pdl);
+    case 3: return launch_stream_t<3>(L, grid, smem, s, pdl);
+    case 4: return launch_stream_t<4>(L, grid, smem, s, pdl);
+    case 5: return launch_stream_t<5>(L, grid, smem, s, pdl);
+    case 6: return launch_stream_t<6>(L, grid, smem, s, pdl);
+    case 7: return launch_stream_t<7>(L, grid, smem, s, pdl);
+    case 8: return launch_stream_t<8>(L, grid, smem, s, pdl);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace ouroq

@@ -167,14 +167,17 @@ size_t gemm_tc_smem_bytes(int N, int stages);
 // q: int8 activations [Btot][K] (16-byte aligned rows). One launch; the grid
 // covers (128-row tiles) x (token tiles) x (parts of K), sizes chosen by the
 // launcher.
+// pdl: programmatic dependent launch (the weight copies and the set-up
+// overlap the previous kernel; the activations are read after it).
 cudaError_t launch_gemm_tc(const TcLaunch& L, const int8_t* q, int Btot, int smem_optin,
-                           int num_sms, cudaStream_t s);
+                           int num_sms, cudaStream_t s, bool pdl);
 // Sign weights (kSign1) on the tensor cores: one group accumulator per 128 k,
 // the fp32 fold in ascending group order. The grid covers (128-row tiles) x
-// (token tiles of 16, 32 or 64).
+// (token tiles of 16 or 32) x (parts of the groups, a cluster chaining the
+// fold), sizes chosen by the launcher.
 bool gemm_sign_tc_supported(int M, int K, int B);
 cudaError_t launch_gemm_sign_tc(const TcLaunch& L, const int8_t* q, int Btot, int smem_optin,
-                                cudaStream_t s);
+                                int num_sms, cudaStream_t s, bool pdl);
 
 // The reference's own shard formats (PTQ1_0 "Tl1", TQ1_0), stored on the device
 // exactly as in the shard (row-major, no repack): fp32 x [B][K] -> y [B][ldy].
@@ -212,6 +215,8 @@ cudaError_t launch_head(const HeadLaunch& L, cudaStream_t s, bool pdl);
 
 // Limits of the small-batch GEMV path.
 constexpr int kGemvMaxB = 8;
+// Largest batch of the stream GEMV (gemv_stream_kernel, fused quantisation).
+constexpr int kStreamMaxB = 8;
 // Above this batch the fp32-activation entry points quantise once in a separate
 // launch instead of in every GEMV CTA's prologue (which repeats it per CTA).
 constexpr int kFusedMaxB = 2;

@@ -224,6 +224,33 @@ def test_gemm_sign1_tensor_core(ctx, oracle, M, K, B):
     w.free()
 
 
+@pytest.mark.parametrize("M,K,B,Z", [(256, 1664, 32, 4), (300, 2048, 17, 2), (128, 1152, 16, 4),
+                                     (4096, 4096, 32, 4), (77, 512, 40, 4), (200, 1024, 64, 2),
+                                     (128, 256, 16, 4), (256, 4096, 32, 2)])
+def test_gemm_sign1_tensor_core_split(ctx, oracle, monkeypatch, M, K, B, Z):
+    # the groups split over a cluster of Z CTAs (forced through
+    # OUROQ_SIGN_KSPLIT), the fp32 fold chained from CTA to CTA: still the
+    # oracle's order bit for bit. Ragged splits (13 groups over 4, 9 over 4),
+    # token tiles of 16 and 32, two token tiles, one group per CTA, and splits
+    # the launcher refuses (more CTAs than groups; more groups per CTA than
+    # tensor memory holds) falling back to one CTA per row tile. With and
+    # without the debug accumulators (two instantiations of the kernel).
+    import torch
+    monkeypatch.setenv("OUROQ_SIGN_KSPLIT", str(Z))
+    packed, sc, x = sign_case(oracle, M, K, B, seed=5 * M + K + B + Z)
+    qr, sr = oracle.quantize_act(x, None, 0)
+    accr, yr = oracle.gemm_sign1(packed, sc, M, K, qr, sr)
+    w = ctx.upload(oq.SIGN1G128, packed, M, K, scales=sc)
+    acc = torch.empty((B, M, K // 128), dtype=torch.int32, device="cuda")
+    y1 = ctx.gemm(w, dev(qr), dev(sr), acc=acc)
+    y2 = ctx.gemm(w, dev(qr), dev(sr))
+    assert np.array_equal(host(acc), accr)
+    assert np.array_equal(host(y1), yr)
+    assert np.array_equal(host(y2), yr)
+    ctx.check_device()
+    w.free()
+
+
 # ---------------------------------------------------------------- grouped / host mirrors
 def test_gemm_group_c2_layer(ctx, oracle):
     shapes = [(3840, 2560), (2560, 2560), (6912, 2560), (6912, 2560), (2560, 6912)]
@@ -245,10 +272,12 @@ def test_gemm_group_c2_layer(ctx, oracle):
         w.free()
 
 
-@pytest.mark.parametrize("B", [1, 2, 4, 8])
+@pytest.mark.parametrize("B", [1, 2, 3, 4, 5, 8])
 def test_gemm_group_f32act_c2_layer(ctx, oracle, B):
-    # B <= 2: one fused launch (fp32 activations quantised in the GEMV prologue);
-    # larger B: each distinct input quantised once, then the grouped GEMV
+    # up to eight tokens: one fused stream-GEMV launch for the five projections
+    # (fp32 activations quantised in the prologue, each distinct input once per
+    # CTA or cluster; four tiles a stage up to two tokens, two up to four, one
+    # beyond)
     import torch
     shapes = [(3840, 2560), (2560, 2560), (6912, 2560), (6912, 2560), (2560, 6912)]
     inputs = [oracle.normals(400 + i, B * k).reshape(B, k) for i, k in enumerate([2560, 2560, 2560, 6912])]
@@ -263,11 +292,31 @@ def test_gemm_group_f32act_c2_layer(ctx, oracle, B):
         ws_.append(ctx.upload(oq.TERNARY2, packed, M, K, w_scale=wsc))
         xs.append(dev_inputs[input_of[i]])
         ys.append(torch.empty((B, M), dtype=torch.float32, device="cuda"))
+    n0 = ctx.launch_count()
     ctx.gemm_group_f32act(ws_, xs, ys)
+    assert ctx.launch_count() - n0 == 1
     for y, yr in zip(ys, want):
         assert np.array_equal(host(y), yr)
     for w in ws_:
         w.free()
+
+
+@pytest.mark.parametrize("M,K,B", [(300, 2560, 3), (77, 6912, 6), (1000, 1152, 7), (33, 128, 8)])
+def test_stream_gemv_batches_exact(ctx, oracle, M, K, B):
+    # three to eight tokens through the one-launch stream GEMV: rows off the
+    # 32-row tile, K of one 128-value unit, a token of zeros (scale 0) and
+    # outliers; codes, sums and outputs equal the oracle's bit for bit
+    x = oracle.outliers(M + B, oracle.normals(K + B, B * K), 0.01, 20.0).reshape(B, K)
+    x[B - 1] = 0.0
+    packed, ws, _ = tern_case(oracle, M, K, 1, seed=M * B + K)
+    qr, sr = oracle.quantize_act(x)
+    _, yr = oracle.gemm_tern2(packed, M, K, ws, qr, sr)
+    w = ctx.upload(oq.TERNARY2, packed, M, K, w_scale=ws)
+    n0 = ctx.launch_count()
+    y = ctx.gemm_f32act(w, dev(x))
+    assert ctx.launch_count() - n0 == 1
+    assert np.array_equal(host(y), yr)
+    w.free()
 
 
 @pytest.mark.parametrize("block", [64, 128, 1024])
@@ -283,7 +332,7 @@ def test_fused_hadamard_sign_gemv(ctx, oracle, M, K, B, block):
     w.free()
 
 
-@pytest.mark.parametrize("M,K,B", [(8192, 28672, 1), (1024, 28672, 2), (2048, 8192, 2)])
+@pytest.mark.parametrize("M,K,B", [(8192, 28672, 1), (1024, 28672, 2), (2048, 8192, 2), (1024, 28672, 4)])
 def test_fused_wide_rows_exact(ctx, oracle, M, K, B):
     # one fused launch quantising rows too wide for one round of loads per
     # warp (28672 values = 224 units of 128): the later rounds must give the
@@ -312,7 +361,7 @@ def test_fused_group_cluster_shared_quantisation(ctx, oracle, B):
     xs = [oracle.outliers(600, oracle.normals(601, B * 28672), 0.01, 20.0).reshape(B, 28672),
           oracle.normals(602, B * 12800).reshape(B, 12800),
           oracle.normals(603, B * 384).reshape(B, 384)]
-    if B == 2:
+    if B >= 2:
         xs[1][1] = 0.0
     xd = [dev(x) for x in xs]
     ws_, ys, want = [], [], []
