@@ -237,15 +237,17 @@ def gate(torch, replays: int):
     torch.cuda._sleep(int(seconds * 2.0e9))  # cycles at ~2 GHz
 
 
-def graph_plan(steps: int, ncop: int, max_passes: int = 64):
-    """Cover exactly `steps` steps with CUDA graphs: a graph of G steps (G a
-    multiple of the copy count, so replays keep the rotation) replayed
-    `reps` times, then one graph of the remaining `rest` steps (copies
-    0..rest-1, which follow a full pass). Returns (G, reps, rest)."""
+def graph_plan(steps: int, ncop: int, max_passes: int = 64, max_single: int = 4096):
+    """Cover exactly `steps` steps with CUDA graphs. Up to `max_single` steps:
+    one graph of all of them (the copies rotate inside it), so the timed
+    region holds no graph-to-graph boundary. Beyond: a graph of G steps (G a
+    multiple of the copy count, so replays keep the rotation) replayed `reps`
+    times, then one graph of the remaining `rest` steps (copies 0..rest-1,
+    which follow a full pass). Returns (G, reps, rest)."""
+    if steps <= max_single:
+        return 0, 0, steps
     passes = max(1, min(steps // ncop, max_passes))
     G = passes * ncop
-    if steps < G:
-        return 0, 0, steps
     return G, steps // G, steps % G
 
 
@@ -512,8 +514,9 @@ def run_ouroq(args, rank, world, local_rank):
         else:
             ctx.quantize_group(xin, qbuf, sbuf, signs=signs if block else None,
                                blocks=[block] * len(widths) if block else None, stream=stream)
-            for j, (_, _, _, xi) in enumerate(mats):
-                ctx.gemm(wl_[j], qbuf[xi], sbuf[xi], y=yout[j], stream=stream)
+            # the projections as one grouped product (one tensor-core launch for ternary weights)
+            ctx.gemm_group(wl_, [qbuf[xi] for _, _, _, xi in mats], [sbuf[xi] for _, _, _, xi in mats],
+                           yout, stream=stream)
 
     prefetch = args.prefetch == "on" and fused and fmt not in REF_FMTS
 
@@ -523,8 +526,8 @@ def run_ouroq(args, rank, world, local_rank):
         run_step(wts[i % ncop], xs[i % ncop], ys[i % 2], qs[i % 2], sxs[i % 2])
 
     def gemm_only(i):
-        for j, (_, _, _, xi) in enumerate(mats):
-            ctx.gemm(wts[i % ncop][j], qs[0][xi], sxs[0][xi], y=ys[i % 2][j], stream=stream)
+        ctx.gemm_group(wts[i % ncop], [qs[0][xi] for _, _, _, xi in mats], [sxs[0][xi] for _, _, _, xi in mats],
+                       ys[i % 2], stream=stream)
 
     def capture(fn, n):
         """One CUDA graph of steps 0..n-1 (launch-bound loop -> graph replay)."""
@@ -612,7 +615,7 @@ def run_ouroq(args, rank, world, local_rank):
         kms = timed(g2)
         kern_s = kms / 1e3 / steps
         kern_bytes = nb["gemm"]
-        kernel = ("gemm_tc_kernel (tcgen05 kind::i8)" if fmt == TERN and B >= 16
+        kernel = (("gemm_tc_kernel (tcgen05 kind::i8, one grouped launch)" if len(mats) > 1 else "gemm_tc_kernel (tcgen05 kind::i8)") if fmt == TERN and B >= 16
                   else "gemm_sign_tc_kernel (tcgen05 kind::i8, group accumulators)" if B >= 16
                   else "gemv_kernel (8-token chunks)")
         del g2

@@ -164,8 +164,11 @@ ouroq_status ouroq_rotate(ouroq_ctx *ctx, const float *x, float *out, int B, int
 ouroq_status ouroq_gemm(ouroq_ctx *ctx, const ouroq_weight *w, const int8_t *q, const float *s_x,
                         int B, float *y, int32_t *acc_debug, void *stream);
 
-/* Grouped GEMV: n (<= 8) independent products y_i = W_i . q_i in ONE launch.
- * All weights share one format; B <= 8. Used for the projections of a layer. */
+/* Grouped product: n (<= 8) independent products y_i = W_i . q_i, all weights
+ * of one format. Up to 8 tokens one GEMV launch; from 16 tokens TERNARY2
+ * weights run as ONE tensor-core launch over every matrix's row tiles (the
+ * projections of a layer), SIGN1G128 weights one tensor-core launch each.
+ * Used for the projections of a layer. */
 ouroq_status ouroq_gemm_group(ouroq_ctx *ctx, int n, const ouroq_weight *const *w,
                               const int8_t *const *q, const float *const *s_x, int B,
                               float *const *y, void *stream);
@@ -174,7 +177,9 @@ ouroq_status ouroq_gemm_group(ouroq_ctx *ctx, int n, const ouroq_weight *const *
  * y_i = W_i . quant(rotate(x_i)) in ONE launch, x_i fp32 [B][K_i] (16-byte
  * aligned). Per entry optional rotation: signs[i] (nullable) and blocks[i]
  * (0 = none, else 32, 64 or 128, the same for every entry); both arrays may be
- * NULL. OUROQ_ERR_UNSUPPORTED when B > 8 or the activations of the matrices
+ * NULL. Beyond 8 tokens the distinct inputs are quantised in one launch and the
+ * products run as in ouroq_gemm_group. OUROQ_ERR_UNSUPPORTED when B <= 8 and
+ * the activations of the matrices
  * one CTA covers do not fit in shared memory. */
 ouroq_status ouroq_gemm_group_f32act(ouroq_ctx *ctx, int n, const ouroq_weight *const *w,
                                      const float *const *x, int B, const float *const *signs,

@@ -364,6 +364,42 @@ ouroq_status gemm_impl(ouroq_ctx* ctx, const ouroq_weight* w, const int8_t* q, c
   return OUROQ_OK;
 }
 
+// y_i = W_i . q_i (pre-quantised, L.jobs[i].q / s_x / y) for the n weights
+// of a group and B tokens: up to kGemvMaxB tokens one grouped GEMV launch;
+// from kTcMinBatch ternary weights one grouped tensor-core launch; otherwise
+// one product per weight.
+ouroq_status group_product(ouroq_ctx* ctx, GemvLaunch& L, const ouroq_weight* const* w, int n, int B,
+                           cudaStream_t s) {
+  if (B <= kGemvMaxB) return run_gemv(ctx, L, s);
+  bool tc = B >= kTcMinBatch && ctx->use_tc;
+  for (int i = 0; i < n && tc; ++i)
+    tc = w[i]->fmt == OUROQ_FMT_TERNARY2 && gemm_tc_supported(kTern2, w[i]->M, w[i]->K, B) &&
+         aligned16(L.jobs[i].q);
+  if (tc && n > 1) {
+    TcJob jobs[kMaxTcJobs];
+    const int8_t* qs[kMaxTcJobs];
+    for (int i = 0; i < n; ++i) {
+      const GemvJob& J = L.jobs[i];
+      jobs[i] = TcJob{J.w, J.y, J.acc, J.s_x, J.w_scale, J.M, J.K, J.ldy};
+      qs[i] = J.q;
+    }
+    TcLaunch T{};
+    T.tok0 = 0;
+    T.nvalid = B;
+    T.status = ctx->d_status;
+    CU(ctx, launch_gemm_tc_group(T, jobs, qs, n, B, ctx->smem_optin, ctx->num_sms, s, ctx->pdl),
+       "grouped tensor-core gemm launch");
+    ctx->launches++;
+    return OUROQ_OK;
+  }
+  for (int i = 0; i < n; ++i) {
+    const GemvJob& J = L.jobs[i];
+    ouroq_status st = gemm_impl(ctx, w[i], J.q, J.s_x, B, J.y, J.acc, s);
+    if (st != OUROQ_OK) return st;
+  }
+  return OUROQ_OK;
+}
+
 ouroq_status quantize_impl(ouroq_ctx* ctx, const float* x, int B, int K, const float* signs,
                            int block, int8_t* q, float* s_x, cudaStream_t s) {
   QuantLaunch L{};
@@ -1007,7 +1043,7 @@ ouroq_status ouroq_gemm_group(ouroq_ctx* ctx, int n, const ouroq_weight* const* 
                               float* const* y, void* stream) {
   if (!ctx) return OUROQ_ERR_BAD_ARG;
   if (n < 0 || n > kMaxGemvJobs) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "group size %d (max %d)", n, kMaxGemvJobs);
-  if (B < 0 || B > kGemvMaxB) return fail(ctx, OUROQ_ERR_UNSUPPORTED, "grouped GEMV needs B <= %d", kGemvMaxB);
+  if (B < 0) return fail(ctx, OUROQ_ERR_BAD_SHAPE, "B=%d", B);
   if (n == 0 || B == 0) return OUROQ_OK;
   if (!w || !q || !s_x || !y) return fail(ctx, OUROQ_ERR_BAD_ARG, "null array");
   GemvLaunch L{};
@@ -1018,7 +1054,7 @@ ouroq_status ouroq_gemm_group(ouroq_ctx* ctx, int n, const ouroq_weight* const* 
     if (is_ref_format(w[i]->fmt))
       return fail(ctx, OUROQ_ERR_UNSUPPORTED, "grouped calls take TERNARY2 / SIGN1G128 weights");
     if (w[i]->fmt != w[0]->fmt) return fail(ctx, OUROQ_ERR_UNSUPPORTED, "mixed formats in a group");
-    if ((size_t)B * w[i]->K > kGemvMaxXBytes)
+    if (B <= kGemvMaxB && (size_t)B * w[i]->K > kGemvMaxXBytes)
       return fail(ctx, OUROQ_ERR_UNSUPPORTED, "B*K=%zu exceeds the grouped GEMV limit",
                   (size_t)B * w[i]->K);
     if (!aligned16(q[i])) return fail(ctx, OUROQ_ERR_BAD_ALIGN, "q[%d] not 16-byte aligned", i);
@@ -1026,7 +1062,7 @@ ouroq_status ouroq_gemm_group(ouroq_ctx* ctx, int n, const ouroq_weight* const* 
   }
   L.fmt = w[0]->fmt == OUROQ_FMT_TERNARY2 ? kTern2 : kSign1;
   DeviceGuard g(ctx->device);
-  return run_gemv(ctx, L, static_cast<cudaStream_t>(stream));
+  return group_product(ctx, L, w, n, B, static_cast<cudaStream_t>(stream));
 }
 
 ouroq_status ouroq_gemm_group_f32act(ouroq_ctx* ctx, int n, const ouroq_weight* const* w,
@@ -1068,7 +1104,7 @@ ouroq_status ouroq_gemm_group_f32act(ouroq_ctx* ctx, int n, const ouroq_weight* 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // ternary without rotation, up to kStreamMaxB tokens: one stream-GEMV launch
   if (B <= kGemvMaxB && stream_takes(ctx, L)) return run_gemv(ctx, L, s);
-  if (B > kGemvMaxB || !gemv_fits(ctx, L))
+  if (B <= kGemvMaxB && !gemv_fits(ctx, L))
     return fail(ctx, OUROQ_ERR_UNSUPPORTED,
                 "B=%d, K=%d: activations do not fit the fused GEMV (use quantize + gemm_group)",
                 B, maxK);
@@ -1116,7 +1152,7 @@ ouroq_status ouroq_gemm_group_f32act(ouroq_ctx* ctx, int n, const ouroq_weight* 
     L.jobs[i].s_x = Q.jobs[set_of[i]].s_x;
     L.jobs[i].xf = nullptr;
   }
-  return run_gemv(ctx, L, s);
+  return group_product(ctx, L, w, n, B, s);
 }
 
 // PTQ1_0 order of an fp32-activation product: kAuto = matvec_tl1's for one
@@ -1896,11 +1932,14 @@ ouroq_status ouroq_gemm_norm_f32act(ouroq_ctx* ctx, int n, const ouroq_weight* c
   if (st != OUROQ_OK) return st;
   st = ouroq_quantize_act(ctx, a, B, K, nullptr, 0, ctx->q_scratch, ctx->s_scratch, stream);
   if (st != OUROQ_OK) return st;
+  // the group's products on the shared codes (one tensor-core launch for ternary weights)
+  const int8_t* qs[kMaxGemvJobs];
+  const float* ss[kMaxGemvJobs];
   for (int i = 0; i < n; ++i) {
-    st = ouroq_gemm(ctx, w[i], ctx->q_scratch, ctx->s_scratch, B, y[i], nullptr, stream);
-    if (st != OUROQ_OK) return st;
+    qs[i] = ctx->q_scratch;
+    ss[i] = ctx->s_scratch;
   }
-  return OUROQ_OK;
+  return ouroq_gemm_group(ctx, n, w, qs, ss, B, y, stream);
 }
 
 }  // extern "C"

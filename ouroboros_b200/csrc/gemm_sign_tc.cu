@@ -38,11 +38,12 @@
 // of K. So the launcher may split the groups over a cluster of Z CTAs (grid
 // z): CTA z runs the MMAs of its own range of at most ND groups at once, all
 // its accumulators resident in tensor memory. The fp32 fold must still run in
-// ascending group order, so it is chained: CTA 0 folds its groups from zero,
-// sends its 128 x NT partial sums to CTA 1 with one bulk shared-to-shared copy
-// (completion on an mbarrier of CTA 1), CTA 1 continues the same sums with its
-// groups, and so on; the last CTA writes y. The additions are the oracle's, in
-// the oracle's order; only where they run changes.
+// ascending group order, so it is chained: CTA 0 folds its groups from zero
+// and sends its 128 x NT partial sums to CTA 1 (each fold warp its slice, one
+// bulk shared-to-shared copy, completion on an mbarrier of CTA 1); CTA 1, which
+// has meanwhile parked its own groups' terms in tensor memory, continues the
+// same sums with them, and so on; the last CTA writes y. The additions are the
+// oracle's, in the oracle's order; only where they run changes.
 //
 // Tensor memory (512 columns x 128 lanes): accumulators D in columns [0, 256)
 // (ND = min(8, 256 / NT) of NT columns each), expanded bit blocks A in eight
@@ -76,7 +77,7 @@ constexpr int kSgMaxTok = 32;     // largest token tile
 constexpr int kSgMaxSplit = 4;    // CTAs of a cluster splitting the groups
 
 struct SgPlan {
-  uint32_t bars, tmem, qs, chain, chain_bytes, stage0, w_off, sc_off, stage_bytes, total;
+  uint32_t bars, tmem, sxs, qs, chain, chain_bytes, stage0, w_off, sc_off, stage_bytes, total;
   int nd;  // accumulators (groups in flight between the MMAs and the fold)
 };
 
@@ -90,7 +91,8 @@ __host__ __device__ inline SgPlan sg_plan(int NT, int stages) {
   SgPlan p;
   p.bars = 0;    // full[6], sfree[6], afull[8], afree[8], dfull[8], dfree[8], xfull
   p.tmem = 384;  // allocated tensor-memory address
-  p.qs = 512;
+  p.sxs = 512;   // the token tile's activation scales, fp32 [32]
+  p.qs = 640;
   p.chain = p.qs + (uint32_t)stages * kSgGroupsPerStage * kSgMaxTok * 4;
   p.chain_bytes = 2u * kSgRows * (uint32_t)(NT / 2 + 4) * 4u;
   p.stage0 = (p.chain + p.chain_bytes + 1023) & ~1023u;
@@ -163,6 +165,7 @@ __global__ void __launch_bounds__(kSgThreads, 1)
   uint64_t* dfree = dfull + kSgMaxD;
   uint64_t* xfull = dfree + kSgMaxD;  // the previous CTA's partial sums have landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + pl.tmem);
+  float* sxs = reinterpret_cast<float*>(smem + pl.sxs);
   int* qsb = reinterpret_cast<int*>(smem + pl.qs);
   float* chain = reinterpret_cast<float*>(smem + pl.chain);
   uint8_t* stages = smem + pl.stage0;
@@ -198,19 +201,25 @@ __global__ void __launch_bounds__(kSgThreads, 1)
       mbar_init(&dfree[i], kSgFWarps);
     }
     mbar_init(xfull, 1);
-    if (z > 0) mbar_arrive_expect_tx(xfull, pl.chain_bytes);
+    if (z > 0) mbar_arrive_expect_tx(xfull, pl.chain_bytes);  // every fold warp's slice
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 512);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  __syncthreads();  // barriers initialised
   // cluster phase A: every CTA's barriers are initialised (waited for before
-  // the chain copy is sent, or at the end)
+  // the chain's sums are sent, or at the end)
   if (Z > 1) sg_cluster_arrive();
   bool waited_a = Z == 1;
   pdl_launch_dependents();
+  // tensor memory for every warp but the producer, whose first copies do not
+  // wait for it
+  uint32_t tmem = 0;
+  if (warp != 0) {
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    named_bar_sync(3, kSgThreads - 32);
+    tc_fence_after();
+    tmem = *tmem_slot;
+  }
 
   if (warp == 0) {
     // ---------------- producer ----------------
@@ -356,6 +365,9 @@ __global__ void __launch_bounds__(kSgThreads, 1)
         }
         qs[fw * kSgMaxTok + t] = sq;
       }
+      // the tile's activation scales, once (written by the previous grid,
+      // which has completed: the stage's activations were loaded after it)
+      if (i == 0 && fw == kSgFWarps - 1 && lane < nv) sxs[lane] = P.s_x[tok_base + lane];
       // this row's fp16 scales of the stage's groups
       float sc[kSgGroupsPerStage];
 #pragma unroll
@@ -448,7 +460,9 @@ __global__ void __launch_bounds__(kSgThreads, 1)
       }
     }
     if (z < Z - 1) {
-      // pass the sums on to the next CTA of the split: each warp its slice
+      // pass the sums on to the next CTA of the split: each warp its slice,
+      // one bulk shared-to-shared copy (measured faster than remote stores
+      // with a release arrive)
       sg_cluster_wait();  // phase A: its barriers are initialised
       waited_a = true;
 #pragma unroll
@@ -463,7 +477,7 @@ __global__ void __launch_bounds__(kSgThreads, 1)
 #pragma unroll
       for (int j = 0; j < TW; ++j) {
         const int n = j0 + j;
-        if (n < nv && row < P.M) P.y[(size_t)(tok_base + n) * P.ldy + row] = __fmul_rn(sum[j], P.s_x[tok_base + n]);
+        if (n < nv && row < P.M) P.y[(size_t)(tok_base + n) * P.ldy + row] = __fmul_rn(sum[j], sxs[n]);
       }
     }
   }

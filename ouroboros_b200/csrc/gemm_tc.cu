@@ -85,8 +85,30 @@ __host__ __device__ inline TcPlan tc_plan(int N, int stages) {
 }
 
 __global__ void __launch_bounds__(kTcThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap act_map, const __grid_constant__ TcLaunch P) {
+    gemm_tc_kernel(const __grid_constant__ TcGroup Gp, const __grid_constant__ TcLaunch P0) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // this CTA's job of the group (parameter reads at fixed offsets only)
+  int jj = 0;
+#pragma unroll
+  for (int q = 1; q < kMaxTcJobs; ++q)
+    if (q < Gp.njobs && (int)blockIdx.x >= Gp.tile_begin[q]) jj = q;
+  TcLaunch P = P0;
+  const CUtensorMap* act_map = &Gp.maps[0];
+  int tile0 = 0;
+#pragma unroll
+  for (int q = 0; q < kMaxTcJobs; ++q)
+    if (q == jj) {
+      P.w = Gp.jobs[q].w;
+      P.y = Gp.jobs[q].y;
+      P.acc = Gp.jobs[q].acc;
+      P.s_x = Gp.jobs[q].s_x;
+      P.w_scale = Gp.jobs[q].w_scale;
+      P.M = Gp.jobs[q].M;
+      P.K = Gp.jobs[q].K;
+      P.ldy = Gp.jobs[q].ldy;
+      act_map = &Gp.maps[q];
+      tile0 = Gp.tile_begin[q];
+    }
   // 1024-byte alignment for the swizzled activation tiles
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -104,7 +126,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t* stages = smem + pl.stage0;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = blockIdx.x * kTcRows;
+  const int row0 = ((int)blockIdx.x - tile0) * kTcRows;
   // token tile of this CTA: [tok_base, tok_base + nv), at most P.N tokens
   const int tok_base = P.tok0 + blockIdx.y * P.N;
   const int nv = P.nvalid - blockIdx.y * P.N < P.N ? P.nvalid - blockIdx.y * P.N : P.N;
@@ -167,7 +189,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           waited = true;
         }
         for (int u = 0; u < SUB; ++u)
-          tma_load_2d(st + pl.act_off + (uint32_t)u * (uint32_t)P.N * 128u, &act_map,
+          tma_load_2d(st + pl.act_off + (uint32_t)u * (uint32_t)P.N * 128u, act_map,
                       k0 + u * kSliceK, tok_base, &full[slot]);
       }
     }
@@ -403,10 +425,11 @@ int tc_cluster_capacity(int cs, size_t smem) {
 }
 }  // namespace
 
-cudaError_t launch_gemm_tc(const TcLaunch& L0, const int8_t* q, int Btot, int smem_optin,
-                           int num_sms, cudaStream_t s, bool pdl) {
+cudaError_t launch_gemm_tc_group(const TcLaunch& L0, const TcJob* jobs, const int8_t* const* q, int n,
+                                 int Btot, int smem_optin, int num_sms, cudaStream_t s, bool pdl) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return cudaErrorNotSupported;
+  if (n < 1 || n > kMaxTcJobs) return cudaErrorInvalidValue;
   cudaError_t e = ensure_max_smem<gemm_tc_kernel>();
   if (e != cudaSuccess) return e;
   if (L0.nvalid <= 0) return cudaSuccess;
@@ -428,14 +451,24 @@ cudaError_t launch_gemm_tc(const TcLaunch& L0, const int8_t* q, int Btot, int sm
     while (st > 2 && tc_plan(N, st).total > (uint32_t)smem_optin - 2048u) --st;
     return st;
   };
+  TcGroup G{};
+  G.njobs = n;
+  int tiles = 0, min_nsb = 1 << 30;
+  for (int j = 0; j < n; ++j) {
+    G.jobs[j] = jobs[j];
+    G.tile_begin[j] = tiles;
+    tiles += (jobs[j].M + kTcRows - 1) / kTcRows;
+    const int nsb = jobs[j].K / kSliceK;
+    min_nsb = nsb < min_nsb ? nsb : min_nsb;
+  }
+  for (int j = n; j <= kMaxTcJobs; ++j) G.tile_begin[j] = tiles;
   // Token tile N (even tiles: N = ceil(B / nt) rounded up to 16) and K split
-  // Z: the pair with the smallest modelled time. Model (clocks, from traces of
-  // this kernel on B200): waves x (K / 32 / Z MMAs x (200 + 0.75 N) + the
-  // split's exchange, 1000 + 30 N (Z - 1)). A split needs a sub-block per
-  // part, room in CTA 0's stage area for the partials, and its clusters
-  // resident at once.
-  const int mt = (L.M + kTcRows - 1) / kTcRows;
-  const int nsb = L.K / kSliceK;
+  // Z: the pair with the smallest modelled time. A CTA of job j costs (clocks,
+  // from traces of this kernel on B200) K_j / 32 / Z MMAs x (200 + 0.75 N),
+  // plus the split's exchange 1000 + 30 N (Z - 1). One job: waves x that
+  // cost; a group: the larger of its longest CTA and all CTAs' work spread
+  // over the SMs. A split needs a sub-block per part, room in CTA 0's stage
+  // area for the partials, and its clusters resident at once.
   double best = -1.0;
   int bestN = 16, bestZ = 1;
   for (int nt = 1; nt <= (L.nvalid + 15) / 16; ++nt) {
@@ -447,16 +480,26 @@ cudaError_t launch_gemm_tc(const TcLaunch& L0, const int8_t* q, int Btot, int sm
     const TcPlan pl = tc_plan(N, st);
     for (int Z = 1; Z <= 4; Z *= 2) {
       if (Z > 1) {
-        if (nsb < Z) break;
+        if (min_nsb < Z) break;
         if ((size_t)(Z - 1) * (kTcRows * (N + 4) + N) * 4 > (size_t)st * pl.stage_bytes) break;
         const long cap = tc_cluster_capacity(Z, smem_floor);
         if (cap <= 0) break;
       }
-      const long ctas = (long)mt * nt * Z;
       const long slots = Z > 1 ? (long)tc_cluster_capacity(Z, smem_floor) * Z : num_sms;
-      const long waves = (ctas + slots - 1) / slots;
-      const double t = (double)waves * ((double)L.K / 32.0 / Z * (200.0 + 0.75 * N) +
-                                        (Z > 1 ? 1000.0 + 30.0 * N * (Z - 1) : 0.0));
+      const double xchg = Z > 1 ? 1000.0 + 30.0 * N * (Z - 1) : 0.0;
+      double t;
+      if (n == 1) {
+        const long ctas = (long)tiles * nt * Z;
+        t = (double)((ctas + slots - 1) / slots) * ((double)jobs[0].K / 32.0 / Z * (200.0 + 0.75 * N) + xchg);
+      } else {
+        double longest = 0.0, work = 0.0;
+        for (int j = 0; j < n; ++j) {
+          const double c = (double)jobs[j].K / 32.0 / Z * (200.0 + 0.75 * N) + xchg;
+          longest = c > longest ? c : longest;
+          work += c * (double)((jobs[j].M + kTcRows - 1) / kTcRows) * nt * Z;
+        }
+        t = work / (double)slots > longest ? work / (double)slots : longest;
+      }
       if (best < 0.0 || t < best) {
         best = t;
         bestN = N;
@@ -472,18 +515,19 @@ cudaError_t launch_gemm_tc(const TcLaunch& L0, const int8_t* q, int Btot, int sm
   if (smem < smem_floor) smem = smem_floor;
   if (smem > (size_t)smem_optin) return cudaErrorInvalidValue;
   const int nt = (L.nvalid + L.N - 1) / L.N;
-  // activations [Btot][K] int8, box 128 B x N rows, 128-byte swizzle, zero fill
-  CUtensorMap map;
-  const cuuint64_t dims[2] = {(cuuint64_t)L.K, (cuuint64_t)Btot};
-  const cuuint64_t strides[1] = {(cuuint64_t)L.K};
-  const cuuint32_t box[2] = {128u, (cuuint32_t)L.N};
-  const cuuint32_t estr[2] = {1u, 1u};
-  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), dims, strides, box, estr,
-          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return cudaErrorInvalidValue;
-  // one CTA per (128-row tile, token tile, part of K)
-  const dim3 grid(mt, nt, L.ksplit);
+  // activations [Btot][K_j] int8, box 128 B x N rows, 128-byte swizzle, zero fill
+  for (int j = 0; j < n; ++j) {
+    const cuuint64_t dims[2] = {(cuuint64_t)jobs[j].K, (cuuint64_t)Btot};
+    const cuuint64_t strides[1] = {(cuuint64_t)jobs[j].K};
+    const cuuint32_t box[2] = {128u, (cuuint32_t)L.N};
+    const cuuint32_t estr[2] = {1u, 1u};
+    if (enc(&G.maps[j], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q[j]), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  // one CTA per (128-row tile of a job, token tile, part of K)
+  const dim3 grid(tiles, nt, L.ksplit);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kTcThreads, 1, 1);
@@ -505,7 +549,21 @@ cudaError_t launch_gemm_tc(const TcLaunch& L0, const int8_t* q, int Btot, int sm
   }
   cfg.attrs = attr;
   cfg.numAttrs = (unsigned)na;
-  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, map, L);
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, G, L);
+}
+
+cudaError_t launch_gemm_tc(const TcLaunch& L, const int8_t* q, int Btot, int smem_optin, int num_sms,
+                           cudaStream_t s, bool pdl) {
+  TcJob j{};
+  j.w = L.w;
+  j.y = L.y;
+  j.acc = L.acc;
+  j.s_x = L.s_x;
+  j.w_scale = L.w_scale;
+  j.M = L.M;
+  j.K = L.K;
+  j.ldy = L.ldy;
+  return launch_gemm_tc_group(L, &j, &q, 1, Btot, smem_optin, num_sms, s, pdl);
 }
 
 }  // namespace ouroq

@@ -4,6 +4,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace ouroq {
@@ -162,6 +163,25 @@ struct TcLaunch {
   unsigned* status;
 };
 
+// A grouped tensor-core launch: up to kMaxTcJobs ternary products
+// y_j = W_j . q_j with the same batch, in ONE launch (the projections of a
+// layer). The grid's x covers the 128-row tiles of every job in order.
+constexpr int kMaxTcJobs = 8;
+struct TcJob {
+  const uint8_t* w;
+  float* y;
+  int32_t* acc;       // optional debug [tokens][M]
+  const float* s_x;   // [tokens]
+  float w_scale;
+  int M, K, ldy;
+};
+struct TcGroup {
+  CUtensorMap maps[kMaxTcJobs];    // each job's activations [Btot][K] int8
+  TcJob jobs[kMaxTcJobs];
+  int tile_begin[kMaxTcJobs + 1];  // job j: 128-row tiles [tile_begin[j], tile_begin[j + 1])
+  int njobs;
+};
+
 bool gemm_tc_supported(int fmt, int M, int K, int B);
 size_t gemm_tc_smem_bytes(int N, int stages);
 // q: int8 activations [Btot][K] (16-byte aligned rows). One launch; the grid
@@ -171,6 +191,10 @@ size_t gemm_tc_smem_bytes(int N, int stages);
 // overlap the previous kernel; the activations are read after it).
 cudaError_t launch_gemm_tc(const TcLaunch& L, const int8_t* q, int Btot, int smem_optin,
                            int num_sms, cudaStream_t s, bool pdl);
+// n jobs (same K % 128 == 0 rule, ternary) in one launch: q[j] int8 [Btot][K_j];
+// L carries the batch (nvalid, tok0) and the status word.
+cudaError_t launch_gemm_tc_group(const TcLaunch& L, const TcJob* jobs, const int8_t* const* q, int n,
+                                 int Btot, int smem_optin, int num_sms, cudaStream_t s, bool pdl);
 // Sign weights (kSign1) on the tensor cores: one group accumulator per 128 k,
 // the fp32 fold in ascending group order. The grid covers (128-row tiles) x
 // (token tiles of 16 or 32) x (parts of the groups, a cluster chaining the

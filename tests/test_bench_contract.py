@@ -81,3 +81,5 @@ def test_graph_plan_runs_exactly_the_requested_steps(steps):
     G, reps, rest = bench.graph_plan(steps, ncop)
     assert G * reps + rest == steps
     assert G % ncop == 0 and G <= 64 * ncop and rest < max(G, steps + 1)
+    if steps <= 4096:
+        assert reps == 0 and rest == steps  # one graph, no boundary inside the timed region

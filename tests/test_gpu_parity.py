@@ -301,6 +301,63 @@ def test_gemm_group_f32act_c2_layer(ctx, oracle, B):
         w.free()
 
 
+@pytest.mark.parametrize("B", [16, 64, 100])
+def test_gemm_group_tensor_core_c2_layer(ctx, oracle, B):
+    # from 16 tokens the five projections of a layer run as ONE tensor-core
+    # launch over every matrix's row tiles (each CTA finds its matrix, K of
+    # 2560 and 6912 in one grid); the fp32 entry quantises the four distinct
+    # inputs in one launch first
+    import torch
+    shapes = [(3840, 2560), (2560, 2560), (6912, 2560), (6912, 2560), (2560, 6912)]
+    inputs = [oracle.normals(700 + i, B * k).reshape(B, k) for i, k in enumerate([2560, 2560, 2560, 6912])]
+    input_of = [0, 1, 2, 2, 3]
+    ws_, want, qs, ss = [], [], [], []
+    for i, (M, K) in enumerate(shapes):
+        packed, wsc, _ = tern_case(oracle, M, K, 1, seed=800 + i)
+        qr, sr = oracle.quantize_act(inputs[input_of[i]])
+        want.append(oracle.gemm_tern2(packed, M, K, wsc, qr, sr)[1])
+        ws_.append(ctx.upload(oq.TERNARY2, packed, M, K, w_scale=wsc))
+        qs.append(dev(qr))
+        ss.append(dev(sr))
+    ys = [torch.empty((B, M), dtype=torch.float32, device="cuda") for M, _ in shapes]
+    n0 = ctx.launch_count()
+    ctx.gemm_group(ws_, qs, ss, ys)
+    assert ctx.launch_count() - n0 == 1
+    for y, yr in zip(ys, want):
+        assert np.array_equal(host(y), yr)
+    xd = [dev(x) for x in inputs]
+    ys2 = [torch.empty((B, M), dtype=torch.float32, device="cuda") for M, _ in shapes]
+    n0 = ctx.launch_count()
+    ctx.gemm_group_f32act(ws_, [xd[input_of[i]] for i in range(len(shapes))], ys2)
+    assert ctx.launch_count() - n0 == 2  # quantise + one grouped tensor-core launch
+    for y, yr in zip(ys2, want):
+        assert np.array_equal(host(y), yr)
+    for w in ws_:
+        w.free()
+    ctx.check_device()
+
+
+def test_gemm_group_sign_tensor_core(ctx, oracle):
+    # sign weights from 16 tokens in a group: one tensor-core launch per matrix
+    import torch
+    B = 32
+    shapes = [(300, 1024), (4096, 4096)]
+    ws_, want, qs, ss = [], [], [], []
+    for i, (M, K) in enumerate(shapes):
+        packed, sc, x = sign_case(oracle, M, K, B, seed=900 + i)
+        qr, sr = oracle.quantize_act(x, None, 0)
+        want.append(oracle.gemm_sign1(packed, sc, M, K, qr, sr)[1])
+        ws_.append(ctx.upload(oq.SIGN1G128, packed, M, K, scales=sc))
+        qs.append(dev(qr))
+        ss.append(dev(sr))
+    ys = [torch.empty((B, M), dtype=torch.float32, device="cuda") for M, _ in shapes]
+    ctx.gemm_group(ws_, qs, ss, ys)
+    for y, yr in zip(ys, want):
+        assert np.array_equal(host(y), yr)
+    for w in ws_:
+        w.free()
+
+
 @pytest.mark.parametrize("M,K,B", [(300, 2560, 3), (77, 6912, 6), (1000, 1152, 7), (33, 128, 8)])
 def test_stream_gemv_batches_exact(ctx, oracle, M, K, B):
     # three to eight tokens through the one-launch stream GEMV: rows off the
