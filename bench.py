@@ -92,9 +92,10 @@ def parse():
     ap.add_argument("--workload", default="layer", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ouroq", choices=["ouroq", "reference"])
     ap.add_argument("--no-pdl", action="store_true")
-    ap.add_argument("--prefetch", default="on", choices=["on", "off"],
+    ap.add_argument("--prefetch", default="off", choices=["on", "off"],
                     help="each step's GEMV launch prefetches the next step's weights into L2 "
-                         "(ouroq_set_prefetch), as a decode loop does for its next projection group")
+                         "(ouroq_set_prefetch), as a decode loop may for its next projection group "
+                         "(measured no faster on the layer workload, so off by default)")
     ap.add_argument("--prefetch-ahead", type=int, default=1,
                     help="with --prefetch on: the step whose weights each launch prefetches, counted "
                          "ahead of the current one (1 = the next step)")
