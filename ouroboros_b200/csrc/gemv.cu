@@ -891,59 +891,65 @@ cudaError_t launch_fmt(const GemvLaunch& L, int grid, size_t smem, cudaStream_t 
 
 }  // namespace
 
-void balance_tiles(GemvLaunch& L, int grid, int per_chunk) {
-  // Tiles of job j weigh K_j / per_chunk (proportional to their bytes). The
-  // contiguous split that minimises the heaviest CTA: the smallest bound cap
-  // for which filling CTAs greedily (a CTA takes the next tile while its load
-  // stays within cap) needs at most `grid` CTAs, found by bisection. A launch
-  // ends with its heaviest CTA, so this bound is what the split costs.
+void balance_tiles(GemvLaunch& L, int grid, int per_chunk, int unit_q) {
+  // Tiles of job j weigh K_j / per_chunk (proportional to their bytes); with
+  // unit_q > 0 a CTA also pays unit_q / 4 x B per 128-value unit of every
+  // distinct input it quantises (its prologue); loads are kept in quarters. The contiguous split that minimises
+  // the heaviest CTA: the smallest bound cap for which filling CTAs greedily
+  // (a CTA takes the next tile while its load stays within cap) needs at most
+  // `grid` CTAs, found by bisection. A launch ends with its heaviest CTA, so
+  // this bound is what the split costs.
   const int tiles = L.ntiles;
-  auto weight = [&](int t, int& j) {
-    while (j + 1 < L.njobs && t >= L.jobs[j + 1].tile_begin) ++j;
-    return (long long)(L.jobs[j].K / per_chunk);
+  auto tile_w = [&](int j) { return 4LL * (L.jobs[j].K / per_chunk); };
+  auto input_w = [&](int j) { return (long long)unit_q * L.B * (L.jobs[j].K / 128); };
+  // does job j read an input that jobs jf .. j-1 (the CTA's earlier jobs) do not?
+  auto new_input = [&](int jf, int j) {
+    for (int i = jf; i < j; ++i)
+      if (L.jobs[i].xf == L.jobs[j].xf && L.jobs[i].K == L.jobs[j].K) return false;
+    return true;
   };
-  long long total = 0, heaviest = 0;
+  // greedy fill under cap; returns the CTAs it needs (and writes the split)
+  auto fill = [&](long long cap, bool write) {
+    int n = 1, j = 0, jf = -1, jprev = -1;
+    long long load = 0;
+    if (write) L.cta_tile[0] = 0;
+    for (int t = 0; t < tiles; ++t) {
+      while (j + 1 < L.njobs && t >= L.jobs[j + 1].tile_begin) ++j;
+      const long long w = tile_w(j);
+      long long x = 0;
+      if (jf < 0 || (j != jprev && new_input(jf, j))) x = input_w(j);
+      if (jf >= 0 && load + w + x > cap) {
+        if (write && n <= grid) L.cta_tile[n] = (uint16_t)t;
+        ++n;
+        load = 0;
+        jf = -1;
+        x = input_w(j);
+      }
+      if (jf < 0) jf = j;
+      load += w + x;
+      jprev = j;
+    }
+    if (write)
+      for (int c = n; c <= grid; ++c) L.cta_tile[c] = (uint16_t)tiles;
+    return n;
+  };
+  long long lo = 0, hi = 0;
   {
     int j = 0;
     for (int t = 0; t < tiles; ++t) {
-      const long long w = weight(t, j);
-      total += w;
-      heaviest = w > heaviest ? w : heaviest;
+      while (j + 1 < L.njobs && t >= L.jobs[j + 1].tile_begin) ++j;
+      const long long one = tile_w(j) + input_w(j);
+      lo = one > lo ? one : lo;
+      hi += one;
     }
   }
-  auto ctas_needed = [&](long long cap) {
-    int n = 1, j = 0;
-    long long load = 0;
-    for (int t = 0; t < tiles; ++t) {
-      const long long w = weight(t, j);
-      if (load + w > cap) {
-        ++n;
-        load = 0;
-      }
-      load += w;
-    }
-    return n;
-  };
-  long long lo = (total + grid - 1) / grid;
-  if (lo < heaviest) lo = heaviest;
-  long long hi = lo + heaviest;  // greedy under this cap never needs more than grid CTAs
+  if (hi < lo) hi = lo;
   while (lo < hi) {
     const long long mid = (lo + hi) / 2;
-    if (ctas_needed(mid) <= grid) hi = mid;
+    if (fill(mid, false) <= grid) hi = mid;
     else lo = mid + 1;
   }
-  int c = 0, j = 0;
-  long long load = 0;
-  L.cta_tile[0] = 0;
-  for (int t = 0; t < tiles; ++t) {
-    const long long w = weight(t, j);
-    if (load + w > lo) {
-      L.cta_tile[++c] = (uint16_t)t;
-      load = 0;
-    }
-    load += w;
-  }
-  while (c < grid) L.cta_tile[++c] = (uint16_t)tiles;
+  fill(lo, true);
 }
 
 bool gemv_prepare(GemvLaunch& L, int num_sms, int smem_optin, int* grid_out, size_t* smem_out) {
@@ -964,7 +970,7 @@ bool gemv_prepare(GemvLaunch& L, int num_sms, int smem_optin, int* grid_out, siz
   int grid = tiles < num_sms ? tiles : num_sms;
   if (grid > kMaxGemvCtas) grid = kMaxGemvCtas;
   (void)total;
-  balance_tiles(L, grid, wpc);
+  balance_tiles(L, grid, wpc, 0);
   // activations one CTA keeps resident: the jobs its tile range touches (one
   // row for all of them under a fused norm)
   int xcap = 0, gcap = 0;

@@ -974,6 +974,21 @@ int cluster_ctas(int B) {
 
 }  // namespace
 
+// The prologue's cost in the tile split: quarters of a weight chunk (512
+// bytes) that quantising one 128-value input unit of a token is worth on a
+// CTA's critical path. Measured on the BitNet-2B layer (B = 1, 5,000 steps):
+// 0 (weights only) 8.31 us a step, 2 to 7 quarters 7.85 us, 8 and 12 quarters
+// 8.54 us (B = 2: 11.71 us at 0, 11.73 us from 2 to 6). OUROQ_STREAM_UNIT_Q
+// overrides it.
+int stream_unit_weight() {
+  const char* e = getenv("OUROQ_STREAM_UNIT_Q");
+  if (e && *e) {
+    const int v = atoi(e);
+    if (v >= 0 && v <= 256) return v;
+  }
+  return 4;
+}
+
 bool gemv_stream_prepare(GemvLaunch& L, int num_sms, int* grid_out, size_t* smem_out) {
   *grid_out = 0;
   *smem_out = 0;
@@ -1004,7 +1019,7 @@ bool gemv_stream_prepare(GemvLaunch& L, int num_sms, int* grid_out, size_t* smem
   // the split over single CTAs; the largest share of codes a CTA quantises
   auto split = [&](int grid_max, int cs) {
     int grid = tiles < grid_max ? tiles : grid_max;
-    balance_tiles(L, grid, 64);
+    balance_tiles(L, grid, 64, stream_unit_weight());
     // no empty CTA beyond the last cluster: the split fills CTAs from the first one on
     while (grid > 1 && L.cta_tile[grid - 1] >= L.cta_tile[grid]) --grid;
     const int used = grid;

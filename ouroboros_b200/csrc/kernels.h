@@ -133,8 +133,10 @@ cudaError_t launch_rotate(const float* x, float* out, const float* signs, int B,
 bool gemv_prepare(GemvLaunch& L, int num_sms, int smem_optin, int* grid, size_t* smem);
 cudaError_t launch_gemv(GemvLaunch& L, int num_sms, int smem_optin, cudaStream_t s, bool pdl);
 // Contiguous tile ranges per CTA (L.cta_tile[0..grid]) that minimise the
-// heaviest CTA's weight bytes; needs L.ntiles and the jobs' tile_begin.
-void balance_tiles(GemvLaunch& L, int grid, int per_chunk);
+// heaviest CTA's load: its weight chunks, plus unit_q / 4 chunks x B per
+// 128-value unit of each distinct input it quantises (0: weights only); needs
+// L.ntiles and the jobs' tile_begin.
+void balance_tiles(GemvLaunch& L, int grid, int per_chunk, int unit_q);
 // The streaming decode GEMV (gemv_stream.cu): fused ternary launches of one or
 // two tokens without rotation or norm. prepare returns false when the launch
 // is not of that kind (the caller then uses launch_gemv).
