@@ -667,8 +667,8 @@ def run_ouroq(args, rank, world, local_rank):
             kms = timed(g2)
         kern_s = kms / 1e3 / steps
         kern_bytes = nb["gemm"]
-        kernel = (("gemm_tc_kernel (tcgen05 kind::i8, one grouped launch)" if len(mats) > 1 else "gemm_tc_kernel (tcgen05 kind::i8)") if fmt == TERN and B >= 16
-                  else "gemm_sign_tc_kernel (tcgen05 kind::i8, group accumulators)" if B >= 16
+        kernel = (("gemm_tc_kernel (tcgen05 kind::i8, one grouped launch)" if len(mats) > 1 else "gemm_tc_kernel (tcgen05 kind::i8)") if fmt == TERN and B >= 9
+                  else "gemm_sign_tc_kernel (tcgen05 kind::i8, group accumulators)" if B >= 9
                   else "gemv_kernel (8-token chunks)")
         del g2
     if tensor_bound:

@@ -165,7 +165,7 @@ ouroq_status ouroq_gemm(ouroq_ctx *ctx, const ouroq_weight *w, const int8_t *q, 
                         int B, float *y, int32_t *acc_debug, void *stream);
 
 /* Grouped product: n (<= 8) independent products y_i = W_i . q_i, all weights
- * of one format. Up to 8 tokens one GEMV launch; from 16 tokens TERNARY2
+ * of one format. Up to 8 tokens one GEMV launch; from 9 tokens TERNARY2
  * weights run as ONE tensor-core launch over every matrix's row tiles (the
  * projections of a layer), SIGN1G128 weights one tensor-core launch each.
  * Used for the projections of a layer. */

@@ -307,7 +307,9 @@ ouroq_status run_gemv(ouroq_ctx* ctx, GemvLaunch& L, cudaStream_t s) {
 }
 
 // Token batches from this size up run on the tensor cores (ternary and sign weights).
-constexpr int kTcMinBatch = 16;
+// (From 9 tokens one tensor-core launch, its token tile of 16 padded with
+// zero rows by the TMA, beats the two GEMV launches that 9-15 tokens take.)
+constexpr int kTcMinBatch = 9;
 
 ouroq_status gemm_impl(ouroq_ctx* ctx, const ouroq_weight* w, const int8_t* q, const float* s_x,
                        int B, float* y, int32_t* acc, cudaStream_t s) {

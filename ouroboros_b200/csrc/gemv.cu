@@ -58,7 +58,7 @@ constexpr int kCThreads = kCWarps * 32;
 constexpr int kThreads = kCThreads + 32;
 constexpr int kMaxStages = kMaxGemvStages;
 constexpr int kTernSliceChunks = 64;  // 16-B chunks per row per stage (32 KB stage)
-constexpr int kSignSliceChunks = 16;  // 16 groups per row per stage (8 KB + 1 KB scales)
+constexpr int kSignSliceChunks = 32;  // 32 groups per row per stage (16 KB + 2 KB scales)
 
 // Stage layout: weights [chunk][32 rows][16 B]; sign stages append the fp16
 // group scales of the slice as [group][32 rows].
@@ -86,7 +86,7 @@ __host__ __device__ constexpr uint32_t align128(uint32_t v) { return (v + 127u) 
 //   xwork       xcap bytes: int8 activations [job][B][K] of the CTA's jobs
 //   qg          gcap ints: per-(token, 128-group) activation sums
 //   sx / qtot   [8 jobs][8 tokens] per-token scales / sums
-//   red         ternary: max(2, defer) x kCWarps*B*32 ints; sign: B*slice*32 floats
+//   red         ternary: max(2, defer) x kCWarps*B*32 ints; sign: 2 x B*slice*32 floats
 struct Plan {
   uint32_t bars, ring, xwork, qg, sx, qtot, red, total;
 };
@@ -112,7 +112,7 @@ __host__ __device__ inline Plan make_plan(int fmt, int B, int stages, int xcap, 
   // ternary: two buffers of per-warp partials (one barrier per tile), or one
   // slot per tile of the CTA (deferred reduction)
   const uint32_t nbuf = defer > 2 ? (uint32_t)defer : 2u;
-  const uint32_t red_bytes = fmt == kTern2 ? nbuf * kCWarps * b * 32u * 4u : b * slice * 32u * 4u;
+  const uint32_t red_bytes = fmt == kTern2 ? nbuf * kCWarps * b * 32u * 4u : 2u * b * slice * 32u * 4u;
   p.total = p.red + align128(red_bytes);
   return p;
 }
@@ -781,6 +781,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         int c0, c1;
         slice_range<FMT>(K, s, ns, c0, c1);
         const uint8_t* stg = ring + (size_t)slot * STAGE;
+        // the stage's terms, in one of two buffers: a buffer is rewritten two
+        // stages later, after its reader (the token's owner warp) has passed
+        // the next stage's barrier -- one CTA barrier per stage
+        float* tb = terms + (st & 1) * (B * SC * 32);
         const int sfirst = ((warp - st) % kCWarps + kCWarps) % kCWarps;
         for (int kc = sfirst; kc < c1 - c0; kc += kCWarps) {
           const uint4 wv = *reinterpret_cast<const uint4*>(stg + kc * 512 + lane * 16);
@@ -810,7 +814,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             const int sb = a[0] + (a[1] >> 1) + (a[2] >> 2) + (a[3] >> 3) + (a[4] >> 4) +
                            (a[5] >> 5) + (a[6] >> 6) + (a[7] >> 7);
             const int accg = 2 * sb - qg[b * G + g];
-            terms[(b * SC + kc) * 32 + lane] = __fmul_rn(__int2float_rn(accg), sc);
+            tb[(b * SC + kc) * 32 + lane] = __fmul_rn(__int2float_rn(accg), sc);
             if (J.acc && row_ok) J.acc[((size_t)b * J.M + row) * G + g] = accg;
           }
         }
@@ -822,10 +826,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         for (int b = 0; b < B; ++b) {
           if (b % kCWarps != warp) continue;  // static index keeps sum[] in registers
           float v = sum[b];
-          for (int kc = 0; kc < c1 - c0; ++kc) v = __fadd_rn(v, terms[(b * SC + kc) * 32 + lane]);
+          for (int kc = 0; kc < c1 - c0; ++kc) v = __fadd_rn(v, tb[(b * SC + kc) * 32 + lane]);
           sum[b] = v;
         }
-        named_bar_sync(2, kCThreads);
       }
 #pragma unroll
       for (int b = 0; b < B; ++b) {

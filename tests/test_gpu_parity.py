@@ -137,8 +137,9 @@ def test_gemm_tern2_batched_c2(ctx, oracle, B):
     w.free()
 
 
-# B >= 16: tcgen05 tensor-core path (u8 codes x s8 activations, TMEM accumulators)
-@pytest.mark.parametrize("M,K,B", [(128, 128, 16), (256, 256, 17), (200, 384, 33), (96, 512, 64),
+# B >= 9: tcgen05 tensor-core path (u8 codes x s8 activations, TMEM accumulators)
+@pytest.mark.parametrize("M,K,B", [(128, 128, 16), (256, 256, 17), (200, 384, 33), (96, 512, 64), (300, 640, 9),
+                                   (1000, 2560, 12),
                                    (6912, 2560, 64), (2560, 6912, 100), (3840, 2560, 256),
                                    (1000, 1024, 300), (2560, 2560, 512)])
 def test_gemm_tern2_tensor_core(ctx, oracle, M, K, B):
@@ -202,10 +203,10 @@ def test_gemm_sign1_c3_batch32(ctx, oracle, M):
     w.free()
 
 
-@pytest.mark.parametrize("M,K,B", [(4096, 4096, 32), (11008, 4096, 32), (300, 384, 17), (77, 128, 16),
+@pytest.mark.parametrize("M,K,B", [(4096, 4096, 32), (11008, 4096, 32), (300, 384, 17), (77, 128, 16), (200, 512, 9),
                                    (256, 2176, 40), (128, 512, 100)])
 def test_gemm_sign1_tensor_core(ctx, oracle, M, K, B):
-    # batches from 16 tokens run the sign tensor-core kernel (one launch): the
+    # batches from 9 tokens run the sign tensor-core kernel (one launch): the
     # per-group accumulators and the ascending-group fp32 fold must equal the
     # oracle's bit for bit; row counts off the 128-row tile, K off the 512-k
     # stage (a last stage of one group), token tiles of 16 and 32 with padding
@@ -301,9 +302,9 @@ def test_gemm_group_f32act_c2_layer(ctx, oracle, B):
         w.free()
 
 
-@pytest.mark.parametrize("B", [16, 64, 100])
+@pytest.mark.parametrize("B", [11, 16, 64, 100])
 def test_gemm_group_tensor_core_c2_layer(ctx, oracle, B):
-    # from 16 tokens the five projections of a layer run as ONE tensor-core
+    # from 9 tokens the five projections of a layer run as ONE tensor-core
     # launch over every matrix's row tiles (each CTA finds its matrix, K of
     # 2560 and 6912 in one grid); the fp32 entry quantises the four distinct
     # inputs in one launch first
@@ -338,7 +339,7 @@ def test_gemm_group_tensor_core_c2_layer(ctx, oracle, B):
 
 
 def test_gemm_group_sign_tensor_core(ctx, oracle):
-    # sign weights from 16 tokens in a group: one tensor-core launch per matrix
+    # sign weights from 9 tokens in a group: one tensor-core launch per matrix
     import torch
     B = 32
     shapes = [(300, 1024), (4096, 4096)]

@@ -93,11 +93,11 @@ def _weight(ctx, oracle, fmt, M, K, seed):
     return ctx.upload(fmt, payload, M, K), ref
 
 
-# (format, M, K, B, hadamard block): B <= 2 takes the single fused launch,
-# larger batches go through the fixed scratch (tensor cores for ternary
-# B >= 16, several token passes at B = 300; GEMV chunks for sign weights);
-# the reference formats and F16 need no scratch (matvec_tl1's order for one
-# token, matmul_tl1's K columns for several).
+# (format, M, K, B, hadamard block): ternary weights without a rotation up to
+# 8 tokens take the single fused launch (no scratch); the other batches go
+# through the fixed scratch (tensor cores from 9 tokens, several token passes
+# at B = 300); the reference formats and F16 need no scratch (matvec_tl1's
+# order for one token, matmul_tl1's K columns for several).
 CASES = [
     (oq.TERNARY2, 2560, 2560, 2, 0),
     (oq.TERNARY2, 2560, 2560, 4, 0),
