@@ -580,12 +580,18 @@ def run_ouroq(args, rank, world, local_rank):
 
     PREFIX = 2  # untimed steps ahead of the timed window, in the same graph
 
+    side = torch.cuda.Stream(device)
+
     def capture_windowed(fn, n):
         """One CUDA graph: PREFIX untimed steps (the rotation's last copies),
-        an event-record node, steps 0..n-1, an event-record node. The timed
-        window then holds exactly n steps and opens on a running pipeline: no
-        graph launch, and no first launch without a predecessor to overlap,
-        inside it."""
+        then steps 0..n-1, with an event-record node on a branch after the
+        last untimed step and one after the last timed step. The timed window
+        then runs from the end of step -1 to the end of step n-1: exactly n
+        steps, opening on a running pipeline (no graph launch inside it). The
+        event nodes sit on a side branch, so each step's kernels keep their
+        programmatic dependency on the previous step's: an event node on the
+        main chain would make the first timed launch wait for its
+        predecessor's completion instead of overlapping its tail."""
         e0 = torch.cuda.Event(enable_timing=True, external=True)
         e1 = torch.cuda.Event(enable_timing=True, external=True)
         g = torch.cuda.CUDAGraph()
@@ -593,10 +599,13 @@ def run_ouroq(args, rank, world, local_rank):
             for i in range(-PREFIX, 0):
                 fn(i)
             n0 = ctx.launch_count()
-            e0.record(stream)
+            side.wait_stream(stream)
+            e0.record(side)
             for i in range(n):
                 fn(i)
-            e1.record(stream)
+            side.wait_stream(stream)
+            e1.record(side)
+            stream.wait_stream(side)
             per = (ctx.launch_count() - n0) / max(n, 1)
         return g, e0, e1, per
 
