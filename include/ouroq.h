@@ -365,7 +365,12 @@ ouroq_status ouroq_matmul_q(ouroq_ctx *ctx, const ouroq_weight *w, const float *
  * k = 1). Synchronous. Page-locked host buffers (cudaHostAlloc /
  * cudaHostRegister) are copied by DMA directly, and buffers that sit back to
  * back in memory cross in one copy; pageable ones go through the context's
- * page-locked staging buffer. */
+ * page-locked staging buffer. When k <= 8, the weights are TERNARY2 or
+ * SIGN1G128 and every y_host[i] is page-locked, mapped and covers its
+ * [k][M_i] floats inside one allocation, the kernel stores the results into
+ * y_host directly (no staging buffer, no copy back); otherwise y goes
+ * through the device stage. Either way y_host holds the results when the
+ * call returns OUROQ_OK. */
 ouroq_status ouroq_matmul_q_group(ouroq_ctx *ctx, int n, const ouroq_weight *const *w,
                                   const float *const *x_host, int k, float *const *y_host);
 /* hadamard::rotate_fwd (hadamard.rs:41-53) in place on a host buffer of n floats. */

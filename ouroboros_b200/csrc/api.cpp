@@ -1345,6 +1345,42 @@ static bool host_pinned(const void* p) {
   return a.type == cudaMemoryTypeHost;
 }
 
+// cuPointerGetAttributes, resolved once through the runtime (no libcuda link).
+using PointerAttrsFn = CUresult (*)(unsigned int, CUpointer_attribute*, void**, CUdeviceptr);
+static PointerAttrsFn pointer_attrs_fn() {
+  static PointerAttrsFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuPointerGetAttributes", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return static_cast<PointerAttrsFn>(nullptr);
+    }
+    return reinterpret_cast<PointerAttrsFn>(p);
+  }();
+  return fn;
+}
+
+// A page-locked host buffer that kernels address at its host address, with
+// [p, p + bytes) inside one allocation: a product may store into it directly.
+// Any doubt (unknown pointer, a different device address, a range the
+// allocation does not cover, a refused query) answers no.
+static bool host_mapped(const void* p, size_t bytes) {
+  PointerAttrsFn fn = pointer_attrs_fn();
+  if (!fn || !p) return false;
+  unsigned int type = 0;
+  CUdeviceptr dev = 0, start = 0;
+  size_t size = 0;
+  CUpointer_attribute at[4] = {CU_POINTER_ATTRIBUTE_MEMORY_TYPE, CU_POINTER_ATTRIBUTE_DEVICE_POINTER,
+                               CU_POINTER_ATTRIBUTE_RANGE_START_ADDR, CU_POINTER_ATTRIBUTE_RANGE_SIZE};
+  void* out[4] = {&type, &dev, &start, &size};
+  const CUdeviceptr a = static_cast<CUdeviceptr>(reinterpret_cast<uintptr_t>(p));
+  if (fn(4, at, out, a) != CUDA_SUCCESS) return false;
+  return type == CU_MEMORYTYPE_HOST && dev == a && size > 0 && start <= a && bytes <= size &&
+         a - start <= size - bytes;
+}
+
 static ouroq_status grow_pinned(ouroq_ctx* ctx, float*& buf, size_t& cap, size_t n,
                                 const char* what) {
   if (n <= cap) return OUROQ_OK;
@@ -1424,9 +1460,20 @@ ouroq_status ouroq_matmul_q_group(ouroq_ctx* ctx, int n, const ouroq_weight* con
   if (st != OUROQ_OK) return st;
   st = grow(ctx, ctx->y_stage, ctx->y_cap, ytot, "y stage");
   if (st != OUROQ_OK) return st;
+  bool same_fmt = true;
+  for (int i = 0; i < n; ++i) same_fmt &= w[i]->fmt == w[0]->fmt;
+  // the quantised formats at small k: one grouped GEMV launch (as
+  // ouroq_gemm_group_f32act), whose kernels store y with plain stores; when
+  // every output is page-locked and mapped, they store into it directly (no
+  // stage, no download)
+  const bool grouped =
+      same_fmt && !is_ref_format(w[0]->fmt) && !is_half_format(w[0]->fmt) && k <= kGemvMaxB;
+  bool y_direct = grouped;
+  for (const HostSeg& sg : ys) y_direct = y_direct && host_mapped(sg.host, sg.n * 4);
   bool x_staged = false, y_staged = false;
   for (HostSeg& sg : xs) x_staged |= !(sg.pinned = host_pinned(sg.host));
-  for (HostSeg& sg : ys) y_staged |= !(sg.pinned = host_pinned(sg.host));
+  if (!y_direct)
+    for (HostSeg& sg : ys) y_staged |= !(sg.pinned = host_pinned(sg.host));
   if (x_staged) {
     st = grow_pinned(ctx, ctx->hx_stage, ctx->hx_cap, xtot, "pinned x stage");
     if (st != OUROQ_OK) return st;
@@ -1442,28 +1489,38 @@ ouroq_status ouroq_matmul_q_group(ouroq_ctx* ctx, int n, const ouroq_weight* con
   if (st != OUROQ_OK) return st;
   const float* xd[kMaxGemvJobs];
   float* yd[kMaxGemvJobs];
-  bool same_fmt = true;
   for (int i = 0; i < n; ++i) {
     xd[i] = ctx->x_stage + xs[slot[i]].dev_off;
-    yd[i] = ctx->y_stage + ys[i].dev_off;
-    same_fmt &= w[i]->fmt == w[0]->fmt;
+    yd[i] = y_direct ? y_host[i] : ctx->y_stage + ys[i].dev_off;
   }
-  // the quantised formats at small k: one grouped launch (as ouroq_gemm_group_f32act)
   bool done = false;
-  if (same_fmt && !is_ref_format(w[0]->fmt) && !is_half_format(w[0]->fmt) && k <= kGemvMaxB) {
+  if (grouped) {
+    // UNSUPPORTED is answered before any launch that stores y
     st = ouroq_gemm_group_f32act(ctx, n, w, xd, k, nullptr, nullptr, yd, s);
     if (st == OUROQ_OK) done = true;
     else if (st != OUROQ_ERR_UNSUPPORTED) return st;
+  }
+  if (!done && y_direct) {  // other routes write the device stage
+    y_direct = false;
+    for (HostSeg& sg : ys) y_staged |= !(sg.pinned = host_pinned(sg.host));
+    if (y_staged) {
+      st = grow_pinned(ctx, ctx->hy_stage, ctx->hy_cap, ytot, "pinned y stage");
+      if (st != OUROQ_OK) return st;
+    }
+    for (int i = 0; i < n; ++i) yd[i] = ctx->y_stage + ys[i].dev_off;
   }
   for (int i = 0; i < n && !done; ++i) {
     st = f32act_impl(ctx, w[i], xd[i], k, nullptr, 0, yd[i], s, Tl1Order::kAuto);
     if (st != OUROQ_OK) return st;
   }
-  st = copy_segs(ctx, ys, ctx->y_stage, ctx->hy_stage, false, s);
-  if (st != OUROQ_OK) return st;
+  if (!y_direct) {
+    st = copy_segs(ctx, ys, ctx->y_stage, ctx->hy_stage, false, s);
+    if (st != OUROQ_OK) return st;
+  }
   CU(ctx, cudaStreamSynchronize(s), "stream sync");
-  for (const HostSeg& sg : ys)
-    if (!sg.pinned) std::memcpy(sg.host, ctx->hy_stage + sg.dev_off, sg.n * 4);
+  if (!y_direct)
+    for (const HostSeg& sg : ys)
+      if (!sg.pinned) std::memcpy(sg.host, ctx->hy_stage + sg.dev_off, sg.n * 4);
   return OUROQ_OK;
 }
 
