@@ -503,6 +503,14 @@ def test_host_group_call_matches_oracle(ctx, oracle, k):
     for y, r in zip(mixed, want):
         yn = y if isinstance(y, np.ndarray) else y.numpy()
         assert np.array_equal(yn.reshape(r.shape), r)
+    # page-locked inputs off the 16-byte grid (the device stage's slots stay
+    # aligned for the kernels)
+    xodd = torch.empty(xcat.numel() + 1, dtype=torch.float32).pin_memory()
+    xodd[1:].copy_(xcat)
+    ycat.zero_()
+    ctx.matmul_q_group(ws, [xodd[1 + off[xi]:1 + off[xi + 1]] for _, _, xi in shapes], ys)
+    for y, r in zip(ys, want):
+        assert np.array_equal(y.numpy().reshape(r.shape), r)
     with pytest.raises(oq.OuroqError):
         ctx.matmul_q_group(ws[:1], [xs[0][:, :100]])
     for w in ws:
