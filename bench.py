@@ -737,8 +737,9 @@ def run_ouroq(args, rank, world, local_rank):
                 ctx.matmul_q_group(wts[i % ncop], [xhv[i % 2][xi] for _, _, _, xi in mats], yhv)
         wrapper = e2e_wrapper
         how = ("ouroq_matmul_q_group called through its C ABI as a foreign caller binds it (one "
-               "synchronous call a step, page-locked host x in, host y out, status checked), "
-               "host clock around the calls")
+               "synchronous call a step, status checked): page-locked host x copied in, the "
+               "results stored by the kernel into the page-locked host y (d2h bytes = those "
+               "stores); host clock around the calls")
     else:
         xcat = torch.empty(xoff[-1], device=device)
         ycat = torch.empty(yoff[-1], device=device)
