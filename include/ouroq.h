@@ -353,7 +353,10 @@ ouroq_status ouroq_matvec_q(ouroq_ctx *ctx, const ouroq_weight *w, const float *
                             float *y_host);
 /* ops::matmul_q (ops.rs:219-230): x_host [k][K] -> y_host [k][M]
  * (= the reference's y[c*out_len + r]); PTQ1_0 in matmul_tl1's K-column
- * order for every k, as matmul_q gives. */
+ * order for every k, as matmul_q gives. Both mirrors are synchronous: x is
+ * copied in, y copied back -- or, for TERNARY2 / SIGN1G128 weights at
+ * k <= 8 with a page-locked mapped y_host that covers its [k][M] floats in
+ * one allocation, stored into y_host by the kernel directly. */
 ouroq_status ouroq_matmul_q(ouroq_ctx *ctx, const ouroq_weight *w, const float *x_host, int k,
                             float *y_host);
 /* The projections of one stage call in one round trip: Stage::wm /

@@ -1300,7 +1300,11 @@ ouroq_status ouroq_gemm_f32act_noalloc(ouroq_ctx* ctx, const ouroq_weight* w, co
   return gemm_impl(ctx, w, q, s_x, B, y, nullptr, s);
 }
 
-// The host-buffer mirrors: x staged in, the product, y copied back, synchronous.
+static bool host_mapped(const void* p, size_t bytes);
+
+// The host-buffer mirrors: x staged in, the product, y copied back (or, for
+// the quantised formats at k <= 8, whose GEMV stores y with plain stores,
+// stored straight into a page-locked mapped y_host), synchronous.
 static ouroq_status host_product(ouroq_ctx* ctx, const ouroq_weight* w, const float* x_host, int k,
                                  float* y_host, Tl1Order order) {
   if (!ctx || !w) return fail(ctx, OUROQ_ERR_BAD_ARG, "null handle");
@@ -1310,15 +1314,20 @@ static ouroq_status host_product(ouroq_ctx* ctx, const ouroq_weight* w, const fl
   DeviceGuard g(ctx->device);
   ouroq_status st = grow(ctx, ctx->x_stage, ctx->x_cap, (size_t)k * w->K, "x stage");
   if (st != OUROQ_OK) return st;
-  st = grow(ctx, ctx->y_stage, ctx->y_cap, (size_t)k * w->M, "y stage");
-  if (st != OUROQ_OK) return st;
+  const bool y_direct = !is_ref_format(w->fmt) && !is_half_format(w->fmt) && k <= kGemvMaxB &&
+                        host_mapped(y_host, (size_t)k * w->M * 4);
+  if (!y_direct) {
+    st = grow(ctx, ctx->y_stage, ctx->y_cap, (size_t)k * w->M, "y stage");
+    if (st != OUROQ_OK) return st;
+  }
   cudaStream_t s = ctx->host_stream;
   CU(ctx, cudaMemcpyAsync(ctx->x_stage, x_host, (size_t)k * w->K * 4, cudaMemcpyHostToDevice, s),
      "x upload");
-  st = f32act_impl(ctx, w, ctx->x_stage, k, nullptr, 0, ctx->y_stage, s, order);
+  st = f32act_impl(ctx, w, ctx->x_stage, k, nullptr, 0, y_direct ? y_host : ctx->y_stage, s, order);
   if (st != OUROQ_OK) return st;
-  CU(ctx, cudaMemcpyAsync(y_host, ctx->y_stage, (size_t)k * w->M * 4, cudaMemcpyDeviceToHost, s),
-     "y download");
+  if (!y_direct)
+    CU(ctx, cudaMemcpyAsync(y_host, ctx->y_stage, (size_t)k * w->M * 4, cudaMemcpyDeviceToHost, s),
+       "y download");
   CU(ctx, cudaStreamSynchronize(s), "stream sync");
   return OUROQ_OK;
 }

@@ -467,6 +467,36 @@ def test_host_mirrors_matvec_matmul(ctx, oracle):
     w.free()
 
 
+@pytest.mark.parametrize("fmt,k", [("tern", 1), ("tern", 5), ("tern", 12), ("sign", 1), ("sign", 3)])
+def test_host_mirrors_page_locked_outputs(ctx, oracle, fmt, k):
+    # ouroq_matvec_q / ouroq_matmul_q through the C ABI with page-locked host
+    # buffers (as a caller that registers its buffers passes them): up to
+    # k = 8 the kernel stores into y directly, from 9 y is copied back; the
+    # NaN fill shows every element is written
+    import torch
+    M, K = 700, 2560
+    if fmt == "tern":
+        packed, ws, x = tern_case(oracle, M, K, k, seed=300 + k)
+        qr, sr = oracle.quantize_act(x)
+        yr = oracle.gemm_tern2(packed, M, K, ws, qr, sr)[1]
+        w = ctx.upload(oq.TERNARY2, packed, M, K, w_scale=ws)
+    else:
+        packed, sc, x = sign_case(oracle, M, K, k, seed=400 + k)
+        qr, sr = oracle.quantize_act(x)
+        yr = oracle.gemm_sign1(packed, sc, M, K, qr, sr)[1]
+        w = ctx.upload(oq.SIGN1G128, packed, M, K, scales=sc)
+    xh = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).pin_memory()
+    yh = torch.full((k, M), float("nan"), dtype=torch.float32).pin_memory()
+    ctx._check(ctx.lib.ouroq_matmul_q(ctx.ctx, w.handle, xh.data_ptr(), k, yh.data_ptr()))
+    assert np.array_equal(yh.numpy(), yr)
+    if k == 1:
+        yh.fill_(float("nan"))
+        ctx._check(ctx.lib.ouroq_matvec_q(ctx.ctx, w.handle, xh.data_ptr(), yh.data_ptr()))
+        assert np.array_equal(yh.numpy(), yr)
+    w.free()
+    ctx.check_device()
+
+
 @pytest.mark.parametrize("k", [1, 2, 5, 20])
 def test_host_group_call_matches_oracle(ctx, oracle, k):
     # ouroq_matmul_q_group: the projections of one layer call (shapes of the
